@@ -1,0 +1,141 @@
+/*
+ * tinyserve-b200 C ABI: quantized MoE expert hot path on B200 (sm_100a).
+ *
+ * All pointers are device pointers owned by the caller unless stated
+ * otherwise; `stream` is a cudaStream_t passed as void*.  Every function
+ * returns TSB_OK (0) or an error code and never aborts; the message of the
+ * last error on the calling thread is available from tsb_last_error().
+ * Kernels never allocate: scratch space is the caller's `workspace`.
+ *
+ * Reference interfaces replaced (tinyserve, file:line):
+ *   tsb_quant_matvec  <- torch.ops.tinyserve_ggml.ggml_mul_mat_vec
+ *                        (tinyserve/csrc/ggml_ops.cu:461-574) and the MXFP4
+ *                        batch-1 vecmat dot_scaled_vecmat
+ *                        (tinyserve/triton_dot_scaled.py:68-122)
+ *   tsb_dequant       <- gguf_dequant_torch.dequant_tensor
+ *                        (tinyserve/gguf_dequant_torch.py:35-78) and
+ *                        mxfp4.dequant_mxfp4_no_transpose (tinyserve/mxfp4.py:20-44)
+ *   tsb_moe_decode    <- the per-token expert loop of
+ *                        ExpertPipeline.execute_layer_experts[_native]
+ *                        (tinyserve/expert_pipeline.py:140-164,241-285) with
+ *                        GGMLExpertForward / the MXFP4 inline forward
+ *                        (tinyserve/ggml_forward.py:68-115,
+ *                        tinyserve/expert_forward.py:197-246) and the router
+ *                        (tinyserve/_model_hooks.py:466-473); one call per layer.
+ */
+#ifndef TSB_MOE_H
+#define TSB_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define TSB_OK 0
+#define TSB_ERR_INVALID 1     /* bad argument (shape, alignment, null pointer) */
+#define TSB_ERR_UNSUPPORTED 2 /* format / layout / size not supported */
+#define TSB_ERR_CUDA 3        /* a CUDA runtime call failed */
+#define TSB_ERR_WORKSPACE 4   /* workspace too small */
+#define TSB_ERR_DEVICE 5      /* a kernel reported an error (see tsb_read_device_error) */
+
+/* weight formats: GGUF type ids (tinyserve/gguf_reader.py:15-29) + MXFP4 */
+#define TSB_FMT_Q8_0 8
+#define TSB_FMT_Q4_K 12
+#define TSB_FMT_Q5_K 13
+#define TSB_FMT_Q6_K 14
+#define TSB_FMT_MXFP4 39 /* no ggml id in the reference; HF *_blocks / *_scales */
+
+/* element types of activations / outputs */
+#define TSB_DT_F32 0
+#define TSB_DT_BF16 1
+#define TSB_DT_F16 2
+
+/* gate/up arrangement */
+#define TSB_GU_SEPARATE 0    /* gate [I,H] and up [I,H] (GGUF stores, ggml_forward.py:103-110) */
+#define TSB_GU_INTERLEAVED 1 /* gate_up [2I,H]: row 2j = gate j, 2j+1 = up j (expert_forward.py:239-240) */
+#define TSB_GU_CHUNKED 2     /* gate_up [2I,H]: rows [0,I) gate, [I,2I) up (expert_forward.py:171-172) */
+
+/* activation between up and down */
+#define TSB_ACT_SILU 0       /* silu(gate) * up (ggml_forward.py:112) */
+#define TSB_ACT_SWIGLU_OAI 1 /* clamp-SwiGLU (expert_forward.py:185-187) */
+
+typedef struct {
+  int32_t fmt_gate_up; /* format of gate and up projections */
+  int32_t fmt_down;    /* format of the down projection */
+  int32_t hidden;      /* H */
+  int32_t inter;       /* I */
+  int32_t n_experts;   /* E */
+  int32_t top_k;       /* 1..8 */
+  int32_t gate_up_layout; /* TSB_GU_* */
+  int32_t activation;  /* TSB_ACT_* */
+  float limit;         /* SwiGLU clamp (7.0 for GPT-OSS) */
+  float alpha;         /* SwiGLU sigmoid slope (1.702 for GPT-OSS) */
+} TsbMoeSpec;
+
+/* One expert's weights (device pointers).  Weights are raw GGUF block streams
+ * (row-major flat stream, tinyserve/gguf_dequant_torch.py:72-78) or MXFP4
+ * nibble blocks [rows, cols/32, 16] with E8M0 scales [rows, cols/32]. */
+typedef struct {
+  const void* gate;        /* gate [I,H], or gate_up [2I,H] for interleaved/chunked */
+  const void* up;          /* up [I,H] for TSB_GU_SEPARATE, else NULL */
+  const void* down;        /* down [H,I] */
+  const void* gate_scales; /* MXFP4 scales of gate / gate_up, else NULL */
+  const void* up_scales;   /* MXFP4 scales of up, else NULL */
+  const void* down_scales; /* MXFP4 scales of down, else NULL */
+  const float* gate_bias;  /* optional fp32 [I] */
+  const float* up_bias;    /* optional fp32 [I] */
+  const float* down_bias;  /* optional fp32 [H] */
+} TsbExpert;
+
+/* library version (major*10000 + minor*100 + patch) */
+int tsb_version(void);
+
+/* copy the calling thread's last error message into buf; returns its length */
+int tsb_last_error(char* buf, size_t n);
+
+/* block geometry of a format: elements and bytes per block */
+int tsb_format_info(int fmt, int32_t* block_elems, int32_t* block_bytes);
+
+/* bytes of a [rows, cols] weight: nibble/block stream and (MXFP4) scales */
+int tsb_weight_bytes(int fmt, int64_t rows, int64_t cols, int64_t* data_bytes, int64_t* scale_bytes);
+
+/* Bit-exact dequantisation of a [rows, cols] weight into out (fp32 or bf16),
+ * identical to dequant_tensor / dequant_mxfp4_no_transpose. */
+int tsb_dequant(int fmt, const void* w, const void* scales, int64_t rows, int64_t cols, void* out,
+                int out_dtype, void* stream);
+
+/* y[v, :N] = W[N, K] @ x[v, :K] for v < nvec (nvec <= 8 per call is fastest;
+ * larger nvec is processed in groups).  x rows are x_stride elements apart,
+ * y rows y_stride apart.  W: 16-byte aligned.  K % 32 == 0 (Q8_0, MXFP4) or
+ * K % 32 == 0 and N*K % 256 == 0 (K-quants).  dev_err (may be NULL): device
+ * int32 the kernel sets non-zero if a bounded wait timed out. */
+int tsb_quant_matvec(int fmt, const void* w, const void* scales, int64_t N, int64_t K, const void* x,
+                     int x_dtype, int64_t nvec, int64_t x_stride, void* y, int y_dtype, int64_t y_stride,
+                     int32_t* dev_err, void* stream);
+
+/* workspace bytes tsb_moe_decode needs for T tokens */
+size_t tsb_moe_decode_workspace(const TsbMoeSpec* spec, int32_t T);
+
+/* One MoE layer for T tokens (T = 1 fused path).
+ *   experts   device array of n_experts TsbExpert
+ *   x         bf16 [T, H]
+ *   router_w  bf16 [E, H] (NULL: ids/weights are inputs)
+ *   router_b  fp32 [E] or NULL
+ *   ids       int32 [T, top_k]  (output if router_w != NULL, else input)
+ *   weights   fp32  [T, top_k]  (same)
+ *   out       bf16 [T, H] = sum_k weights[t,k] * expert_{ids[t,k]}(x[t]) */
+int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void* x, int32_t T,
+                   const void* router_w, const float* router_b, int32_t* ids, float* weights, void* out,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* read (and clear) the device error word kept in a tsb_moe_decode workspace;
+ * synchronises the stream.  *code = 0 when no kernel reported an error. */
+int tsb_read_device_error(void* workspace, int32_t* code, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TSB_MOE_H */

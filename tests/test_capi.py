@@ -1,0 +1,79 @@
+"""The C-ABI library loads and exports every symbol include/tsb_moe.h declares;
+argument checking and error reporting work without a GPU (no kernel runs)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from tinyserve_b200 import _lib
+from tinyserve_b200.formats import FORMATS, GGML_Q4_K, TSB_MXFP4
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "tsb_moe.h"
+
+
+def declared_symbols() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(tsb_\w+)\s*\(", text, re.M))
+
+
+def test_header_declares_what_python_binds():
+    assert declared_symbols() == set(_lib.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    for name in declared_symbols():
+        assert hasattr(L, name), name
+
+
+def test_version_and_format_table():
+    L = _lib.lib()
+    assert L.tsb_version() >= 100
+    for fmt, (_, bb, be) in FORMATS.items():
+        e, b = ctypes.c_int32(), ctypes.c_int32()
+        _lib.check(L.tsb_format_info(fmt, ctypes.byref(e), ctypes.byref(b)))
+        assert (e.value, b.value) == (be, bb)
+
+
+def test_weight_bytes():
+    L = _lib.lib()
+    d, s = ctypes.c_int64(), ctypes.c_int64()
+    _lib.check(L.tsb_weight_bytes(GGML_Q4_K, 2880, 2880, ctypes.byref(d), ctypes.byref(s)))
+    assert (d.value, s.value) == (4665600, 0)
+    _lib.check(L.tsb_weight_bytes(TSB_MXFP4, 5760, 2880, ctypes.byref(d), ctypes.byref(s)))
+    assert (d.value, s.value) == (8294400, 518400)
+
+
+def test_unsupported_type_message():
+    """Same wording as the reference op (ggml_ops.cu:473-476; its test matches
+    'Unsupported ggml_type')."""
+    L = _lib.lib()
+    rc = L.tsb_quant_matvec(99, None, None, 10, 32, None, 0, 1, 32, None, 0, 10, None, None)
+    assert rc == _lib.TSB_ERR_UNSUPPORTED
+    assert "Unsupported ggml_type" in _lib.last_error()
+    with pytest.raises(RuntimeError, match="Unsupported ggml_type"):
+        _lib.check(rc)
+
+
+def test_bad_shapes_rejected_before_launch():
+    L = _lib.lib()
+    assert L.tsb_quant_matvec(GGML_Q4_K, None, None, 3, 40, None, 0, 1, 40, None, 0, 3, None, None) == _lib.TSB_ERR_INVALID
+    assert L.tsb_quant_matvec(GGML_Q4_K, None, None, 3, 32, None, 0, 1, 32, None, 0, 3, None, None) == _lib.TSB_ERR_INVALID
+    # misaligned weight pointer
+    assert L.tsb_quant_matvec(GGML_Q4_K, 8, None, 16, 256, 64, 0, 1, 256, 128, 0, 16, None, None) == _lib.TSB_ERR_INVALID
+    assert "aligned" in _lib.last_error()
+
+
+def test_moe_decode_argument_checks():
+    L = _lib.lib()
+    spec = _lib.TsbMoeSpec(GGML_Q4_K, GGML_Q4_K, 2880, 2880, 32, 4, 0, 1, 7.0, 1.702)
+    ws = L.tsb_moe_decode_workspace(ctypes.byref(spec), 1)
+    assert ws >= 4 * 2880 * 4
+    bad = _lib.TsbMoeSpec(GGML_Q4_K, GGML_Q4_K, 2880, 2880, 32, 9, 0, 1, 7.0, 1.702)
+    rc = L.tsb_moe_decode(ctypes.byref(bad), 16, 16, 1, None, None, 16, 16, 16, 256, 1 << 20, None)
+    assert rc == _lib.TSB_ERR_INVALID and "top_k" in _lib.last_error()
+    rc = L.tsb_moe_decode(ctypes.byref(spec), 16, 16, 1, None, None, 16, 16, 16, 256, 16, None)
+    assert rc == _lib.TSB_ERR_WORKSPACE

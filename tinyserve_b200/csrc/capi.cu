@@ -1,0 +1,201 @@
+// extern "C" entry points of libtsb_moe.so (declared in include/tsb_moe.h).
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/tsb_moe.h"
+#include "qformats.cuh"
+#include "tsb_internal.h"
+
+namespace tsb {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const char* msg) {
+  g_last_error = msg ? msg : "";
+  return code;
+}
+
+void weight_bytes_of(int fmt, int64_t rows, int64_t cols, int64_t& data, int64_t& scales) {
+  const int64_t n = rows * cols;
+  scales = 0;
+  switch (fmt) {
+    case FMT_Q8_0: data = n / 32 * 34; break;
+    case FMT_Q4_K: data = n / 256 * 144; break;
+    case FMT_Q5_K: data = n / 256 * 176; break;
+    case FMT_Q6_K: data = n / 256 * 210; break;
+    case FMT_MXFP4: data = n / 2; scales = n / 32; break;
+    default: data = 0;
+  }
+}
+
+static bool known_fmt(int f) {
+  return f == FMT_Q8_0 || f == FMT_Q4_K || f == FMT_Q5_K || f == FMT_Q6_K || f == FMT_MXFP4;
+}
+
+static int check_shape(int fmt, int64_t rows, int64_t cols) {
+  char buf[256];
+  if (!known_fmt(fmt)) {
+    snprintf(buf, sizeof buf, "Unsupported ggml_type: %d. Supported: Q8_0(8), Q4_K(12), Q5_K(13), Q6_K(14), MXFP4(39)",
+             fmt);
+    return set_error(TSB_ERR_UNSUPPORTED, buf);
+  }
+  if (rows < 0 || cols <= 0 || cols % 32) {
+    snprintf(buf, sizeof buf, "in_features (%lld) must be a positive multiple of 32", (long long)cols);
+    return set_error(TSB_ERR_INVALID, buf);
+  }
+  const bool kq = fmt == FMT_Q4_K || fmt == FMT_Q5_K || fmt == FMT_Q6_K;
+  if (kq && (rows * cols) % 256) {
+    snprintf(buf, sizeof buf, "rows*cols (%lld) must be a multiple of 256 for K-quants", (long long)(rows * cols));
+    return set_error(TSB_ERR_INVALID, buf);
+  }
+  return TSB_OK;
+}
+
+// Workspace layout of tsb_moe_decode (offsets in bytes).
+struct WsLayout {
+  size_t err, counter, logits, act, total;
+};
+
+static WsLayout ws_layout(const TsbMoeSpec& sp, int T) {
+  WsLayout L;
+  auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
+  L.err = 0;
+  L.counter = 4;
+  L.logits = 256;
+  L.act = L.logits + al(sizeof(float) * (size_t)T * sp.n_experts);
+  L.total = L.act + al(sizeof(float) * (size_t)T * sp.top_k * sp.inter);
+  return L;
+}
+
+}  // namespace tsb
+
+using namespace tsb;
+
+extern "C" {
+
+int tsb_version(void) { return 100; }
+
+int tsb_last_error(char* buf, size_t n) {
+  const std::string& s = g_last_error;
+  if (buf && n) {
+    const size_t m = s.size() < n - 1 ? s.size() : n - 1;
+    memcpy(buf, s.data(), m);
+    buf[m] = 0;
+  }
+  return (int)s.size();
+}
+
+int tsb_format_info(int fmt, int32_t* be, int32_t* bb) {
+  int e = 0, b = 0;
+  switch (fmt) {
+    case FMT_Q8_0: e = 32; b = 34; break;
+    case FMT_Q4_K: e = 256; b = 144; break;
+    case FMT_Q5_K: e = 256; b = 176; break;
+    case FMT_Q6_K: e = 256; b = 210; break;
+    case FMT_MXFP4: e = 32; b = 17; break;
+    default: return check_shape(fmt, 0, 32);
+  }
+  if (be) *be = e;
+  if (bb) *bb = b;
+  return TSB_OK;
+}
+
+int tsb_weight_bytes(int fmt, int64_t rows, int64_t cols, int64_t* data_bytes, int64_t* scale_bytes) {
+  int rc = check_shape(fmt, rows, cols);
+  if (rc) return rc;
+  int64_t d, s;
+  weight_bytes_of(fmt, rows, cols, d, s);
+  if (data_bytes) *data_bytes = d;
+  if (scale_bytes) *scale_bytes = s;
+  return TSB_OK;
+}
+
+int tsb_dequant(int fmt, const void* w, const void* scales, int64_t rows, int64_t cols, void* out, int out_dtype,
+                void* stream) {
+  int rc = check_shape(fmt, rows, cols);
+  if (rc) return rc;
+  if (!w || !out || (fmt == FMT_MXFP4 && !scales)) return set_error(TSB_ERR_INVALID, "null pointer");
+  if (out_dtype != TSB_DT_F32 && out_dtype != TSB_DT_BF16) return set_error(TSB_ERR_INVALID, "out_dtype must be f32 or bf16");
+  return launch_dequant(fmt, w, scales, rows, cols, out, out_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int tsb_quant_matvec(int fmt, const void* w, const void* scales, int64_t N, int64_t K, const void* x, int x_dtype,
+                     int64_t nvec, int64_t x_stride, void* y, int y_dtype, int64_t y_stride, int32_t* dev_err,
+                     void* stream) {
+  int rc = check_shape(fmt, N, K);
+  if (rc) return rc;
+  if (!w || !x || !y || (fmt == FMT_MXFP4 && !scales)) return set_error(TSB_ERR_INVALID, "null pointer");
+  if (reinterpret_cast<uintptr_t>(w) & 15) return set_error(TSB_ERR_INVALID, "weight pointer must be 16-byte aligned");
+  if (x_dtype < 0 || x_dtype > 2 || y_dtype < 0 || y_dtype > 2) return set_error(TSB_ERR_INVALID, "bad dtype");
+  if (nvec <= 0 || N == 0) return TSB_OK;
+  if (x_stride < K || y_stride < N) {
+    if (nvec > 1) return set_error(TSB_ERR_INVALID, "x_stride must be >= K and y_stride >= N");
+  }
+  const int maxv = max_vectors_for((int)K);
+  if (maxv <= 0) return set_error(TSB_ERR_UNSUPPORTED, "K too large for the activation stage");
+  const size_t xes = x_dtype == TSB_DT_F32 ? 4 : 2, yes = y_dtype == TSB_DT_F32 ? 4 : 2;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int64_t v0 = 0; v0 < nvec; v0 += maxv) {
+    const int nv = (int)((nvec - v0) < maxv ? (nvec - v0) : maxv);
+    rc = launch_matvec(fmt, w, scales, N, K, static_cast<const char*>(x) + v0 * x_stride * xes, x_dtype, nv, x_stride,
+                       static_cast<char*>(y) + v0 * y_stride * yes, y_dtype, y_stride, dev_err, st);
+    if (rc) return rc;
+  }
+  return TSB_OK;
+}
+
+size_t tsb_moe_decode_workspace(const TsbMoeSpec* spec, int32_t T) {
+  if (!spec || T <= 0) return 0;
+  return ws_layout(*spec, T).total;
+}
+
+int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void* x, int32_t T, const void* router_w,
+                   const float* router_b, int32_t* ids, float* weights, void* out, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  if (!spec || !experts || !x || !ids || !weights || !out || !workspace) return set_error(TSB_ERR_INVALID, "null pointer");
+  const TsbMoeSpec& sp = *spec;
+  if (T != 1) return set_error(TSB_ERR_UNSUPPORTED, "tsb_moe_decode: only T == 1 is fused; use the grouped path for T > 1");
+  if (sp.top_k < 1 || sp.top_k > 8 || sp.top_k > sp.n_experts) return set_error(TSB_ERR_INVALID, "top_k must be in [1, min(8, E)]");
+  if (sp.n_experts < 1 || sp.n_experts > 1024) return set_error(TSB_ERR_INVALID, "n_experts must be in [1, 1024]");
+  if (sp.hidden % 32 || sp.inter % 32 || sp.hidden <= 0 || sp.inter <= 0)
+    return set_error(TSB_ERR_INVALID, "hidden and inter must be positive multiples of 32");
+  if (router_w && sp.hidden % 8) return set_error(TSB_ERR_INVALID, "hidden must be a multiple of 8 for the router");
+  if (sp.gate_up_layout < 0 || sp.gate_up_layout > 2) return set_error(TSB_ERR_INVALID, "bad gate_up_layout");
+  if (sp.activation < 0 || sp.activation > 1) return set_error(TSB_ERR_INVALID, "bad activation");
+  int rc = check_shape(sp.fmt_gate_up, sp.inter, sp.hidden);
+  if (rc) return rc;
+  rc = check_shape(sp.fmt_down, sp.hidden, sp.inter);
+  if (rc) return rc;
+  const WsLayout L = ws_layout(sp, T);
+  if (workspace_bytes < L.total) return set_error(TSB_ERR_WORKSPACE, "workspace too small");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(TSB_ERR_INVALID, "workspace must be 256-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  int32_t* err = reinterpret_cast<int32_t*>(ws + L.err);
+  float* act = reinterpret_cast<float*>(ws + L.act);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool routed = router_w != nullptr;
+  if (routed) {
+    rc = launch_router(x, router_w, router_b, sp.hidden, sp.n_experts, T, sp.top_k,
+                       reinterpret_cast<float*>(ws + L.logits), ids, weights,
+                       reinterpret_cast<unsigned*>(ws + L.counter), st);
+    if (rc) return rc;
+  }
+  rc = launch_gate_up(sp, experts, ids, x, act, err, st, routed);
+  if (rc) return rc;
+  return launch_down(sp, experts, ids, weights, act, out, err, st, true);
+}
+
+int tsb_read_device_error(void* workspace, int32_t* code, void* stream) {
+  if (!workspace || !code) return set_error(TSB_ERR_INVALID, "null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t h = 0;
+  cudaError_t e = cudaMemcpyAsync(&h, workspace, sizeof h, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && h) e = cudaMemsetAsync(workspace, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  *code = h;
+  return TSB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,454 @@
+// Decode-side kernels and launchers: plain quantised matvec, router, fused
+// gate/up + activation, fused down + weighted top-k combine.
+#include <algorithm>
+#include <cstdio>
+
+#include "../../include/tsb_moe.h"
+#include "qmv_engine.cuh"
+#include "tsb_internal.h"
+
+namespace tsb {
+
+// ------------------------------------------------------------------ config
+constexpr int kNCW = 8;
+constexpr int kNStage = 4;
+constexpr int kStageBytes = 32768;
+using SPlan = SmemPlan<kNCW, kNStage, kStageBytes>;
+
+__device__ __forceinline__ float load_act(const void* p, int dtype, int64_t i) {
+  if (dtype == TSB_DT_F32) return static_cast<const float*>(p)[i];
+  if (dtype == TSB_DT_BF16) return bf16_bits_to_f32(static_cast<const uint16_t*>(p)[i]);
+  return __half2float(static_cast<const __half*>(p)[i]);
+}
+
+__device__ __forceinline__ void store_out(void* p, int dtype, int64_t i, float v) {
+  if (dtype == TSB_DT_F32) static_cast<float*>(p)[i] = v;
+  else if (dtype == TSB_DT_BF16) static_cast<uint16_t*>(p)[i] = f32_to_bf16_bits(v);
+  else static_cast<__half*>(p)[i] = __float2half_rn(v);
+}
+
+__device__ __forceinline__ float act_fn(int act, float gate, float up, float limit, float alpha) {
+  if (act == TSB_ACT_SWIGLU_OAI) {
+    const float g = fminf(gate, limit);
+    const float u = fminf(fmaxf(up, -limit), limit);
+    return (u + 1.f) * g * (1.f / (1.f + __expf(-alpha * g)));
+  }
+  return gate / (1.f + __expf(-gate)) * up;
+}
+
+// ------------------------------------------------------------------ plans
+template <int F>
+struct PlanMatvec {
+  StageGeom geom;
+  int* err;
+  static constexpr bool kProducerWaits = false;
+  const uint8_t* w;
+  const uint8_t* s;
+  int64_t N, mat_bytes;
+  const void* x;
+  int x_dtype, nv;
+  int64_t x_stride;
+  void* y;
+  int y_dtype;
+  int64_t y_stride;
+
+  __device__ int num_vectors() const { return nv; }
+  __device__ float load_x(int v, int k) const { return load_act(x, x_dtype, v * x_stride + k); }
+  __device__ int num_blocks() const { return (int)((N + 15) / 16); }
+  __device__ int nseg(int) const { return 1; }
+  __device__ Seg seg(int rb, int) const {
+    return Seg{w, s, 16 * (int64_t)rb, (int)(N - 16 * (int64_t)rb < 16 ? N - 16 * (int64_t)rb : 16), mat_bytes};
+  }
+  __device__ void rowmap(int, int m, int& sg, int& lr) const { sg = 0; lr = m; }
+  __device__ void columns(int, int g, int t, int& vb, int& v0, int& v1, int& na, int& nb) const {
+    vb = min(g, nv - 1);
+    v0 = min(2 * t, nv - 1);
+    v1 = min(2 * t + 1, nv - 1);
+    na = nb = 0;
+  }
+  __device__ void epilogue(int rb, const float* rd, int nw, int ct) const {
+    if (ct >= 128) return;
+    const int m = ct >> 3, n = ct & 7;
+    const int64_t row = 16 * (int64_t)rb + m;
+    if (row >= N || n >= nv) return;
+    float v = 0.f;
+    for (int i = 0; i < nw; ++i) v += rd[i * 128 + ct];
+    store_out(y, y_dtype, n * y_stride + row, v);
+  }
+};
+
+template <int F>
+struct PlanGateUp {
+  StageGeom geom;
+  int* err;
+  static constexpr bool kProducerWaits = true;  // expert ids come from the router kernel
+  const TsbExpert* experts;
+  const int32_t* ids;
+  int top_k, I, layout, act;
+  float limit, alpha;
+  const uint16_t* x;  // bf16 [H]
+  float* act_out;     // [top_k, I]
+  int64_t gu_bytes, up_bytes;
+  int tpe;  // row blocks per expert
+
+  __device__ int num_vectors() const { return 1; }
+  __device__ float load_x(int, int k) const { return bf16_bits_to_f32(x[k]); }
+  __device__ int num_blocks() const { return top_k * tpe; }
+  __device__ int nseg(int) const { return layout == TSB_GU_INTERLEAVED ? 1 : 2; }
+  __device__ Seg seg(int rb, int s) const {
+    const int u = rb / tpe, j0 = 8 * (rb % tpe);
+    const int nr = min(8, I - j0);
+    const TsbExpert& E = experts[ids[u]];
+    const uint8_t* g = static_cast<const uint8_t*>(E.gate);
+    const uint8_t* gs = static_cast<const uint8_t*>(E.gate_scales);
+    if (layout == TSB_GU_INTERLEAVED) return Seg{g, gs, 2 * (int64_t)j0, 2 * nr, gu_bytes};
+    if (layout == TSB_GU_CHUNKED) return Seg{g, gs, (int64_t)(s ? I + j0 : j0), nr, gu_bytes};
+    if (s == 0) return Seg{g, gs, (int64_t)j0, nr, gu_bytes};
+    return Seg{static_cast<const uint8_t*>(E.up), static_cast<const uint8_t*>(E.up_scales), (int64_t)j0, nr,
+               up_bytes};
+  }
+  __device__ void rowmap(int, int m, int& sg, int& lr) const {
+    if (layout == TSB_GU_INTERLEAVED) {
+      sg = 0;
+      lr = m < 8 ? 2 * m : 2 * (m - 8) + 1;
+    } else {
+      sg = m >> 3;
+      lr = m & 7;
+    }
+  }
+  __device__ void columns(int, int, int, int& vb, int& v0, int& v1, int& na, int& nb) const {
+    vb = v0 = v1 = 0;
+    na = nb = 0;
+  }
+  __device__ void epilogue(int rb, const float* rd, int nw, int ct) const {
+    if (ct >= 8) return;
+    const int u = rb / tpe, j = 8 * (rb % tpe) + ct;
+    if (j >= I) return;
+    float gate = 0.f, up = 0.f;
+    for (int i = 0; i < nw; ++i) {
+      gate += rd[i * 128 + ct * 8];
+      up += rd[i * 128 + (ct + 8) * 8];
+    }
+    const TsbExpert& E = experts[ids[u]];
+    if (E.gate_bias) gate += E.gate_bias[j];
+    if (E.up_bias) up += E.up_bias[j];
+    act_out[(int64_t)u * I + j] = act_fn(act, gate, up, limit, alpha);
+  }
+};
+
+template <int F>
+struct PlanDownT1 {
+  StageGeom geom;
+  int* err;
+  // Expert ids were written two kernels back (router) or before the chain
+  // started, so weight streaming may begin before the gate/up kernel ends.
+  static constexpr bool kProducerWaits = false;
+  const TsbExpert* experts;
+  const int32_t* ids;
+  const float* wts;
+  int top_k, rpe, H, I;
+  const float* act;  // [top_k, I]
+  uint16_t* out;     // bf16 [H]
+  int64_t dn_bytes;
+
+  __device__ int num_vectors() const { return top_k; }
+  __device__ float load_x(int v, int k) const { return act[(int64_t)v * I + k]; }
+  __device__ int num_blocks() const { return (H + rpe - 1) / rpe; }
+  __device__ int nseg(int) const { return top_k; }
+  __device__ Seg seg(int rb, int s) const {
+    const TsbExpert& E = experts[ids[s]];
+    const int h0 = rpe * rb;
+    return Seg{static_cast<const uint8_t*>(E.down), static_cast<const uint8_t*>(E.down_scales), (int64_t)h0,
+               min(rpe, H - h0), dn_bytes};
+  }
+  __device__ void rowmap(int, int m, int& sg, int& lr) const {
+    sg = m / rpe;
+    lr = m % rpe;
+    if (sg >= top_k) sg = -1;
+  }
+  __device__ void columns(int, int g, int, int& vb, int& v0, int& v1, int& na, int& nb) const {
+    vb = g < top_k ? g : 0;
+    v0 = v1 = 0;
+    na = (g / rpe < top_k) ? g / rpe : -1;
+    nb = ((g + 8) / rpe < top_k) ? (g + 8) / rpe : -1;
+  }
+  __device__ void epilogue(int rb, const float* rd, int nw, int ct) const {
+    if (ct >= rpe) return;
+    const int h = rpe * rb + ct;
+    if (h >= H) return;
+    float o = 0.f;
+    for (int k = 0; k < top_k; ++k) {
+      float v = 0.f;
+      for (int i = 0; i < nw; ++i) v += rd[i * 128 + (k * rpe + ct) * 8 + k];
+      const TsbExpert& E = experts[ids[k]];
+      if (E.down_bias) v += E.down_bias[h];
+      o = fmaf(wts[k], v, o);
+    }
+    out[h] = f32_to_bf16_bits(o);
+  }
+};
+
+// ------------------------------------------------------------------ router
+// logits[t, e] = bf16(x[t] . W[e] + b[e]); the last CTA to finish selects the
+// top-k per token (ties -> lower expert id) and softmaxes the k logits
+// (tinyserve/_model_hooks.py:466-473).
+__global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ W,
+                                                     const float* __restrict__ b, int H, int E, int T, int top_k,
+                                                     float* logits, int32_t* ids, float* wts, unsigned* counter) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int p = blockIdx.x * 4 + warp;
+  if (p < E * T) {
+    const int t = p / E, e = p % E;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
+    const uint4* wr = reinterpret_cast<const uint4*>(W + (int64_t)e * H);
+    float acc = 0.f;
+    for (int i = lane; i < H / 8; i += 32) {
+      const uint4 a = xr[i], w = __ldg(wr + i);
+      const uint32_t av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc = fmaf(__uint_as_float(av[j] << 16), __uint_as_float(wv[j] << 16), acc);
+        acc = fmaf(__uint_as_float(av[j] & 0xFFFF0000u), __uint_as_float(wv[j] & 0xFFFF0000u), acc);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      if (b) acc += b[e];
+      logits[p] = bf16_bits_to_f32(f32_to_bf16_bits(acc));
+    }
+  }
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(counter, 1u) == gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int t = warp; t < T; t += 4) {
+    const float* lg = logits + (int64_t)t * E;
+    float sel[8];
+    int sid[8];
+    uint32_t taken = 0;  // bit j: expert lane + 32*j already selected (E <= 1024)
+    for (int k = 0; k < top_k; ++k) {
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int j = 0; lane + 32 * j < E; ++j) {
+        if ((taken >> j) & 1u) continue;
+        const int e = lane + 32 * j;
+        const float v = lg[e];
+        if (v > best || (v == best && e < bi)) { best = v; bi = e; }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+      }
+      sel[k] = best;
+      sid[k] = bi;
+      if (bi != 0x7fffffff && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+    }
+    if (lane == 0) {
+      float mx = sel[0], den = 0.f;
+      float ex[8];
+      for (int k = 0; k < top_k; ++k) { ex[k] = __expf(sel[k] - mx); den += ex[k]; }
+      for (int k = 0; k < top_k; ++k) {
+        ids[(int64_t)t * top_k + k] = sid[k];
+        wts[(int64_t)t * top_k + k] = ex[k] / den;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *counter = 0u;
+}
+
+// ------------------------------------------------------------------ launch helpers
+template <typename Kern, typename... Args>
+static cudaError_t launch(Kern k, int grid, int block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int F>
+static bool choose_geom(int K, int nseg, int rows_per_seg, StageGeom& G) {
+  int slot, scb;
+  G.K = K;
+  if (host_stage_bytes<F>(K, K, nseg, rows_per_seg, slot, scb) <= kStageBytes) {
+    G.KC = K;
+    G.slot = slot;
+    G.sc_base = scb;
+    return true;
+  }
+  for (int KC = (K / 256) * 256; KC >= 256; KC -= 256) {
+    if (host_stage_bytes<F>(K, KC, nseg, rows_per_seg, slot, scb) <= kStageBytes) {
+      G.KC = KC;
+      G.slot = slot;
+      G.sc_base = scb;
+      return true;
+    }
+  }
+  return false;
+}
+
+template <int F, int MODE, class P>
+static cudaError_t run_plan(const P& plan, int nblocks, int nv, cudaStream_t st, bool pdl) {
+  auto kern = qmv_kernel<F, MODE, kNCW, kNStage, kStageBytes, P>;
+  const int smem = SPlan::total(plan.geom.K, nv);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  const int grid = std::max(1, std::min(nblocks, num_sms()));
+  return launch(kern, grid, 32 * (kNCW + 1), (size_t)smem, st, pdl, plan);
+}
+
+int max_vectors_for(int K) {
+  const int avail = 227 * 1024 - SPlan::off_x;
+  const int per = SPlan::x_bytes(K, 1);
+  return std::max(0, std::min(8, avail / per));
+}
+
+// ------------------------------------------------------------------ matvec
+template <int F>
+static int matvec_t(const void* w, const void* s, int64_t N, int64_t K, const void* x, int xdt, int nv, int64_t xs,
+                    void* y, int ydt, int64_t ys, int32_t* err, cudaStream_t st) {
+  PlanMatvec<F> p{};
+  if (!choose_geom<F>((int)K, 1, 16, p.geom)) return set_error(TSB_ERR_UNSUPPORTED, "row too long for a stage");
+  p.err = err;
+  p.w = static_cast<const uint8_t*>(w);
+  p.s = static_cast<const uint8_t*>(s);
+  p.N = N;
+  int64_t db, sb;
+  weight_bytes_of(F, N, K, db, sb);
+  p.mat_bytes = db;
+  p.x = x;
+  p.x_dtype = xdt;
+  p.nv = nv;
+  p.x_stride = xs;
+  p.y = y;
+  p.y_dtype = ydt;
+  p.y_stride = ys;
+  const int nb = (int)((N + 15) / 16);
+  cudaError_t e = nv == 1 ? run_plan<F, COLS_DUP>(p, nb, nv, st, false) : run_plan<F, COLS_FULL>(p, nb, nv, st, false);
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return TSB_OK;
+}
+
+int launch_matvec(int fmt, const void* w, const void* s, int64_t N, int64_t K, const void* x, int xdt, int nv,
+                  int64_t xs, void* y, int ydt, int64_t ys, int32_t* err, cudaStream_t st) {
+  switch (fmt) {
+    case FMT_Q8_0: return matvec_t<FMT_Q8_0>(w, s, N, K, x, xdt, nv, xs, y, ydt, ys, err, st);
+    case FMT_Q4_K: return matvec_t<FMT_Q4_K>(w, s, N, K, x, xdt, nv, xs, y, ydt, ys, err, st);
+    case FMT_Q5_K: return matvec_t<FMT_Q5_K>(w, s, N, K, x, xdt, nv, xs, y, ydt, ys, err, st);
+    case FMT_Q6_K: return matvec_t<FMT_Q6_K>(w, s, N, K, x, xdt, nv, xs, y, ydt, ys, err, st);
+    case FMT_MXFP4: return matvec_t<FMT_MXFP4>(w, s, N, K, x, xdt, nv, xs, y, ydt, ys, err, st);
+  }
+  return set_error(TSB_ERR_UNSUPPORTED, "unsupported format");
+}
+
+// ------------------------------------------------------------------ MoE decode (T = 1)
+template <int F>
+static int gate_up_t(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* ids, const void* x, float* act,
+                     int32_t* err, cudaStream_t st, bool pdl) {
+  PlanGateUp<F> p{};
+  const bool inter = sp.gate_up_layout == TSB_GU_INTERLEAVED;
+  if (!choose_geom<F>(sp.hidden, inter ? 1 : 2, inter ? 16 : 8, p.geom))
+    return set_error(TSB_ERR_UNSUPPORTED, "hidden size too large for a stage");
+  p.err = err;
+  p.experts = ex;
+  p.ids = ids;
+  p.top_k = sp.top_k;
+  p.I = sp.inter;
+  p.layout = sp.gate_up_layout;
+  p.act = sp.activation;
+  p.limit = sp.limit;
+  p.alpha = sp.alpha;
+  p.x = static_cast<const uint16_t*>(x);
+  p.act_out = act;
+  int64_t db, sb;
+  weight_bytes_of(F, (sp.gate_up_layout == TSB_GU_SEPARATE ? 1 : 2) * (int64_t)sp.inter, sp.hidden, db, sb);
+  p.gu_bytes = db;
+  weight_bytes_of(F, sp.inter, sp.hidden, db, sb);
+  p.up_bytes = db;
+  p.tpe = (sp.inter + 7) / 8;
+  cudaError_t e = run_plan<F, COLS_DUP>(p, sp.top_k * p.tpe, 1, st, pdl);
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return TSB_OK;
+}
+
+template <int F>
+static int down_t(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* ids, const float* wts, const float* act,
+                  void* out, int32_t* err, cudaStream_t st, bool pdl) {
+  PlanDownT1<F> p{};
+  int kp = 1;
+  while (kp < sp.top_k) kp <<= 1;
+  p.rpe = 16 / kp;
+  if (!choose_geom<F>(sp.inter, sp.top_k, p.rpe, p.geom))
+    return set_error(TSB_ERR_UNSUPPORTED, "intermediate size too large for a stage");
+  p.err = err;
+  p.experts = ex;
+  p.ids = ids;
+  p.wts = wts;
+  p.top_k = sp.top_k;
+  p.H = sp.hidden;
+  p.I = sp.inter;
+  p.act = act;
+  p.out = static_cast<uint16_t*>(out);
+  int64_t db, sb;
+  weight_bytes_of(F, sp.hidden, sp.inter, db, sb);
+  p.dn_bytes = db;
+  cudaError_t e = run_plan<F, COLS_DIAG>(p, (sp.hidden + p.rpe - 1) / p.rpe, sp.top_k, st, pdl);
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return TSB_OK;
+}
+
+#define TSB_DISPATCH(fmt, CALL)                              \
+  switch (fmt) {                                             \
+    case FMT_Q8_0: { constexpr int F_ = FMT_Q8_0; return CALL; } \
+    case FMT_Q4_K: { constexpr int F_ = FMT_Q4_K; return CALL; } \
+    case FMT_Q5_K: { constexpr int F_ = FMT_Q5_K; return CALL; } \
+    case FMT_Q6_K: { constexpr int F_ = FMT_Q6_K; return CALL; } \
+    case FMT_MXFP4: { constexpr int F_ = FMT_MXFP4; return CALL; } \
+  }                                                          \
+  return set_error(TSB_ERR_UNSUPPORTED, "unsupported format");
+
+int launch_gate_up(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* ids, const void* x, float* act,
+                   int32_t* err, cudaStream_t st, bool pdl) {
+  TSB_DISPATCH(sp.fmt_gate_up, gate_up_t<F_>(sp, ex, ids, x, act, err, st, pdl))
+}
+
+int launch_down(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* ids, const float* wts, const float* act,
+                void* out, int32_t* err, cudaStream_t st, bool pdl) {
+  TSB_DISPATCH(sp.fmt_down, down_t<F_>(sp, ex, ids, wts, act, out, err, st, pdl))
+}
+
+int launch_router(const void* x, const void* W, const float* b, int H, int E, int T, int top_k, float* logits,
+                  int32_t* ids, float* wts, unsigned* counter, cudaStream_t st) {
+  const int grid = (E * T + 3) / 4;
+  router_kernel<<<grid, 128, 0, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(W), b, H, E, T,
+                                      top_k, logits, ids, wts, counter);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return TSB_OK;
+}
+
+}  // namespace tsb

@@ -1,0 +1,29 @@
+// Internal declarations shared by the C-ABI layer and the kernel files.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../../include/tsb_moe.h"
+
+namespace tsb {
+
+// Records msg as the calling thread's last error and returns code.
+int set_error(int code, const char* msg);
+
+// Data / scale bytes of a [rows, cols] weight (scale bytes are 0 except MXFP4).
+void weight_bytes_of(int fmt, int64_t rows, int64_t cols, int64_t& data, int64_t& scales);
+
+int max_vectors_for(int K);
+
+int launch_matvec(int fmt, const void* w, const void* s, int64_t N, int64_t K, const void* x, int xdt, int nv,
+                  int64_t xs, void* y, int ydt, int64_t ys, int32_t* err, cudaStream_t st);
+int launch_gate_up(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* ids, const void* x, float* act,
+                   int32_t* err, cudaStream_t st, bool pdl);
+int launch_down(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* ids, const float* wts, const float* act,
+                void* out, int32_t* err, cudaStream_t st, bool pdl);
+int launch_router(const void* x, const void* W, const float* b, int H, int E, int T, int top_k, float* logits,
+                  int32_t* ids, float* wts, unsigned* counter, cudaStream_t st);
+int launch_dequant(int fmt, const void* w, const void* s, int64_t rows, int64_t cols, void* out, int odt,
+                   cudaStream_t st);
+
+}  // namespace tsb

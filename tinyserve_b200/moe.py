@@ -1,0 +1,109 @@
+"""HBM-resident quantised MoE layer driven through the C-ABI.
+
+``QuantMoE`` holds one layer's expert weights in device memory (raw GGUF
+block streams or MXFP4 blocks + scales, exactly as the reference stores them,
+``tinyserve/mmap_store.py:86-91`` and ``tinyserve/expert_store.py:365-387``),
+builds the device table of expert pointers once, and runs a whole layer per
+call: router -> top-k -> gate/up -> activation -> down -> weighted combine.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .formats import TSB_MXFP4
+
+ACTIVATIONS = {"silu": _lib.ACT_SILU, "swiglu_oai": _lib.ACT_SWIGLU_OAI}
+LAYOUTS = {"separate": _lib.GU_SEPARATE, "interleaved": _lib.GU_INTERLEAVED, "chunked": _lib.GU_CHUNKED}
+
+
+@dataclass
+class ExpertWeights:
+    """Device tensors of one expert (uint8 block streams; fp32 biases)."""
+    gate: torch.Tensor                 # gate [I,H] stream, or gate_up [2I,H] for interleaved/chunked
+    down: torch.Tensor                 # down [H,I] stream
+    up: torch.Tensor | None = None     # up [I,H] stream for the separate layout
+    gate_scales: torch.Tensor | None = None
+    up_scales: torch.Tensor | None = None
+    down_scales: torch.Tensor | None = None
+    gate_bias: torch.Tensor | None = None
+    up_bias: torch.Tensor | None = None
+    down_bias: torch.Tensor | None = None
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+class QuantMoE:
+    def __init__(self, experts: list[ExpertWeights], *, fmt_gate_up: int, fmt_down: int, hidden: int, inter: int,
+                 top_k: int, router_w: torch.Tensor | None = None, router_b: torch.Tensor | None = None,
+                 gate_up_layout: str = "separate", activation: str = "swiglu_oai", limit: float = 7.0,
+                 alpha: float = 1.702):
+        if not experts:
+            raise ValueError("no experts")
+        self.device = experts[0].gate.device
+        if self.device.type != "cuda":
+            raise RuntimeError("QuantMoE needs the expert weights on a CUDA device")
+        self.experts = experts
+        self.spec = _lib.TsbMoeSpec(fmt_gate_up, fmt_down, hidden, inter, len(experts), top_k,
+                                    LAYOUTS[gate_up_layout], ACTIVATIONS[activation], limit, alpha)
+        self.hidden, self.inter, self.top_k = hidden, inter, top_k
+        self.router_w = router_w.contiguous() if router_w is not None else None
+        self.router_b = router_b.float().contiguous() if router_b is not None else None
+        table = (_lib.TsbExpert * len(experts))()
+        for i, e in enumerate(experts):
+            table[i] = _lib.TsbExpert(_p(e.gate), _p(e.up), _p(e.down), _p(e.gate_scales), _p(e.up_scales),
+                                      _p(e.down_scales), _p(e.gate_bias), _p(e.up_bias), _p(e.down_bias))
+        raw = bytes(ctypes.string_at(ctypes.addressof(table), ctypes.sizeof(table)))
+        self._table = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.device)
+        self._ws_cache: dict[int, torch.Tensor] = {}
+
+    def workspace(self, T: int) -> torch.Tensor:
+        if T not in self._ws_cache:
+            n = _lib.lib().tsb_moe_decode_workspace(ctypes.byref(self.spec), T)
+            self._ws_cache[T] = torch.zeros(n, dtype=torch.uint8, device=self.device)
+        return self._ws_cache[T]
+
+    def decode(self, x: torch.Tensor, ids: torch.Tensor | None = None, weights: torch.Tensor | None = None,
+               out: torch.Tensor | None = None):
+        """One token through the layer.  x: bf16 [1, H].  With a router, returns
+        (out, ids, weights) where ids / weights are the routing it chose; without
+        one, ``ids`` (int32 [1, k]) and ``weights`` (fp32 [1, k]) are inputs."""
+        if x.dtype != torch.bfloat16:
+            raise TypeError("x must be bfloat16")
+        x = x.contiguous()
+        T = x.shape[0] if x.dim() == 2 else 1
+        given = ids is not None
+        if not given:
+            if self.router_w is None:
+                raise ValueError("no router weights: pass ids and weights")
+            ids = torch.empty(T, self.top_k, dtype=torch.int32, device=self.device)
+            weights = torch.empty(T, self.top_k, dtype=torch.float32, device=self.device)
+        else:
+            ids = ids.to(device=self.device, dtype=torch.int32).contiguous()
+            weights = weights.to(device=self.device, dtype=torch.float32).contiguous()
+        if out is None:
+            out = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=self.device)
+        ws = self.workspace(T)
+        rc = _lib.lib().tsb_moe_decode(
+            ctypes.byref(self.spec), self._table.data_ptr(), x.data_ptr(), T,
+            None if given else _p(self.router_w), None if given else _p(self.router_b),
+            ids.data_ptr(), weights.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
+            torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc)
+        return out, ids, weights
+
+    def device_error(self, T: int = 1) -> int:
+        code = ctypes.c_int32()
+        ws = self.workspace(T)
+        _lib.check(_lib.lib().tsb_read_device_error(ws.data_ptr(), ctypes.byref(code),
+                                                    torch.cuda.current_stream(self.device).cuda_stream))
+        return code.value
+
+    @property
+    def is_mxfp4(self) -> bool:
+        return self.spec.fmt_gate_up == TSB_MXFP4
