@@ -226,3 +226,30 @@ def test_moe_decode_top8(dev):
     out, ids, wts = layer.decode(x.to(dev))
     ref = _oracle_layer(x.float().numpy(), ids.cpu().numpy()[0], wts.cpu().numpy()[0], dense)
     assert rel_l2(out.float().cpu().numpy()[0], ref) <= TOL + 4e-3
+
+
+def test_router_nan_input_gives_valid_ids(dev):
+    """NaN logits sort lowest; the router still returns in-range ids."""
+    H, I, E, k = 512, 256, 8, 4
+    layer, _, _ = _build_layer(dev, GGML_Q8_0, GGML_Q8_0, H, I, E, k, "separate", seed=5)
+    x = torch.full((1, H), float("nan"), dtype=torch.bfloat16, device=dev)
+    _, ids, _ = layer.decode(x)
+    torch.cuda.synchronize()
+    got = ids.cpu().numpy()[0]
+    assert ((got >= 0) & (got < E)).all() and len(set(got)) == k
+    assert layer.device_error() == 0
+
+
+def test_bad_expert_ids_are_reported_not_dereferenced(dev):
+    """Caller-provided ids outside [0, E) set the device error word (2) and
+    contribute nothing; valid ids still contribute."""
+    H, I, E, k = 512, 256, 4, 2
+    layer, dense, _ = _build_layer(dev, GGML_Q4_K, GGML_Q4_K, H, I, E, k, "separate", seed=6)
+    x = torch.randn(1, H, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16)
+    out, _, _ = layer.decode(x.to(dev), ids=torch.tensor([[1, 1000]], device=dev),
+                             weights=torch.tensor([[0.5, 0.5]], device=dev))
+    torch.cuda.synchronize()
+    assert layer.device_error() == 2
+    ref = _oracle_layer(x.float().numpy(), [1], [0.5], dense)
+    assert rel_l2(out.float().cpu().numpy()[0], ref) <= TOL + 4e-3
+    assert layer.device_error() == 0

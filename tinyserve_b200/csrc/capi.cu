@@ -125,10 +125,10 @@ int tsb_quant_matvec(int fmt, const void* w, const void* scales, int64_t N, int6
                      void* stream) {
   int rc = check_shape(fmt, N, K);
   if (rc) return rc;
+  if (nvec <= 0 || N == 0) return TSB_OK;
   if (!w || !x || !y || (fmt == FMT_MXFP4 && !scales)) return set_error(TSB_ERR_INVALID, "null pointer");
   if (reinterpret_cast<uintptr_t>(w) & 15) return set_error(TSB_ERR_INVALID, "weight pointer must be 16-byte aligned");
   if (x_dtype < 0 || x_dtype > 2 || y_dtype < 0 || y_dtype > 2) return set_error(TSB_ERR_INVALID, "bad dtype");
-  if (nvec <= 0 || N == 0) return TSB_OK;
   if (x_stride < K || y_stride < N) {
     if (nvec > 1) return set_error(TSB_ERR_INVALID, "x_stride must be >= K and y_stride >= N");
   }

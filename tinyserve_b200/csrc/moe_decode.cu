@@ -36,6 +36,17 @@ __device__ __forceinline__ float act_fn(int act, float gate, float up, float lim
   return gate / (1.f + __expf(-gate)) * up;
 }
 
+// Expert id from a routing table, validated: an id outside [0, E) (a corrupt
+// caller-provided table) records kDevBadPlan and yields -1 so the tile holds no rows.
+__device__ __forceinline__ int safe_expert(const int32_t* ids, int i, int E, int* err) {
+  const int e = ids[i];
+  if ((unsigned)e >= (unsigned)E) {
+    if (err) atomicExch(err, kDevBadPlan);
+    return -1;
+  }
+  return e;
+}
+
 // ------------------------------------------------------------------ plans
 template <int F>
 struct PlanMatvec {
@@ -84,6 +95,7 @@ struct PlanGateUp {
   static constexpr bool kProducerWaits = true;  // expert ids come from the router kernel
   const TsbExpert* experts;
   const int32_t* ids;
+  int n_experts;
   int top_k, I, layout, act;
   float limit, alpha;
   const uint16_t* x;  // bf16 [H]
@@ -97,8 +109,9 @@ struct PlanGateUp {
   __device__ int nseg(int) const { return layout == TSB_GU_INTERLEAVED ? 1 : 2; }
   __device__ Seg seg(int rb, int s) const {
     const int u = rb / tpe, j0 = 8 * (rb % tpe);
-    const int nr = min(8, I - j0);
-    const TsbExpert& E = experts[ids[u]];
+    const int e = safe_expert(ids, u, n_experts, err);
+    const int nr = e < 0 ? 0 : min(8, I - j0);
+    const TsbExpert& E = experts[e < 0 ? 0 : e];
     const uint8_t* g = static_cast<const uint8_t*>(E.gate);
     const uint8_t* gs = static_cast<const uint8_t*>(E.gate_scales);
     if (layout == TSB_GU_INTERLEAVED) return Seg{g, gs, 2 * (int64_t)j0, 2 * nr, gu_bytes};
@@ -129,7 +142,9 @@ struct PlanGateUp {
       gate += rd[i * 128 + ct * 8];
       up += rd[i * 128 + (ct + 8) * 8];
     }
-    const TsbExpert& E = experts[ids[u]];
+    const int e = safe_expert(ids, u, n_experts, nullptr);
+    if (e < 0) { act_out[(int64_t)u * I + j] = 0.f; return; }
+    const TsbExpert& E = experts[e];
     if (E.gate_bias) gate += E.gate_bias[j];
     if (E.up_bias) up += E.up_bias[j];
     act_out[(int64_t)u * I + j] = act_fn(act, gate, up, limit, alpha);
@@ -146,6 +161,7 @@ struct PlanDownT1 {
   const TsbExpert* experts;
   const int32_t* ids;
   const float* wts;
+  int n_experts;
   int top_k, rpe, H, I;
   const float* act;  // [top_k, I]
   uint16_t* out;     // bf16 [H]
@@ -156,10 +172,11 @@ struct PlanDownT1 {
   __device__ int num_blocks() const { return (H + rpe - 1) / rpe; }
   __device__ int nseg(int) const { return top_k; }
   __device__ Seg seg(int rb, int s) const {
-    const TsbExpert& E = experts[ids[s]];
+    const int e = safe_expert(ids, s, n_experts, err);
+    const TsbExpert& E = experts[e < 0 ? 0 : e];
     const int h0 = rpe * rb;
     return Seg{static_cast<const uint8_t*>(E.down), static_cast<const uint8_t*>(E.down_scales), (int64_t)h0,
-               min(rpe, H - h0), dn_bytes};
+               e < 0 ? 0 : min(rpe, H - h0), dn_bytes};
   }
   __device__ void rowmap(int, int m, int& sg, int& lr) const {
     sg = m / rpe;
@@ -180,7 +197,9 @@ struct PlanDownT1 {
     for (int k = 0; k < top_k; ++k) {
       float v = 0.f;
       for (int i = 0; i < nw; ++i) v += rd[i * 128 + (k * rpe + ct) * 8 + k];
-      const TsbExpert& E = experts[ids[k]];
+      const int e = safe_expert(ids, k, n_experts, nullptr);
+      if (e < 0) continue;
+      const TsbExpert& E = experts[e];
       if (E.down_bias) v += E.down_bias[h];
       o = fmaf(wts[k], v, o);
     }
@@ -236,7 +255,8 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
       for (int j = 0; lane + 32 * j < E; ++j) {
         if ((taken >> j) & 1u) continue;
         const int e = lane + 32 * j;
-        const float v = lg[e];
+        float v = lg[e];
+        if (v != v) v = -INFINITY;  // NaN sorts lowest; ties (incl. all -inf) go to the lower id
         if (v > best || (v == best && e < bi)) { best = v; bi = e; }
       }
 #pragma unroll
@@ -294,6 +314,7 @@ template <int F>
 static bool choose_geom(int K, int nseg, int rows_per_seg, StageGeom& G) {
   int slot, scb;
   G.K = K;
+  G.rps = rows_per_seg;
   if (host_stage_bytes<F>(K, K, nseg, rows_per_seg, slot, scb) <= kStageBytes) {
     G.KC = K;
     G.slot = slot;
@@ -376,6 +397,7 @@ static int gate_up_t(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* i
   p.err = err;
   p.experts = ex;
   p.ids = ids;
+  p.n_experts = sp.n_experts;
   p.top_k = sp.top_k;
   p.I = sp.inter;
   p.layout = sp.gate_up_layout;
@@ -408,6 +430,7 @@ static int down_t(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* ids,
   p.experts = ex;
   p.ids = ids;
   p.wts = wts;
+  p.n_experts = sp.n_experts;
   p.top_k = sp.top_k;
   p.H = sp.hidden;
   p.I = sp.inter;

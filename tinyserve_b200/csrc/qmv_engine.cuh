@@ -25,8 +25,8 @@
 //
 // Stage layout: segment s of a row block occupies the fixed slot
 // [s*slot, (s+1)*slot) when chunks cover whole rows (one contiguous copy per
-// segment); otherwise row r of segment s occupies [(s*16+r)*slot, ...) (one
-// copy per row).  MXFP4 scale bytes follow at sc_base.  Offsets are closed
+// segment); otherwise row r of segment s occupies [(s*rps+r)*slot, ...) (one
+// copy per row, rps = rows per segment).  MXFP4 scale bytes follow at sc_base.  Offsets are closed
 // form, so producer and consumers compute them independently.
 #pragma once
 #include "qformats.cuh"
@@ -56,6 +56,7 @@ struct StageGeom {
   int KC;       // chunk length (elements, multiple of 32)
   int slot;     // bytes per segment (whole-row chunks) or per row (partial chunks)
   int sc_base;  // MXFP4: stage offset of the scale bytes
+  int rps;      // rows per segment (at most)
 };
 
 template <int F>
@@ -82,7 +83,7 @@ __device__ __forceinline__ Piece make_piece(const Seg& sg, int si, int r, const 
   } else {
     const int64_t rr = sg.row0 + r;
     byte_range<F>(rr * G.K + k0, rr * G.K + k1, b0, b1);
-    soff = (uint32_t)((si * 16 + r) * G.slot);
+    soff = (uint32_t)((si * G.rps + r) * G.slot);
   }
   Piece p;
   p.cs = b0 & ~int64_t(15);
@@ -121,7 +122,7 @@ __device__ __forceinline__ RowInfo row_info(const Seg& sg, int si, int lr, const
   }
   if (F == FMT_MXFP4) {
     const int cb = (k1 - k0) / 32;
-    ri.soff = G.sc_base + si * (((16 * cb) + 15) & ~15) + lr * cb;
+    ri.soff = G.sc_base + si * (((G.rps * cb) + 15) & ~15) + lr * cb;
   }
   ri.valid = 1;
   return ri;
@@ -278,7 +279,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
           }
           if (F == FMT_MXFP4) {
             const int cb = (k1 - k0) / 32;
-            const int base = G.sc_base + s * (((16 * cb) + 15) & ~15);
+            const int base = G.sc_base + s * (((G.rps * cb) + 15) & ~15);
             for (int r = 0; r < sg.nrows; ++r) {
               const uint8_t* sp = sg.s + (sg.row0 + r) * (int64_t)(K / 32) + k0 / 32;
               for (int b = lane; b < cb; b += 32) stage[base + r * cb + b] = sp[b];
@@ -461,11 +462,11 @@ template <int F>
 inline int host_stage_bytes(int K, int KC, int nseg, int rows_per_seg, int& slot, int& sc_base) {
   const bool whole = (KC >= K);
   slot = host_slot_bytes<F>(K, KC, rows_per_seg);
-  sc_base = whole ? nseg * slot : nseg * 16 * slot;
+  sc_base = whole ? nseg * slot : nseg * rows_per_seg * slot;
   int total = sc_base;
   if (F == FMT_MXFP4) {
     const int cb = (whole ? K : KC) / 32;
-    total += nseg * (((16 * cb) + 15) & ~15);
+    total += nseg * (((rows_per_seg * cb) + 15) & ~15);
   }
   return total;
 }
