@@ -10,10 +10,9 @@
 namespace tsb {
 
 // ------------------------------------------------------------------ config
-constexpr int kNCW = 8;
+constexpr int kNCW = 16;
 constexpr int kNStage = 4;
 constexpr int kStageBytes = 32768;
-using SPlan = SmemPlan<kNCW, kNStage, kStageBytes>;
 
 __device__ __forceinline__ float load_act(const void* p, int dtype, int64_t i) {
   if (dtype == TSB_DT_F32) return static_cast<const float*>(p)[i];
@@ -53,18 +52,19 @@ struct PlanMatvec {
   StageGeom geom;
   int* err;
   static constexpr bool kProducerWaits = false;
+  static constexpr bool kXIndependent = true;
   const uint8_t* w;
   const uint8_t* s;
   int64_t N, mat_bytes;
   const void* x;
-  int x_dtype, nv;
+  int x_dtype, nv, x_vec_ok;
   int64_t x_stride;
   void* y;
   int y_dtype;
   int64_t y_stride;
 
   __device__ int num_vectors() const { return nv; }
-  __device__ float load_x(int v, int k) const { return load_act(x, x_dtype, v * x_stride + k); }
+  __device__ XSrc xsrc() const { return XSrc{x, x_stride, x_dtype, x_vec_ok}; }
   __device__ int num_blocks() const { return (int)((N + 15) / 16); }
   __device__ int nseg(int) const { return 1; }
   __device__ Seg seg(int rb, int) const {
@@ -77,14 +77,23 @@ struct PlanMatvec {
     v1 = min(2 * t + 1, nv - 1);
     na = nb = 0;
   }
-  __device__ void epilogue(int rb, const float* rd, int nw, int ct) const {
-    if (ct >= 128) return;
-    const int m = ct >> 3, n = ct & 7;
-    const int64_t row = 16 * (int64_t)rb + m;
-    if (row >= N || n >= nv) return;
-    float v = 0.f;
-    for (int i = 0; i < nw; ++i) v += rd[i * 128 + ct];
-    store_out(y, y_dtype, n * y_stride + row, v);
+  __device__ void epilogue(int rb, const float* rd, int nw, int lane) const {
+    if (nv == 1) {
+      const int64_t row = 16 * (int64_t)rb + lane;
+      if (lane >= 16 || row >= N) return;
+      float v = 0.f;
+      for (int i = 0; i < nw; ++i) v += rd[i * 16 + lane];
+      store_out(y, y_dtype, row, v);
+      return;
+    }
+    for (int c = lane; c < 128; c += 32) {
+      const int m = c >> 3, n = c & 7;
+      const int64_t row = 16 * (int64_t)rb + m;
+      if (row >= N || n >= nv) continue;
+      float v = 0.f;
+      for (int i = 0; i < nw; ++i) v += rd[i * 128 + c];
+      store_out(y, y_dtype, n * y_stride + row, v);
+    }
   }
 };
 
@@ -93,18 +102,20 @@ struct PlanGateUp {
   StageGeom geom;
   int* err;
   static constexpr bool kProducerWaits = true;  // expert ids come from the router kernel
+  static constexpr bool kXIndependent = true;   // x was written before the router ran
   const TsbExpert* experts;
   const int32_t* ids;
   int n_experts;
   int top_k, I, layout, act;
   float limit, alpha;
   const uint16_t* x;  // bf16 [H]
+  int x_vec_ok;
   float* act_out;     // [top_k, I]
   int64_t gu_bytes, up_bytes;
   int tpe;  // row blocks per expert
 
   __device__ int num_vectors() const { return 1; }
-  __device__ float load_x(int, int k) const { return bf16_bits_to_f32(x[k]); }
+  __device__ XSrc xsrc() const { return XSrc{x, 0, TSB_DT_BF16, x_vec_ok}; }
   __device__ int num_blocks() const { return top_k * tpe; }
   __device__ int nseg(int) const { return layout == TSB_GU_INTERLEAVED ? 1 : 2; }
   __device__ Seg seg(int rb, int s) const {
@@ -133,14 +144,14 @@ struct PlanGateUp {
     vb = v0 = v1 = 0;
     na = nb = 0;
   }
-  __device__ void epilogue(int rb, const float* rd, int nw, int ct) const {
-    if (ct >= 8) return;
-    const int u = rb / tpe, j = 8 * (rb % tpe) + ct;
+  __device__ void epilogue(int rb, const float* rd, int nw, int lane) const {
+    if (lane >= 8) return;
+    const int u = rb / tpe, j = 8 * (rb % tpe) + lane;
     if (j >= I) return;
     float gate = 0.f, up = 0.f;
     for (int i = 0; i < nw; ++i) {
-      gate += rd[i * 128 + ct * 8];
-      up += rd[i * 128 + (ct + 8) * 8];
+      gate += rd[i * 16 + lane];
+      up += rd[i * 16 + lane + 8];
     }
     const int e = safe_expert(ids, u, n_experts, nullptr);
     if (e < 0) { act_out[(int64_t)u * I + j] = 0.f; return; }
@@ -158,6 +169,7 @@ struct PlanDownT1 {
   // Expert ids were written two kernels back (router) or before the chain
   // started, so weight streaming may begin before the gate/up kernel ends.
   static constexpr bool kProducerWaits = false;
+  static constexpr bool kXIndependent = false;  // activations come from the gate/up kernel
   const TsbExpert* experts;
   const int32_t* ids;
   const float* wts;
@@ -168,7 +180,7 @@ struct PlanDownT1 {
   int64_t dn_bytes;
 
   __device__ int num_vectors() const { return top_k; }
-  __device__ float load_x(int v, int k) const { return act[(int64_t)v * I + k]; }
+  __device__ XSrc xsrc() const { return XSrc{act, I, TSB_DT_F32, 1}; }
   __device__ int num_blocks() const { return (H + rpe - 1) / rpe; }
   __device__ int nseg(int) const { return top_k; }
   __device__ Seg seg(int rb, int s) const {
@@ -189,14 +201,14 @@ struct PlanDownT1 {
     na = (g / rpe < top_k) ? g / rpe : -1;
     nb = ((g + 8) / rpe < top_k) ? (g + 8) / rpe : -1;
   }
-  __device__ void epilogue(int rb, const float* rd, int nw, int ct) const {
-    if (ct >= rpe) return;
-    const int h = rpe * rb + ct;
+  __device__ void epilogue(int rb, const float* rd, int nw, int lane) const {
+    if (lane >= rpe) return;
+    const int h = rpe * rb + lane;
     if (h >= H) return;
     float o = 0.f;
     for (int k = 0; k < top_k; ++k) {
       float v = 0.f;
-      for (int i = 0; i < nw; ++i) v += rd[i * 128 + (k * rpe + ct) * 8 + k];
+      for (int i = 0; i < nw; ++i) v += rd[i * 16 + k * rpe + lane];
       const int e = safe_expert(ids, k, n_experts, nullptr);
       if (e < 0) continue;
       const TsbExpert& E = experts[e];
@@ -208,44 +220,65 @@ struct PlanDownT1 {
 };
 
 // ------------------------------------------------------------------ router
-// logits[t, e] = bf16(x[t] . W[e] + b[e]); the last CTA to finish selects the
-// top-k per token (ties -> lower expert id) and softmaxes the k logits
-// (tinyserve/_model_hooks.py:466-473).
+// logits[t, e] = bf16(x[t] . W[e] + b[e]) with one CTA per (token, expert): the
+// four warps split H and issue all their loads before reducing, so a logit
+// costs one memory round trip.  The last CTA to finish selects the top-k per
+// token (ties -> lower expert id; NaN sorts lowest) and softmaxes the k
+// selected logits (tinyserve/_model_hooks.py:466-473).
 __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ W,
                                                      const float* __restrict__ b, int H, int E, int T, int top_k,
                                                      float* logits, int32_t* ids, float* wts, unsigned* counter) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int p = blockIdx.x * 4 + warp;
-  if (p < E * T) {
-    const int t = p / E, e = p % E;
-    const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
-    const uint4* wr = reinterpret_cast<const uint4*>(W + (int64_t)e * H);
-    float acc = 0.f;
-    for (int i = lane; i < H / 8; i += 32) {
-      const uint4 a = xr[i], w = __ldg(wr + i);
-      const uint32_t av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+  const int p = blockIdx.x;
+  const int t = p / E, e = p % E;
+  const int n8 = H / 8;
+  const int per = (n8 + 3) / 4;
+  const int i0 = warp * per, i1 = min(n8, i0 + per);
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
+  const uint4* wr = reinterpret_cast<const uint4*>(W + (int64_t)e * H);
+  constexpr int kU = 8;
+  float acc = 0.f;
+  for (int base = i0 + lane; base < i1; base += 32 * kU) {
+    uint4 a[kU], w[kU];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc = fmaf(__uint_as_float(av[j] << 16), __uint_as_float(wv[j] << 16), acc);
-        acc = fmaf(__uint_as_float(av[j] & 0xFFFF0000u), __uint_as_float(wv[j] & 0xFFFF0000u), acc);
+    for (int j = 0; j < kU; ++j) {
+      const int i = base + 32 * j;
+      if (i < i1) {
+        a[j] = xr[i];
+        w[j] = __ldg(wr + i);
+      } else {
+        a[j] = make_uint4(0, 0, 0, 0);
+        w[j] = make_uint4(0, 0, 0, 0);
       }
     }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) {
-      if (b) acc += b[e];
-      logits[p] = bf16_bits_to_f32(f32_to_bf16_bits(acc));
+    for (int j = 0; j < kU; ++j) {
+      const uint32_t av[4] = {a[j].x, a[j].y, a[j].z, a[j].w}, wv[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc = fmaf(__uint_as_float(av[q] << 16), __uint_as_float(wv[q] << 16), acc);
+        acc = fmaf(__uint_as_float(av[q] & 0xFFFF0000u), __uint_as_float(wv[q] & 0xFFFF0000u), acc);
+      }
     }
   }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ float part[4];
   __shared__ int s_last;
-  __threadfence();
+  if (lane == 0) part[warp] = acc;
   __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(counter, 1u) == gridDim.x - 1);
+  if (threadIdx.x == 0) {
+    float l = (part[0] + part[1]) + (part[2] + part[3]);
+    if (b) l += b[e];
+    logits[p] = bf16_bits_to_f32(f32_to_bf16_bits(l));
+    __threadfence();
+    s_last = (atomicAdd(counter, 1u) == gridDim.x - 1);
+  }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  for (int t = warp; t < T; t += 4) {
-    const float* lg = logits + (int64_t)t * E;
+  for (int tt = warp; tt < T; tt += 4) {
+    const float* lg = logits + (int64_t)tt * E;
     float sel[8];
     int sid[8];
     uint32_t taken = 0;  // bit j: expert lane + 32*j already selected (E <= 1024)
@@ -254,10 +287,10 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
       int bi = 0x7fffffff;
       for (int j = 0; lane + 32 * j < E; ++j) {
         if ((taken >> j) & 1u) continue;
-        const int e = lane + 32 * j;
-        float v = lg[e];
+        const int ee = lane + 32 * j;
+        float v = __ldcg(lg + ee);
         if (v != v) v = -INFINITY;  // NaN sorts lowest; ties (incl. all -inf) go to the lower id
-        if (v > best || (v == best && e < bi)) { best = v; bi = e; }
+        if (v > best || (v == best && ee < bi)) { best = v; bi = ee; }
       }
 #pragma unroll
       for (int o = 16; o; o >>= 1) {
@@ -270,12 +303,12 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
       if (bi != 0x7fffffff && (bi & 31) == lane) taken |= 1u << (bi >> 5);
     }
     if (lane == 0) {
-      float mx = sel[0], den = 0.f;
-      float ex[8];
+      const float mx = sel[0];
+      float den = 0.f, ex[8];
       for (int k = 0; k < top_k; ++k) { ex[k] = __expf(sel[k] - mx); den += ex[k]; }
       for (int k = 0; k < top_k; ++k) {
-        ids[(int64_t)t * top_k + k] = sid[k];
-        wts[(int64_t)t * top_k + k] = ex[k] / den;
+        ids[(int64_t)tt * top_k + k] = sid[k];
+        wts[(int64_t)tt * top_k + k] = ex[k] / den;
       }
     }
   }
@@ -315,14 +348,15 @@ static bool choose_geom(int K, int nseg, int rows_per_seg, StageGeom& G) {
   int slot, scb;
   G.K = K;
   G.rps = rows_per_seg;
-  if (host_stage_bytes<F>(K, K, nseg, rows_per_seg, slot, scb) <= kStageBytes) {
+  constexpr int kData = kStageBytes - 256;  // stage minus its RowInfo header
+  if (host_stage_bytes<F>(K, K, nseg, rows_per_seg, slot, scb) <= kData) {
     G.KC = K;
     G.slot = slot;
     G.sc_base = scb;
     return true;
   }
   for (int KC = (K / 256) * 256; KC >= 256; KC -= 256) {
-    if (host_stage_bytes<F>(K, KC, nseg, rows_per_seg, slot, scb) <= kStageBytes) {
+    if (host_stage_bytes<F>(K, KC, nseg, rows_per_seg, slot, scb) <= kData) {
       G.KC = KC;
       G.slot = slot;
       G.sc_base = scb;
@@ -335,7 +369,7 @@ static bool choose_geom(int K, int nseg, int rows_per_seg, StageGeom& G) {
 template <int F, int MODE, class P>
 static cudaError_t run_plan(const P& plan, int nblocks, int nv, cudaStream_t st, bool pdl) {
   auto kern = qmv_kernel<F, MODE, kNCW, kNStage, kStageBytes, P>;
-  const int smem = SPlan::total(plan.geom.K, nv);
+  const int smem = SmemPlan<kNCW, kNStage, kStageBytes, MODE, F>::total(plan.geom.K, nv);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   const int grid = std::max(1, std::min(nblocks, num_sms()));
@@ -343,8 +377,9 @@ static cudaError_t run_plan(const P& plan, int nblocks, int nv, cudaStream_t st,
 }
 
 int max_vectors_for(int K) {
-  const int avail = 227 * 1024 - SPlan::off_x;
-  const int per = SPlan::x_bytes(K, 1);
+  using SP = SmemPlan<kNCW, kNStage, kStageBytes, COLS_FULL, FMT_Q6_K>;  // largest layout
+  const int avail = 227 * 1024 - SP::off_x;
+  const int per = SP::x_bytes(K, 1);
   return std::max(0, std::min(8, avail / per));
 }
 
@@ -365,6 +400,10 @@ static int matvec_t(const void* w, const void* s, int64_t N, int64_t K, const vo
   p.x_dtype = xdt;
   p.nv = nv;
   p.x_stride = xs;
+  {
+    const size_t es = xdt == TSB_DT_F32 ? 4 : 2, need = es * 4;
+    p.x_vec_ok = (reinterpret_cast<uintptr_t>(x) % need == 0) && ((xs * es) % need == 0);
+  }
   p.y = y;
   p.y_dtype = ydt;
   p.y_stride = ys;
@@ -405,6 +444,7 @@ static int gate_up_t(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* i
   p.limit = sp.limit;
   p.alpha = sp.alpha;
   p.x = static_cast<const uint16_t*>(x);
+  p.x_vec_ok = reinterpret_cast<uintptr_t>(x) % 8 == 0;
   p.act_out = act;
   int64_t db, sb;
   weight_bytes_of(F, (sp.gate_up_layout == TSB_GU_SEPARATE ? 1 : 2) * (int64_t)sp.inter, sp.hidden, db, sb);
@@ -466,7 +506,7 @@ int launch_down(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* ids, c
 
 int launch_router(const void* x, const void* W, const float* b, int H, int E, int T, int top_k, float* logits,
                   int32_t* ids, float* wts, unsigned* counter, cudaStream_t st) {
-  const int grid = (E * T + 3) / 4;
+  const int grid = E * T;
   router_kernel<<<grid, 128, 0, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(W), b, H, E, T,
                                       top_k, logits, ids, wts, counter);
   cudaError_t e = cudaGetLastError();

@@ -29,6 +29,8 @@
 // copy per row, rps = rows per segment).  MXFP4 scale bytes follow at sc_base.  Offsets are closed
 // form, so producer and consumers compute them independently.
 #pragma once
+#include <type_traits>
+
 #include "qformats.cuh"
 
 namespace tsb {
@@ -158,80 +160,150 @@ enum ColMode : int {
 //       rounding to f16 (keeps the block maximum in (2^14, 2^15]); sx0 / sx1 =
 //       sums of the f16 values actually fed to the tensor cores, rescaled by xs
 //       (sx1 only for Q6_K, whose 16-element halves carry separate scales).
-template <int F, typename LoadFn>
-__device__ void stage_x(uint8_t* xq_raw, float4* xsx, int K, int nv, LoadFn load, int tid, int nthreads) {
-  const int U = K / 32;
-  const int lane = tid & 31, wid = tid >> 5, nw = nthreads >> 5;
+// Each thread owns 4 consecutive elements per round (8 threads per 32-block);
+// all rounds of a batch are loaded before any is processed, so the global
+// load latency is paid once per batch rather than once per block.
+struct XSrc {
+  const void* p;   // vector 0
+  int64_t stride;  // elements between vectors
+  int dtype;       // TSB_DT_F32 (0) / TSB_DT_BF16 (1) / TSB_DT_F16 (2)
+  int vec_ok;      // rows 16-B (fp32) / 8-B (16-bit) aligned: vector loads allowed
+};
+
+__device__ __forceinline__ float4 load4(const XSrc& X, int v, int k) {
+  const int64_t i = v * X.stride + k;
+  if (X.dtype == 0) {
+    if (X.vec_ok) return *reinterpret_cast<const float4*>(static_cast<const float*>(X.p) + i);
+    const float* q = static_cast<const float*>(X.p) + i;
+    return make_float4(q[0], q[1], q[2], q[3]);
+  }
+  uint32_t a, b;
+  if (X.vec_ok) {
+    const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(X.p) + i);
+    a = w.x;
+    b = w.y;
+  } else {
+    const uint16_t* q = static_cast<const uint16_t*>(X.p) + i;
+    a = q[0] | ((uint32_t)q[1] << 16);
+    b = q[2] | ((uint32_t)q[3] << 16);
+  }
+  if (X.dtype == 1)
+    return make_float4(__uint_as_float(a << 16), __uint_as_float(a & 0xFFFF0000u), __uint_as_float(b << 16),
+                       __uint_as_float(b & 0xFFFF0000u));
+  const __half2 h0 = *reinterpret_cast<__half2*>(&a), h1 = *reinterpret_cast<__half2*>(&b);
+  const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+  return make_float4(f0.x, f0.y, f1.x, f1.y);
+}
+
+template <int F>
+__device__ void stage_x(uint8_t* xq_raw, float4* xsx, int K, int nv, const XSrc& X, int tid, int nthreads) {
+  constexpr int kBatch = 8;
   __half* xq = reinterpret_cast<__half*>(xq_raw);
-  int dst = 0;
-  for (int t = 0; t < 4; ++t)
-    for (int s = 0; s < 8; ++s)
-      if (elem_order<F>(t, s) == lane) dst = 8 * t + s;
-  for (int job = wid; job < U * nv; job += nw) {
-    const int u = job / nv, v = job % nv;
-    const float x = load(v, 32 * u + lane);
-    float amax = fabsf(x);
+  const int total4 = nv * K / 4;
+  const int p = (tid & 7) * 4;  // position of this thread's first element in its block
+  int dst[4];
+  for (int i = 0; i < 4; ++i)
+    for (int t = 0; t < 4; ++t)
+      for (int s = 0; s < 8; ++s)
+        if (elem_order<F>(t, s) == p + i) dst[i] = 8 * t + s;
+  for (int r0 = 0; r0 * nthreads < total4; r0 += kBatch) {
+    float4 v[kBatch];
 #pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    int e = 0;
-    if (amax > 0.f && amax <= 3.0e38f) {
-      int ex;
-      frexpf(amax, &ex);
-      e = ex - 15;
+    for (int j = 0; j < kBatch; ++j) {
+      const int f = (r0 + j) * nthreads + tid;
+      v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (f < total4) v[j] = load4(X, (4 * f) / K, (4 * f) % K);
     }
-    const __half h = __float2half_rn(ldexpf(x, -e));
-    const float hv = __half2float(h);
-    xq[(size_t)(u * nv + v) * 32 + dst] = h;
-    float s_all = hv, s_lo = (lane < 16) ? hv : 0.f;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      s_all += __shfl_xor_sync(0xffffffffu, s_all, o);
-      s_lo += __shfl_xor_sync(0xffffffffu, s_lo, o);
-    }
-    if (lane == 0) {
-      const float xs = ldexpf(1.f, e);
-      if (F == FMT_Q6_K)
-        xsx[u * nv + v] = make_float4(xs, s_lo * xs, (s_all - s_lo) * xs, 0.f);
-      else
-        xsx[u * nv + v] = make_float4(xs, s_all * xs, 0.f, 0.f);
+    for (int j = 0; j < kBatch; ++j) {
+      if ((r0 + j) * nthreads >= total4) break;  // uniform across the CTA
+      const int f = (r0 + j) * nthreads + tid;
+      float amax = fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w)));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      int e = 0;
+      if (amax > 0.f && amax <= 3.0e38f) {
+        int ex;
+        frexpf(amax, &ex);
+        e = ex - 15;
+      }
+      const float xv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+      float hs = 0.f;
+      __half hh[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        hh[i] = __float2half_rn(ldexpf(xv[i], -e));
+        hs += __half2float(hh[i]);
+      }
+      float s_all = hs, s_lo = (p < 16) ? hs : 0.f;
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        s_all += __shfl_xor_sync(0xffffffffu, s_all, o);
+        s_lo += __shfl_xor_sync(0xffffffffu, s_lo, o);
+      }
+      if (f < total4) {
+        const int vv = (4 * f) / K, u = ((4 * f) % K) / 32;
+        __half* blk = xq + (size_t)(u * nv + vv) * 32;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) blk[dst[i]] = hh[i];
+        if (p == 0) {
+          const float xs = ldexpf(1.f, e);
+          if (F == FMT_Q6_K)
+            xsx[u * nv + vv] = make_float4(xs, s_lo * xs, (s_all - s_lo) * xs, 0.f);
+          else
+            xsx[u * nv + vv] = make_float4(xs, s_all * xs, 0.f, 0.f);
+        }
+      }
     }
   }
 }
 
 // Shared-memory map of one CTA.
-template <int NCW, int NSTAGE, int STAGE_BYTES>
+//   bars     full[NSTAGE], empty[NSTAGE] mbarriers
+//   cnt      per-stage counters of warps done with a row block (last one runs the epilogue)
+//   red      per-stage partial sums: [NSTAGE][NCW][16] (one column) or [..][128] (8 columns)
+//   coef     per-warp fold coefficients of the current coefficient chunk
+//   stages   NSTAGE x STAGE_BYTES; each stage starts with a 256-B header of 16 RowInfo
+//   x        staged activation vectors
+template <int NCW, int NSTAGE, int STAGE_BYTES, int MODE, int F>
 struct SmemPlan {
   static constexpr int kCoefCh = 8;  // steps per coefficient chunk
-  static constexpr int kRed = 2 * NCW * 128 * 4;
-  static constexpr int kCoef = NCW * 16 * kCoefCh * 16;
-  static constexpr int kRinfo = NCW * 16 * 16;
+  static constexpr int kCoefW = (F == FMT_Q6_K) ? 16 : 8;  // bytes per coefficient entry
+  static constexpr int kRedW = (MODE == COLS_FULL) ? 128 : 16;
+  static constexpr int kRed = NSTAGE * NCW * kRedW * 4;
+  static constexpr int kCoef = NCW * 16 * kCoefCh * kCoefW;
+  static constexpr int kHdr = 256;
   static constexpr int off_bars = 0;
-  static constexpr int off_red = 128;
+  static constexpr int off_cnt = 128;
+  static constexpr int off_red = 256;
   static constexpr int off_coef = off_red + kRed;
-  static constexpr int off_rinfo = off_coef + kCoef;
-  static constexpr int off_stage = ((off_rinfo + kRinfo + 127) / 128) * 128;
+  static constexpr int off_stage = ((off_coef + kCoef + 127) / 128) * 128;
   static constexpr int off_x = off_stage + NSTAGE * STAGE_BYTES;
   static __host__ __device__ constexpr int x_bytes(int K, int nv) { return (K / 32) * nv * (64 + 16); }
   static __host__ __device__ constexpr int total(int K, int nv) { return off_x + x_bytes(K, nv); }
 };
 
 // Plan interface (all device-side, const):
-//   int K; StageGeom geom; int* err;
-//   static constexpr bool kProducerWaits;   tiles depend on the previous kernel's output
+//   StageGeom geom; int* err;
+//   static constexpr bool kProducerWaits;   row blocks depend on the previous kernel's output
+//   static constexpr bool kXIndependent;    activations were written before the previous kernel
 //   int num_vectors() const;                activation vectors (<= 8)
-//   float load_x(int v, int k) const;       activation v, element k (fp32)
+//   XSrc xsrc() const;                      where the activation vectors live
 //   int num_blocks() const;                 row blocks
 //   int nseg(int rb) const;  Seg seg(int rb, int s) const;
 //   void rowmap(int rb, int m, int& s, int& lr) const;   A-row m -> (segment, row)  (s<0: none)
 //   void columns(int rb, int g, int t, int& vb, int& v0, int& v1, int& na, int& nb) const;
-//   void epilogue(int rb, const float* red, int nwarps, int ct) const;
-//       ct = consumer thread (0 .. 32*NCW-1); red[w*128 + m*8 + n] = warp w's partial sum.
+//   void epilogue(int rb, const float* red, int nwarps, int lane) const;
+//       run by the last warp to finish the row block; red[w*W + i] = warp w's partial
+//       sums, W = 16 (i = A-row, one column) or 128 (i = row*8 + column).
 template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, class P>
 __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
-  using SP = SmemPlan<NCW, NSTAGE, STAGE_BYTES>;
+  using SP = SmemPlan<NCW, NSTAGE, STAGE_BYTES, MODE, F>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + SP::off_bars);
   uint64_t* empty = full + NSTAGE;
+  int* cnt = reinterpret_cast<int*>(smem + SP::off_cnt);
   float* red = reinterpret_cast<float*>(smem + SP::off_red);
   uint8_t* stages = smem + SP::off_stage;
 
@@ -248,6 +320,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
     for (int s = 0; s < NSTAGE; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NCW);
+      cnt[s] = 0;
     }
     fence_barrier_init();
   }
@@ -260,6 +333,12 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
     int it = 0;
     for (int rb = blockIdx.x; rb < nblocks; rb += gridDim.x) {
       const int ns = plan.nseg(rb);
+      int rs = -1, rl = 0;
+      Seg rseg{};
+      if (lane < 16) {
+        plan.rowmap(rb, lane, rs, rl);
+        if (rs >= 0) rseg = plan.seg(rb, rs);
+      }
       for (int kc = 0; kc < nkc; ++kc, ++it) {
         const int k0 = kc * KC, k1 = min(K, k0 + KC);
         const bool whole = (k0 == 0 && k1 == K);
@@ -267,36 +346,45 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
         const uint32_t ph = ((it / NSTAGE) & 1) ^ 1;
         if (!mbar_wait(&empty[st], ph, err)) return;
         uint8_t* stage = stages + st * STAGE_BYTES;
-        uint32_t total = 0;
-        // pass 1: plain-load ragged ends and scales, count bulk bytes
-        for (int s = 0; s < ns; ++s) {
+        uint8_t* data = stage + SP::kHdr;
+        if (lane < 16) {
+          const RowInfo ri = row_info<F>(rseg, rs, rl, G, k0, k1);
+          reinterpret_cast<int4*>(stage)[lane] = make_int4(ri.off, ri.sub0, ri.soff, ri.valid);
+        }
+        // pieces: one per segment (whole rows) or one per row; lane i owns pieces i, i+32, ...
+        const int npc = whole ? ns : ns * G.rps;
+        uint32_t mybulk = 0;
+        for (int i = lane; i < npc; i += 32) {
+          const int s = whole ? i : i / G.rps, r = whole ? -1 : i % G.rps;
           const Seg sg = plan.seg(rb, s);
-          const int npr = whole ? 1 : sg.nrows;
-          for (int r = 0; r < npr; ++r) {
-            const Piece p = make_piece<F>(sg, s, whole ? -1 : r, G, k0, k1);
-            total += p.bulk;
-            for (int64_t b = p.cs + p.bulk + lane; b < p.end; b += 32) stage[p.soff + (b - p.cs)] = sg.w[b];
-          }
-          if (F == FMT_MXFP4) {
-            const int cb = (k1 - k0) / 32;
+          if (!whole && r >= sg.nrows) continue;
+          const Piece p = make_piece<F>(sg, s, r, G, k0, k1);
+          mybulk += p.bulk;
+          for (int64_t b = p.cs + p.bulk; b < p.end; ++b) data[p.soff + (b - p.cs)] = sg.w[b];
+        }
+        if (F == FMT_MXFP4) {
+          const int cb = (k1 - k0) / 32;
+          for (int s = 0; s < ns; ++s) {
+            const Seg sg = plan.seg(rb, s);
             const int base = G.sc_base + s * (((G.rps * cb) + 15) & ~15);
-            for (int r = 0; r < sg.nrows; ++r) {
-              const uint8_t* sp = sg.s + (sg.row0 + r) * (int64_t)(K / 32) + k0 / 32;
-              for (int b = lane; b < cb; b += 32) stage[base + r * cb + b] = sp[b];
+            for (int i = lane; i < sg.nrows * cb; i += 32) {
+              const int r = i / cb, b = i % cb;
+              data[base + i] = sg.s[(sg.row0 + r) * (int64_t)(K / 32) + k0 / 32 + b];
             }
           }
         }
+        uint32_t total = mybulk;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full[st], total);
-          for (int s = 0; s < ns; ++s) {
-            const Seg sg = plan.seg(rb, s);
-            const int npr = whole ? 1 : sg.nrows;
-            for (int r = 0; r < npr; ++r) {
-              const Piece p = make_piece<F>(sg, s, whole ? -1 : r, G, k0, k1);
-              if (p.bulk) bulk_g2s(stage + p.soff, sg.w + p.cs, p.bulk, &full[st]);
-            }
-          }
+        if (lane == 0) mbar_arrive_expect_tx(&full[st], total);
+        __syncwarp();
+        for (int i = lane; i < npc; i += 32) {
+          const int s = whole ? i : i / G.rps, r = whole ? -1 : i % G.rps;
+          const Seg sg = plan.seg(rb, s);
+          if (!whole && r >= sg.nrows) continue;
+          const Piece p = make_piece<F>(sg, s, r, G, k0, k1);
+          if (p.bulk) bulk_g2s(data + p.soff, sg.w + p.cs, p.bulk, &full[st]);
         }
       }
     }
@@ -305,65 +393,50 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
 
   // ------------------------------ consumers ------------------------------
   const int ctid = tid - 32;
-  pdl_wait();
-  stage_x<F>(xq_raw, xsx, K, nv, [&](int v, int k) { return plan.load_x(v, k); }, ctid, 32 * NCW);
+  if (!P::kXIndependent) pdl_wait();
+  stage_x<F>(xq_raw, xsx, K, nv, plan.xsrc(), ctid, 32 * NCW);
   named_bar_sync(1, 32 * NCW);
+  if (P::kXIndependent) pdl_wait();
   pdl_launch_dependents();
 
   const int cw = warp - 1;
   const int g = lane >> 2, t = lane & 3;
-  float4* coef = reinterpret_cast<float4*>(smem + SP::off_coef) + cw * 16 * SP::kCoefCh;
-  int4* rinfo = reinterpret_cast<int4*>(smem + SP::off_rinfo) + cw * 16;
+  uint8_t* coef = smem + SP::off_coef + cw * 16 * SP::kCoefCh * SP::kCoefW;
   const uint4* xq = reinterpret_cast<const uint4*>(xq_raw);
   constexpr bool kKQ = (F == FMT_Q4_K || F == FMT_Q5_K || F == FMT_Q6_K);
 
-  int it = 0, blk = 0;
-  for (int rb = blockIdx.x; rb < nblocks; rb += gridDim.x, ++blk) {
+  int it = 0;
+  for (int rb = blockIdx.x; rb < nblocks; rb += gridDim.x) {
     int vb, v0, v1, n_a, n_b;
     plan.columns(rb, g, t, vb, v0, v1, n_a, n_b);
-    // this lane's two rows (A rows g and g+8) and their segments
-    int sa, la_r, sb, lb_r;
-    plan.rowmap(rb, g, sa, la_r);
-    plan.rowmap(rb, g + 8, sb, lb_r);
-    Seg sega{}, segb{};
-    if (sa >= 0) sega = plan.seg(rb, sa);
-    if (sb >= 0) segb = plan.seg(rb, sb);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 
     for (int kc = 0; kc < nkc; ++kc, ++it) {
       const int k0 = kc * KC, k1 = min(K, k0 + KC);
       const int st = it % NSTAGE;
       const uint32_t ph = (it / NSTAGE) & 1;
-      const RowInfo r0 = row_info<F>(sega, sa, la_r, G, k0, k1);
-      const RowInfo r1 = row_info<F>(segb, sb, lb_r, G, k0, k1);
-      if (kKQ) {
-        // row table for the coefficient pass: lane m < 16 fills entry m
-        __syncwarp();
-        if (lane < 16) {
-          int s_, l_;
-          plan.rowmap(rb, lane, s_, l_);
-          Seg sg{};
-          if (s_ >= 0) sg = plan.seg(rb, s_);
-          const RowInfo ri = row_info<F>(sg, s_, l_, G, k0, k1);
-          rinfo[lane] = make_int4(ri.off, ri.sub0, ri.soff, ri.valid);
-        }
-      }
       const int Uc = (k1 - k0) / 32, ub = k0 / 32;
       const int u_beg = (cw * Uc) / NCW, u_end = ((cw + 1) * Uc) / NCW;
       if (!mbar_wait(&full[st], ph, err)) return;
       const uint8_t* stage = stages + st * STAGE_BYTES;
+      const uint8_t* data = stage + SP::kHdr;
+      const int4* hdr = reinterpret_cast<const int4*>(stage);
+      const int4 h0 = hdr[g], h1 = hdr[g + 8];
+      const RowInfo r0{h0.x, h0.y, h0.z, h0.w}, r1{h1.x, h1.y, h1.z, h1.w};
 
       for (int uc = u_beg; uc < u_end; uc += SP::kCoefCh) {
         const int nst = min(SP::kCoefCh, u_end - uc);
         if (kKQ) {
           __syncwarp();
-          for (int e = lane; e < 16 * nst; e += 32) {
-            const int m = e / nst, s = e % nst;
-            const int4 q = rinfo[m];
+          for (int e = lane; e < 16 * SP::kCoefCh; e += 32) {
+            const int m = e / SP::kCoefCh, s = e % SP::kCoefCh;
+            if (s >= nst) continue;
+            const int4 q = hdr[m];
             const RowInfo ri{q.x, q.y, q.z, q.w};
             float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (ri.valid) c = fold_coef<F>(row_loc<F>(stage, ri, uc + s));
-            coef[m * SP::kCoefCh + s] = c;
+            if (ri.valid) c = fold_coef<F>(row_loc<F>(data, ri, uc + s));
+            if (F == FMT_Q6_K) reinterpret_cast<float4*>(coef)[m * SP::kCoefCh + s] = c;
+            else reinterpret_cast<float2*>(coef)[m * SP::kCoefCh + s] = make_float2(c.x, c.y);
           }
           __syncwarp();
         }
@@ -375,8 +448,8 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
           uint32_t pa[4] = {kMagic, kMagic, kMagic, kMagic};
           uint32_t pb[4] = {kMagic, kMagic, kMagic, kMagic};
           RowLoc la{}, lb{};
-          if (r0.valid) { la = row_loc<F>(stage, r0, u); decode_a<F>(la, t, pa); }
-          if (r1.valid) { lb = row_loc<F>(stage, r1, u); decode_a<F>(lb, t, pb); }
+          if (r0.valid) { la = row_loc<F>(data, r0, u); decode_a<F>(la, t, pa); }
+          if (r1.valid) { lb = row_loc<F>(data, r1, u); decode_a<F>(lb, t, pb); }
           if (F == FMT_MXFP4) {
             if (!r0.valid) pa[0] = pa[1] = pa[2] = pa[3] = 0u;
             if (!r1.valid) pb[0] = pb[1] = pb[2] = pb[3] = 0u;
@@ -390,8 +463,15 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
           else mma_f16(c1, a2, b.z, b.w);
           float4 ka, kb;
           if (kKQ) {
-            ka = coef[g * SP::kCoefCh + s];
-            kb = coef[(g + 8) * SP::kCoefCh + s];
+            if (F == FMT_Q6_K) {
+              ka = reinterpret_cast<const float4*>(coef)[g * SP::kCoefCh + s];
+              kb = reinterpret_cast<const float4*>(coef)[(g + 8) * SP::kCoefCh + s];
+            } else {
+              const float2 qa = reinterpret_cast<const float2*>(coef)[g * SP::kCoefCh + s];
+              const float2 qb = reinterpret_cast<const float2*>(coef)[(g + 8) * SP::kCoefCh + s];
+              ka = make_float4(qa.x, qa.y, 0.f, 0.f);
+              kb = make_float4(qb.x, qb.y, 0.f, 0.f);
+            }
           } else {
             ka = r0.valid ? fold_coef<F>(la) : make_float4(0.f, 0.f, 0.f, 0.f);
             kb = r1.valid ? fold_coef<F>(lb) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -425,28 +505,51 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
           }
         }
       }
+      if (kc + 1 < nkc) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        continue;
+      }
+      // Last chunk of the row block: publish partials; the last warp to do so runs
+      // the epilogue (fixed summation order, so results are deterministic).  The
+      // stage is released only after that, so the partial-sum slot `st` cannot be
+      // reused before the epilogue has read it.
+      float* rd = red + st * (NCW * SP::kRedW);
+      float* mine = rd + cw * SP::kRedW;
+      if (MODE == COLS_FULL) {
+        mine[g * 8 + 2 * t] = acc[0];
+        mine[g * 8 + 2 * t + 1] = acc[1];
+        mine[(g + 8) * 8 + 2 * t] = acc[2];
+        mine[(g + 8) * 8 + 2 * t + 1] = acc[3];
+      } else if (MODE == COLS_DUP) {
+        if (t == 0) {
+          mine[g] = acc[0];
+          mine[g + 8] = acc[2];
+        }
+      } else {
+        if (n_a >= 0 && (n_a >> 1) == t) mine[g] = acc[0];
+        if (n_b >= 0 && (n_b >> 1) == t) mine[g + 8] = acc[2];
+      }
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        __threadfence_block();
+        last = (atomicAdd(&cnt[st], 1) == NCW - 1);
+        __threadfence_block();
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        plan.epilogue(rb, rd, NCW, lane);
+        __syncwarp();
+        if (lane == 0) cnt[st] = 0;
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
-
-    // cross-warp reduction of this row block
-    float* rd = red + (blk & 1) * (NCW * 128);
-    float* mine = rd + cw * 128;
-    if (MODE == COLS_DIAG) {
-      if (n_a >= 0 && (n_a >> 1) == t) mine[g * 8 + n_a] = acc[0];
-      if (n_b >= 0 && (n_b >> 1) == t) mine[(g + 8) * 8 + n_b] = acc[2];
-    } else {
-      mine[g * 8 + 2 * t] = acc[0];
-      mine[g * 8 + 2 * t + 1] = acc[1];
-      mine[(g + 8) * 8 + 2 * t] = acc[2];
-      mine[(g + 8) * 8 + 2 * t + 1] = acc[3];
-    }
-    named_bar_sync(1, 32 * NCW);
-    plan.epilogue(rb, rd, NCW, ctid);
   }
 }
 
-// Host-side geometry: stage slot size for a given chunk.
+// Host-side geometry (excluding the 256-B RowInfo header): stage slot size for a given chunk.
 template <int F>
 inline int host_slot_bytes(int K, int KC, int rows_per_seg) {
   using T = FmtT<F>;
