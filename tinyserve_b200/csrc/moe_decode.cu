@@ -67,7 +67,8 @@ struct PlanMatvec {
   __device__ XSrc xsrc() const { return XSrc{x, x_stride, x_dtype, x_vec_ok}; }
   __device__ int num_blocks() const { return (int)((N + 15) / 16); }
   __device__ int nseg(int) const { return 1; }
-  __device__ Seg seg(int rb, int) const {
+  __device__ void fill_cache(SlotCache*, int) const {}
+  __device__ Seg seg(const SlotCache*, int rb, int) const {
     return Seg{w, s, 16 * (int64_t)rb, (int)(N - 16 * (int64_t)rb < 16 ? N - 16 * (int64_t)rb : 16), mat_bytes};
   }
   __device__ void rowmap(int, int m, int& sg, int& lr) const { sg = 0; lr = m; }
@@ -77,7 +78,7 @@ struct PlanMatvec {
     v1 = min(2 * t + 1, nv - 1);
     na = nb = 0;
   }
-  __device__ void epilogue(int rb, const float* rd, int nw, int lane) const {
+  __device__ void epilogue(const SlotCache*, int rb, const float* rd, int nw, int lane) const {
     if (nv == 1) {
       const int64_t row = 16 * (int64_t)rb + lane;
       if (lane >= 16 || row >= N) return;
@@ -118,18 +119,29 @@ struct PlanGateUp {
   __device__ XSrc xsrc() const { return XSrc{x, 0, TSB_DT_BF16, x_vec_ok}; }
   __device__ int num_blocks() const { return top_k * tpe; }
   __device__ int nseg(int) const { return layout == TSB_GU_INTERLEAVED ? 1 : 2; }
-  __device__ Seg seg(int rb, int s) const {
-    const int u = rb / tpe, j0 = 8 * (rb % tpe);
-    const int e = safe_expert(ids, u, n_experts, err);
-    const int nr = e < 0 ? 0 : min(8, I - j0);
+  __device__ void fill_cache(SlotCache* c, int lane) const {
+    if (lane >= top_k) return;
+    const int e = safe_expert(ids, lane, n_experts, err);
     const TsbExpert& E = experts[e < 0 ? 0 : e];
-    const uint8_t* g = static_cast<const uint8_t*>(E.gate);
-    const uint8_t* gs = static_cast<const uint8_t*>(E.gate_scales);
-    if (layout == TSB_GU_INTERLEAVED) return Seg{g, gs, 2 * (int64_t)j0, 2 * nr, gu_bytes};
-    if (layout == TSB_GU_CHUNKED) return Seg{g, gs, (int64_t)(s ? I + j0 : j0), nr, gu_bytes};
-    if (s == 0) return Seg{g, gs, (int64_t)j0, nr, gu_bytes};
-    return Seg{static_cast<const uint8_t*>(E.up), static_cast<const uint8_t*>(E.up_scales), (int64_t)j0, nr,
-               up_bytes};
+    SlotCache s;
+    s.w[0] = static_cast<const uint8_t*>(E.gate);
+    s.w[1] = static_cast<const uint8_t*>(E.up);
+    s.s[0] = static_cast<const uint8_t*>(E.gate_scales);
+    s.s[1] = static_cast<const uint8_t*>(E.up_scales);
+    s.b[0] = E.gate_bias;
+    s.b[1] = E.up_bias;
+    s.e = e;
+    s.pad = 0;
+    c[lane] = s;
+  }
+  __device__ Seg seg(const SlotCache* c, int rb, int s) const {
+    const int u = rb / tpe, j0 = 8 * (rb % tpe);
+    const SlotCache& C = c[u];
+    const int nr = C.e < 0 ? 0 : min(8, I - j0);
+    if (layout == TSB_GU_INTERLEAVED) return Seg{C.w[0], C.s[0], 2 * (int64_t)j0, 2 * nr, gu_bytes};
+    if (layout == TSB_GU_CHUNKED) return Seg{C.w[0], C.s[0], (int64_t)(s ? I + j0 : j0), nr, gu_bytes};
+    if (s == 0) return Seg{C.w[0], C.s[0], (int64_t)j0, nr, gu_bytes};
+    return Seg{C.w[1], C.s[1], (int64_t)j0, nr, up_bytes};
   }
   __device__ void rowmap(int, int m, int& sg, int& lr) const {
     if (layout == TSB_GU_INTERLEAVED) {
@@ -144,7 +156,7 @@ struct PlanGateUp {
     vb = v0 = v1 = 0;
     na = nb = 0;
   }
-  __device__ void epilogue(int rb, const float* rd, int nw, int lane) const {
+  __device__ void epilogue(const SlotCache* c, int rb, const float* rd, int nw, int lane) const {
     if (lane >= 8) return;
     const int u = rb / tpe, j = 8 * (rb % tpe) + lane;
     if (j >= I) return;
@@ -153,11 +165,10 @@ struct PlanGateUp {
       gate += rd[i * 16 + lane];
       up += rd[i * 16 + lane + 8];
     }
-    const int e = safe_expert(ids, u, n_experts, nullptr);
-    if (e < 0) { act_out[(int64_t)u * I + j] = 0.f; return; }
-    const TsbExpert& E = experts[e];
-    if (E.gate_bias) gate += E.gate_bias[j];
-    if (E.up_bias) up += E.up_bias[j];
+    const SlotCache& C = c[u];
+    if (C.e < 0) { act_out[(int64_t)u * I + j] = 0.f; return; }
+    if (C.b[0]) gate += C.b[0][j];
+    if (C.b[1]) up += C.b[1][j];
     act_out[(int64_t)u * I + j] = act_fn(act, gate, up, limit, alpha);
   }
 };
@@ -183,12 +194,25 @@ struct PlanDownT1 {
   __device__ XSrc xsrc() const { return XSrc{act, I, TSB_DT_F32, 1}; }
   __device__ int num_blocks() const { return (H + rpe - 1) / rpe; }
   __device__ int nseg(int) const { return top_k; }
-  __device__ Seg seg(int rb, int s) const {
-    const int e = safe_expert(ids, s, n_experts, err);
+  __device__ void fill_cache(SlotCache* c, int lane) const {
+    if (lane >= top_k) return;
+    const int e = safe_expert(ids, lane, n_experts, err);
     const TsbExpert& E = experts[e < 0 ? 0 : e];
+    SlotCache s;
+    s.w[0] = static_cast<const uint8_t*>(E.down);
+    s.w[1] = nullptr;
+    s.s[0] = static_cast<const uint8_t*>(E.down_scales);
+    s.s[1] = nullptr;
+    s.b[0] = E.down_bias;
+    s.b[1] = nullptr;
+    s.e = e;
+    s.pad = 0;
+    c[lane] = s;
+  }
+  __device__ Seg seg(const SlotCache* c, int rb, int s) const {
+    const SlotCache& C = c[s];
     const int h0 = rpe * rb;
-    return Seg{static_cast<const uint8_t*>(E.down), static_cast<const uint8_t*>(E.down_scales), (int64_t)h0,
-               e < 0 ? 0 : min(rpe, H - h0), dn_bytes};
+    return Seg{C.w[0], C.s[0], (int64_t)h0, C.e < 0 ? 0 : min(rpe, H - h0), dn_bytes};
   }
   __device__ void rowmap(int, int m, int& sg, int& lr) const {
     sg = m / rpe;
@@ -201,7 +225,7 @@ struct PlanDownT1 {
     na = (g / rpe < top_k) ? g / rpe : -1;
     nb = ((g + 8) / rpe < top_k) ? (g + 8) / rpe : -1;
   }
-  __device__ void epilogue(int rb, const float* rd, int nw, int lane) const {
+  __device__ void epilogue(const SlotCache* c, int rb, const float* rd, int nw, int lane) const {
     if (lane >= rpe) return;
     const int h = rpe * rb + lane;
     if (h >= H) return;
@@ -209,10 +233,9 @@ struct PlanDownT1 {
     for (int k = 0; k < top_k; ++k) {
       float v = 0.f;
       for (int i = 0; i < nw; ++i) v += rd[i * 16 + k * rpe + lane];
-      const int e = safe_expert(ids, k, n_experts, nullptr);
-      if (e < 0) continue;
-      const TsbExpert& E = experts[e];
-      if (E.down_bias) v += E.down_bias[h];
+      const SlotCache& C = c[k];
+      if (C.e < 0) continue;
+      if (C.b[0]) v += C.b[0][h];
       o = fmaf(wts[k], v, o);
     }
     out[h] = f32_to_bf16_bits(o);
@@ -377,10 +400,13 @@ static cudaError_t run_plan(const P& plan, int nblocks, int nv, cudaStream_t st,
 }
 
 int max_vectors_for(int K) {
-  using SP = SmemPlan<kNCW, kNStage, kStageBytes, COLS_FULL, FMT_Q6_K>;  // largest layout
-  const int avail = 227 * 1024 - SP::off_x;
-  const int per = SP::x_bytes(K, 1);
-  return std::max(0, std::min(8, avail / per));
+  // one vector: single-column layout; several: 8-column partial sums (largest coefficients: Q6_K)
+  using S1 = SmemPlan<kNCW, kNStage, kStageBytes, COLS_DUP, FMT_Q6_K>;
+  using S8 = SmemPlan<kNCW, kNStage, kStageBytes, COLS_FULL, FMT_Q6_K>;
+  const int limit = 227 * 1024;
+  const int n8 = (limit - S8::off_x) / S8::x_bytes(K, 1);
+  if (n8 >= 2) return std::min(8, n8);
+  return (limit - S1::off_x) >= S1::x_bytes(K, 1) ? 1 : 0;
 }
 
 // ------------------------------------------------------------------ matvec

@@ -45,6 +45,17 @@ struct Seg {
   int64_t mat_bytes;  // bytes of the whole matrix (clamp for the last copy)
 };
 
+// Per-launch table the producer fills once (plan.fill_cache) so that seg() and
+// the epilogue never chase pointers through global memory per row block.
+struct SlotCache {
+  const uint8_t* w[2];  // weight matrices of slot (e.g. gate / up, or down)
+  const uint8_t* s[2];  // their MXFP4 scale tensors
+  const float* b[2];    // optional biases
+  int e;                // expert id (-1: invalid id in the routing table)
+  int pad;
+};
+constexpr int kMaxSlots = 8;
+
 struct Piece {
   int64_t cs;     // first kept source byte (16-B aligned, relative to the matrix)
   int64_t end;    // one past the last needed source byte
@@ -277,7 +288,8 @@ struct SmemPlan {
   static constexpr int off_bars = 0;
   static constexpr int off_cnt = 128;
   static constexpr int off_red = 256;
-  static constexpr int off_coef = off_red + kRed;
+  static constexpr int off_cache = off_red + kRed;
+  static constexpr int off_coef = off_cache + kMaxSlots * (int)sizeof(SlotCache);
   static constexpr int off_stage = ((off_coef + kCoef + 127) / 128) * 128;
   static constexpr int off_x = off_stage + NSTAGE * STAGE_BYTES;
   static __host__ __device__ constexpr int x_bytes(int K, int nv) { return (K / 32) * nv * (64 + 16); }
@@ -291,10 +303,11 @@ struct SmemPlan {
 //   int num_vectors() const;                activation vectors (<= 8)
 //   XSrc xsrc() const;                      where the activation vectors live
 //   int num_blocks() const;                 row blocks
-//   int nseg(int rb) const;  Seg seg(int rb, int s) const;
+//   void fill_cache(SlotCache* c, int lane) const;   producer warp, once, before any seg()
+//   int nseg(int rb) const;  Seg seg(const SlotCache*, int rb, int s) const;
 //   void rowmap(int rb, int m, int& s, int& lr) const;   A-row m -> (segment, row)  (s<0: none)
 //   void columns(int rb, int g, int t, int& vb, int& v0, int& v1, int& na, int& nb) const;
-//   void epilogue(int rb, const float* red, int nwarps, int lane) const;
+//   void epilogue(const SlotCache*, int rb, const float* red, int nwarps, int lane) const;
 //       run by the last warp to finish the row block; red[w*W + i] = warp w's partial
 //       sums, W = 16 (i = A-row, one column) or 128 (i = row*8 + column).
 template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, class P>
@@ -306,6 +319,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
   int* cnt = reinterpret_cast<int*>(smem + SP::off_cnt);
   float* red = reinterpret_cast<float*>(smem + SP::off_red);
   uint8_t* stages = smem + SP::off_stage;
+  SlotCache* cache = reinterpret_cast<SlotCache*>(smem + SP::off_cache);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const StageGeom G = plan.geom;
@@ -330,6 +344,8 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
     if (P::kProducerWaits) pdl_wait();
+    plan.fill_cache(cache, lane);
+    __syncwarp();
     int it = 0;
     for (int rb = blockIdx.x; rb < nblocks; rb += gridDim.x) {
       const int ns = plan.nseg(rb);
@@ -337,7 +353,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
       Seg rseg{};
       if (lane < 16) {
         plan.rowmap(rb, lane, rs, rl);
-        if (rs >= 0) rseg = plan.seg(rb, rs);
+        if (rs >= 0) rseg = plan.seg(cache, rb, rs);
       }
       for (int kc = 0; kc < nkc; ++kc, ++it) {
         const int k0 = kc * KC, k1 = min(K, k0 + KC);
@@ -356,7 +372,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
         uint32_t mybulk = 0;
         for (int i = lane; i < npc; i += 32) {
           const int s = whole ? i : i / G.rps, r = whole ? -1 : i % G.rps;
-          const Seg sg = plan.seg(rb, s);
+          const Seg sg = plan.seg(cache, rb, s);
           if (!whole && r >= sg.nrows) continue;
           const Piece p = make_piece<F>(sg, s, r, G, k0, k1);
           mybulk += p.bulk;
@@ -365,7 +381,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
         if (F == FMT_MXFP4) {
           const int cb = (k1 - k0) / 32;
           for (int s = 0; s < ns; ++s) {
-            const Seg sg = plan.seg(rb, s);
+            const Seg sg = plan.seg(cache, rb, s);
             const int base = G.sc_base + s * (((G.rps * cb) + 15) & ~15);
             for (int i = lane; i < sg.nrows * cb; i += 32) {
               const int r = i / cb, b = i % cb;
@@ -381,7 +397,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
         __syncwarp();
         for (int i = lane; i < npc; i += 32) {
           const int s = whole ? i : i / G.rps, r = whole ? -1 : i % G.rps;
-          const Seg sg = plan.seg(rb, s);
+          const Seg sg = plan.seg(cache, rb, s);
           if (!whole && r >= sg.nrows) continue;
           const Piece p = make_piece<F>(sg, s, r, G, k0, k1);
           if (p.bulk) bulk_g2s(data + p.soff, sg.w + p.cs, p.bulk, &full[st]);
@@ -539,7 +555,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
       }
       last = __shfl_sync(0xffffffffu, last, 0);
       if (last) {
-        plan.epilogue(rb, rd, NCW, lane);
+        plan.epilogue(cache, rb, rd, NCW, lane);
         __syncwarp();
         if (lane == 0) cnt[st] = 0;
       }
