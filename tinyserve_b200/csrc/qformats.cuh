@@ -159,19 +159,31 @@ __device__ __forceinline__ void kq_scale_min(const uint8_t* s12, int j, int& sc,
   }
 }
 
+// Small non-negative integer (< 2^23) to float without the conversion unit:
+// the float with bits 0x4B000000 | v is exactly 2^23 + v.
+__device__ __forceinline__ float small_u2f(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.f; }
+
 template <int F>
 __device__ __forceinline__ float4 fold_coef(const RowLoc& L) {
   if (F == FMT_Q4_K || F == FMT_Q5_K) {
-    const uint32_t dd = *reinterpret_cast<const uint32_t*>(L.blk);
-    const float d = half_bits_to_f32(dd & 0xFFFF), dmin = half_bits_to_f32(dd >> 16);
-    int sc, m;
-    kq_scale_min(L.blk + 4, L.sub, sc, m);
-    const float a = d * (float)sc;
-    return make_float4(a, fmaf(FoldBias<F>::v, a, dmin * (float)m), 0.f, 0.f);
+    // superblocks are 16-B aligned in the stage: read d/dmin and the 12 scale bytes as words
+    const uint4 hw = *reinterpret_cast<const uint4*>(L.blk);
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&hw.x));
+    const int j = L.sub, sh = 8 * (j & 3);
+    // j < 4: sc = s[j] & 63, m = s[j+4] & 63
+    // j >= 4: sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4, m = (s[j+4] >> 4) | (s[j] >> 6) << 4
+    const uint32_t lo_sc = (hw.y >> sh) & 63u, lo_m = (hw.z >> sh) & 63u;
+    const uint32_t hi_sc = ((hw.w >> sh) & 15u) | (((hw.y >> sh) >> 2) & 0x30u);
+    const uint32_t hi_m = (((hw.w >> sh) >> 4) & 15u) | (((hw.z >> sh) >> 2) & 0x30u);
+    const uint32_t sc = j < 4 ? lo_sc : hi_sc, m = j < 4 ? lo_m : hi_m;
+    const float a = dd.x * small_u2f(sc);
+    return make_float4(a, fmaf(FoldBias<F>::v, a, dd.y * small_u2f(m)), 0.f, 0.f);
   } else if (F == FMT_Q6_K) {
     const float d = half_bits_to_f32(*reinterpret_cast<const uint16_t*>(L.blk + 208));
-    const int8_t* sc = reinterpret_cast<const int8_t*>(L.blk + 192) + 2 * L.sub;
-    const float a0 = d * (float)sc[0], a1 = d * (float)sc[1];
+    const uint32_t sp = *reinterpret_cast<const uint16_t*>(L.blk + 192 + 2 * L.sub);  // two int8 scales
+    const float s0 = small_u2f((sp & 0xFFu) ^ 0x80u) - 128.f;
+    const float s1 = small_u2f((sp >> 8) ^ 0x80u) - 128.f;
+    const float a0 = d * s0, a1 = d * s1;
     return make_float4(a0, FoldBias<F>::v * a0, a1, FoldBias<F>::v * a1);
   } else if (F == FMT_Q8_0) {
     const float d = half_bits_to_f32(*reinterpret_cast<const uint16_t*>(L.blk));

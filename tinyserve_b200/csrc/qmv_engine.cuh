@@ -440,17 +440,42 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
       const int4 h0 = hdr[g], h1 = hdr[g + 8];
       const RowInfo r0{h0.x, h0.y, h0.z, h0.w}, r1{h1.x, h1.y, h1.z, h1.w};
 
+      // Running per-row positions.  Rows outside the matrix (valid == 0) read
+      // the stage from offset 0 instead of branching: every decoded A value is
+      // finite (magic f16 <= 1279, e2m1 <= 6), and their fold coefficient is 0.
+      // Rows g and g+8 are 8 rows apart and 8*K/32 is a multiple of 8 for any
+      // K % 32 == 0, so both rows sit at the same 32-block phase within their
+      // superblocks: one sub-block counter serves both.
+      using T = FmtT<F>;
+      const uint8_t* pA = data + (r0.valid ? r0.off : 0);
+      const uint8_t* pB = data + (r1.valid ? r1.off : 0);
+      int sA = 0;
+      if (kKQ) {
+        sA = (r0.valid ? r0.sub0 : r1.sub0) + u_beg;
+        pA += (sA >> 3) * T::BB;
+        pB += (sA >> 3) * T::BB;
+        sA &= 7;
+      } else {
+        pA += u_beg * T::BB;
+        pB += u_beg * T::BB;
+      }
+      const uint8_t* scA = data + r0.soff + u_beg;  // MXFP4 scale bytes
+      const uint8_t* scB = data + r1.soff + u_beg;
+      const uint4* xqp = xq + ((size_t)(ub + u_beg) * nv + vb) * 4 + t;
+      const float4* xsp = xsx + (size_t)(ub + u_beg) * nv;
+
       for (int uc = u_beg; uc < u_end; uc += SP::kCoefCh) {
         const int nst = min(SP::kCoefCh, u_end - uc);
         if (kKQ) {
           __syncwarp();
-          for (int e = lane; e < 16 * SP::kCoefCh; e += 32) {
+#pragma unroll
+          for (int e0 = 0; e0 < 16 * SP::kCoefCh; e0 += 32) {
+            const int e = e0 + lane;
             const int m = e / SP::kCoefCh, s = e % SP::kCoefCh;
-            if (s >= nst) continue;
             const int4 q = hdr[m];
             const RowInfo ri{q.x, q.y, q.z, q.w};
             float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (ri.valid) c = fold_coef<F>(row_loc<F>(data, ri, uc + s));
+            if (ri.valid && s < nst) c = fold_coef<F>(row_loc<F>(data, ri, uc + s));
             if (F == FMT_Q6_K) reinterpret_cast<float4*>(coef)[m * SP::kCoefCh + s] = c;
             else reinterpret_cast<float2*>(coef)[m * SP::kCoefCh + s] = make_float2(c.x, c.y);
           }
@@ -458,18 +483,14 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
         }
 #pragma unroll 2
         for (int s = 0; s < nst; ++s) {
-          const int u = uc + s;   // step within the chunk
-          const int ug = ub + u;  // step within the row
-          const uint4 b = xq[((size_t)ug * nv + vb) * 4 + t];
-          uint32_t pa[4] = {kMagic, kMagic, kMagic, kMagic};
-          uint32_t pb[4] = {kMagic, kMagic, kMagic, kMagic};
-          RowLoc la{}, lb{};
-          if (r0.valid) { la = row_loc<F>(data, r0, u); decode_a<F>(la, t, pa); }
-          if (r1.valid) { lb = row_loc<F>(data, r1, u); decode_a<F>(lb, t, pb); }
-          if (F == FMT_MXFP4) {
-            if (!r0.valid) pa[0] = pa[1] = pa[2] = pa[3] = 0u;
-            if (!r1.valid) pb[0] = pb[1] = pb[2] = pb[3] = 0u;
-          }
+          const uint4 b = *xqp;
+          xqp += nv * 4;
+          RowLoc la, lb;
+          la.blk = pA; la.sub = sA; la.mx_scale = (F == FMT_MXFP4) ? scA[0] : 0u;
+          lb.blk = pB; lb.sub = sA; lb.mx_scale = (F == FMT_MXFP4) ? scB[0] : 0u;
+          uint32_t pa[4], pb[4];
+          decode_a<F>(la, t, pa);
+          decode_a<F>(lb, t, pb);
           float c1[4] = {0.f, 0.f, 0.f, 0.f};
           float c2[4] = {0.f, 0.f, 0.f, 0.f};
           const uint32_t a1[4] = {pa[0], pb[0], pa[1], pb[1]};
@@ -489,11 +510,20 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
               kb = make_float4(qb.x, qb.y, 0.f, 0.f);
             }
           } else {
-            ka = r0.valid ? fold_coef<F>(la) : make_float4(0.f, 0.f, 0.f, 0.f);
-            kb = r1.valid ? fold_coef<F>(lb) : make_float4(0.f, 0.f, 0.f, 0.f);
+            ka = fold_coef<F>(la);
+            kb = fold_coef<F>(lb);
+            ka.x = r0.valid ? ka.x : 0.f; ka.y = r0.valid ? ka.y : 0.f;
+            kb.x = r1.valid ? kb.x : 0.f; kb.y = r1.valid ? kb.y : 0.f;
           }
-          auto fold = [&](float& a, float cv1, float cv2, const float4& k, int v) {
-            const float4 q = xsx[ug * nv + v];
+          // advance both rows by one 32-element step
+          if (kKQ) {
+            if (++sA == 8) { sA = 0; pA += T::BB; pB += T::BB; }
+          } else {
+            pA += T::BB;
+            pB += T::BB;
+          }
+          if (F == FMT_MXFP4) { ++scA; ++scB; }
+          auto fold = [&](float& a, float cv1, float cv2, const float4& k, const float4& q) {
             if (F == FMT_Q6_K) {
               a = fmaf(k.x, cv1 * q.x, a);
               a = fmaf(-k.y, q.y, a);
@@ -507,18 +537,22 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
             }
           };
           if (MODE == COLS_DUP) {
-            fold(acc[0], c1[0], c2[0], ka, 0);
-            fold(acc[2], c1[2], c2[2], kb, 0);
+            const float4 q0 = xsp[0];
+            fold(acc[0], c1[0], c2[0], ka, q0);
+            fold(acc[2], c1[2], c2[2], kb, q0);
           } else if (MODE == COLS_FULL) {
-            fold(acc[0], c1[0], c2[0], ka, v0);
-            fold(acc[1], c1[1], c2[1], ka, v1);
-            fold(acc[2], c1[2], c2[2], kb, v0);
-            fold(acc[3], c1[3], c2[3], kb, v1);
+            const float4 qv0 = xsp[v0], qv1 = xsp[v1];
+            fold(acc[0], c1[0], c2[0], ka, qv0);
+            fold(acc[1], c1[1], c2[1], ka, qv1);
+            fold(acc[2], c1[2], c2[2], kb, qv0);
+            fold(acc[3], c1[3], c2[3], kb, qv1);
           } else {
             const bool oa = n_a & 1, ob = n_b & 1;
-            fold(acc[0], oa ? c1[1] : c1[0], oa ? c2[1] : c2[0], ka, n_a < 0 ? 0 : n_a);
-            fold(acc[2], ob ? c1[3] : c1[2], ob ? c2[3] : c2[2], kb, n_b < 0 ? 0 : n_b);
+            const float4 qa_ = xsp[n_a < 0 ? 0 : n_a], qb_ = xsp[n_b < 0 ? 0 : n_b];
+            fold(acc[0], oa ? c1[1] : c1[0], oa ? c2[1] : c2[0], ka, qa_);
+            fold(acc[2], ob ? c1[3] : c1[2], ob ? c2[3] : c2[2], kb, qb_);
           }
+          xsp += nv;
         }
       }
       if (kc + 1 < nkc) {
