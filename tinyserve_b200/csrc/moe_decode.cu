@@ -391,11 +391,17 @@ static bool choose_geom(int K, int nseg, int rows_per_seg, StageGeom& G) {
 
 template <int F, int MODE, class P>
 static cudaError_t run_plan(const P& plan, int nblocks, int nv, cudaStream_t st, bool pdl) {
-  auto kern = qmv_kernel<F, MODE, kNCW, kNStage, kStageBytes, P>;
   const int smem = SmemPlan<kNCW, kNStage, kStageBytes, MODE, F>::total(plan.geom.K, nv);
+  const int grid = std::max(1, std::min(nblocks, num_sms()));
+  if (plan.geom.KC >= plan.geom.K) {
+    auto kern = qmv_kernel<F, MODE, kNCW, kNStage, kStageBytes, 2, P>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    return launch(kern, grid, 32 * (kNCW + 1), (size_t)smem, st, pdl, plan);
+  }
+  auto kern = qmv_kernel<F, MODE, kNCW, kNStage, kStageBytes, 1, P>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  const int grid = std::max(1, std::min(nblocks, num_sms()));
   return launch(kern, grid, 32 * (kNCW + 1), (size_t)smem, st, pdl, plan);
 }
 

@@ -279,7 +279,7 @@ __device__ void stage_x(uint8_t* xq_raw, float4* xsx, int K, int nv, const XSrc&
 //   x        staged activation vectors
 template <int NCW, int NSTAGE, int STAGE_BYTES, int MODE, int F>
 struct SmemPlan {
-  static constexpr int kCoefCh = 8;  // steps per coefficient chunk
+  static constexpr int kCoefCh = (F == FMT_Q6_K) ? 8 : 16;  // steps per coefficient chunk
   static constexpr int kCoefW = (F == FMT_Q6_K) ? 16 : 8;  // bytes per coefficient entry
   static constexpr int kRedW = (MODE == COLS_FULL) ? 128 : 16;
   static constexpr int kRed = NSTAGE * NCW * kRedW * 4;
@@ -310,9 +310,15 @@ struct SmemPlan {
 //   void epilogue(const SlotCache*, int rb, const float* red, int nwarps, int lane) const;
 //       run by the last warp to finish the row block; red[w*W + i] = warp w's partial
 //       sums, W = 16 (i = A-row, one column) or 128 (i = row*8 + column).
-template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, class P>
+// NG consumer groups of NCW/NG warps: row block i goes to group i % NG, and the
+// warps of a group split its K range.  NG = 2 when a row block is one stage
+// (whole rows), so two row blocks are in flight and each warp covers twice as
+// many steps; NG = 1 for k-chunked rows (a group must see all chunks of its rows).
+template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, int NG, class P>
 __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
   using SP = SmemPlan<NCW, NSTAGE, STAGE_BYTES, MODE, F>;
+  constexpr int WPG = NCW / NG;
+  static_assert(NCW % NG == 0, "groups must split the consumer warps evenly");
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + SP::off_bars);
   uint64_t* empty = full + NSTAGE;
@@ -333,7 +339,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
   if (tid == 0) {
     for (int s = 0; s < NSTAGE; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NCW);
+      mbar_init(&empty[s], WPG);
       cnt[s] = 0;
     }
     fence_barrier_init();
@@ -416,13 +422,16 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
   pdl_launch_dependents();
 
   const int cw = warp - 1;
+  const int grp = cw / WPG, wg = cw % WPG;
   const int g = lane >> 2, t = lane & 3;
   uint8_t* coef = smem + SP::off_coef + cw * 16 * SP::kCoefCh * SP::kCoefW;
   const uint4* xq = reinterpret_cast<const uint4*>(xq_raw);
   constexpr bool kKQ = (F == FMT_Q4_K || F == FMT_Q5_K || F == FMT_Q6_K);
 
-  int it = 0;
-  for (int rb = blockIdx.x; rb < nblocks; rb += gridDim.x) {
+  int bi = 0;
+  for (int rb = blockIdx.x; rb < nblocks; rb += gridDim.x, ++bi) {
+    if (bi % NG != grp) continue;
+    int it = bi * nkc;
     int vb, v0, v1, n_a, n_b;
     plan.columns(rb, g, t, vb, v0, v1, n_a, n_b);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -432,7 +441,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
       const int st = it % NSTAGE;
       const uint32_t ph = (it / NSTAGE) & 1;
       const int Uc = (k1 - k0) / 32, ub = k0 / 32;
-      const int u_beg = (cw * Uc) / NCW, u_end = ((cw + 1) * Uc) / NCW;
+      const int u_beg = (wg * Uc) / WPG, u_end = ((wg + 1) * Uc) / WPG;
       if (!mbar_wait(&full[st], ph, err)) return;
       const uint8_t* stage = stages + st * STAGE_BYTES;
       const uint8_t* data = stage + SP::kHdr;
@@ -565,7 +574,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
       // stage is released only after that, so the partial-sum slot `st` cannot be
       // reused before the epilogue has read it.
       float* rd = red + st * (NCW * SP::kRedW);
-      float* mine = rd + cw * SP::kRedW;
+      float* mine = rd + wg * SP::kRedW;
       if (MODE == COLS_FULL) {
         mine[g * 8 + 2 * t] = acc[0];
         mine[g * 8 + 2 * t + 1] = acc[1];
@@ -584,12 +593,12 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
       int last = 0;
       if (lane == 0) {
         __threadfence_block();
-        last = (atomicAdd(&cnt[st], 1) == NCW - 1);
+        last = (atomicAdd(&cnt[st], 1) == WPG - 1);
         __threadfence_block();
       }
       last = __shfl_sync(0xffffffffu, last, 0);
       if (last) {
-        plan.epilogue(cache, rb, rd, NCW, lane);
+        plan.epilogue(cache, rb, rd, WPG, lane);
         __syncwarp();
         if (lane == 0) cnt[st] = 0;
       }
