@@ -368,21 +368,23 @@ static int num_sms() {
 
 template <int F>
 static bool choose_geom(int K, int nseg, int rows_per_seg, StageGeom& G) {
-  int slot, scb;
+  int slot, scb, ssl;
   G.K = K;
   G.rps = rows_per_seg;
   constexpr int kData = kStageBytes - 256;  // stage minus its RowInfo header
-  if (host_stage_bytes<F>(K, K, nseg, rows_per_seg, slot, scb) <= kData) {
+  if (host_stage_bytes<F>(K, K, nseg, rows_per_seg, slot, scb, ssl) <= kData) {
     G.KC = K;
     G.slot = slot;
     G.sc_base = scb;
+    G.sslot = ssl;
     return true;
   }
   for (int KC = (K / 256) * 256; KC >= 256; KC -= 256) {
-    if (host_stage_bytes<F>(K, KC, nseg, rows_per_seg, slot, scb) <= kData) {
+    if (host_stage_bytes<F>(K, KC, nseg, rows_per_seg, slot, scb, ssl) <= kData) {
       G.KC = KC;
       G.slot = slot;
       G.sc_base = scb;
+      G.sslot = ssl;
       return true;
     }
   }

@@ -69,6 +69,7 @@ struct StageGeom {
   int KC;       // chunk length (elements, multiple of 32)
   int slot;     // bytes per segment (whole-row chunks) or per row (partial chunks)
   int sc_base;  // MXFP4: stage offset of the scale bytes
+  int sslot;    // MXFP4: bytes per scale slot (per segment or per row, like `slot`)
   int rps;      // rows per segment (at most)
 };
 
@@ -110,6 +111,37 @@ __device__ __forceinline__ Piece make_piece(const Seg& sg, int si, int r, const 
   return p;
 }
 
+// MXFP4 scale bytes of segment `si` (whole rows, r < 0) or of row r, as a piece
+// of the scale tensor.  The scale tensor need not be 16-B aligned, so alignment
+// is taken on absolute addresses (cs may be up to 15 bytes before the tensor;
+// those bytes lie inside the same allocation, whose start is 256-B aligned).
+template <int F>
+__device__ __forceinline__ Piece make_scale_piece(const Seg& sg, int si, int r, const StageGeom& G, int k0, int k1) {
+  const int64_t bpr = G.K / 32;  // scale bytes per row
+  int64_t b0, b1;
+  uint32_t soff;
+  if (r < 0) {
+    b0 = sg.row0 * bpr;
+    b1 = (sg.row0 + sg.nrows) * bpr;
+    soff = (uint32_t)(G.sc_base + si * G.sslot);
+  } else {
+    b0 = (sg.row0 + r) * bpr + k0 / 32;
+    b1 = b0 + (k1 - k0) / 32;
+    soff = (uint32_t)(G.sc_base + (si * G.rps + r) * G.sslot);
+  }
+  const int64_t base = (int64_t)reinterpret_cast<uintptr_t>(sg.s);
+  Piece p;
+  p.cs = ((base + b0) & ~int64_t(15)) - base;
+  p.end = b1;
+  int64_t be = ((base + b1 + 15) & ~int64_t(15)) - base;
+  const int64_t mat_end = ((base + sg.mat_bytes / 16) & ~int64_t(15)) - base;  // scales = blocks / 16
+  if (be > mat_end) be = mat_end;
+  if (be < p.cs) be = p.cs;
+  p.bulk = (uint32_t)(be - p.cs);
+  p.soff = soff;
+  return p;
+}
+
 // Per-row addressing within a stage for the current chunk.
 struct RowInfo {
   int32_t off;   // stage offset of the block (Q8_0/MXFP4) or superblock (K-quants) holding element k0
@@ -135,7 +167,9 @@ __device__ __forceinline__ RowInfo row_info(const Seg& sg, int si, int lr, const
   }
   if (F == FMT_MXFP4) {
     const int cb = (k1 - k0) / 32;
-    ri.soff = G.sc_base + si * (((G.rps * cb) + 15) & ~15) + lr * cb;
+    (void)cb;
+    const Piece sp = make_scale_piece<F>(sg, si, whole ? -1 : lr, G, k0, k1);
+    ri.soff = (int32_t)(sp.soff + (((sg.row0 + lr) * (int64_t)(G.K / 32) + k0 / 32) - sp.cs));
   }
   ri.valid = 1;
   return ri;
@@ -385,14 +419,13 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
           for (int64_t b = p.cs + p.bulk; b < p.end; ++b) data[p.soff + (b - p.cs)] = sg.w[b];
         }
         if (F == FMT_MXFP4) {
-          const int cb = (k1 - k0) / 32;
-          for (int s = 0; s < ns; ++s) {
+          for (int i = lane; i < npc; i += 32) {
+            const int s = whole ? i : i / G.rps, r = whole ? -1 : i % G.rps;
             const Seg sg = plan.seg(cache, rb, s);
-            const int base = G.sc_base + s * (((G.rps * cb) + 15) & ~15);
-            for (int i = lane; i < sg.nrows * cb; i += 32) {
-              const int r = i / cb, b = i % cb;
-              data[base + i] = sg.s[(sg.row0 + r) * (int64_t)(K / 32) + k0 / 32 + b];
-            }
+            if (!whole && r >= sg.nrows) continue;
+            const Piece p = make_scale_piece<F>(sg, s, r, G, k0, k1);
+            mybulk += p.bulk;
+            for (int64_t b = p.cs + p.bulk; b < p.end; ++b) data[p.soff + (b - p.cs)] = sg.s[b];
           }
         }
         uint32_t total = mybulk;
@@ -407,6 +440,10 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
           if (!whole && r >= sg.nrows) continue;
           const Piece p = make_piece<F>(sg, s, r, G, k0, k1);
           if (p.bulk) bulk_g2s(data + p.soff, sg.w + p.cs, p.bulk, &full[st]);
+          if (F == FMT_MXFP4) {
+            const Piece q = make_scale_piece<F>(sg, s, r, G, k0, k1);
+            if (q.bulk) bulk_g2s(data + q.soff, sg.s + q.cs, q.bulk, &full[st]);
+          }
         }
       }
     }
@@ -621,14 +658,16 @@ inline int host_slot_bytes(int K, int KC, int rows_per_seg) {
 }
 
 template <int F>
-inline int host_stage_bytes(int K, int KC, int nseg, int rows_per_seg, int& slot, int& sc_base) {
+inline int host_stage_bytes(int K, int KC, int nseg, int rows_per_seg, int& slot, int& sc_base, int& sslot) {
   const bool whole = (KC >= K);
   slot = host_slot_bytes<F>(K, KC, rows_per_seg);
   sc_base = whole ? nseg * slot : nseg * rows_per_seg * slot;
   int total = sc_base;
+  sslot = 0;
   if (F == FMT_MXFP4) {
     const int cb = (whole ? K : KC) / 32;
-    total += nseg * (((rows_per_seg * cb) + 15) & ~15);
+    sslot = ((whole ? rows_per_seg * cb : cb) + 32 + 15) & ~15;
+    total += (whole ? nseg : nseg * rows_per_seg) * sslot;
   }
   return total;
 }
