@@ -512,7 +512,44 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
 
       for (int uc = u_beg; uc < u_end; uc += SP::kCoefCh) {
         const int nst = min(SP::kCoefCh, u_end - uc);
-        if (kKQ) {
+        if (F == FMT_Q4_K || F == FMT_Q5_K) {
+          // One task per (row, superblock): decode d, dmin and the 12 scale bytes
+          // once and emit the coefficients of the sub-blocks that fall in this
+          // chunk of steps (16 steps from any phase span at most 3 superblocks).
+          __syncwarp();
+          float2* cf = reinterpret_cast<float2*>(coef);
+          for (int task = lane; task < 48; task += 32) {
+            const int m = task / 3, j = task - 3 * (task / 3);
+            const int4 q = hdr[m];
+            if (!q.w) {
+              if (j == 0)
+                for (int u = 0; u < nst; ++u) cf[m * SP::kCoefCh + u] = make_float2(0.f, 0.f);
+              continue;
+            }
+            const int sb = ((q.y + uc) >> 3) + j;  // superblock index relative to the row's first
+            const int ubase = sb * 8 - q.y - uc;   // chunk step of sub-block 0 of this superblock
+            if (ubase >= nst) continue;
+            const uint4 hw = *reinterpret_cast<const uint4*>(data + q.x + sb * FmtT<F>::BB);
+            const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&hw.x));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int u = ubase + i;
+              if (u < 0 || u >= nst) continue;
+              const int sh = 8 * (i & 3);
+              uint32_t sc, mn;
+              if (i < 4) {
+                sc = (hw.y >> sh) & 63u;
+                mn = (hw.z >> sh) & 63u;
+              } else {
+                sc = ((hw.w >> sh) & 15u) | (((hw.y >> sh) >> 2) & 0x30u);
+                mn = (((hw.w >> sh) >> 4) & 15u) | (((hw.z >> sh) >> 2) & 0x30u);
+              }
+              const float a = dd.x * small_u2f(sc);
+              cf[m * SP::kCoefCh + u] = make_float2(a, fmaf(FoldBias<F>::v, a, dd.y * small_u2f(mn)));
+            }
+          }
+          __syncwarp();
+        } else if (kKQ) {
           __syncwarp();
 #pragma unroll
           for (int e0 = 0; e0 < 16 * SP::kCoefCh; e0 += 32) {
