@@ -213,12 +213,16 @@ struct XSrc {
   int64_t stride;  // elements between vectors
   int dtype;       // TSB_DT_F32 (0) / TSB_DT_BF16 (1) / TSB_DT_F16 (2)
   int vec_ok;      // rows 16-B (fp32) / 8-B (16-bit) aligned: vector loads allowed
+  int cg;          // fp32 source written by other CTAs of this grid: load through L2 (ld.global.cg)
 };
 
 __device__ __forceinline__ float4 load4(const XSrc& X, int v, int k) {
   const int64_t i = v * X.stride + k;
   if (X.dtype == 0) {
-    if (X.vec_ok) return *reinterpret_cast<const float4*>(static_cast<const float*>(X.p) + i);
+    if (X.vec_ok) {
+      const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(X.p) + i);
+      return X.cg ? __ldcg(q) : *q;
+    }
     const float* q = static_cast<const float*>(X.p) + i;
     return make_float4(q[0], q[1], q[2], q[3]);
   }
@@ -348,45 +352,39 @@ struct SmemPlan {
 // warps of a group split its K range.  NG = 2 when a row block is one stage
 // (whole rows), so two row blocks are in flight and each warp covers twice as
 // many steps; NG = 1 for k-chunked rows (a group must see all chunks of its rows).
+// Shared-memory pointers of the engine (one CTA).
+struct EngSmem {
+  uint64_t* full;
+  uint64_t* empty;
+  int* cnt;
+  float* red;
+  uint8_t* stages;
+  uint8_t* coef;  // 2 KB per consumer warp
+};
+
+// Number of stage units (row block x k-chunk) this CTA processes for a plan.
+template <class P>
+__device__ __forceinline__ int eng_units(const P& plan) {
+  const int nb = plan.num_blocks();
+  const int mine = nb > (int)blockIdx.x ? (nb - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  return mine * ((plan.geom.K + plan.geom.KC - 1) / plan.geom.KC);
+}
+
+// Producer warp: stream every row block of this CTA for `plan` into the stage
+// ring, continuing the ring position `it`.  Returns false if a wait timed out.
 template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, int NG, class P>
-__global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
+__device__ __forceinline__ bool eng_produce(const P& plan, const SlotCache* cache, const EngSmem& S, int& it, int lane,
+                                            int* err) {
   using SP = SmemPlan<NCW, NSTAGE, STAGE_BYTES, MODE, F>;
   constexpr int WPG = NCW / NG;
   static_assert(NCW % NG == 0, "groups must split the consumer warps evenly");
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SP::off_bars);
-  uint64_t* empty = full + NSTAGE;
-  int* cnt = reinterpret_cast<int*>(smem + SP::off_cnt);
-  float* red = reinterpret_cast<float*>(smem + SP::off_red);
-  uint8_t* stages = smem + SP::off_stage;
-  SlotCache* cache = reinterpret_cast<SlotCache*>(smem + SP::off_cache);
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint64_t* full = S.full;
+  uint64_t* empty = S.empty;
   const StageGeom G = plan.geom;
   const int K = G.K, KC = G.KC;
   const int nkc = (K + KC - 1) / KC;
-  const int nv = plan.num_vectors();
-  uint8_t* xq_raw = smem + SP::off_x;
-  float4* xsx = reinterpret_cast<float4*>(xq_raw + (size_t)(K / 32) * nv * 64);
-  int* err = plan.err;
-
-  if (tid == 0) {
-    for (int s = 0; s < NSTAGE; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], WPG);
-      cnt[s] = 0;
-    }
-    fence_barrier_init();
-  }
-  __syncthreads();
   const int nblocks = plan.num_blocks();
-
-  if (warp == 0) {
-    // ------------------------------ producer ------------------------------
-    if (P::kProducerWaits) pdl_wait();
-    plan.fill_cache(cache, lane);
-    __syncwarp();
-    int it = 0;
+  uint8_t* stages = S.stages;
     for (int rb = blockIdx.x; rb < nblocks; rb += gridDim.x) {
       const int ns = plan.nseg(rb);
       int rs = -1, rl = 0;
@@ -400,7 +398,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
         const bool whole = (k0 == 0 && k1 == K);
         const int st = it % NSTAGE;
         const uint32_t ph = ((it / NSTAGE) & 1) ^ 1;
-        if (!mbar_wait(&empty[st], ph, err)) return;
+        if (!mbar_wait(&empty[st], ph, err)) return false;
         uint8_t* stage = stages + st * STAGE_BYTES;
         uint8_t* data = stage + SP::kHdr;
         if (lane < 16) {
@@ -447,28 +445,35 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
         }
       }
     }
-    return;
-  }
+  return true;
+}
 
-  // ------------------------------ consumers ------------------------------
-  const int ctid = tid - 32;
-  if (!P::kXIndependent) pdl_wait();
-  stage_x<F>(xq_raw, xsx, K, nv, plan.xsrc(), ctid, 32 * NCW);
-  named_bar_sync(1, 32 * NCW);
-  if (P::kXIndependent) pdl_wait();
-  pdl_launch_dependents();
-
-  const int cw = warp - 1;
+// Consumer warp cw: process this CTA's row blocks of `plan` (its group's share),
+// whose stage units start at ring position it0.  Returns false on a timeout.
+template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, int NG, class P>
+__device__ __forceinline__ bool eng_consume(const P& plan, const SlotCache* cache, const EngSmem& S, int it0,
+                                            const uint4* xq, const float4* xsx, int cw, int lane, int* err) {
+  using SP = SmemPlan<NCW, NSTAGE, STAGE_BYTES, MODE, F>;
+  constexpr int WPG = NCW / NG;
+  static_assert(NCW % NG == 0, "groups must split the consumer warps evenly");
+  uint64_t* full = S.full;
+  uint64_t* empty = S.empty;
+  const StageGeom G = plan.geom;
+  const int K = G.K, KC = G.KC;
+  const int nkc = (K + KC - 1) / KC;
+  const int nblocks = plan.num_blocks();
+  uint8_t* stages = S.stages;
+  int* cnt = S.cnt;
+  float* red = S.red;
+  const int nv = plan.num_vectors();
   const int grp = cw / WPG, wg = cw % WPG;
   const int g = lane >> 2, t = lane & 3;
-  uint8_t* coef = smem + SP::off_coef + cw * 16 * SP::kCoefCh * SP::kCoefW;
-  const uint4* xq = reinterpret_cast<const uint4*>(xq_raw);
+  uint8_t* coef = S.coef + cw * 2048;
   constexpr bool kKQ = (F == FMT_Q4_K || F == FMT_Q5_K || F == FMT_Q6_K);
-
   int bi = 0;
   for (int rb = blockIdx.x; rb < nblocks; rb += gridDim.x, ++bi) {
     if (bi % NG != grp) continue;
-    int it = bi * nkc;
+    int it = it0 + bi * nkc;
     int vb, v0, v1, n_a, n_b;
     plan.columns(rb, g, t, vb, v0, v1, n_a, n_b);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -479,7 +484,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
       const uint32_t ph = (it / NSTAGE) & 1;
       const int Uc = (k1 - k0) / 32, ub = k0 / 32;
       const int u_beg = (wg * Uc) / WPG, u_end = ((wg + 1) * Uc) / WPG;
-      if (!mbar_wait(&full[st], ph, err)) return;
+      if (!mbar_wait(&full[st], ph, err)) return false;
       const uint8_t* stage = stages + st * STAGE_BYTES;
       const uint8_t* data = stage + SP::kHdr;
       const int4* hdr = reinterpret_cast<const int4*>(stage);
@@ -680,6 +685,53 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
       if (lane == 0) mbar_arrive(&empty[st]);
     }
   }
+  return true;
+}
+
+template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, int NG, class P>
+__global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
+  using SP = SmemPlan<NCW, NSTAGE, STAGE_BYTES, MODE, F>;
+  constexpr int WPG = NCW / NG;
+  extern __shared__ __align__(128) uint8_t smem[];
+  EngSmem S;
+  S.full = reinterpret_cast<uint64_t*>(smem + SP::off_bars);
+  S.empty = S.full + NSTAGE;
+  S.cnt = reinterpret_cast<int*>(smem + SP::off_cnt);
+  S.red = reinterpret_cast<float*>(smem + SP::off_red);
+  S.stages = smem + SP::off_stage;
+  S.coef = smem + SP::off_coef;
+  SlotCache* cache = reinterpret_cast<SlotCache*>(smem + SP::off_cache);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = plan.geom.K;
+  const int nv = plan.num_vectors();
+  uint8_t* xq_raw = smem + SP::off_x;
+  float4* xsx = reinterpret_cast<float4*>(xq_raw + (size_t)(K / 32) * nv * 64);
+  int* err = plan.err;
+  if (tid == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], WPG);
+      S.cnt[s] = 0;
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (P::kProducerWaits) pdl_wait();
+    plan.fill_cache(cache, lane);
+    __syncwarp();
+    int it = 0;
+    eng_produce<F, MODE, NCW, NSTAGE, STAGE_BYTES, NG>(plan, cache, S, it, lane, err);
+    return;
+  }
+  const int ctid = tid - 32;
+  if (!P::kXIndependent) pdl_wait();
+  stage_x<F>(xq_raw, xsx, K, nv, plan.xsrc(), ctid, 32 * NCW);
+  named_bar_sync(1, 32 * NCW);
+  if (P::kXIndependent) pdl_wait();
+  pdl_launch_dependents();
+  eng_consume<F, MODE, NCW, NSTAGE, STAGE_BYTES, NG>(plan, cache, S, 0, reinterpret_cast<const uint4*>(xq_raw), xsx,
+                                                     warp - 1, lane, err);
 }
 
 // Host-side geometry (excluding the 256-B RowInfo header): stage slot size for a given chunk.
