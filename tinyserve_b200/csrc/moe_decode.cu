@@ -580,7 +580,7 @@ struct FusedParams {
   float* wts_out;
   float* act;         // [top_k, I]
   uint16_t* out;      // bf16 [H]
-  int H, I, E, top_k, layout, act_kind, rpe, tpe, redundant_router, x_vec_ok;
+  int H, I, E, top_k, layout, act_kind, rpe, tpe, x_vec_ok;
   float limit, alpha;
   int64_t gu_bytes, up_bytes, dn_bytes;
 };
@@ -601,22 +601,23 @@ struct FusedSmem {
 };
 
 // Bounded grid-wide barrier for one thread per CTA (generation counting).
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void grid_barrier(unsigned* bar, int* err) {
   __threadfence();
-  volatile unsigned* vb = bar;
-  const unsigned gen = vb[1];
+  const unsigned gen = ld_acquire(bar + 1);
   if (atomicAdd(&bar[0], 1u) == gridDim.x - 1) {
     bar[0] = 0u;
     __threadfence();
     atomicAdd(&bar[1], 1u);
     return;
   }
-  for (uint32_t i = 0; i < (1u << 25); ++i) {
-    if (vb[1] != gen) {
-      __threadfence();
-      return;
-    }
-    __nanosleep(64);
+  for (uint32_t i = 0; i < (1u << 28); ++i) {
+    if (ld_acquire(bar + 1) != gen) return;
   }
   atomicExch(err, kDevWaitTimeout);
 }
@@ -662,36 +663,6 @@ __device__ __forceinline__ PlanDownT1<FDN> fused_dn_plan(const FusedParams& p, c
   q.out = p.out;
   q.dn_bytes = p.dn_bytes;
   return q;
-}
-
-// logit of expert e = bf16(x . W[e] + b[e]), one warp.
-__device__ __forceinline__ float router_logit(const FusedParams& p, int e, int lane) {
-  const uint4* xr = reinterpret_cast<const uint4*>(p.x);
-  const uint4* wr = reinterpret_cast<const uint4*>(p.router_w + (int64_t)e * p.H);
-  const int n8 = p.H / 8;
-  float acc = 0.f;
-  for (int base = lane; base < n8; base += 32 * 8) {
-    uint4 a[8], w[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int i = base + 32 * j;
-      a[j] = i < n8 ? xr[i] : make_uint4(0, 0, 0, 0);
-      w[j] = i < n8 ? __ldg(wr + i) : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t av[4] = {a[j].x, a[j].y, a[j].z, a[j].w}, wv[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        acc = fmaf(__uint_as_float(av[q] << 16), __uint_as_float(wv[q] << 16), acc);
-        acc = fmaf(__uint_as_float(av[q] & 0xFFFF0000u), __uint_as_float(wv[q] & 0xFFFF0000u), acc);
-      }
-    }
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (p.router_b) acc += p.router_b[e];
-  return bf16_bits_to_f32(f32_to_bf16_bits(acc));
 }
 
 template <int FGU, int FDN>
@@ -749,19 +720,39 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1) moe_decode_fused(const Fus
   constexpr int NCT = 32 * kNCW;
   // x for gate/up (does not depend on routing)
   stage_x<FGU>(xgu, xsgu, p.H, 1, XSrc{p.x, 0, TSB_DT_BF16, p.x_vec_ok, 0}, ctid, NCT);
-  // router
-  if (p.redundant_router) {
-    for (int e = cw; e < p.E; e += kNCW) {
-      const float l = router_logit(p, e, lane);
-      if (lane == 0) slog[e] = l;
+  // Router: expert e belongs to CTA e % grid; the CTA's consumer warps split
+  // its H range (all loads in flight at once), then a grid barrier publishes
+  // the logits and every CTA reads all of them.
+  {
+    const int n8 = p.H / 8;
+    const int per = (n8 + kNCW - 1) / kNCW;
+    const int i0 = cw * per, i1 = min(n8, i0 + per);
+    float* part = S.red;  // scratch: [kNCW] partial dots (free until the first row block)
+    for (int e = blockIdx.x; e < p.E; e += gridDim.x) {
+      const uint4* xr = reinterpret_cast<const uint4*>(p.x);
+      const uint4* wr = reinterpret_cast<const uint4*>(p.router_w + (int64_t)e * p.H);
+      float acc = 0.f;
+      for (int i = i0 + lane; i < i1; i += 32) {
+        const uint4 a = xr[i], w = __ldg(wr + i);
+        const uint32_t av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc = fmaf(__uint_as_float(av[q] << 16), __uint_as_float(wv[q] << 16), acc);
+          acc = fmaf(__uint_as_float(av[q] & 0xFFFF0000u), __uint_as_float(wv[q] & 0xFFFF0000u), acc);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) part[cw] = acc;
+      named_bar_sync(1, NCT);
+      if (ctid == 0) {
+        float l = 0.f;
+        for (int w = 0; w < kNCW; ++w) l += part[w];
+        if (p.router_b) l += p.router_b[e];
+        p.logits[e] = bf16_bits_to_f32(f32_to_bf16_bits(l));
+      }
+      named_bar_sync(1, NCT);
     }
-    named_bar_sync(1, NCT);
-  } else {
-    for (int e = blockIdx.x + cw * gridDim.x; e < p.E; e += kNCW * gridDim.x) {
-      const float l = router_logit(p, e, lane);
-      if (lane == 0) p.logits[e] = l;
-    }
-    named_bar_sync(1, NCT);
     if (ctid == 0) grid_barrier(p.gridbar, p.err);
     named_bar_sync(1, NCT);
     for (int e = ctid; e < p.E; e += NCT) slog[e] = __ldcg(p.logits + e);
@@ -856,7 +847,6 @@ static int fused_t(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, con
   p.limit = sp.limit;
   p.alpha = sp.alpha;
   p.tpe = (sp.inter + 7) / 8;
-  p.redundant_router = (int64_t)sp.n_experts * sp.hidden * 2 <= 256 * 1024;
   p.x_vec_ok = reinterpret_cast<uintptr_t>(x) % 8 == 0;
   int64_t db, sb;
   weight_bytes_of(FGU, (inter || sp.gate_up_layout == TSB_GU_CHUNKED ? 2 : 1) * (int64_t)sp.inter, sp.hidden, db, sb);

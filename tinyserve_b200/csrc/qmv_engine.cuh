@@ -271,18 +271,21 @@ __device__ void stage_x(uint8_t* xq_raw, float4* xsx, int K, int nv, const XSrc&
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      // e = exponent such that amax * 2^-e lies in (2^14, 2^15], from the float's
+      // exponent bits (clamped so 2^-e and 2^e stay normal floats); scaling by a
+      // power of two is exact.
       int e = 0;
       if (amax > 0.f && amax <= 3.0e38f) {
-        int ex;
-        frexpf(amax, &ex);
-        e = ex - 15;
+        const int ex = (int)((__float_as_uint(amax) >> 23) & 255u) - 126;  // amax = m * 2^ex, m in [0.5, 1)
+        e = min(126, max(-126, ex - 15));
       }
+      const float inv = __uint_as_float((uint32_t)(127 - e) << 23);
       const float xv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
       float hs = 0.f;
       __half hh[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        hh[i] = __float2half_rn(ldexpf(xv[i], -e));
+        hh[i] = __float2half_rn(xv[i] * inv);
         hs += __half2float(hh[i]);
       }
       float s_all = hs, s_lo = (p < 16) ? hs : 0.f;
@@ -297,7 +300,7 @@ __device__ void stage_x(uint8_t* xq_raw, float4* xsx, int K, int nv, const XSrc&
 #pragma unroll
         for (int i = 0; i < 4; ++i) blk[dst[i]] = hh[i];
         if (p == 0) {
-          const float xs = ldexpf(1.f, e);
+          const float xs = __uint_as_float((uint32_t)(127 + e) << 23);
           if (F == FMT_Q6_K)
             xsx[u * nv + vv] = make_float4(xs, s_lo * xs, (s_all - s_lo) * xs, 0.f);
           else
