@@ -594,7 +594,8 @@ struct FusedSmem {
   static constexpr int off_cgu = off_red + kNStage * kNCW * 16 * 4;
   static constexpr int off_cdn = off_cgu + kMaxSlots * (int)sizeof(SlotCache);
   static constexpr int off_logit = off_cdn + kMaxSlots * (int)sizeof(SlotCache);  // float[1024]
-  static constexpr int off_coef = off_logit + 4096;
+  static constexpr int off_ptab = off_logit + 4096;
+  static constexpr int off_coef = ((off_ptab + kPtabBytes + 15) / 16) * 16;
   static constexpr int off_stage = ((off_coef + kNCW * 2048 + 127) / 128) * 128;
   static constexpr int off_x = off_stage + kNStage * kStageBytes;
   static int total(int H, int I, int k) { return off_x + (H / 32) * 80 + (I / 32) * k * 80; }
@@ -679,6 +680,7 @@ __global__ void __launch_bounds__(32 * (kNCW + 1), 1) moe_decode_fused(const Fus
   S.red = reinterpret_cast<float*>(smem + FS::off_red);
   S.stages = smem + FS::off_stage;
   S.coef = smem + FS::off_coef;
+  S.ptab = smem + FS::off_ptab;
   int32_t* sid = reinterpret_cast<int32_t*>(smem + FS::off_ids);
   float* swt = reinterpret_cast<float*>(smem + FS::off_wts);
   float* slog = reinterpret_cast<float*>(smem + FS::off_logit);

@@ -311,6 +311,17 @@ __device__ void stage_x(uint8_t* xq_raw, float4* xsx, int K, int nv, const XSrc&
   }
 }
 
+// Producer tables for whole-row plans: the row headers, bulk pieces and byte
+// totals of the next kPtabUnits units are computed ahead, one lane per item, so
+// that filling a stage is only a header copy, expect_tx and 1-2 bulk copies.
+constexpr int kPtabUnits = 4;
+struct PtabPiece {
+  const uint8_t* src;
+  uint32_t bytes;
+  uint32_t soff;  // bit 31: the piece also has a plain-load tail (matrix end)
+};
+constexpr int kPtabBytes = kPtabUnits * 16 * 16 + kPtabUnits * 16 * (int)sizeof(PtabPiece) + kPtabUnits * 4;
+
 // Shared-memory map of one CTA.
 //   bars     full[NSTAGE], empty[NSTAGE] mbarriers
 //   cnt      per-stage counters of warps done with a row block (last one runs the epilogue)
@@ -330,7 +341,8 @@ struct SmemPlan {
   static constexpr int off_cnt = 128;
   static constexpr int off_red = 256;
   static constexpr int off_cache = off_red + kRed;
-  static constexpr int off_coef = off_cache + kMaxSlots * (int)sizeof(SlotCache);
+  static constexpr int off_ptab = off_cache + kMaxSlots * (int)sizeof(SlotCache);
+  static constexpr int off_coef = ((off_ptab + kPtabBytes + 15) / 16) * 16;
   static constexpr int off_stage = ((off_coef + kCoef + 127) / 128) * 128;
   static constexpr int off_x = off_stage + NSTAGE * STAGE_BYTES;
   static __host__ __device__ constexpr int x_bytes(int K, int nv) { return (K / 32) * nv * (64 + 16); }
@@ -357,6 +369,7 @@ struct SmemPlan {
 // many steps; NG = 1 for k-chunked rows (a group must see all chunks of its rows).
 // Shared-memory pointers of the engine (one CTA).
 struct EngSmem {
+  uint8_t* ptab;  // producer tables (kPtabBytes): headers and bulk pieces of upcoming units
   uint64_t* full;
   uint64_t* empty;
   int* cnt;
@@ -388,6 +401,76 @@ __device__ __forceinline__ bool eng_produce(const P& plan, const SlotCache* cach
   const int nkc = (K + KC - 1) / KC;
   const int nblocks = plan.num_blocks();
   uint8_t* stages = S.stages;
+  if (nkc == 1) {
+    // whole rows: table-driven
+    int4* htab = reinterpret_cast<int4*>(S.ptab);
+    PtabPiece* ptab = reinterpret_cast<PtabPiece*>(S.ptab + kPtabUnits * 256);
+    uint32_t* ttab = reinterpret_cast<uint32_t*>(S.ptab + kPtabUnits * 256 + kPtabUnits * 16 * sizeof(PtabPiece));
+    constexpr int kPiecesPerSeg = (F == FMT_MXFP4) ? 2 : 1;
+    int u = 0;
+    for (int rb0 = blockIdx.x; rb0 < nblocks; rb0 += kPtabUnits * gridDim.x) {
+      // ---- precompute up to kPtabUnits units (lane = item within a unit)
+      __syncwarp();
+      for (int j = 0; j < kPtabUnits; ++j) {
+        const int rb = rb0 + j * gridDim.x;
+        if (rb >= nblocks) break;
+        const int ns = plan.nseg(rb);
+        uint32_t bytes = 0;
+        if (lane < 16) {
+          int rs, rl;
+          plan.rowmap(rb, lane, rs, rl);
+          Seg sg{};
+          if (rs >= 0) sg = plan.seg(cache, rb, rs);
+          const RowInfo ri = row_info<F>(sg, rs, rl, G, 0, K);
+          htab[j * 16 + lane] = make_int4(ri.off, ri.sub0, ri.soff, ri.valid);
+        } else if (lane - 16 < ns * kPiecesPerSeg) {
+          const int i = lane - 16, s = i % ns;
+          const Seg sg = plan.seg(cache, rb, s);
+          const Piece p = (i < ns) ? make_piece<F>(sg, s, -1, G, 0, K) : make_scale_piece<F>(sg, s, -1, G, 0, K);
+          PtabPiece q;
+          q.src = ((i < ns) ? sg.w : sg.s) + p.cs;
+          q.bytes = p.bulk;
+          q.soff = p.soff | ((p.cs + p.bulk < p.end) ? 0x80000000u : 0u);
+          ptab[j * 16 + i] = q;
+          bytes = p.bulk;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+        if (lane == 0) ttab[j] = bytes;
+      }
+      __syncwarp();
+      // ---- fill stages from the tables
+      for (int j = 0; j < kPtabUnits; ++j, ++u, ++it) {
+        const int rb = rb0 + j * gridDim.x;
+        if (rb >= nblocks) break;
+        const int ns = plan.nseg(rb);
+        const int st = it % NSTAGE;
+        const uint32_t ph = ((it / NSTAGE) & 1) ^ 1;
+        if (!mbar_wait(&empty[st], ph, err)) return false;
+        uint8_t* stage = stages + st * STAGE_BYTES;
+        uint8_t* data = stage + SP::kHdr;
+        if (lane < 16) reinterpret_cast<int4*>(stage)[lane] = htab[j * 16 + lane];
+        if (lane < ns * kPiecesPerSeg) {
+          const PtabPiece q = ptab[j * 16 + lane];
+          if (q.soff & 0x80000000u) {  // ragged end of the matrix: plain loads for the tail
+            const int s = lane % ns;
+            const Seg sg = plan.seg(cache, rb, s);
+            const Piece p = (lane < ns) ? make_piece<F>(sg, s, -1, G, 0, K) : make_scale_piece<F>(sg, s, -1, G, 0, K);
+            const uint8_t* src = (lane < ns) ? sg.w : sg.s;
+            for (int64_t b = p.cs + p.bulk; b < p.end; ++b) data[p.soff + (b - p.cs)] = src[b];
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&full[st], ttab[j]);
+        __syncwarp();
+        if (lane < ns * kPiecesPerSeg) {
+          const PtabPiece q = ptab[j * 16 + lane];
+          if (q.bytes) bulk_g2s(data + (q.soff & 0x7FFFFFFFu), q.src, q.bytes, &full[st]);
+        }
+      }
+    }
+    return true;
+  }
     for (int rb = blockIdx.x; rb < nblocks; rb += gridDim.x) {
       const int ns = plan.nseg(rb);
       int rs = -1, rl = 0;
@@ -703,6 +786,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
   S.red = reinterpret_cast<float*>(smem + SP::off_red);
   S.stages = smem + SP::off_stage;
   S.coef = smem + SP::off_coef;
+  S.ptab = smem + SP::off_ptab;
   SlotCache* cache = reinterpret_cast<SlotCache*>(smem + SP::off_cache);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = plan.geom.K;

@@ -20,9 +20,8 @@ enum : int {
   kDevBadPlan = 2,       // routing plan inconsistent (expert id out of range)
 };
 
-// Poll budget for mbarrier waits: try_wait suspends for a hardware-defined
-// interval per poll, so this bounds a wait at well under a few seconds.
-constexpr uint32_t kMaxPolls = 1u << 22;
+// Poll budget for mbarrier waits (each poll may suspend up to kSuspendNs).
+constexpr uint32_t kMaxPolls = 4096;  // with the 1 ms suspend hint: a few seconds at most
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -49,18 +48,24 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting thread sleeps in hardware until
+// the phase completes or ~kSuspendNs elapse, so waiting warps do not take issue
+// slots from the warps that are working (the producer in particular).
+constexpr uint32_t kSuspendNs = 1000000;  // 1 ms per poll
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait.  Returns false (and records kDevWaitTimeout) when the poll
-// budget runs out; the caller then skips its work and unwinds.
+// Bounded wait (at most ~kMaxPolls hinted polls, i.e. a few seconds).  Returns
+// false (and records kDevWaitTimeout) when the budget runs out; the caller then
+// skips its work and unwinds.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   for (uint32_t i = 0; i < kMaxPolls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
