@@ -1,5 +1,6 @@
 // extern "C" entry points of libtsb_moe.so (declared in include/tsb_moe.h).
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -176,7 +177,13 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
   float* act = reinterpret_cast<float*>(ws + L.act);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool routed = router_w != nullptr;
-  if (routed) {
+  // The single-launch persistent kernel is opt-in (TSB_DECODE_FUSED=1): on the
+  // GPT-OSS-20B shape the three PDL-chained launches are currently faster.
+  static const bool fused = [] {
+    const char* v = getenv("TSB_DECODE_FUSED");
+    return v && v[0] == '1';
+  }();
+  if (routed && fused) {
     rc = launch_moe_fused(sp, experts, x, router_w, router_b, ids, weights, out, act,
                           reinterpret_cast<float*>(ws + L.logits), reinterpret_cast<unsigned*>(ws + L.gridbar), err, st);
     if (rc != -1) return rc;
