@@ -33,6 +33,11 @@ class CPUMoELayer:
         self.top_k = top_k
         self.num_threads = num_threads
 
+    def prefetch(self, experts) -> None:
+        """Decode the given experts now, so timed tokens only run the math."""
+        for e in experts:
+            self._expert(int(e))
+
     def _expert(self, e: int):
         if e not in self._cache:
             self._cache[e] = self._fetch(e)
@@ -57,10 +62,10 @@ class CPUMoELayer:
         return out
 
 
-def gguf_expert_fetcher(layer_host: dict, fmt_gu: int, fmt_dn: int, H: int, I: int):
-    """layer_host[e] = (gate bytes, up bytes, down bytes) numpy uint8 streams."""
+def gguf_expert_fetcher(host_bytes, fmt_gu: int, fmt_dn: int, H: int, I: int):
+    """host_bytes(e) -> (gate bytes, up bytes, down bytes) numpy uint8 streams."""
     def fetch(e):
-        g, u, d = layer_host(e)
+        g, u, d = host_bytes(e)
         wg = OD.dequant_tensor(g, fmt_gu, (I, H))
         wu = OD.dequant_tensor(u, fmt_gu, (I, H))
         wgu = np.empty((2 * I, H), np.float32)
