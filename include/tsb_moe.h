@@ -135,6 +135,22 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
  * synchronises the stream.  *code = 0 when no kernel reported an error. */
 int tsb_read_device_error(void* workspace, int32_t* code, void* stream);
 
+/* tsb_moe_decode without a caller-provided workspace (no counterpart in the
+ * reference).  For callers that cannot allocate device memory (for example
+ * while their stream is being captured into a CUDA graph, or inside a host
+ * with a fixed memory plan): the scratch is a 1 MiB array inside the library,
+ * which every GPU that loads the library keeps until the process exits.
+ * Layers needing more scratch than that (tsb_moe_decode_workspace) are
+ * rejected with TSB_ERR_WORKSPACE.  Allocates nothing.  The first call on a
+ * device looks up the array's device address; make that first call before
+ * any stream capture on that device.  All calls share the one array: calls
+ * that overlap on the GPU (other streams, other threads) race and must be
+ * serialised by the caller.  Kernel-side errors of this variant are not
+ * reported (there is no workspace to read them from). */
+int tsb_moe_decode_noalloc(const TsbMoeSpec* spec, const TsbExpert* experts, const void* x, int32_t T,
+                           const void* router_w, const float* router_b, int32_t* ids, float* weights, void* out,
+                           void* stream);
+
 #ifdef __cplusplus
 }
 #endif

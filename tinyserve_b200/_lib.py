@@ -28,6 +28,7 @@ ACT_SILU, ACT_SWIGLU_OAI = 0, 1
 EXPORTS = (
     "tsb_version", "tsb_last_error", "tsb_format_info", "tsb_weight_bytes", "tsb_dequant",
     "tsb_quant_matvec", "tsb_moe_decode_workspace", "tsb_moe_decode", "tsb_read_device_error",
+    "tsb_moe_decode_noalloc",
 )
 
 
@@ -67,6 +68,7 @@ def _declare(L: ctypes.CDLL) -> None:
     L.tsb_moe_decode_workspace.restype = _sz
     L.tsb_moe_decode.argtypes = [ctypes.POINTER(TsbMoeSpec), _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
     L.tsb_read_device_error.argtypes = [_vp, ctypes.POINTER(_i32), _vp]
+    L.tsb_moe_decode_noalloc.argtypes = [ctypes.POINTER(TsbMoeSpec), _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp]
 
 
 def lib() -> ctypes.CDLL:

@@ -2,6 +2,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/tsb_moe.h"
@@ -212,3 +213,58 @@ int tsb_read_device_error(void* workspace, int32_t* code, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of tsb_moe_decode.
+//
+// Some callers have no way to hand us device scratch memory: code that runs
+// while its stream is being captured into a CUDA graph (cudaMalloc is not
+// allowed there), hosts whose memory is planned ahead and that forbid any
+// allocation behind their back, or language bindings that only ever see the
+// tensors they pass in.  For them the workspace lives in this file-scope
+// device array, sized for one layer of up to kNoAllocBytes of scratch.
+// ---------------------------------------------------------------------------
+namespace tsb {
+constexpr size_t kNoAllocBytes = size_t(1) << 20;  // 1 MiB, held on every GPU that loads the library
+static __device__ __align__(256) unsigned char g_noalloc_ws[kNoAllocBytes];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64];  // device address of g_noalloc_ws, per device ordinal
+}  // namespace tsb
+
+extern "C" int tsb_moe_decode_noalloc(const TsbMoeSpec* spec, const TsbExpert* experts, const void* x, int32_t T,
+                                      const void* router_w, const float* router_b, int32_t* ids, float* weights,
+                                      void* out, void* stream) {
+  using namespace tsb;
+  if (!spec) return set_error(TSB_ERR_INVALID, "null pointer");
+  const size_t need = tsb_moe_decode_workspace(spec, T);
+  if (need == 0) return set_error(TSB_ERR_INVALID, "T must be positive");
+  if (need > kNoAllocBytes) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "tsb_moe_decode_noalloc: this layer needs %zu bytes of scratch, more than the %zu-byte static workspace",
+             need, kNoAllocBytes);
+    return set_error(TSB_ERR_WORKSPACE, buf);
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(TSB_ERR_UNSUPPORTED, "device ordinal out of range");
+  void* ws = nullptr;
+  {
+    // First call on a device: look up the array's device address with that
+    // device current (the host-side symbol is not a device address).
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_ws);
+      if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+      g_noalloc_ptr[dev] = p;
+    }
+    ws = g_noalloc_ptr[dev];
+  }
+  // The array keeps the previous call's contents: clear the error word and the
+  // counters at its start, which must begin at zero.
+  e = cudaMemsetAsync(ws, 0, 256, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return tsb_moe_decode(spec, experts, x, T, router_w, router_b, ids, weights, out, ws, kNoAllocBytes, stream);
+}
