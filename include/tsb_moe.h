@@ -131,6 +131,23 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
                    const void* router_w, const float* router_b, int32_t* ids, float* weights, void* out,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* workspace bytes tsb_moe_prefill needs for T tokens (holds the permuted
+ * token tiles, the expert weights decoded to fp16 tiles for every expert, the
+ * activation tiles and fp32 expert outputs) */
+size_t tsb_moe_prefill_workspace(const TsbMoeSpec* spec, int32_t T);
+
+/* One MoE layer for T >= 1 tokens as grouped GEMMs on the tensor cores
+ * (replaces ExpertPipeline.execute_layer_experts_batched,
+ * tinyserve/expert_pipeline.py:166-239, and group_tokens_by_expert,
+ * tinyserve/_fast_cache.pyx:60-85).  Same arguments and routing rule as
+ * tsb_moe_decode.  Tokens are grouped by expert on the GPU in (token, slot)
+ * order; products run in fp16 with fp32 accumulation (token rows are scaled by
+ * exact powers of two to use the fp16 range; weights and the intermediate
+ * activations must lie within it). */
+int tsb_moe_prefill(const TsbMoeSpec* spec, const TsbExpert* experts, const void* x, int32_t T,
+                    const void* router_w, const float* router_b, int32_t* ids, float* weights, void* out,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* read (and clear) the device error word kept in a tsb_moe_decode workspace;
  * synchronises the stream.  *code = 0 when no kernel reported an error. */
 int tsb_read_device_error(void* workspace, int32_t* code, void* stream);

@@ -1,0 +1,166 @@
+"""GPU parity of the grouped (prefill) MoE layer, tsb_moe_prefill, against
+float64 math on the oracle-dequantised weights.
+
+The reference's batched path groups tokens by expert and runs one expert
+forward per group (tinyserve/expert_pipeline.py:166-239); its tests check the
+grouped result against the per-token loop (tests/test_batched_prefill.py:52-119).
+Here every case is checked against the exact per-token sum.  Products run in
+fp16 with fp32 accumulation, so the layer math stays within 1e-3 relative L2;
+the bf16 output adds its own rounding (4e-3), as for decode.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import expert as OE
+from tests.helpers import rel_l2
+from tests.test_kernels_gpu import _build_layer
+from tinyserve_b200.formats import GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_Q8_0, TSB_MXFP4
+
+TOL = 1e-3 + 4e-3
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    return torch.device("cuda:0")
+
+
+def _oracle(x, ids, wts, dense, act="swiglu_oai"):
+    """Per-expert grouped float64 forward; out[t] = sum_j w[t,j] * expert(x[t])."""
+    x = np.asarray(x, dtype=np.float64)
+    out = np.zeros_like(x)
+    for e in np.unique(ids):
+        if e < 0 or e >= len(dense):
+            continue
+        tok, kk = np.nonzero(ids == e)
+        wg, wu, wd, bg, bu, bd = dense[e]
+        y = OE.expert_forward(x[tok], wg, wu, wd, act, None if bg is None else bg.numpy(),
+                              None if bu is None else bu.numpy(), None if bd is None else bd.numpy())
+        np.add.at(out, tok, wts[tok, kk][:, None] * y)
+    return out
+
+
+def _routing(T, E, k, seed):
+    from tinyserve_b200.workloads import zipf_routing
+    return zipf_routing(T, E, k, seed=seed)
+
+
+@pytest.mark.parametrize("fmt_gu,fmt_dn,layout", [
+    (GGML_Q4_K, GGML_Q4_K, "separate"),
+    (TSB_MXFP4, TSB_MXFP4, "interleaved"),
+    (GGML_Q8_0, GGML_Q6_K, "separate"),
+    (GGML_Q5_K, GGML_Q8_0, "chunked"),
+])
+def test_prefill_layer_formats(dev, fmt_gu, fmt_dn, layout):
+    H, I, E, k, T = 512, 256, 8, 2, 300
+    layer, dense, _ = _build_layer(dev, fmt_gu, fmt_dn, H, I, E, k, layout, seed=fmt_gu * 7 + fmt_dn)
+    ids, wts = _routing(T, E, k, seed=1)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
+    out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
+    torch.cuda.synchronize()
+    ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
+    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert layer.prefill_error(T) == 0
+
+
+def test_prefill_gpt_oss_shape_with_bias(dev):
+    """H = I = 2880 (N tiles of 240 rows, 45 k-blocks), MXFP4 with biases,
+    Zipf routing so that some experts get several 128-row blocks."""
+    H = I = 2880
+    E, k, T = 8, 4, 384
+    layer, dense, _ = _build_layer(dev, TSB_MXFP4, TSB_MXFP4, H, I, E, k, "interleaved", seed=11, bias=True)
+    ids, wts = _routing(T, E, k, seed=2)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
+    torch.cuda.synchronize()
+    ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
+    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    per_tok = np.linalg.norm(out.float().cpu().numpy() - ref, axis=1) / np.linalg.norm(ref, axis=1)
+    assert per_tok.max() <= 3e-2
+
+
+def test_prefill_router_matches_oracle_routing(dev):
+    H, I, E, k, T = 1024, 512, 16, 4, 200
+    layer, dense, router = _build_layer(dev, GGML_Q4_K, GGML_Q8_0, H, I, E, k, "separate", seed=21)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    out, ids, wts = layer.prefill(x.to(dev))
+    torch.cuda.synchronize()
+    ids_o, wts_o, lg = OE.router_topk_softmax(x.float().numpy(), router.float().numpy(), k)
+    ids_g = ids.cpu().numpy()
+    for t in range(T):
+        if set(ids_g[t]) != set(ids_o[t]):
+            srt = np.sort(lg[t])[::-1]
+            assert abs(srt[k - 1] - srt[k]) <= 1e-2 * abs(srt[k - 1]) + 1e-6, "routing differs away from a tie"
+    ref = _oracle(x.float().numpy(), ids_g, wts.cpu().numpy(), dense)
+    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+
+
+def test_prefill_one_token_matches_decode(dev):
+    H, I, E, k = 1024, 512, 8, 4
+    layer, _, _ = _build_layer(dev, GGML_Q4_K, GGML_Q4_K, H, I, E, k, "separate", seed=31)
+    x = torch.randn(1, H, generator=torch.Generator().manual_seed(6)).to(torch.bfloat16).to(dev)
+    o1, ids1, w1 = layer.decode(x)
+    o2, ids2, w2 = layer.prefill(x)
+    torch.cuda.synchronize()
+    assert torch.equal(ids1.cpu(), ids2.cpu())
+    assert rel_l2(o2.float().cpu().numpy(), o1.float().cpu().numpy()) <= 2 * TOL
+
+
+def test_prefill_unused_experts_and_all_to_one(dev):
+    """Every token on expert 3 (several row blocks) and some experts unused."""
+    H, I, E, k, T = 256, 128, 6, 1, 513
+    layer, dense, _ = _build_layer(dev, GGML_Q8_0, GGML_Q8_0, H, I, E, k, "separate", seed=41)
+    ids = torch.full((T, k), 3, dtype=torch.int32)
+    wts = torch.ones(T, k)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16)
+    out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
+    ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
+    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+
+
+def test_prefill_row_scaling_wide_dynamic_range(dev):
+    """Token rows of very different magnitudes (1e-6 .. 1e4) keep their own
+    relative accuracy: each row is scaled by a power of two into fp16 range."""
+    H, I, E, k, T = 512, 256, 4, 2, 64
+    layer, dense, _ = _build_layer(dev, TSB_MXFP4, TSB_MXFP4, H, I, E, k, "interleaved", seed=51)
+    ids, wts = _routing(T, E, k, seed=4)
+    g = torch.Generator().manual_seed(8)
+    mags = torch.tensor([1e-6, 1e-3, 1.0, 30.0, 1e4]).repeat(T // 5 + 1)[:T]
+    x = (torch.randn(T, H, generator=g) * mags[:, None] * 0.05).to(torch.bfloat16)
+    out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
+    ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
+    got = out.float().cpu().numpy()
+    for t in range(T):
+        assert rel_l2(got[t], ref[t]) <= 2e-2, t
+
+
+def test_prefill_deterministic(dev):
+    H, I, E, k, T = 512, 256, 8, 4, 777
+    layer, _, _ = _build_layer(dev, GGML_Q4_K, GGML_Q6_K, H, I, E, k, "separate", seed=61)
+    ids, wts = _routing(T, E, k, seed=5)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16).to(dev)
+    a, _, _ = layer.prefill(x, ids=ids, weights=wts)
+    b, _, _ = layer.prefill(x, ids=ids, weights=wts)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_prefill_bad_ids_reported(dev):
+    H, I, E, k, T = 256, 128, 4, 2, 40
+    layer, dense, _ = _build_layer(dev, GGML_Q4_K, GGML_Q4_K, H, I, E, k, "separate", seed=71)
+    ids, wts = _routing(T, E, k, seed=6)
+    ids[5, 1] = 1000
+    ids[7, 0] = -3
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(10)).to(torch.bfloat16)
+    out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
+    torch.cuda.synchronize()
+    assert layer.prefill_error(T) == 2
+    ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
+    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert layer.prefill_error(T) == 0

@@ -212,6 +212,38 @@ int tsb_read_device_error(void* workspace, int32_t* code, void* stream) {
   return TSB_OK;
 }
 
+size_t tsb_moe_prefill_workspace(const TsbMoeSpec* spec, int32_t T) {
+  if (!spec || T < 0) return 0;
+  return prefill_layout(*spec, T).total;
+}
+
+int tsb_moe_prefill(const TsbMoeSpec* spec, const TsbExpert* experts, const void* x, int32_t T, const void* router_w,
+                    const float* router_b, int32_t* ids, float* weights, void* out, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (!spec) return set_error(TSB_ERR_INVALID, "null pointer");
+  if (T < 0) return set_error(TSB_ERR_INVALID, "T must be >= 0");
+  if (T == 0) return TSB_OK;
+  if (!experts || !x || !ids || !weights || !out || !workspace) return set_error(TSB_ERR_INVALID, "null pointer");
+  const TsbMoeSpec& sp = *spec;
+  if (sp.n_experts < 1 || sp.n_experts > 1024) return set_error(TSB_ERR_INVALID, "n_experts must be in [1, 1024]");
+  if (sp.top_k < 1 || sp.top_k > 8 || sp.top_k > sp.n_experts) return set_error(TSB_ERR_INVALID, "top_k must be in [1, min(8, E)]");
+  if (sp.hidden % 32 || sp.inter % 32 || sp.hidden <= 0 || sp.inter <= 0)
+    return set_error(TSB_ERR_INVALID, "hidden and inter must be positive multiples of 32");
+  if (sp.gate_up_layout < 0 || sp.gate_up_layout > 2) return set_error(TSB_ERR_INVALID, "bad gate_up_layout");
+  if (sp.activation < 0 || sp.activation > 1) return set_error(TSB_ERR_INVALID, "bad activation");
+  if ((int64_t)T * sp.top_k > (int64_t)1 << 26) return set_error(TSB_ERR_UNSUPPORTED, "T * top_k too large");
+  int rc = check_shape(sp.fmt_gate_up, sp.inter, sp.hidden);
+  if (rc) return rc;
+  rc = check_shape(sp.fmt_down, sp.hidden, sp.inter);
+  if (rc) return rc;
+  const PrefillLayout L = prefill_layout(sp, T);
+  if (!L.nt_gu || !L.nt_dn) return set_error(TSB_ERR_UNSUPPORTED, "no tensor-core tile divides hidden / inter");
+  if (workspace_bytes < L.total) return set_error(TSB_ERR_WORKSPACE, "workspace too small");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(TSB_ERR_INVALID, "workspace must be 256-byte aligned");
+  return launch_moe_prefill(sp, experts, x, T, router_w, router_b, ids, weights, out, static_cast<char*>(workspace), L,
+                            static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

@@ -4,6 +4,7 @@
 #include <cstdio>
 
 #include "../../include/tsb_moe.h"
+#include "moe_math.cuh"
 #include "qmv_engine.cuh"
 #include "tsb_internal.h"
 
@@ -26,14 +27,6 @@ __device__ __forceinline__ void store_out(void* p, int dtype, int64_t i, float v
   else static_cast<__half*>(p)[i] = __float2half_rn(v);
 }
 
-__device__ __forceinline__ float act_fn(int act, float gate, float up, float limit, float alpha) {
-  if (act == TSB_ACT_SWIGLU_OAI) {
-    const float g = fminf(gate, limit);
-    const float u = fminf(fmaxf(up, -limit), limit);
-    return (u + 1.f) * g * (1.f / (1.f + __expf(-alpha * g)));
-  }
-  return gate / (1.f + __expf(-gate)) * up;
-}
 
 // Expert id from a routing table, validated: an id outside [0, E) (a corrupt
 // caller-provided table) records kDevBadPlan and yields -1 so the tile holds no rows.

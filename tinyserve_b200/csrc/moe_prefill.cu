@@ -1,0 +1,768 @@
+// Grouped (prefill) MoE layer: T tokens, each routed to top_k experts.
+//
+// Replaces the reference's batched expert path
+// (tinyserve/expert_pipeline.py:166-239 execute_layer_experts_batched with
+// group_tokens_by_expert, tinyserve/_fast_cache.pyx:60-85): tokens are grouped
+// by expert on the GPU, every expert runs one grouped GEMM over its tokens on
+// the tcgen05 tensor cores, and the k expert outputs of a token are combined in
+// slot order.
+//
+// Stages (all on one stream, nothing returns to the host):
+//   route_count / route_place  deterministic grouping: expert e owns permuted
+//                              rows [start_e, start_e + count_e), padded to 128;
+//                              inside an expert, rows keep (token, slot) order
+//   gather_rows                token rows -> permuted fp16 tiles, each row
+//                              scaled by a power of two (exact) so that its
+//                              largest element sits in [2^14, 2^15)
+//   tile_weights<F>            each routed expert's weights decoded bit-exactly
+//                              (same arithmetic as tsb_dequant) and rounded to
+//                              fp16 tiles
+//   grouped_gemm (gate/up)     D = X_e W_gu^T on tcgen05, fp32 accumulators in
+//                              tensor memory; epilogue undoes the row scale,
+//                              adds biases, applies the activation and writes
+//                              fp16 activation tiles
+//   grouped_gemm (down)        D = A_e W_dn^T; epilogue adds the bias, writes
+//                              fp32 rows
+//   combine                    out[t] = sum_j w[t,j] * Y[row(t,j)], j ascending
+//
+// Numerics: the products run in fp16 x fp16 with fp32 accumulation.  Weight
+// rounding to fp16 (11-bit significand) keeps layer outputs within ~3e-4
+// relative L2 of fp32 math on the dequantised weights; bf16 operands (8-bit)
+// would not meet 1e-3.  MXFP4 weights within the fp16 range are exact.
+//
+// Operand tiles live in HBM already in the tensor core's shared-memory image
+// (K-major, 128-byte swizzle, 64 K-elements per 128-byte row), so a pipeline
+// stage is two plain bulk copies (cp.async.bulk, no tensor map) completing on
+// an mbarrier.
+#include <algorithm>
+#include <cstdio>
+
+#include "../../include/tsb_moe.h"
+#include "moe_math.cuh"
+#include "qformats.cuh"
+#include "tc05.cuh"
+#include "tsb_internal.h"
+
+namespace tsb {
+
+constexpr int kBM = 128;                  // permuted rows per tile (tensor-memory lanes)
+constexpr int kBK = 64;                   // K elements per k-block (one 128-byte row)
+constexpr int kATile = kBM * 128;         // 16 KB
+constexpr int kBTileMax = 256 * 128;      // 32 KB (N tile <= 256 rows)
+constexpr int kStage = kATile + kBTileMax;
+constexpr int kNS = 4;                    // pipeline depth
+constexpr int kGemmThreads = 256;         // warp 0 producer, warp 1 MMA, warps 4-7 epilogue
+constexpr int kTmemCols = 512;            // two accumulators of <= 256 columns
+constexpr size_t kGemmSmem = 1024 + (size_t)kNS * kStage + 256;
+
+// ------------------------------------------------------------------ routing
+// counts[e] = #(t, j) with ids[t, j] == e.  Ids outside [0, E) are reported in
+// the error word and get row_of = -1 (they contribute nothing, as in decode).
+__global__ void __launch_bounds__(256) route_count_kernel(const int32_t* __restrict__ ids, int n, int E,
+                                                          int* __restrict__ counts, int* __restrict__ row_of,
+                                                          int* err) {
+  const int e = blockIdx.x;
+  int c = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int v = ids[i];
+    c += (v == e);
+    if (e == 0 && (unsigned)v >= (unsigned)E) {
+      row_of[i] = -1;
+      atomicExch(err, kDevBadPlan);
+    }
+  }
+  __shared__ int part[8];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int w = 0; w < 8; ++w) s += part[w];
+    counts[e] = s;
+  }
+}
+
+// Expert e's rows: start_e = sum over e' < e of count rounded up to 128.  The
+// rank of (t, j) inside its expert is its position in flattened (t, j) order,
+// so the grouping is deterministic.  Writes row_of[t*k+j], row_src[row] (the
+// token, -1 for padding), mb_expert[row/128] and the number of row blocks.
+__global__ void __launch_bounds__(1024) route_place_kernel(const int32_t* __restrict__ ids, int n, int top_k, int E,
+                                                           const int* __restrict__ counts, int* __restrict__ row_of,
+                                                           int* __restrict__ row_src, int* __restrict__ mb_expert,
+                                                           int* __restrict__ total_mb) {
+  const int e = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int s_start, s_run, s_woff[32], s_tot;
+  if (threadIdx.x == 0) {
+    int st = 0;
+    for (int q = 0; q < e; ++q) st += (counts[q] + kBM - 1) / kBM * kBM;
+    s_start = st;
+    s_run = 0;
+    if (e == E - 1) *total_mb = (st + (counts[e] + kBM - 1) / kBM * kBM) / kBM;
+  }
+  __syncthreads();
+  const int start = s_start, cnt = counts[e], pad = (cnt + kBM - 1) / kBM * kBM;
+  for (int base = 0; base < n; base += 1024) {
+    const int i = base + threadIdx.x;
+    const bool f = i < n && ids[i] == e;
+    const unsigned bal = __ballot_sync(0xffffffffu, f);
+    if (lane == 0) s_woff[warp] = __popc(bal);
+    __syncthreads();
+    if (warp == 0) {
+      const int v = s_woff[lane];
+      int inc = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
+      }
+      s_woff[lane] = inc - v;
+      if (lane == 31) s_tot = inc;
+    }
+    __syncthreads();
+    if (f) {
+      const int r = start + s_run + s_woff[warp] + __popc(bal & ((1u << lane) - 1u));
+      row_of[i] = r;
+      row_src[r] = i / top_k;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_run += s_tot;
+    __syncthreads();
+  }
+  for (int r = cnt + threadIdx.x; r < pad; r += blockDim.x) row_src[start + r] = -1;
+  for (int b = threadIdx.x; b < pad / kBM; b += blockDim.x) mb_expert[start / kBM + b] = e;
+}
+
+// One warp per permuted row: copy token row x[src] (bf16) into the fp16 A
+// tiles, scaled by 2^-shift (shift = exponent of the row's largest |x| - 14,
+// so the row uses the fp16 range fully and nothing overflows).  Padding rows
+// are zero.  K columns beyond H are zero.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __restrict__ x, int H, int KB,
+                                                          const int* __restrict__ row_src,
+                                                          const int* __restrict__ total_mb, uint8_t* __restrict__ Xp,
+                                                          int8_t* __restrict__ row_shift) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = blockIdx.x * 8 + warp;
+  if (R >= *total_mb * kBM) return;
+  const int src = row_src[R];
+  const int mb = R / kBM, m = R % kBM;
+  const int n8 = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)(src < 0 ? 0 : src) * H);
+  uint32_t mx = 0;  // max |x| as bits (bf16 magnitude << 16 orders like the value)
+  if (src >= 0) {
+    for (int c = lane; c < n8; c += 32) {
+      const uint4 v = xr[c];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        mx = max(mx, (w[q] << 16) & 0x7FFF0000u);
+        mx = max(mx, w[q] & 0x7FFF0000u);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  int sh = 0;
+  if (mx != 0 && mx < 0x7F800000u) sh = max(-100, min(100, (int)(mx >> 23) - 127 - 14));
+  const float sc = __uint_as_float((uint32_t)(127 - sh) << 23);  // 2^-sh, exact
+  uint8_t* rowp = Xp + (size_t)mb * KB * kATile + (size_t)m * 128;
+  for (int c = lane; c < KB * 8; c += 32) {
+    uint4 o = make_uint4(0, 0, 0, 0);
+    if (src >= 0 && c < n8) {
+      const uint4 v = xr[c];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      uint32_t h[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float lo = __fmul_rn(__uint_as_float(w[q] << 16), sc);
+        const float hi = __fmul_rn(__uint_as_float(w[q] & 0xFFFF0000u), sc);
+        const __half2 p = __halves2half2(__float2half_rn(lo), __float2half_rn(hi));
+        h[q] = *reinterpret_cast<const uint32_t*>(&p);
+      }
+      o = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    *reinterpret_cast<uint4*>(rowp + (size_t)(c >> 3) * kATile + (((c & 7) ^ (m & 7)) << 4)) = o;
+  }
+  if (lane == 0) row_shift[R] = (int8_t)sh;
+}
+
+// ------------------------------------------------------------------ weights
+__constant__ float kE2m1[16] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f,
+                                -0.f, -0.5f, -1.f, -1.5f, -2.f, -3.f, -4.f, -6.f};
+
+// Eight consecutive elements (flat index q0, a multiple of 8) of a weight
+// stream, decoded with tsb_dequant's arithmetic (gguf_dequant_torch.py:118-249,
+// mxfp4.py:20-44).
+template <int F>
+__device__ __forceinline__ void deq8(const uint8_t* __restrict__ w, const uint8_t* __restrict__ s, int64_t q0,
+                                     float (&v)[8]) {
+  const int l0 = (int)(q0 & 31);
+  if (F == FMT_Q8_0) {
+    const uint8_t* b = w + (q0 >> 5) * 34;
+    const float d = half_bits_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(d, (float)(int8_t)b[2 + l0 + i]);
+  } else if (F == FMT_Q4_K || F == FMT_Q5_K) {
+    const uint8_t* b = w + (q0 >> 8) * FmtT<F>::BB;
+    const int j = (int)((q0 >> 5) & 7);
+    const float d = half_bits_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+    const float dmin = half_bits_to_f32((uint16_t)(b[2] | (b[3] << 8)));
+    int sc, m;
+    kq_scale_min(b + 4, j, sc, m);
+    const float dsc = __fmul_rn(d, (float)sc), dm = __fmul_rn(dmin, (float)m);
+    const uint8_t* qs = b + (F == FMT_Q4_K ? 16 : 48) + 32 * (j >> 1) + l0;
+    const int sh = 4 * (j & 1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int q = (qs[i] >> sh) & 0xF;
+      if (F == FMT_Q5_K) q |= ((b[16 + l0 + i] >> j) & 1) << 4;
+      v[i] = __fsub_rn(__fmul_rn(dsc, (float)q), dm);
+    }
+  } else if (F == FMT_Q6_K) {
+    const uint8_t* b = w + (q0 >> 8) * 210;
+    const int g = (int)((q0 >> 5) & 7), h = g >> 2, gg = g & 3;
+    const float d = half_bits_to_f32((uint16_t)(b[208] | (b[209] << 8)));
+    const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192) + 2 * g;
+    const float dd = __fmul_rn(d, (float)sc[l0 < 16 ? 0 : 1]);  // 8 elements never straddle l = 16
+    const uint8_t* ql = b + 64 * h + 32 * (gg & 1) + l0;
+    const uint8_t* qh = b + 128 + 32 * h + l0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int q = (((ql[i] >> (4 * (gg >> 1))) & 0xF) | (((qh[i] >> (2 * gg)) & 3) << 4)) - 32;
+      v[i] = __fmul_rn(dd, (float)q);
+    }
+  } else {  // MXFP4
+    const uint8_t* b = w + (q0 >> 5) * 16 + (l0 >> 1);
+    const int e = (int)s[q0 >> 5] - 127;
+    const int e1 = e / 2, e2 = e - e1;
+    const float p1 = __uint_as_float((uint32_t)(e1 + 127) << 23), p2 = __uint_as_float((uint32_t)(e2 + 127) << 23);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __fmul_rn(__fmul_rn(kE2m1[b[i] & 0xF], p1), p2);
+      v[2 * i + 1] = __fmul_rn(__fmul_rn(kE2m1[b[i] >> 4], p1), p2);
+    }
+  }
+}
+
+struct TileWArgs {
+  const TsbExpert* experts;
+  const int* counts;
+  int proj;     // 0: gate/up, 1: down
+  int layout;   // TSB_GU_*
+  int I;        // intermediate size
+  int N;        // output rows of the projection (2I or H)
+  int K;        // input columns (H or I)
+  int KB;       // k-blocks (K rounded up to 64, / 64)
+  int NT;       // rows per N tile
+  uint8_t* out;
+  int64_t estride;  // bytes per expert
+};
+
+// One thread per 16-byte chunk of the tiled output, in output order.  For the
+// gate/up projection a tile's first NT/2 rows are gate features and the next
+// NT/2 the same up features, whatever the source layout.
+template <int F>
+__global__ void __launch_bounds__(256) tile_weights_kernel(const TileWArgs a) {
+  const int e = blockIdx.y;
+  if (a.counts[e] == 0) return;
+  const TsbExpert& E = a.experts[e];
+  const int64_t nchunks = (int64_t)a.N * a.KB * 8;
+  const int half = a.NT / 2;
+  uint8_t* base = a.out + (int64_t)e * a.estride;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nchunks; q += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(q & 7);
+    int64_t t = q >> 3;
+    const int r = (int)(t % a.NT);
+    t /= a.NT;
+    const int kb = (int)(t % a.KB);
+    const int nt = (int)(t / a.KB);
+    const int k0 = kb * kBK + c * 8;
+    const uint8_t* w;
+    const uint8_t* s;
+    int64_t row;
+    if (a.proj == 1) {
+      w = static_cast<const uint8_t*>(E.down);
+      s = static_cast<const uint8_t*>(E.down_scales);
+      row = (int64_t)nt * a.NT + r;
+    } else {
+      const bool up = r >= half;
+      const int64_t j = (int64_t)nt * half + (up ? r - half : r);
+      if (a.layout == TSB_GU_SEPARATE) {
+        w = static_cast<const uint8_t*>(up ? E.up : E.gate);
+        s = static_cast<const uint8_t*>(up ? E.up_scales : E.gate_scales);
+        row = j;
+      } else {
+        w = static_cast<const uint8_t*>(E.gate);
+        s = static_cast<const uint8_t*>(E.gate_scales);
+        row = a.layout == TSB_GU_INTERLEAVED ? 2 * j + (up ? 1 : 0) : (up ? a.I + j : j);
+      }
+    }
+    uint4 o = make_uint4(0, 0, 0, 0);
+    if (k0 < a.K) {
+      float v[8];
+      deq8<F>(w, s, row * a.K + k0, v);
+      uint32_t h[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 p = __halves2half2(__float2half_rn(v[2 * i]), __float2half_rn(v[2 * i + 1]));
+        h[i] = *reinterpret_cast<const uint32_t*>(&p);
+      }
+      o = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    *reinterpret_cast<uint4*>(base + ((int64_t)(nt * a.KB + kb) * a.NT + r) * 128 + (((c ^ (r & 7)) & 7) << 4)) = o;
+  }
+}
+
+// ------------------------------------------------------------------ grouped GEMM
+struct GemmArgs {
+  const uint8_t* A;        // [mb][kb] tiles of 128 rows x 64 fp16
+  int KB;                  // k-blocks
+  const uint8_t* W;        // per expert: [nt][kb] tiles of NT rows x 64 fp16
+  int64_t w_estride;       // bytes per expert
+  int NT;                  // N tile (<= 256, multiple of 16)
+  int ntiles;              // N tiles per expert
+  const int* mb_expert;
+  const int* total_mb;
+  const int* row_src;
+  const int8_t* row_shift;
+  const TsbExpert* experts;
+  int mode;                // 0: gate/up -> activation tiles, 1: down -> fp32 rows
+  uint8_t* act;            // mode 0 output tiles
+  int KBo;                 // mode 0: k-blocks of the activation tiles
+  int act_kind;
+  float limit, alpha;
+  float* Y;                // mode 1 output [rows, H]
+  int H;
+  int* err;
+};
+
+__device__ __forceinline__ float pow2f(int e) {  // 2^e for |e| <= 126, exact
+  return __uint_as_float((uint32_t)(127 + e) << 23);
+}
+
+// Power-of-two scale of a row's intermediate activations.  Rows whose largest
+// |x| is below 2^-3 (x shift < -17) could give activations in or below the fp16
+// subnormal range; they are stored multiplied by 2^-ash (ash < 0) and the down
+// epilogue multiplies by 2^ash.  For small arguments clamp-SwiGLU is linear
+// in the row scale ((u+1) g sigmoid(a g) ~ g / 2) and silu(g) u quadratic.
+// Rows at or above that size are stored as they are (clamp-SwiGLU is bounded
+// by (limit + 1) * limit).
+__device__ __forceinline__ int act_shift(int xsh, int kind) {
+  const int s = min(0, xsh + 17);
+  return kind == TSB_ACT_SWIGLU_OAI ? s : max(-120, 2 * s);
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 p = __halves2half2(__float2half_rn(a), __float2half_rn(b));
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+
+// Persistent: CTA c takes tiles c, c + grid, ... of the (row block, N tile)
+// grid, N fastest so that neighbouring CTAs share the token tile in L2.
+// Warp 0 (one lane) streams A and W k-blocks into a kNS-stage ring; warp 1
+// (one lane) issues 4 MMAs (K = 16 each) per k-block into one of two
+// tensor-memory accumulators; warps 4-7 drain the other accumulator (warp
+// 4+q reads lanes 32q..32q+31, i.e. rows 32q..32q+31 of the tile).
+__global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kNS * kStage);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kNS;
+  uint64_t* tfull = bars + 2 * kNS;
+  uint64_t* tempty = bars + 2 * kNS + 2;
+  uint64_t* fin = bars + 2 * kNS + 4;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2 * kNS + 5);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kNS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(fin, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const int total_tiles = *g.total_mb * g.ntiles;
+  const uint32_t btile = (uint32_t)g.NT * 128u;
+
+  if (warp == 0 && lane == 0) {
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      const int mb = tile / g.ntiles, nt = tile % g.ntiles;
+      const int e = g.mb_expert[mb];
+      const uint8_t* a = g.A + (size_t)mb * g.KB * kATile;
+      const uint8_t* b = g.W + e * g.w_estride + (size_t)nt * g.KB * btile;
+      for (int kb = 0; kb < g.KB; ++kb, ++it) {
+        const int s = it % kNS;
+        if (!mbar_wait(&empty[s], ((it / kNS) & 1) ^ 1, g.err)) { ok = false; break; }
+        uint8_t* sa = smem + (size_t)s * kStage;
+        mbar_arrive_expect_tx(&full[s], kATile + btile);
+        bulk_g2s(sa, a + (size_t)kb * kATile, kATile, &full[s]);
+        bulk_g2s(sa + kATile, b + (size_t)kb * btile, btile, &full[s]);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    const uint32_t idesc = idesc_f16(kBM, g.NT, 0);
+    uint32_t it = 0, tc = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++tc) {
+      const int buf = tc & 1;
+      if (!mbar_wait(&tempty[buf], ((tc >> 1) & 1) ^ 1, g.err)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d = tbase + (uint32_t)buf * 256u;
+      for (int kb = 0; kb < g.KB; ++kb, ++it) {
+        const int s = it % kNS;
+        if (!mbar_wait(&full[s], (it / kNS) & 1, g.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + (size_t)s * kStage), sb = sa + kATile;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(d, sw128_desc(sa + 32 * kk), sw128_desc(sb + 32 * kk), idesc, (kb | kk) != 0);
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(&tfull[buf]);
+    }
+    // Every MMA issued above completes before tensor memory is released.
+    umma_commit(fin);
+    mbar_wait(fin, 0, g.err);
+  } else if (warp >= 4) {
+    const int q = warp - 4;
+    const int m = 32 * q + lane;
+    uint32_t tc = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tc) {
+      const int buf = tc & 1;
+      if (!mbar_wait(&tfull[buf], (tc >> 1) & 1, g.err)) break;
+      tc_fence_after();
+      const int mb = tile / g.ntiles, nt = tile % g.ntiles;
+      const int R = mb * kBM + m;
+      const int src = g.row_src[R];
+      const TsbExpert& E = g.experts[g.mb_expert[mb]];
+      const uint32_t tl = tbase + (uint32_t)buf * 256u + ((uint32_t)(32 * q) << 16);
+      const int xsh = src >= 0 ? g.row_shift[R] : 0;
+      const int ash = act_shift(xsh, g.act_kind);
+      if (g.mode == 0) {
+        const int half = g.NT / 2, j0 = nt * half;
+        const float sc = pow2f(xsh);
+        const float asc = pow2f(-ash);
+        const float* gb = E.gate_bias;
+        const float* ub = E.up_bias;
+        for (int c = 0; c < half; c += 8) {
+          uint32_t gr[8], ur[8];
+          tmem_ld8(tl + c, gr);
+          tmem_ld8(tl + half + c, ur);
+          tmem_ld_wait();
+          if (src >= 0) {
+            const int j = j0 + c;
+            float a[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float gv = __fmul_rn(__uint_as_float(gr[i]), sc), uv = __fmul_rn(__uint_as_float(ur[i]), sc);
+              if (gb) gv += gb[j + i];
+              if (ub) uv += ub[j + i];
+              a[i] = __fmul_rn(act_fn(g.act_kind, gv, uv, g.limit, g.alpha), asc);
+            }
+            const uint4 o = make_uint4(pack_h2(a[0], a[1]), pack_h2(a[2], a[3]), pack_h2(a[4], a[5]),
+                                       pack_h2(a[6], a[7]));
+            uint8_t* dst = g.act + ((size_t)mb * g.KBo + j / kBK) * kATile + sw128_off(m, (j % kBK) / 8);
+            *reinterpret_cast<uint4*>(dst) = o;
+          }
+        }
+      } else {
+        const float* db = E.down_bias;
+        const float dsc = pow2f(ash);
+        for (int c = 0; c < g.NT; c += 8) {
+          uint32_t r[8];
+          tmem_ld8(tl + c, r);
+          tmem_ld_wait();
+          if (src >= 0) {
+            const int h = nt * g.NT + c;
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__uint_as_float(r[i]), dsc) + (db ? db[h + i] : 0.f);
+            float4* dst = reinterpret_cast<float4*>(g.Y + (size_t)R * g.H + h);
+            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+// out[t] = sum_j w[t,j] * Y[row_of[t,j]], j ascending (fmaf chain from 0, the
+// decode combine's order); rows of invalid experts are skipped.
+__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ Y, int H,
+                                                      const int* __restrict__ row_of, const float* __restrict__ wts,
+                                                      int top_k, uint16_t* __restrict__ out) {
+  const int t = blockIdx.x;
+  for (int h4 = threadIdx.x; h4 < H / 4; h4 += blockDim.x) {
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < top_k; ++j) {
+      const int r = row_of[t * top_k + j];
+      if (r < 0) continue;
+      const float w = wts[t * top_k + j];
+      const float4 y = reinterpret_cast<const float4*>(Y + (size_t)r * H)[h4];
+      o.x = fmaf(w, y.x, o.x);
+      o.y = fmaf(w, y.y, o.y);
+      o.z = fmaf(w, y.z, o.z);
+      o.w = fmaf(w, y.w, o.w);
+    }
+    const uint32_t lo = f32_to_bf16_bits(o.x) | ((uint32_t)f32_to_bf16_bits(o.y) << 16);
+    const uint32_t hi = f32_to_bf16_bits(o.z) | ((uint32_t)f32_to_bf16_bits(o.w) << 16);
+    reinterpret_cast<uint2*>(out + (size_t)t * H)[h4] = make_uint2(lo, hi);
+  }
+}
+
+// ------------------------------------------------------------------ router (T tokens)
+// One warp per token: logits[e] = bf16(x . W[e] + b[e]) for all E experts
+// (kept in shared memory), then top-k (ties -> lower id, NaN lowest) and a
+// softmax over the k selected logits, the decode router's rule
+// (tinyserve/_model_hooks.py:466-473).
+__global__ void __launch_bounds__(128) prefill_router_kernel(const uint16_t* __restrict__ x,
+                                                             const uint16_t* __restrict__ W,
+                                                             const float* __restrict__ b, int H, int E, int T,
+                                                             int top_k, int32_t* __restrict__ ids,
+                                                             float* __restrict__ wts) {
+  extern __shared__ float slog[];  // [4][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + warp;
+  if (t >= T) return;
+  float* lg = slog + warp * E;
+  const int n8 = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
+  for (int e = 0; e < E; ++e) {
+    const uint4* wr = reinterpret_cast<const uint4*>(W + (int64_t)e * H);
+    float acc = 0.f;
+    for (int c = lane; c < n8; c += 32) {
+      const uint4 a = xr[c], w = __ldg(wr + c);
+      const uint32_t av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc = fmaf(__uint_as_float(av[q] << 16), __uint_as_float(wv[q] << 16), acc);
+        acc = fmaf(__uint_as_float(av[q] & 0xFFFF0000u), __uint_as_float(wv[q] & 0xFFFF0000u), acc);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      if (b) acc += b[e];
+      lg[e] = bf16_bits_to_f32(f32_to_bf16_bits(acc));
+    }
+  }
+  __syncwarp();
+  float sel[8];
+  int sid[8];
+  uint32_t taken = 0;
+  for (int k = 0; k < top_k; ++k) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = 0; lane + 32 * j < E; ++j) {
+      if ((taken >> j) & 1u) continue;
+      const int ee = lane + 32 * j;
+      float v = lg[ee];
+      if (v != v) v = -INFINITY;
+      if (v > best || (v == best && ee < bi)) { best = v; bi = ee; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    sel[k] = best;
+    sid[k] = bi;
+    if (bi != 0x7fffffff && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+  }
+  if (lane == 0) {
+    const float mx = sel[0];
+    float den = 0.f, ex[8];
+    for (int k = 0; k < top_k; ++k) { ex[k] = __expf(sel[k] - mx); den += ex[k]; }
+    for (int k = 0; k < top_k; ++k) {
+      ids[(int64_t)t * top_k + k] = sid[k];
+      wts[(int64_t)t * top_k + k] = ex[k] / den;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+// Largest N tile <= 256 (multiple of 16) dividing `rows`; for the gate/up
+// projection the tile holds `pair` = 2 halves (gate, up) of NT/2 features each,
+// and NT/2 must divide I.
+static int pick_nt(int rows, bool pair) {
+  for (int nt = 256; nt >= 16; nt -= 16) {
+    if (pair ? (rows % (nt / 2) == 0 && (nt / 2) % 8 == 0) : rows % nt == 0) return nt;
+  }
+  return 0;
+}
+
+PrefillLayout prefill_layout(const TsbMoeSpec& sp, int T) {
+  PrefillLayout L{};
+  auto al = [](size_t v) { return (v + 1023) & ~size_t(1023); };
+  const int64_t n = (int64_t)T * sp.top_k;
+  L.mb_max = (int)((n + (int64_t)sp.n_experts * (kBM - 1)) / kBM);
+  L.rows_max = (int64_t)L.mb_max * kBM;
+  L.kbh = (sp.hidden + kBK - 1) / kBK;
+  L.kbi = (sp.inter + kBK - 1) / kBK;
+  L.nt_gu = pick_nt(sp.inter, true);
+  L.nt_dn = pick_nt(sp.hidden, false);
+  size_t o = 0;
+  L.err = o;          // int32 error word
+  L.total_mb = 4;     // int32
+  o = 256;
+  L.counts = o;   o = al(o + 4 * (size_t)sp.n_experts);
+  L.mb_expert = o; o = al(o + 4 * (size_t)L.mb_max);
+  L.row_of = o;   o = al(o + 4 * (size_t)n);
+  L.row_src = o;  o = al(o + 4 * (size_t)L.rows_max);
+  L.row_shift = o; o = al(o + (size_t)L.rows_max);
+  L.xp = o;       o = al(o + (size_t)L.mb_max * L.kbh * kATile);
+  L.act = o;      o = al(o + (size_t)L.mb_max * L.kbi * kATile);
+  L.y = o;        o = al(o + 4 * (size_t)L.rows_max * sp.hidden);
+  L.wgu_estride = (int64_t)2 * sp.inter * L.kbh * 128;
+  L.wdn_estride = (int64_t)sp.hidden * L.kbi * 128;
+  L.wgu = o;      o = al(o + (size_t)sp.n_experts * L.wgu_estride);
+  L.wdn = o;      o = al(o + (size_t)sp.n_experts * L.wdn_estride);
+  L.total = o;
+  return L;
+}
+
+static int num_sms() {
+  static int n = [] {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  return n;
+}
+
+template <int F>
+static void launch_tile_weights(const TileWArgs& a, int E, cudaStream_t st) {
+  const int64_t chunks = (int64_t)a.N * a.KB * 8;
+  const int grid = (int)std::min<int64_t>((chunks + 255) / 256, 2048);
+  tile_weights_kernel<F><<<dim3(grid, E), 256, 0, st>>>(a);
+}
+
+static int tile_weights(int fmt, const TileWArgs& a, int E, cudaStream_t st) {
+  switch (fmt) {
+    case FMT_Q8_0: launch_tile_weights<FMT_Q8_0>(a, E, st); break;
+    case FMT_Q4_K: launch_tile_weights<FMT_Q4_K>(a, E, st); break;
+    case FMT_Q5_K: launch_tile_weights<FMT_Q5_K>(a, E, st); break;
+    case FMT_Q6_K: launch_tile_weights<FMT_Q6_K>(a, E, st); break;
+    case FMT_MXFP4: launch_tile_weights<FMT_MXFP4>(a, E, st); break;
+    default: return set_error(TSB_ERR_UNSUPPORTED, "unsupported format");
+  }
+  return TSB_OK;
+}
+
+static int launch_gemm(const GemmArgs& g, int tiles_max, cudaStream_t st) {
+  static bool attr = [] {
+    return cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) ==
+           cudaSuccess;
+  }();
+  if (!attr) return set_error(TSB_ERR_CUDA, "cannot enable the grouped GEMM's shared memory");
+  const int grid = std::max(1, std::min(tiles_max, num_sms()));
+  grouped_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(g);
+  return TSB_OK;
+}
+
+int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, int T, const void* rw,
+                       const float* rb, int32_t* ids, float* wts, void* out, char* ws, const PrefillLayout& L,
+                       cudaStream_t st) {
+  const int E = sp.n_experts, k = sp.top_k, n = T * k;
+  int32_t* err = reinterpret_cast<int32_t*>(ws + L.err);
+  int* total_mb = reinterpret_cast<int*>(ws + L.total_mb);
+  int* counts = reinterpret_cast<int*>(ws + L.counts);
+  int* mb_expert = reinterpret_cast<int*>(ws + L.mb_expert);
+  int* row_of = reinterpret_cast<int*>(ws + L.row_of);
+  int* row_src = reinterpret_cast<int*>(ws + L.row_src);
+  int8_t* row_shift = reinterpret_cast<int8_t*>(ws + L.row_shift);
+  uint8_t* xp = reinterpret_cast<uint8_t*>(ws + L.xp);
+  uint8_t* act = reinterpret_cast<uint8_t*>(ws + L.act);
+  float* Y = reinterpret_cast<float*>(ws + L.y);
+  uint8_t* wgu = reinterpret_cast<uint8_t*>(ws + L.wgu);
+  uint8_t* wdn = reinterpret_cast<uint8_t*>(ws + L.wdn);
+
+  if (rw) {
+    const size_t sm = 4 * sizeof(float) * (size_t)E;  // <= 16 KB for E <= 1024
+    prefill_router_kernel<<<(T + 3) / 4, 128, sm, st>>>(static_cast<const uint16_t*>(x),
+                                                         static_cast<const uint16_t*>(rw), rb, sp.hidden, E, T, k,
+                                                         ids, wts);
+  }
+  route_count_kernel<<<E, 256, 0, st>>>(ids, n, E, counts, row_of, err);
+  route_place_kernel<<<E, 1024, 0, st>>>(ids, n, k, E, counts, row_of, row_src, mb_expert, total_mb);
+  gather_rows_kernel<<<(int)((L.rows_max + 7) / 8), 256, 0, st>>>(static_cast<const uint16_t*>(x), sp.hidden, L.kbh,
+                                                                  row_src, total_mb, xp, row_shift);
+  if (sp.inter % kBK) {
+    // K padding of the activation tiles must read as zero.
+    cudaMemsetAsync(act, 0, (size_t)L.mb_max * L.kbi * kATile, st);
+  }
+  TileWArgs tg{ex, counts, 0, sp.gate_up_layout, sp.inter, 2 * sp.inter, sp.hidden, L.kbh, L.nt_gu, wgu,
+               L.wgu_estride};
+  int rc = tile_weights(sp.fmt_gate_up, tg, E, st);
+  if (rc) return rc;
+  TileWArgs td{ex, counts, 1, sp.gate_up_layout, sp.inter, sp.hidden, sp.inter, L.kbi, L.nt_dn, wdn, L.wdn_estride};
+  rc = tile_weights(sp.fmt_down, td, E, st);
+  if (rc) return rc;
+
+  GemmArgs g{};
+  g.A = xp;
+  g.KB = L.kbh;
+  g.W = wgu;
+  g.w_estride = L.wgu_estride;
+  g.NT = L.nt_gu;
+  g.ntiles = 2 * sp.inter / L.nt_gu;
+  g.mb_expert = mb_expert;
+  g.total_mb = total_mb;
+  g.row_src = row_src;
+  g.row_shift = row_shift;
+  g.experts = ex;
+  g.mode = 0;
+  g.act = act;
+  g.KBo = L.kbi;
+  g.act_kind = sp.activation;
+  g.limit = sp.limit;
+  g.alpha = sp.alpha;
+  g.err = err;
+  rc = launch_gemm(g, L.mb_max * g.ntiles, st);
+  if (rc) return rc;
+  GemmArgs d = g;
+  d.A = act;
+  d.KB = L.kbi;
+  d.W = wdn;
+  d.w_estride = L.wdn_estride;
+  d.NT = L.nt_dn;
+  d.ntiles = sp.hidden / L.nt_dn;
+  d.mode = 1;
+  d.Y = Y;
+  d.H = sp.hidden;
+  rc = launch_gemm(d, L.mb_max * d.ntiles, st);
+  if (rc) return rc;
+  combine_kernel<<<T, 256, 0, st>>>(Y, sp.hidden, row_of, wts, k, static_cast<uint16_t*>(out));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return TSB_OK;
+}
+
+}  // namespace tsb

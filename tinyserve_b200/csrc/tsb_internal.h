@@ -27,6 +27,16 @@ int launch_router(const void* x, const void* W, const float* b, int H, int E, in
 int launch_moe_fused(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, const void* rw, const float* rb,
                      int32_t* ids, float* wts, void* out, float* act, float* logits, unsigned* gridbar, int32_t* err,
                      cudaStream_t st);
+// Workspace layout of tsb_moe_prefill (byte offsets) and its tile geometry.
+struct PrefillLayout {
+  size_t err, total_mb, counts, mb_expert, row_of, row_src, row_shift, xp, act, y, wgu, wdn, total;
+  int64_t rows_max, wgu_estride, wdn_estride;
+  int mb_max, kbh, kbi, nt_gu, nt_dn;
+};
+PrefillLayout prefill_layout(const TsbMoeSpec& sp, int T);
+int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, int T, const void* rw,
+                       const float* rb, int32_t* ids, float* wts, void* out, char* ws, const PrefillLayout& L,
+                       cudaStream_t st);
 int launch_dequant(int fmt, const void* w, const void* s, int64_t rows, int64_t cols, void* out, int odt,
                    cudaStream_t st);
 

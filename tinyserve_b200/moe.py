@@ -61,6 +61,7 @@ class QuantMoE:
         raw = bytes(ctypes.string_at(ctypes.addressof(table), ctypes.sizeof(table)))
         self._table = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.device)
         self._ws_cache: dict[int, torch.Tensor] = {}
+        self._pws_cache: dict[int, torch.Tensor] = {}
 
     def workspace(self, T: int) -> torch.Tensor:
         if T not in self._ws_cache:
@@ -96,6 +97,56 @@ class QuantMoE:
             torch.cuda.current_stream(self.device).cuda_stream)
         _lib.check(rc)
         return out, ids, weights
+
+    def prefill_workspace(self, T: int) -> torch.Tensor:
+        if T not in self._pws_cache:
+            n = _lib.lib().tsb_moe_prefill_workspace(ctypes.byref(self.spec), T)
+            self._pws_cache[T] = torch.zeros(n, dtype=torch.uint8, device=self.device)
+        return self._pws_cache[T]
+
+    def prefill(self, x: torch.Tensor, ids: torch.Tensor | None = None, weights: torch.Tensor | None = None,
+                out: torch.Tensor | None = None):
+        """T tokens through the layer as grouped GEMMs (the reference's batched
+        path, ``ExpertPipeline.execute_layer_experts_batched``,
+        tinyserve/expert_pipeline.py:166-239).  x: bf16 [T, H]; routing as in
+        :meth:`decode`.  Returns (out, ids, weights)."""
+        if x.dtype != torch.bfloat16:
+            raise TypeError("x must be bfloat16")
+        if x.dim() != 2 or x.shape[1] != self.hidden:
+            raise ValueError(f"x must be [T, {self.hidden}]")
+        x = x.contiguous()
+        T = x.shape[0]
+        given = ids is not None
+        if not given:
+            if self.router_w is None:
+                raise ValueError("no router weights: pass ids and weights")
+            ids = torch.empty(T, self.top_k, dtype=torch.int32, device=self.device)
+            weights = torch.empty(T, self.top_k, dtype=torch.float32, device=self.device)
+        else:
+            ids = ids.to(device=self.device, dtype=torch.int32).contiguous()
+            weights = weights.to(device=self.device, dtype=torch.float32).contiguous()
+            if ids.shape != (T, self.top_k) or weights.shape != (T, self.top_k):
+                raise ValueError(f"ids and weights must be [T, {self.top_k}]")
+        if out is None:
+            out = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=self.device)
+        if T == 0:
+            return out, ids, weights
+        ws = self.prefill_workspace(T)
+        rc = _lib.lib().tsb_moe_prefill(
+            ctypes.byref(self.spec), self._table.data_ptr(), x.data_ptr(), T,
+            None if given else _p(self.router_w), None if given else _p(self.router_b),
+            ids.data_ptr(), weights.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
+            torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc)
+        return out, ids, weights
+
+    def prefill_error(self, T: int) -> int:
+        """Read and clear the device error word of the T-token prefill workspace."""
+        code = ctypes.c_int32()
+        ws = self.prefill_workspace(T)
+        _lib.check(_lib.lib().tsb_read_device_error(ws.data_ptr(), ctypes.byref(code),
+                                                    torch.cuda.current_stream(self.device).cuda_stream))
+        return code.value
 
     def device_error(self, T: int = 1) -> int:
         code = ctypes.c_int32()

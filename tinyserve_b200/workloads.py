@@ -63,3 +63,15 @@ def layer_bytes(layer: QuantMoE) -> tuple[int, int]:
     n = sum(t.numel() for t in (e.gate, e.up, e.down, e.gate_scales, e.up_scales, e.down_scales) if t is not None)
     r = layer.router_w.numel() * 2 if layer.router_w is not None else 0
     return n, r
+
+
+def zipf_routing(T: int, n_experts: int = E20, top_k: int = K20, s: float = 1.1, seed: int = 0):
+    """Config 4 routing: top_k distinct experts per token drawn without
+    replacement with p_e proportional to (e + 1)^-s, routing weights the
+    softmax of top_k seeded N(0, 1) logits.  Returns (ids int32 [T, k],
+    weights fp32 [T, k]) on the CPU."""
+    g = torch.Generator().manual_seed(seed)
+    p = torch.arange(1, n_experts + 1, dtype=torch.float64).pow(-s)
+    ids = torch.multinomial(p.expand(T, n_experts), top_k, replacement=False, generator=g).to(torch.int32)
+    w = torch.softmax(torch.randn(T, top_k, generator=g), dim=1).to(torch.float32)
+    return ids, w
