@@ -164,3 +164,55 @@ def test_prefill_bad_ids_reported(dev):
     ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
     assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
     assert layer.prefill_error(T) == 0
+
+
+@pytest.mark.parametrize("layout", ["separate", "chunked"])
+def test_prefill_mxfp4_half_k_blocks(dev, layout):
+    """MXFP4 decoded inside the GEMM with H and I odd multiples of 32 (the last
+    64-wide k-block holds one 32-block) and non-interleaved gate/up."""
+    H, I, E, k, T = 288, 160, 5, 2, 150
+    layer, dense, _ = _build_layer(dev, TSB_MXFP4, TSB_MXFP4, H, I, E, k, layout, seed=81, bias=True)
+    ids, wts = _routing(T, E, k, seed=8)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(11)).to(torch.bfloat16)
+    out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
+    ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
+    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+
+
+def test_prefill_mxfp4_extreme_scales(dev):
+    """E8M0 scale bytes far from the usual range (2^-27 and 2^13) take the
+    fp32 route of the in-kernel decode and still match."""
+    from tinyserve_b200.moe import ExpertWeights, QuantMoE
+    from tests.helpers import make_weight, oracle_dequant
+    H, I, E, k, T = 256, 128, 3, 1, 64
+    experts, dense = [], []
+    for e in range(E):
+        gu, gus = make_weight(TSB_MXFP4, 2 * I, H, 900 + e)
+        dn, dns = make_weight(TSB_MXFP4, H, I, 950 + e)
+        gus = gus.clone()
+        gus.view(-1)[::7] = 100
+        gus.view(-1)[3::11] = 140
+        wgu = oracle_dequant(TSB_MXFP4, gu, gus, 2 * I, H)
+        wd = oracle_dequant(TSB_MXFP4, dn, dns, H, I)
+        experts.append(ExpertWeights(gate=gu.to(dev), down=dn.to(dev), gate_scales=gus.to(dev),
+                                     down_scales=dns.to(dev)))
+        dense.append((wgu[0::2], wgu[1::2], wd, None, None, None))
+    layer = QuantMoE(experts, fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=H, inter=I, top_k=k,
+                     gate_up_layout="interleaved")
+    ids, wts = _routing(T, E, k, seed=9)
+    x = (torch.randn(T, H, generator=torch.Generator().manual_seed(12)) * 1e-3).to(torch.bfloat16)
+    out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
+    ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
+    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+
+
+def test_prefill_mxfp4_in_kernel_decode_subprocess(dev):
+    """The opt-in path that decodes MXFP4 inside the GEMM (TSB_PREFILL_FUSED=1,
+    read once per process) passes the MXFP4 cases of this file."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, TSB_PREFILL_FUSED="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", __file__, "-k", "mxfp4 and not subprocess"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

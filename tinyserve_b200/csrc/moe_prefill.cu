@@ -36,6 +36,7 @@
 // an mbarrier.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 
 #include "../../include/tsb_moe.h"
 #include "moe_math.cuh"
@@ -188,9 +189,6 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint16_t* __rest
 }
 
 // ------------------------------------------------------------------ weights
-__constant__ float kE2m1[16] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f,
-                                -0.f, -0.5f, -1.f, -1.5f, -2.f, -3.f, -4.f, -6.f};
-
 // Eight consecutive elements (flat index q0, a multiple of 8) of a weight
 // stream, decoded with tsb_dequant's arithmetic (gguf_dequant_torch.py:118-249,
 // mxfp4.py:20-44).
@@ -237,10 +235,13 @@ __device__ __forceinline__ void deq8(const uint8_t* __restrict__ w, const uint8_
     const int e = (int)s[q0 >> 5] - 127;
     const int e1 = e / 2, e2 = e - e1;
     const float p1 = __uint_as_float((uint32_t)(e1 + 127) << 23), p2 = __uint_as_float((uint32_t)(e2 + 127) << 23);
+    const uint32_t q = *reinterpret_cast<const uint32_t*>(b);  // 4-byte aligned: l0 is a multiple of 8
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      v[2 * i] = __fmul_rn(__fmul_rn(kE2m1[b[i] & 0xF], p1), p2);
-      v[2 * i + 1] = __fmul_rn(__fmul_rn(kE2m1[b[i] >> 4], p1), p2);
+      // e2m1 -> f16 is exact, so this is the table value of each code
+      const uint32_t h = cvt_e2m1x2((q >> (8 * i)) & 0xFF);
+      v[2 * i] = __fmul_rn(__fmul_rn(half_bits_to_f32((uint16_t)(h & 0xFFFF)), p1), p2);
+      v[2 * i + 1] = __fmul_rn(__fmul_rn(half_bits_to_f32((uint16_t)(h >> 16)), p1), p2);
     }
   }
 }
@@ -259,24 +260,20 @@ struct TileWArgs {
   int64_t estride;  // bytes per expert
 };
 
-// One thread per 16-byte chunk of the tiled output, in output order.  For the
-// gate/up projection a tile's first NT/2 rows are gate features and the next
-// NT/2 the same up features, whatever the source layout.
+// One CTA per (N tile, k-block) of one expert (blockIdx.y): eight threads per
+// tile row, one 16-byte chunk (8 elements) each, so a warp writes four whole
+// 128-byte rows.  For the gate/up projection a tile's first NT/2 rows are gate
+// features and the next NT/2 the same up features, whatever the source layout.
 template <int F>
 __global__ void __launch_bounds__(256) tile_weights_kernel(const TileWArgs a) {
   const int e = blockIdx.y;
   if (a.counts[e] == 0) return;
   const TsbExpert& E = a.experts[e];
-  const int64_t nchunks = (int64_t)a.N * a.KB * 8;
+  const int nt = blockIdx.x / a.KB, kb = blockIdx.x % a.KB;
   const int half = a.NT / 2;
-  uint8_t* base = a.out + (int64_t)e * a.estride;
-  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nchunks; q += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(q & 7);
-    int64_t t = q >> 3;
-    const int r = (int)(t % a.NT);
-    t /= a.NT;
-    const int kb = (int)(t % a.KB);
-    const int nt = (int)(t / a.KB);
+  uint8_t* tile = a.out + (int64_t)e * a.estride + ((int64_t)nt * a.KB + kb) * a.NT * 128;
+  for (int q = threadIdx.x; q < a.NT * 8; q += blockDim.x) {
+    const int r = q >> 3, c = q & 7;
     const int k0 = kb * kBK + c * 8;
     const uint8_t* w;
     const uint8_t* s;
@@ -310,7 +307,7 @@ __global__ void __launch_bounds__(256) tile_weights_kernel(const TileWArgs a) {
       }
       o = make_uint4(h[0], h[1], h[2], h[3]);
     }
-    *reinterpret_cast<uint4*>(base + ((int64_t)(nt * a.KB + kb) * a.NT + r) * 128 + (((c ^ (r & 7)) & 7) << 4)) = o;
+    *reinterpret_cast<uint4*>(tile + sw128_off(r, c)) = o;
   }
 }
 
@@ -335,6 +332,10 @@ struct GemmArgs {
   float* Y;                // mode 1 output [rows, H]
   int H;
   int* err;
+  // in-kernel weight decode (MXFP4): source geometry
+  int Kw;                  // weight columns (H for gate/up, I for down)
+  int I;
+  int layout;              // TSB_GU_*
 };
 
 __device__ __forceinline__ float pow2f(int e) {  // 2^e for |e| <= 126, exact
@@ -358,13 +359,85 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&p);
 }
 
+__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Four MXFP4 bytes (8 e2m1 codes, low nibble first) times 2^e as eight fp16
+// values, the fp16 rounding of tsb_dequant's exact fp32 value: e2m1 -> f16 is
+// exact and, when 2^e is itself an fp16 number (-24 <= e <= 15), one correctly
+// rounded f16 multiply gives that rounding; other exponents take the fp32 route.
+__device__ __forceinline__ uint4 mx_chunk(uint32_t q4, int e) {
+  uint32_t h[4];
+  if (e >= -24 && e <= 15) {
+    const uint32_t sb = e >= -14 ? (uint32_t)(e + 15) << 10 : 1u << (e + 24);
+    const uint32_t s2 = sb | (sb << 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = hmul2_bits(cvt_e2m1x2((q4 >> (8 * i)) & 0xFFu), s2);
+  } else {
+    const int e1 = e / 2, e2 = e - e1;
+    const float p1 = __uint_as_float((uint32_t)(e1 + 127) << 23), p2 = __uint_as_float((uint32_t)(e2 + 127) << 23);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t c = cvt_e2m1x2((q4 >> (8 * i)) & 0xFFu);
+      const float lo = __fmul_rn(__fmul_rn(half_bits_to_f32((uint16_t)(c & 0xFFFF)), p1), p2);
+      const float hi = __fmul_rn(__fmul_rn(half_bits_to_f32((uint16_t)(c >> 16)), p1), p2);
+      const __half2 p = __halves2half2(__float2half_rn(lo), __float2half_rn(hi));
+      h[i] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+  }
+  return make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+// Source of B row r (0 <= r < NT) of tile column nt for the in-kernel decode:
+// MXFP4 blocks and E8M0 scales of the weight row (gate/up tiles hold NT/2 gate
+// rows then the same NT/2 up rows).
+__device__ __forceinline__ void mx_row(const GemmArgs& g, const TsbExpert& E, int nt, int r, const uint8_t*& w,
+                                       const uint8_t*& s) {
+  const int64_t nblk = g.Kw / 32;
+  int64_t row;
+  const void* wm;
+  const void* sm;
+  if (g.mode == 1) {
+    wm = E.down;
+    sm = E.down_scales;
+    row = (int64_t)nt * g.NT + r;
+  } else {
+    const int half = g.NT / 2;
+    const bool up = r >= half;
+    const int64_t j = (int64_t)nt * half + (up ? r - half : r);
+    if (g.layout == TSB_GU_SEPARATE) {
+      wm = up ? E.up : E.gate;
+      sm = up ? E.up_scales : E.gate_scales;
+      row = j;
+    } else {
+      wm = E.gate;
+      sm = E.gate_scales;
+      row = g.layout == TSB_GU_INTERLEAVED ? 2 * j + (up ? 1 : 0) : (up ? g.I + j : j);
+    }
+  }
+  w = static_cast<const uint8_t*>(wm) + row * nblk * 16;
+  s = static_cast<const uint8_t*>(sm) + row * nblk;
+}
+
 // Persistent: CTA c takes tiles c, c + grid, ... of the (row block, N tile)
 // grid, N fastest so that neighbouring CTAs share the token tile in L2.
 // Warp 0 (one lane) streams A and W k-blocks into a kNS-stage ring; warp 1
 // (one lane) issues 4 MMAs (K = 16 each) per k-block into one of two
 // tensor-memory accumulators; warps 4-7 drain the other accumulator (warp
 // 4+q reads lanes 32q..32q+31, i.e. rows 32q..32q+31 of the tile).
-__global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const GemmArgs g) {
+//
+// BF = FMT_MXFP4: the B operand is decoded inside the kernel.  Warps 8-15 (one
+// thread per B row) read each k-block's raw MXFP4 bytes and scales straight
+// from the expert's weight stream (kPf k-blocks ahead, in registers), write
+// the fp16 row into the stage's swizzled B tile and arrive on bfull; the MMA
+// waits for both the A copy and the B decode of a stage.
+constexpr int kPf = 4;
+
+template <int BF>
+__global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kNS * kStage);
@@ -373,7 +446,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const Gem
   uint64_t* tfull = bars + 2 * kNS;
   uint64_t* tempty = bars + 2 * kNS + 2;
   uint64_t* fin = bars + 2 * kNS + 4;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2 * kNS + 5);
+  uint64_t* bfull = bars + 2 * kNS + 5;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3 * kNS + 5);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -386,6 +460,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const Gem
       mbar_init(&tempty[b], 4);
     }
     mbar_init(fin, 1);
+    if (BF)
+      for (int s = 0; s < kNS; ++s) mbar_init(&bfull[s], 8);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -406,14 +482,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const Gem
       const int mb = tile / g.ntiles, nt = tile % g.ntiles;
       const int e = g.mb_expert[mb];
       const uint8_t* a = g.A + (size_t)mb * g.KB * kATile;
-      const uint8_t* b = g.W + e * g.w_estride + (size_t)nt * g.KB * btile;
+      const uint8_t* b = BF ? nullptr : g.W + e * g.w_estride + (size_t)nt * g.KB * btile;
       for (int kb = 0; kb < g.KB; ++kb, ++it) {
         const int s = it % kNS;
         if (!mbar_wait(&empty[s], ((it / kNS) & 1) ^ 1, g.err)) { ok = false; break; }
         uint8_t* sa = smem + (size_t)s * kStage;
-        mbar_arrive_expect_tx(&full[s], kATile + btile);
+        mbar_arrive_expect_tx(&full[s], kATile + (BF ? 0u : btile));
         bulk_g2s(sa, a + (size_t)kb * kATile, kATile, &full[s]);
-        bulk_g2s(sa + kATile, b + (size_t)kb * btile, btile, &full[s]);
+        if (!BF) bulk_g2s(sa + kATile, b + (size_t)kb * btile, btile, &full[s]);
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -428,6 +504,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const Gem
       for (int kb = 0; kb < g.KB; ++kb, ++it) {
         const int s = it % kNS;
         if (!mbar_wait(&full[s], (it / kNS) & 1, g.err)) { ok = false; break; }
+        if (BF && !mbar_wait(&bfull[s], (it / kNS) & 1, g.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + (size_t)s * kStage), sb = sa + kATile;
 #pragma unroll
@@ -440,7 +517,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const Gem
     // Every MMA issued above completes before tensor memory is released.
     umma_commit(fin);
     mbar_wait(fin, 0, g.err);
-  } else if (warp >= 4) {
+  } else if (warp >= 4 && warp < 8) {
     const int q = warp - 4;
     const int m = 32 * q + lane;
     uint32_t tc = 0;
@@ -503,6 +580,68 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_kernel(const Gem
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  } else if (BF && warp >= 8) {
+    const int r = threadIdx.x - 256;
+    const bool active = r < g.NT;
+    const int mine = (int)blockIdx.x < total_tiles ? (total_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int items = mine * g.KB;
+    // load cursor, kPf items ahead of the decode
+    int lt = blockIdx.x, lkb = 0;
+    const uint8_t* lw = nullptr;
+    const uint8_t* ls = nullptr;
+    auto set_row = [&]() {
+      if (active && lt < total_tiles) {
+        const int mb = lt / g.ntiles, nt = lt % g.ntiles;
+        mx_row(g, g.experts[g.mb_expert[mb]], nt, r, lw, ls);
+      }
+    };
+    set_row();
+    uint4 rlo[kPf], rhi[kPf];
+    uint32_t rsc[kPf];
+    auto load = [&](uint4& lo, uint4& hi, uint32_t& sc) {
+      lo = hi = make_uint4(0, 0, 0, 0);
+      sc = 0;
+      if (active && lt < total_tiles) {
+        const uint8_t* p = lw + (size_t)lkb * 32;
+        lo = __ldg(reinterpret_cast<const uint4*>(p));
+        sc = __ldg(ls + 2 * lkb);
+        if (lkb * kBK + 32 < g.Kw) {
+          hi = __ldg(reinterpret_cast<const uint4*>(p + 16));
+          sc |= (uint32_t)__ldg(ls + 2 * lkb + 1) << 8;
+        }
+      }
+      if (++lkb == g.KB) {
+        lkb = 0;
+        lt += gridDim.x;
+        set_row();
+      }
+    };
+#pragma unroll
+    for (int p = 0; p < kPf; ++p) load(rlo[p], rhi[p], rsc[p]);
+    bool ok = true;
+    for (int base = 0; ok && base < items; base += kPf) {
+#pragma unroll
+      for (int p = 0; p < kPf; ++p) {
+        const int item = base + p;
+        if (!ok || item >= items) break;
+        const uint4 lo = rlo[p], hi = rhi[p];
+        const uint32_t sc = rsc[p];
+        load(rlo[p], rhi[p], rsc[p]);
+        const int s = item % kNS;
+        if (!mbar_wait(&empty[s], ((item / kNS) & 1) ^ 1, g.err)) { ok = false; break; }
+        if (active) {
+          uint8_t* brow = smem + (size_t)s * kStage + kATile;
+          const int e0 = (int)(sc & 0xFF) - 127, e1 = (int)(sc >> 8) - 127;
+          const uint32_t q[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(brow + sw128_off(r, c)) = mx_chunk(q[c], c < 4 ? e0 : e1);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bfull[s]);
+      }
     }
   }
   __syncthreads();
@@ -618,6 +757,16 @@ static int pick_nt(int rows, bool pair) {
   return 0;
 }
 
+// MXFP4 weights decoded inside the GEMM (opt-in, TSB_PREFILL_FUSED=1): saves
+// the fp16 weight tiles but is latency-bound on the raw loads at present.
+static bool fused_mxfp4() {
+  static const bool on = [] {
+    const char* v = getenv("TSB_PREFILL_FUSED");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
 PrefillLayout prefill_layout(const TsbMoeSpec& sp, int T) {
   PrefillLayout L{};
   auto al = [](size_t v) { return (v + 1023) & ~size_t(1023); };
@@ -640,8 +789,10 @@ PrefillLayout prefill_layout(const TsbMoeSpec& sp, int T) {
   L.xp = o;       o = al(o + (size_t)L.mb_max * L.kbh * kATile);
   L.act = o;      o = al(o + (size_t)L.mb_max * L.kbi * kATile);
   L.y = o;        o = al(o + 4 * (size_t)L.rows_max * sp.hidden);
-  L.wgu_estride = (int64_t)2 * sp.inter * L.kbh * 128;
-  L.wdn_estride = (int64_t)sp.hidden * L.kbi * 128;
+  const bool fgu = sp.fmt_gate_up == FMT_MXFP4 && fused_mxfp4();
+  const bool fdn = sp.fmt_down == FMT_MXFP4 && fused_mxfp4();
+  L.wgu_estride = fgu ? 0 : (int64_t)2 * sp.inter * L.kbh * 128;
+  L.wdn_estride = fdn ? 0 : (int64_t)sp.hidden * L.kbi * 128;
   L.wgu = o;      o = al(o + (size_t)sp.n_experts * L.wgu_estride);
   L.wdn = o;      o = al(o + (size_t)sp.n_experts * L.wdn_estride);
   L.total = o;
@@ -659,9 +810,7 @@ static int num_sms() {
 
 template <int F>
 static void launch_tile_weights(const TileWArgs& a, int E, cudaStream_t st) {
-  const int64_t chunks = (int64_t)a.N * a.KB * 8;
-  const int grid = (int)std::min<int64_t>((chunks + 255) / 256, 2048);
-  tile_weights_kernel<F><<<dim3(grid, E), 256, 0, st>>>(a);
+  tile_weights_kernel<F><<<dim3((a.N / a.NT) * a.KB, E), 256, 0, st>>>(a);
 }
 
 static int tile_weights(int fmt, const TileWArgs& a, int E, cudaStream_t st) {
@@ -676,14 +825,15 @@ static int tile_weights(int fmt, const TileWArgs& a, int E, cudaStream_t st) {
   return TSB_OK;
 }
 
+template <int BF>
 static int launch_gemm(const GemmArgs& g, int tiles_max, cudaStream_t st) {
   static bool attr = [] {
-    return cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) ==
-           cudaSuccess;
+    return cudaFuncSetAttribute(grouped_gemm_kernel<BF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kGemmSmem) == cudaSuccess;
   }();
   if (!attr) return set_error(TSB_ERR_CUDA, "cannot enable the grouped GEMM's shared memory");
   const int grid = std::max(1, std::min(tiles_max, num_sms()));
-  grouped_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(g);
+  grouped_gemm_kernel<BF><<<grid, BF ? 512 : 256, kGemmSmem, st>>>(g);
   return TSB_OK;
 }
 
@@ -720,10 +870,12 @@ int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x,
   }
   TileWArgs tg{ex, counts, 0, sp.gate_up_layout, sp.inter, 2 * sp.inter, sp.hidden, L.kbh, L.nt_gu, wgu,
                L.wgu_estride};
-  int rc = tile_weights(sp.fmt_gate_up, tg, E, st);
+  const bool fgu = sp.fmt_gate_up == FMT_MXFP4 && fused_mxfp4();
+  const bool fdn = sp.fmt_down == FMT_MXFP4 && fused_mxfp4();
+  int rc = fgu ? TSB_OK : tile_weights(sp.fmt_gate_up, tg, E, st);
   if (rc) return rc;
   TileWArgs td{ex, counts, 1, sp.gate_up_layout, sp.inter, sp.hidden, sp.inter, L.kbi, L.nt_dn, wdn, L.wdn_estride};
-  rc = tile_weights(sp.fmt_down, td, E, st);
+  rc = fdn ? TSB_OK : tile_weights(sp.fmt_down, td, E, st);
   if (rc) return rc;
 
   GemmArgs g{};
@@ -745,7 +897,11 @@ int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x,
   g.limit = sp.limit;
   g.alpha = sp.alpha;
   g.err = err;
-  rc = launch_gemm(g, L.mb_max * g.ntiles, st);
+  g.Kw = sp.hidden;
+  g.I = sp.inter;
+  g.layout = sp.gate_up_layout;
+  rc = fgu ? launch_gemm<FMT_MXFP4>(g, L.mb_max * g.ntiles, st)
+                                   : launch_gemm<0>(g, L.mb_max * g.ntiles, st);
   if (rc) return rc;
   GemmArgs d = g;
   d.A = act;
@@ -757,7 +913,9 @@ int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x,
   d.mode = 1;
   d.Y = Y;
   d.H = sp.hidden;
-  rc = launch_gemm(d, L.mb_max * d.ntiles, st);
+  d.Kw = sp.inter;
+  rc = fdn ? launch_gemm<FMT_MXFP4>(d, L.mb_max * d.ntiles, st)
+                                : launch_gemm<0>(d, L.mb_max * d.ntiles, st);
   if (rc) return rc;
   combine_kernel<<<T, 256, 0, st>>>(Y, sp.hidden, row_of, wts, k, static_cast<uint16_t*>(out));
   const cudaError_t e = cudaGetLastError();
