@@ -338,6 +338,13 @@ struct GemmArgs {
   int layout;              // TSB_GU_*
 };
 
+// Bounded wait by a whole warp with a warp-uniform outcome: if any lane gave up,
+// every lane does, so the warp never splits around a warp-wide instruction.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const bool ok = mbar_wait(bar, parity, err);
+  return __all_sync(0xffffffffu, ok);
+}
+
 __device__ __forceinline__ float pow2f(int e) {  // 2^e for |e| <= 126, exact
   return __uint_as_float((uint32_t)(127 + e) << 23);
 }
@@ -434,24 +441,32 @@ __device__ __forceinline__ void mx_row(const GemmArgs& g, const TsbExpert& E, in
 // from the expert's weight stream (kPf k-blocks ahead, in registers), write
 // the fp16 row into the stage's swizzled B tile and arrive on bfull; the MMA
 // waits for both the A copy and the B decode of a stage.
-constexpr int kPf = 4;
+constexpr int kNSFused = 3;                 // A/B stages of the in-kernel decode variant
+constexpr int kRawItems = 4;                // k-blocks per raw copy
+constexpr int kRawSlots = 2;
+constexpr int kRawPitch = kRawItems * 32 + 16;   // 144 B: row pitch off the 128-byte bank period
+constexpr int kRawSlot = 256 * kRawPitch;
+constexpr size_t kGemmSmemFused = 1024 + (size_t)kNSFused * kStage + (size_t)kRawSlots * kRawSlot + 256;
 
 template <int BF>
 __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const GemmArgs g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kNS * kStage);
+  constexpr int NS = BF ? kNSFused : kNS;
+  uint8_t* raw = smem + (size_t)NS * kStage;  // BF: kRawSlots x kRawSlot raw-weight ring
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + (BF ? kRawSlots * kRawSlot : 0));
   uint64_t* full = bars;
-  uint64_t* empty = bars + kNS;
-  uint64_t* tfull = bars + 2 * kNS;
-  uint64_t* tempty = bars + 2 * kNS + 2;
-  uint64_t* fin = bars + 2 * kNS + 4;
-  uint64_t* bfull = bars + 2 * kNS + 5;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3 * kNS + 5);
+  uint64_t* empty = bars + NS;
+  uint64_t* tfull = bars + 2 * NS;
+  uint64_t* tempty = bars + 2 * NS + 2;
+  uint64_t* fin = bars + 2 * NS + 4;
+  uint64_t* bfull = bars + 2 * NS + 5;
+  uint64_t* rfull = bars + 3 * NS + 5;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3 * NS + 5 + kRawSlots);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kNS; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -460,8 +475,10 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
       mbar_init(&tempty[b], 4);
     }
     mbar_init(fin, 1);
-    if (BF)
-      for (int s = 0; s < kNS; ++s) mbar_init(&bfull[s], 8);
+    if (BF) {
+      for (int s = 0; s < NS; ++s) mbar_init(&bfull[s], 8);
+      for (int s = 0; s < kRawSlots; ++s) mbar_init(&rfull[s], 8);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -484,8 +501,8 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
       const uint8_t* a = g.A + (size_t)mb * g.KB * kATile;
       const uint8_t* b = BF ? nullptr : g.W + e * g.w_estride + (size_t)nt * g.KB * btile;
       for (int kb = 0; kb < g.KB; ++kb, ++it) {
-        const int s = it % kNS;
-        if (!mbar_wait(&empty[s], ((it / kNS) & 1) ^ 1, g.err)) { ok = false; break; }
+        const int s = it % NS;
+        if (!mbar_wait(&empty[s], ((it / NS) & 1) ^ 1, g.err)) { ok = false; break; }
         uint8_t* sa = smem + (size_t)s * kStage;
         mbar_arrive_expect_tx(&full[s], kATile + (BF ? 0u : btile));
         bulk_g2s(sa, a + (size_t)kb * kATile, kATile, &full[s]);
@@ -502,9 +519,9 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
       tc_fence_after();
       const uint32_t d = tbase + (uint32_t)buf * 256u;
       for (int kb = 0; kb < g.KB; ++kb, ++it) {
-        const int s = it % kNS;
-        if (!mbar_wait(&full[s], (it / kNS) & 1, g.err)) { ok = false; break; }
-        if (BF && !mbar_wait(&bfull[s], (it / kNS) & 1, g.err)) { ok = false; break; }
+        const int s = it % NS;
+        if (!mbar_wait(&full[s], (it / NS) & 1, g.err)) { ok = false; break; }
+        if (BF && !mbar_wait(&bfull[s], (it / NS) & 1, g.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + (size_t)s * kStage), sb = sa + kATile;
 #pragma unroll
@@ -523,7 +540,7 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
     uint32_t tc = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tc) {
       const int buf = tc & 1;
-      if (!mbar_wait(&tfull[buf], (tc >> 1) & 1, g.err)) break;
+      if (!warp_wait(&tfull[buf], (tc >> 1) & 1, g.err)) break;
       tc_fence_after();
       const int mb = tile / g.ntiles, nt = tile % g.ntiles;
       const int R = mb * kBM + m;
@@ -582,66 +599,83 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
       if (lane == 0) mbar_arrive(&tempty[buf]);
     }
   } else if (BF && warp >= 8) {
+    // Raw MXFP4 bytes of this thread's B row arrive kRawItems k-blocks at a
+    // time (one bulk copy per row, kRawSlots groups ahead); E8M0 scales are
+    // read with plain loads one group ahead.  Groups never straddle tiles.
     const int r = threadIdx.x - 256;
     const bool active = r < g.NT;
     const int mine = (int)blockIdx.x < total_tiles ? (total_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int items = mine * g.KB;
-    // load cursor, kPf items ahead of the decode
-    int lt = blockIdx.x, lkb = 0;
-    const uint8_t* lw = nullptr;
-    const uint8_t* ls = nullptr;
-    auto set_row = [&]() {
-      if (active && lt < total_tiles) {
-        const int mb = lt / g.ntiles, nt = lt % g.ntiles;
-        mx_row(g, g.experts[g.mb_expert[mb]], nt, r, lw, ls);
-      }
-    };
-    set_row();
-    uint4 rlo[kPf], rhi[kPf];
-    uint32_t rsc[kPf];
-    auto load = [&](uint4& lo, uint4& hi, uint32_t& sc) {
-      lo = hi = make_uint4(0, 0, 0, 0);
-      sc = 0;
-      if (active && lt < total_tiles) {
-        const uint8_t* p = lw + (size_t)lkb * 32;
-        lo = __ldg(reinterpret_cast<const uint4*>(p));
-        sc = __ldg(ls + 2 * lkb);
-        if (lkb * kBK + 32 < g.Kw) {
-          hi = __ldg(reinterpret_cast<const uint4*>(p + 16));
-          sc |= (uint32_t)__ldg(ls + 2 * lkb + 1) << 8;
-        }
-      }
-      if (++lkb == g.KB) {
-        lkb = 0;
-        lt += gridDim.x;
-        set_row();
-      }
-    };
+    const int gpt = (g.KB + kRawItems - 1) / kRawItems;  // groups per tile
+    const int groups = mine * gpt;
+    const int64_t rowbytes = (int64_t)(g.Kw / 32) * 16;
+    const int wrows = max(0, min(32, g.NT - 32 * (warp - 8)));  // active rows of this warp
+    // Issue group q (raw copy into slot q % kRawSlots) and start loading its
+    // scale bytes (combined only when the group is decoded).
+    auto issue = [&](int q, uint32_t (&sb)[2 * kRawItems]) {
 #pragma unroll
-    for (int p = 0; p < kPf; ++p) load(rlo[p], rhi[p], rsc[p]);
+      for (int i = 0; i < 2 * kRawItems; ++i) sb[i] = 0;
+      if (q >= groups) return;
+      const int tile = blockIdx.x + (q / gpt) * gridDim.x;
+      const int g0 = (q % gpt) * kRawItems;
+      const int nk = min(kRawItems, g.KB - g0);
+      const uint32_t bytes = (uint32_t)min((int64_t)nk * 32, rowbytes - (int64_t)g0 * 32);
+      uint64_t* bar = &rfull[q % kRawSlots];
+      if (lane == 0) mbar_arrive_expect_tx(bar, bytes * (uint32_t)wrows);
+      __syncwarp();
+      if (active) {
+        const int mb = tile / g.ntiles, nt = tile % g.ntiles;
+        const uint8_t* w;
+        const uint8_t* sp;
+        mx_row(g, g.experts[g.mb_expert[mb]], nt, r, w, sp);
+        bulk_g2s(raw + (size_t)(q % kRawSlots) * kRawSlot + (size_t)r * kRawPitch, w + (size_t)g0 * 32, bytes, bar);
+        const int nb = (int)(bytes / 16);  // 32-blocks present in this group
+#pragma unroll
+        for (int i = 0; i < 2 * kRawItems; ++i)
+          if (i < nb) sb[i] = __ldg(sp + 2 * g0 + i);
+      }
+    };
+    uint32_t scA[2 * kRawItems], scB[2 * kRawItems];
+    issue(0, scA);
+    issue(1, scB);
+    uint32_t it = 0;
     bool ok = true;
-    for (int base = 0; ok && base < items; base += kPf) {
+    auto consume = [&](int q, const uint32_t (&sb)[2 * kRawItems]) {
+      const int g0 = (q % gpt) * kRawItems;
+      const int nk = min(kRawItems, g.KB - g0);
+      const int slot = q % kRawSlots;
+      if (!warp_wait(&rfull[slot], (q / kRawSlots) & 1, g.err)) { ok = false; return; }
+      const uint8_t* rrow = raw + (size_t)slot * kRawSlot + (size_t)r * kRawPitch;
 #pragma unroll
-      for (int p = 0; p < kPf; ++p) {
-        const int item = base + p;
-        if (!ok || item >= items) break;
-        const uint4 lo = rlo[p], hi = rhi[p];
-        const uint32_t sc = rsc[p];
-        load(rlo[p], rhi[p], rsc[p]);
-        const int s = item % kNS;
-        if (!mbar_wait(&empty[s], ((item / kNS) & 1) ^ 1, g.err)) { ok = false; break; }
+      for (int sub = 0; sub < kRawItems; ++sub) {
+        if (sub >= nk) break;
+        const int s = it % NS;
+        if (!warp_wait(&empty[s], ((it / NS) & 1) ^ 1, g.err)) { ok = false; return; }
         if (active) {
+          const uint4 lo = *reinterpret_cast<const uint4*>(rrow + 32 * sub);
+          const uint4 hi = (g0 + sub) * kBK + 32 < g.Kw ? *reinterpret_cast<const uint4*>(rrow + 32 * sub + 16)
+                                                        : make_uint4(0, 0, 0, 0);
+          const int e0 = (int)sb[2 * sub] - 127, e1 = (int)sb[2 * sub + 1] - 127;
           uint8_t* brow = smem + (size_t)s * kStage + kATile;
-          const int e0 = (int)(sc & 0xFF) - 127, e1 = (int)(sc >> 8) - 127;
-          const uint32_t q[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+          const uint32_t q8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
           for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(brow + sw128_off(r, c)) = mx_chunk(q[c], c < 4 ? e0 : e1);
+            *reinterpret_cast<uint4*>(brow + sw128_off(r, c)) = mx_chunk(q8[c], c < 4 ? e0 : e1);
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bfull[s]);
+        ++it;
       }
+      __syncwarp();
+    };
+    for (int q = 0; ok && q < groups; q += 2) {
+      consume(q, scA);
+      if (!ok) break;
+      issue(q + 2, scA);
+      if (q + 1 >= groups) break;
+      consume(q + 1, scB);
+      if (!ok) break;
+      issue(q + 3, scB);
     }
   }
   __syncthreads();
@@ -829,11 +863,11 @@ template <int BF>
 static int launch_gemm(const GemmArgs& g, int tiles_max, cudaStream_t st) {
   static bool attr = [] {
     return cudaFuncSetAttribute(grouped_gemm_kernel<BF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)kGemmSmem) == cudaSuccess;
+                                (int)(BF ? kGemmSmemFused : kGemmSmem)) == cudaSuccess;
   }();
   if (!attr) return set_error(TSB_ERR_CUDA, "cannot enable the grouped GEMM's shared memory");
   const int grid = std::max(1, std::min(tiles_max, num_sms()));
-  grouped_gemm_kernel<BF><<<grid, BF ? 512 : 256, kGemmSmem, st>>>(g);
+  grouped_gemm_kernel<BF><<<grid, BF ? 512 : 256, BF ? kGemmSmemFused : kGemmSmem, st>>>(g);
   return TSB_OK;
 }
 
