@@ -339,6 +339,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the config-4 prefill leg (--steps layers after --warmup) and print its object")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -347,6 +349,14 @@ def main():
         res = run_reference(args, ws, rank, local)
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
+        return
+    if args.prefill_only:
+        import torch
+        from tinyserve_b200 import _lib
+        _lib.lib()
+        pf = run_prefill(torch.device("cuda", local), steps=args.steps, warmup=args.warmup)
+        if rank == 0:
+            print(json.dumps(pf), flush=True)
         return
     res, layers, xs = run_ours(args, ws, rank, local)
     if not args.no_prefill:
