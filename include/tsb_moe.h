@@ -119,7 +119,12 @@ int tsb_quant_matvec(int fmt, const void* w, const void* scales, int64_t N, int6
 /* workspace bytes tsb_moe_decode needs for T tokens */
 size_t tsb_moe_decode_workspace(const TsbMoeSpec* spec, int32_t T);
 
-/* One MoE layer for T tokens (T = 1 fused path).
+/* One MoE layer for T tokens.  T = 1: router + fused gate/up + fused down
+ * (three PDL-chained launches).  Several requests decoding together
+ * (ExpertBatcher.batch_execute, tinyserve/expert_batcher.py:31-85): up to 16
+ * tokens run the T = 1 kernels token by token; more take the grouped path of
+ * tsb_moe_prefill, so each routed expert's weights are read once for all its
+ * tokens.  tsb_moe_decode_workspace(spec, T) gives the size for either.
  *   experts   device array of n_experts TsbExpert
  *   x         bf16 [T, H]
  *   router_w  bf16 [E, H] (NULL: ids/weights are inputs)

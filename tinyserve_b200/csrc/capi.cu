@@ -148,9 +148,16 @@ int tsb_quant_matvec(int fmt, const void* w, const void* scales, int64_t N, int6
   return TSB_OK;
 }
 
+// Up to this many tokens, tsb_moe_decode runs the batch-1 kernels once per
+// token: each token costs one HBM pass over its 4 experts (~45-55 us on the
+// GPT-OSS-20B shape), which beats the grouped GEMM path until the batch
+// shares enough experts (measured crossover between 16 and 32 tokens).
+constexpr int kDecodeLoopMax = 16;
+
 size_t tsb_moe_decode_workspace(const TsbMoeSpec* spec, int32_t T) {
   if (!spec || T <= 0) return 0;
-  return ws_layout(*spec, T).total;
+  if (T > kDecodeLoopMax) return prefill_layout(*spec, T).total;  // grouped GEMMs
+  return ws_layout(*spec, 1).total;
 }
 
 int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void* x, int32_t T, const void* router_w,
@@ -158,7 +165,22 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
                    size_t workspace_bytes, void* stream) {
   if (!spec || !experts || !x || !ids || !weights || !out || !workspace) return set_error(TSB_ERR_INVALID, "null pointer");
   const TsbMoeSpec& sp = *spec;
-  if (T != 1) return set_error(TSB_ERR_UNSUPPORTED, "tsb_moe_decode: only T == 1 is fused; use the grouped path for T > 1");
+  if (T < 1) return set_error(TSB_ERR_INVALID, "T must be >= 1");
+  // Larger batches (ExpertBatcher) share each expert's weight stream through
+  // the grouped path; small ones run token by token (stream-ordered: the next
+  // token's first kernel is launched without programmatic overlap).
+  if (T > kDecodeLoopMax)
+    return tsb_moe_prefill(spec, experts, x, T, router_w, router_b, ids, weights, out, workspace, workspace_bytes, stream);
+  if (T > 1) {
+    const int64_t H = spec->hidden, k = spec->top_k;
+    for (int t = 0; t < T; ++t) {
+      const int rc = tsb_moe_decode(spec, experts, static_cast<const uint16_t*>(x) + t * H, 1, router_w, router_b,
+                                    ids + t * k, weights + t * k, static_cast<uint16_t*>(out) + t * H, workspace,
+                                    workspace_bytes, stream);
+      if (rc) return rc;
+    }
+    return TSB_OK;
+  }
   if (sp.top_k < 1 || sp.top_k > 8 || sp.top_k > sp.n_experts) return set_error(TSB_ERR_INVALID, "top_k must be in [1, min(8, E)]");
   if (sp.n_experts < 1 || sp.n_experts > 1024) return set_error(TSB_ERR_INVALID, "n_experts must be in [1, 1024]");
   if (sp.hidden % 32 || sp.inter % 32 || sp.hidden <= 0 || sp.inter <= 0)

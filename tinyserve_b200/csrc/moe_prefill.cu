@@ -791,14 +791,19 @@ static int pick_nt(int rows, bool pair) {
   return 0;
 }
 
-// MXFP4 weights decoded inside the GEMM (opt-in, TSB_PREFILL_FUSED=1): saves
-// the fp16 weight tiles but is latency-bound on the raw loads at present.
-static bool fused_mxfp4() {
-  static const bool on = [] {
+// Where the MXFP4 weights are decoded.  Decoding inside the GEMM repeats the
+// decode for every 128-row block of an expert; decoding once into fp16 tiles
+// costs a write and re-read of the tiles through HBM.  With at most ~2 row
+// blocks per expert on average (T*k <= 256*E: batched decode, short prompts)
+// the in-GEMM decode wins; above that the tiles do.  TSB_PREFILL_FUSED=0/1
+// forces one or the other.
+static bool fused_mxfp4(const TsbMoeSpec& sp, int T) {
+  static const int force = [] {
     const char* v = getenv("TSB_PREFILL_FUSED");
-    return v && v[0] == '1';
+    return v ? (v[0] == '1' ? 1 : 0) : -1;
   }();
-  return on;
+  if (force >= 0) return force == 1;
+  return (int64_t)T * sp.top_k <= (int64_t)256 * sp.n_experts;
 }
 
 PrefillLayout prefill_layout(const TsbMoeSpec& sp, int T) {
@@ -823,8 +828,10 @@ PrefillLayout prefill_layout(const TsbMoeSpec& sp, int T) {
   L.xp = o;       o = al(o + (size_t)L.mb_max * L.kbh * kATile);
   L.act = o;      o = al(o + (size_t)L.mb_max * L.kbi * kATile);
   L.y = o;        o = al(o + 4 * (size_t)L.rows_max * sp.hidden);
-  const bool fgu = sp.fmt_gate_up == FMT_MXFP4 && fused_mxfp4();
-  const bool fdn = sp.fmt_down == FMT_MXFP4 && fused_mxfp4();
+  const bool fgu = sp.fmt_gate_up == FMT_MXFP4 && fused_mxfp4(sp, T);
+  const bool fdn = sp.fmt_down == FMT_MXFP4 && fused_mxfp4(sp, T);
+  L.fused_gu = fgu;
+  L.fused_dn = fdn;
   L.wgu_estride = fgu ? 0 : (int64_t)2 * sp.inter * L.kbh * 128;
   L.wdn_estride = fdn ? 0 : (int64_t)sp.hidden * L.kbi * 128;
   L.wgu = o;      o = al(o + (size_t)sp.n_experts * L.wgu_estride);
@@ -904,8 +911,7 @@ int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x,
   }
   TileWArgs tg{ex, counts, 0, sp.gate_up_layout, sp.inter, 2 * sp.inter, sp.hidden, L.kbh, L.nt_gu, wgu,
                L.wgu_estride};
-  const bool fgu = sp.fmt_gate_up == FMT_MXFP4 && fused_mxfp4();
-  const bool fdn = sp.fmt_down == FMT_MXFP4 && fused_mxfp4();
+  const bool fgu = L.fused_gu, fdn = L.fused_dn;
   int rc = fgu ? TSB_OK : tile_weights(sp.fmt_gate_up, tg, E, st);
   if (rc) return rc;
   TileWArgs td{ex, counts, 1, sp.gate_up_layout, sp.inter, sp.hidden, sp.inter, L.kbi, L.nt_dn, wdn, L.wdn_estride};

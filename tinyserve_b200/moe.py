@@ -71,9 +71,11 @@ class QuantMoE:
 
     def decode(self, x: torch.Tensor, ids: torch.Tensor | None = None, weights: torch.Tensor | None = None,
                out: torch.Tensor | None = None):
-        """One token through the layer.  x: bf16 [1, H].  With a router, returns
-        (out, ids, weights) where ids / weights are the routing it chose; without
-        one, ``ids`` (int32 [1, k]) and ``weights`` (fp32 [1, k]) are inputs."""
+        """T tokens through the layer.  x: bf16 [T, H] ([1, H] for batch-1
+        decode; T > 1 runs the grouped path, each routed expert read once for
+        all its tokens).  With a router, returns (out, ids, weights) where ids /
+        weights are the routing it chose; without one, ``ids`` (int32 [T, k])
+        and ``weights`` (fp32 [T, k]) are inputs."""
         if x.dtype != torch.bfloat16:
             raise TypeError("x must be bfloat16")
         x = x.contiguous()
