@@ -136,6 +136,14 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
                    const void* router_w, const float* router_b, int32_t* ids, float* weights, void* out,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* Router alone: logits = bf16(x @ router_w^T + router_b), top-k (ties to the
+ * lower id, NaN lowest), softmax over the k selected logits
+ * (tinyserve/_model_hooks.py:466-473).  Uses spec->hidden, n_experts, top_k.
+ * ids int32 [T, top_k], weights fp32 [T, top_k].  For callers that route
+ * before dispatching tokens (expert parallelism). */
+int tsb_moe_route(const TsbMoeSpec* spec, const void* x, int32_t T, const void* router_w, const float* router_b,
+                  int32_t* ids, float* weights, void* stream);
+
 /* workspace bytes tsb_moe_prefill needs for T tokens (holds the permuted
  * token tiles, the expert weights decoded to fp16 tiles for every expert, the
  * activation tiles and fp32 expert outputs) */

@@ -1,0 +1,56 @@
+"""Worker of tests/test_ep_gpu.py, run under torchrun (one process per GPU,
+NCCL): the layer's experts are split over the ranks, every rank routes its own
+tokens, and the sharded result is compared with the whole layer on one GPU."""
+from __future__ import annotations
+
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from tests.helpers import make_weight, rel_l2  # noqa: E402
+from tinyserve_b200.ep import ExpertParallelMoE, quant_local_forward  # noqa: E402
+from tinyserve_b200.formats import TSB_MXFP4  # noqa: E402
+from tinyserve_b200.moe import ExpertWeights, QuantMoE, Router  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl")
+    H, I, E, k = 512, 256, 8, 2
+    experts = []
+    for e in range(E):
+        gu, gus = make_weight(TSB_MXFP4, 2 * I, H, 500 + e)
+        dn, dns = make_weight(TSB_MXFP4, H, I, 600 + e)
+        experts.append(ExpertWeights(gate=gu.to(dev), down=dn.to(dev), gate_scales=gus.to(dev), down_scales=dns.to(dev)))
+    router_w = (torch.randn(E, H, generator=torch.Generator().manual_seed(7)) * 0.02).to(torch.bfloat16).to(dev)
+    full = QuantMoE(experts, fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=H, inter=I, top_k=k,
+                    gate_up_layout="interleaved")
+    el = E // world
+    mine = QuantMoE(experts[rank * el:(rank + 1) * el], fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=H, inter=I,
+                    top_k=1, gate_up_layout="interleaved")
+    ep = ExpertParallelMoE(E, k, H, quant_local_forward(mine), router=Router(router_w, k))
+    worst = 0.0
+    for T in (3 + 5 * rank, 300 + 40 * rank, 0 if rank == 0 else 20):
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(1000 * rank + T)).to(torch.bfloat16).to(dev)
+        out = ep(x)
+        if T:
+            ids, w = Router(router_w, k)(x)
+            ref, _, _ = full.decode(x, ids=ids, weights=w)
+            torch.cuda.synchronize()
+            err = rel_l2(out.float().cpu().numpy(), ref.float().cpu().numpy())
+            worst = max(worst, err)
+            assert err <= 1e-2, (rank, T, err)
+    dist.barrier()
+    print(f"EP_OK rank={rank} world={world} worst_rel_l2={worst:.2e}", flush=True)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

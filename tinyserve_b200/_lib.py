@@ -29,6 +29,7 @@ EXPORTS = (
     "tsb_version", "tsb_last_error", "tsb_format_info", "tsb_weight_bytes", "tsb_dequant",
     "tsb_quant_matvec", "tsb_moe_decode_workspace", "tsb_moe_decode", "tsb_read_device_error",
     "tsb_moe_decode_noalloc", "tsb_moe_prefill_workspace", "tsb_moe_prefill",
+    "tsb_moe_route",
 )
 
 
@@ -71,6 +72,7 @@ def _declare(L: ctypes.CDLL) -> None:
     L.tsb_moe_prefill_workspace.argtypes = [ctypes.POINTER(TsbMoeSpec), _i32]
     L.tsb_moe_prefill_workspace.restype = _sz
     L.tsb_moe_prefill.argtypes = [ctypes.POINTER(TsbMoeSpec), _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
+    L.tsb_moe_route.argtypes = [ctypes.POINTER(TsbMoeSpec), _vp, _i32, _vp, _vp, _vp, _vp, _vp]
     L.tsb_moe_decode_noalloc.argtypes = [ctypes.POINTER(TsbMoeSpec), _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp]
 
 

@@ -234,6 +234,19 @@ int tsb_read_device_error(void* workspace, int32_t* code, void* stream) {
   return TSB_OK;
 }
 
+int tsb_moe_route(const TsbMoeSpec* spec, const void* x, int32_t T, const void* router_w, const float* router_b,
+                  int32_t* ids, float* weights, void* stream) {
+  if (!spec) return set_error(TSB_ERR_INVALID, "null pointer");
+  if (T < 0) return set_error(TSB_ERR_INVALID, "T must be >= 0");
+  if (T == 0) return TSB_OK;
+  if (!x || !router_w || !ids || !weights) return set_error(TSB_ERR_INVALID, "null pointer");
+  const TsbMoeSpec& sp = *spec;
+  if (sp.n_experts < 1 || sp.n_experts > 1024) return set_error(TSB_ERR_INVALID, "n_experts must be in [1, 1024]");
+  if (sp.top_k < 1 || sp.top_k > 8 || sp.top_k > sp.n_experts) return set_error(TSB_ERR_INVALID, "top_k must be in [1, min(8, E)]");
+  if (sp.hidden <= 0 || sp.hidden % 8) return set_error(TSB_ERR_INVALID, "hidden must be a positive multiple of 8");
+  return launch_route(sp, x, T, router_w, router_b, ids, weights, static_cast<cudaStream_t>(stream));
+}
+
 size_t tsb_moe_prefill_workspace(const TsbMoeSpec* spec, int32_t T) {
   if (!spec || T < 0) return 0;
   return prefill_layout(*spec, T).total;

@@ -878,6 +878,16 @@ static int launch_gemm(const GemmArgs& g, int tiles_max, cudaStream_t st) {
   return TSB_OK;
 }
 
+int launch_route(const TsbMoeSpec& sp, const void* x, int T, const void* rw, const float* rb, int32_t* ids,
+                 float* wts, cudaStream_t st) {
+  const size_t sm = 4 * sizeof(float) * (size_t)sp.n_experts;
+  prefill_router_kernel<<<(T + 3) / 4, 128, sm, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(rw),
+                                                       rb, sp.hidden, sp.n_experts, T, sp.top_k, ids, wts);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return TSB_OK;
+}
+
 int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, int T, const void* rw,
                        const float* rb, int32_t* ids, float* wts, void* out, char* ws, const PrefillLayout& L,
                        cudaStream_t st) {
@@ -896,10 +906,8 @@ int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x,
   uint8_t* wdn = reinterpret_cast<uint8_t*>(ws + L.wdn);
 
   if (rw) {
-    const size_t sm = 4 * sizeof(float) * (size_t)E;  // <= 16 KB for E <= 1024
-    prefill_router_kernel<<<(T + 3) / 4, 128, sm, st>>>(static_cast<const uint16_t*>(x),
-                                                         static_cast<const uint16_t*>(rw), rb, sp.hidden, E, T, k,
-                                                         ids, wts);
+    const int rc = launch_route(sp, x, T, rw, rb, ids, wts, st);
+    if (rc) return rc;
   }
   route_count_kernel<<<E, 256, 0, st>>>(ids, n, E, counts, row_of, err);
   route_place_kernel<<<E, 1024, 0, st>>>(ids, n, k, E, counts, row_of, row_src, mb_expert, total_mb);

@@ -38,6 +38,8 @@ PrefillLayout prefill_layout(const TsbMoeSpec& sp, int T);
 int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, int T, const void* rw,
                        const float* rb, int32_t* ids, float* wts, void* out, char* ws, const PrefillLayout& L,
                        cudaStream_t st);
+int launch_route(const TsbMoeSpec& sp, const void* x, int T, const void* rw, const float* rb, int32_t* ids,
+                 float* wts, cudaStream_t st);
 int launch_dequant(int fmt, const void* w, const void* s, int64_t rows, int64_t cols, void* out, int odt,
                    cudaStream_t st);
 

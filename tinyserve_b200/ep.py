@@ -1,0 +1,113 @@
+"""Expert parallelism: the experts of a layer sharded over the ranks of a
+process group (one process per GPU), token dispatch and combine over NCCL.
+
+Rank r owns experts [r*E/G, (r+1)*E/G) (contiguous ranges) and brings its own
+tokens.  One layer call on every rank:
+
+1. route its tokens (router weights are replicated; ``Router``);
+2. order its (token, slot) rows by owning rank (stable, so the order is
+   deterministic) and exchange the per-rank row counts (all_to_all);
+3. send the rows and their local expert ids to their owners
+   (all_to_all_single with uneven splits: NCCL send/recv over NVLink);
+4. run the received rows through the local experts as one grouped call, one
+   expert per row (``local_forward``);
+5. send the expert outputs back along the reverse splits;
+6. combine on the source rank: out[t] = sum_j w[t,j] * y[t,j] in slot order,
+   accumulated in fp32.
+
+The reference runs every expert of a layer on one device
+(tinyserve/expert_pipeline.py:166-239); sharding is what lets the 120B-shaped
+layer (128 experts) spread over 1/2/4/8 GPUs.  Remote rows land in local
+memory through NCCL before any kernel reads them.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+LocalForward = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
+
+
+class ExpertParallelMoE:
+    """One MoE layer sharded expert-parallel over ``group``.
+
+    ``local_forward(x_rows [R, H], local_ids [R] int32) -> [R, H]`` runs each
+    row through local expert ``local_ids[i]`` (unweighted).  ``router(x) ->
+    (ids [T,k] int32 global, weights [T,k] fp32)`` is used when the caller does
+    not pass routing."""
+
+    def __init__(self, n_experts: int, top_k: int, hidden: int, local_forward: LocalForward, *,
+                 router: Callable | None = None, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if n_experts % self.world:
+            raise ValueError(f"{n_experts} experts do not split evenly over {self.world} ranks")
+        self.n_experts, self.top_k, self.hidden = n_experts, top_k, hidden
+        self.e_local = n_experts // self.world
+        self.base = self.rank * self.e_local
+        self.local_forward = local_forward
+        self.router = router
+
+    def owner(self, ids: torch.Tensor) -> torch.Tensor:
+        return torch.div(ids, self.e_local, rounding_mode="floor")
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor | None = None,
+                weights: torch.Tensor | None = None) -> torch.Tensor:
+        if ids is None:
+            if self.router is None:
+                raise ValueError("no router: pass ids and weights")
+            ids, weights = self.router(x)
+        T, H = x.shape
+        k = ids.shape[1]
+        dev = x.device
+        flat = ids.reshape(-1).to(torch.int64)
+        if flat.numel() and (int(flat.min()) < 0 or int(flat.max()) >= self.n_experts):
+            raise ValueError("expert id out of range")
+        dest = self.owner(flat)
+        order = torch.argsort(dest, stable=True)
+        send_counts = torch.bincount(dest, minlength=self.world).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        n_send, n_recv = sum(sc), sum(rc)
+
+        send_rows = x.index_select(0, torch.div(order, k, rounding_mode="floor")).contiguous()
+        send_lid = (flat.index_select(0, order) - dest.index_select(0, order) * self.e_local).to(torch.int32)
+        recv_rows = torch.empty(n_recv, H, dtype=x.dtype, device=dev)
+        recv_lid = torch.empty(n_recv, dtype=torch.int32, device=dev)
+        dist.all_to_all_single(recv_rows, send_rows, rc, sc, group=self.group)
+        dist.all_to_all_single(recv_lid, send_lid, rc, sc, group=self.group)
+
+        y_recv = self.local_forward(recv_rows, recv_lid) if n_recv else torch.empty(0, H, dtype=x.dtype, device=dev)
+        y_recv = y_recv.to(x.dtype).contiguous()
+        y_send = torch.empty(n_send, H, dtype=x.dtype, device=dev)
+        dist.all_to_all_single(y_send, y_recv, sc, rc, group=self.group)
+
+        y = torch.empty(T * k, H, dtype=torch.float32, device=dev)
+        y[order] = y_send.float()
+        y = y.view(T, k, H)
+        w = weights.to(torch.float32).reshape(T, k)
+        out = torch.zeros(T, H, dtype=torch.float32, device=dev)
+        for j in range(k):
+            out += w[:, j:j + 1] * y[:, j]
+        return out.to(x.dtype)
+
+    __call__ = forward
+
+
+def quant_local_forward(layer) -> LocalForward:
+    """``local_forward`` backed by a :class:`tinyserve_b200.moe.QuantMoE` that
+    holds this rank's experts with top_k = 1: each received row is one
+    (token, expert) pair with weight 1."""
+    if layer.top_k != 1:
+        raise ValueError("the local layer must be built with top_k=1")
+
+    def f(rows: torch.Tensor, lid: torch.Tensor) -> torch.Tensor:
+        ones = torch.ones(rows.shape[0], 1, dtype=torch.float32, device=rows.device)
+        out, _, _ = layer.decode(rows.contiguous(), ids=lid.reshape(-1, 1), weights=ones)
+        return out
+
+    return f

@@ -160,3 +160,29 @@ class QuantMoE:
     @property
     def is_mxfp4(self) -> bool:
         return self.spec.fmt_gate_up == TSB_MXFP4
+
+
+class Router:
+    """The MoE router alone (tsb_moe_route): bf16 logits, top-k, softmax over
+    the k selected logits (tinyserve/_model_hooks.py:466-473)."""
+
+    def __init__(self, router_w: torch.Tensor, top_k: int, router_b: torch.Tensor | None = None):
+        if router_w.dtype != torch.bfloat16 or router_w.dim() != 2:
+            raise TypeError("router_w must be bf16 [E, H]")
+        self.router_w = router_w.contiguous()
+        self.router_b = router_b.float().contiguous() if router_b is not None else None
+        E, H = router_w.shape
+        self.spec = _lib.TsbMoeSpec(TSB_MXFP4, TSB_MXFP4, H, 32, E, top_k, 0, 1, 7.0, 1.702)
+        self.top_k = top_k
+
+    def __call__(self, x: torch.Tensor):
+        if x.dtype != torch.bfloat16:
+            raise TypeError("x must be bfloat16")
+        x = x.contiguous()
+        T = x.shape[0]
+        ids = torch.empty(T, self.top_k, dtype=torch.int32, device=x.device)
+        w = torch.empty(T, self.top_k, dtype=torch.float32, device=x.device)
+        _lib.check(_lib.lib().tsb_moe_route(ctypes.byref(self.spec), x.data_ptr(), T, self.router_w.data_ptr(),
+                                            _p(self.router_b), ids.data_ptr(), w.data_ptr(),
+                                            torch.cuda.current_stream(x.device).cuda_stream))
+        return ids, w
