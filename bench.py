@@ -282,6 +282,62 @@ def run_prefill(dev, steps: int = 10, warmup: int = 3):
             "gpu_launches_per_layer": 8}
 
 
+EP_T = 4096  # tokens per rank per layer call (weak scaling)
+
+
+def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
+    """GPT-OSS-120B-shaped MXFP4 layer (128 experts, top-4,
+    H = I = 2880) sharded expert-parallel over the ranks (128/N experts each),
+    every rank routing its own 4096 tokens (seeded N(0,1), router bf16
+    N(0,0.02)); dispatch and combine over NCCL (all-to-all-v), local experts as
+    grouped tcgen05 GEMMs.  value = tokens of all ranks / max-over-ranks time."""
+    import torch
+    from tinyserve_b200.formats import TSB_MXFP4
+    from tinyserve_b200.moe import QuantMoE, Router
+    from tinyserve_b200.workloads import build_layer, gen_normal, hidden_states
+    E, k = 128, 4
+    el = E // ws
+    # only this rank's experts are built (seeded per rank)
+    full = build_layer(TSB_MXFP4, n_experts=el, top_k=1, seed=5000 + rank, device=dev)
+    local = QuantMoE(full.experts, fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=2880, inter=2880, top_k=1,
+                     gate_up_layout="interleaved")
+    router = Router(gen_normal((E, 2880), 77, 0.02, dev).to(torch.bfloat16), k)
+    x = hidden_states(EP_T, seed=100 + rank, device=dev)
+    if ws > 1:
+        import torch.distributed as dist
+        from tinyserve_b200.ep import ExpertParallelMoE, quant_local_forward
+        layer = ExpertParallelMoE(E, k, 2880, quant_local_forward(local), router=router)
+        call = lambda: layer(x)  # noqa: E731
+    else:
+        whole = QuantMoE(full.experts, fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=2880, inter=2880, top_k=k,
+                         router_w=router.router_w, gate_up_layout="interleaved")
+        call = lambda: whole.decode(x)  # noqa: E731
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"metric": "moe_layer_ep_prefill_tok_s", "value": ws * EP_T / (ms * 1e-3), "unit": "tok/s",
+            "ms_per_layer": ms, "n_gpus": ws, "steps": steps, "warmup": warmup, "scaling": "weak",
+            "config": {"workload": "BASELINE config 5: GPT-OSS-120B-shaped MXFP4 MoE layer (128 experts, top-4), "
+                                   f"{EP_T} tokens per rank, experts sharded {el} per GPU",
+                       "parallelism": f"ep{ws}" if ws > 1 else "single GPU (all 128 experts local)",
+                       "exchange": "NCCL all_to_all_single (uneven splits) for rows, expert ids and outputs",
+                       "timing": "CUDA events, max over ranks"}}
+
+
 def cpu_sample(layers, xs, n_tokens: int, threads: int):
     """Reference CPU path (oracle port of CPUExpertForward) on a bounded sample."""
     import numpy as np
@@ -365,6 +421,8 @@ def main():
         torch.cuda.empty_cache()
         pf = run_prefill(torch.device("cuda", local))
         res["prefill"] = pf
+        torch.cuda.empty_cache()
+        res["expert_parallel"] = run_ep(torch.device("cuda", local), ws, rank)
     if rank == 0:
         if not args.no_cpu_baseline and ws == 1:
             threads = len(os.sched_getaffinity(0))

@@ -376,25 +376,40 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
 // values, the fp16 rounding of tsb_dequant's exact fp32 value: e2m1 -> f16 is
 // exact and, when 2^e is itself an fp16 number (-24 <= e <= 15), one correctly
 // rounded f16 multiply gives that rounding; other exponents take the fp32 route.
-__device__ __forceinline__ uint4 mx_chunk(uint32_t q4, int e) {
+struct MxScale {
+  uint32_t s2;  // 2^e as f16x2 (fast route)
+  int e;
+  bool fast;
+};
+__device__ __forceinline__ MxScale mx_scale(uint32_t byte) {
+  MxScale m;
+  m.e = (int)byte - 127;
+  m.fast = m.e >= -24 && m.e <= 15;
+  const uint32_t sb = m.e >= -14 ? (uint32_t)(m.e + 15) << 10 : 1u << ((m.e + 24) & 31);
+  m.s2 = sb | (sb << 16);
+  return m;
+}
+
+__device__ __noinline__ uint4 mx_chunk_slow(uint32_t q4, int e) {
   uint32_t h[4];
-  if (e >= -24 && e <= 15) {
-    const uint32_t sb = e >= -14 ? (uint32_t)(e + 15) << 10 : 1u << (e + 24);
-    const uint32_t s2 = sb | (sb << 16);
+  const int e1 = e / 2, e2 = e - e1;
+  const float p1 = __uint_as_float((uint32_t)(e1 + 127) << 23), p2 = __uint_as_float((uint32_t)(e2 + 127) << 23);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = hmul2_bits(cvt_e2m1x2((q4 >> (8 * i)) & 0xFFu), s2);
-  } else {
-    const int e1 = e / 2, e2 = e - e1;
-    const float p1 = __uint_as_float((uint32_t)(e1 + 127) << 23), p2 = __uint_as_float((uint32_t)(e2 + 127) << 23);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t c = cvt_e2m1x2((q4 >> (8 * i)) & 0xFFu);
-      const float lo = __fmul_rn(__fmul_rn(half_bits_to_f32((uint16_t)(c & 0xFFFF)), p1), p2);
-      const float hi = __fmul_rn(__fmul_rn(half_bits_to_f32((uint16_t)(c >> 16)), p1), p2);
-      const __half2 p = __halves2half2(__float2half_rn(lo), __float2half_rn(hi));
-      h[i] = *reinterpret_cast<const uint32_t*>(&p);
-    }
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t c = cvt_e2m1x2((q4 >> (8 * i)) & 0xFFu);
+    const float lo = __fmul_rn(__fmul_rn(half_bits_to_f32((uint16_t)(c & 0xFFFF)), p1), p2);
+    const float hi = __fmul_rn(__fmul_rn(half_bits_to_f32((uint16_t)(c >> 16)), p1), p2);
+    const __half2 p = __halves2half2(__float2half_rn(lo), __float2half_rn(hi));
+    h[i] = *reinterpret_cast<const uint32_t*>(&p);
   }
+  return make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+__device__ __forceinline__ uint4 mx_chunk(uint32_t q4, const MxScale& m) {
+  if (!m.fast) return mx_chunk_slow(q4, m.e);
+  uint32_t h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = hmul2_bits(cvt_e2m1x2((q4 >> (8 * i)) & 0xFFu), m.s2);
   return make_uint4(h[0], h[1], h[2], h[3]);
 }
 
@@ -442,7 +457,8 @@ __device__ __forceinline__ void mx_row(const GemmArgs& g, const TsbExpert& E, in
 // the fp16 row into the stage's swizzled B tile and arrive on bfull; the MMA
 // waits for both the A copy and the B decode of a stage.
 constexpr int kNSFused = 3;                 // A/B stages of the in-kernel decode variant
-constexpr int kRawItems = 4;                // k-blocks per raw copy
+constexpr int kRawItems = 4;                // k-blocks per raw copy (the decode loop assumes 4)
+static_assert(kRawItems == 4, "scale-byte selection in the decode loop is written for 4 k-blocks per copy");
 constexpr int kRawSlots = 2;
 constexpr int kRawPitch = kRawItems * 32 + 16;   // 144 B: row pitch off the 128-byte bank period
 constexpr int kRawSlot = 256 * kRawPitch;
@@ -609,6 +625,9 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
     const int groups = mine * gpt;
     const int64_t rowbytes = (int64_t)(g.Kw / 32) * 16;
     const int wrows = max(0, min(32, g.NT - 32 * (warp - 8)));  // active rows of this warp
+    int row_tile = -1;
+    const uint8_t* row_w = nullptr;
+    const uint8_t* row_s = nullptr;
     // Issue group q (raw copy into slot q % kRawSlots) and start loading its
     // scale bytes (combined only when the group is decoded).
     auto issue = [&](int q, uint32_t (&sb)[2 * kRawItems]) {
@@ -623,10 +642,13 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
       if (lane == 0) mbar_arrive_expect_tx(bar, bytes * (uint32_t)wrows);
       __syncwarp();
       if (active) {
-        const int mb = tile / g.ntiles, nt = tile % g.ntiles;
-        const uint8_t* w;
-        const uint8_t* sp;
-        mx_row(g, g.experts[g.mb_expert[mb]], nt, r, w, sp);
+        if (tile != row_tile) {  // row pointers change once per tile
+          const int mb = tile / g.ntiles, nt = tile % g.ntiles;
+          mx_row(g, g.experts[g.mb_expert[mb]], nt, r, row_w, row_s);
+          row_tile = tile;
+        }
+        const uint8_t* w = row_w;
+        const uint8_t* sp = row_s;
         bulk_g2s(raw + (size_t)(q % kRawSlots) * kRawSlot + (size_t)r * kRawPitch, w + (size_t)g0 * 32, bytes, bar);
         const int nb = (int)(bytes / 16);  // 32-blocks present in this group
 #pragma unroll
@@ -645,21 +667,23 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
       const int slot = q % kRawSlots;
       if (!warp_wait(&rfull[slot], (q / kRawSlots) & 1, g.err)) { ok = false; return; }
       const uint8_t* rrow = raw + (size_t)slot * kRawSlot + (size_t)r * kRawPitch;
-#pragma unroll
-      for (int sub = 0; sub < kRawItems; ++sub) {
-        if (sub >= nk) break;
+#pragma unroll 1
+      for (int sub = 0; sub < nk; ++sub) {
         const int s = it % NS;
         if (!warp_wait(&empty[s], ((it / NS) & 1) ^ 1, g.err)) { ok = false; return; }
         if (active) {
           const uint4 lo = *reinterpret_cast<const uint4*>(rrow + 32 * sub);
           const uint4 hi = (g0 + sub) * kBK + 32 < g.Kw ? *reinterpret_cast<const uint4*>(rrow + 32 * sub + 16)
                                                         : make_uint4(0, 0, 0, 0);
-          const int e0 = (int)sb[2 * sub] - 127, e1 = (int)sb[2 * sub + 1] - 127;
-          uint8_t* brow = smem + (size_t)s * kStage + kATile;
+          const uint32_t sbp = (sub & 2) ? ((sub & 1) ? (sb[6] | sb[7] << 8) : (sb[4] | sb[5] << 8))
+                                         : ((sub & 1) ? (sb[2] | sb[3] << 8) : (sb[0] | sb[1] << 8));
+          const MxScale m0 = mx_scale(sbp & 0xFF), m1 = mx_scale(sbp >> 8);
+          uint8_t* brow = smem + (size_t)s * kStage + kATile + (size_t)r * 128;
+          const uint32_t r7 = (uint32_t)(r & 7);
           const uint32_t q8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
           for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(brow + sw128_off(r, c)) = mx_chunk(q8[c], c < 4 ? e0 : e1);
+            *reinterpret_cast<uint4*>(brow + ((c ^ r7) << 4)) = mx_chunk(q8[c], c < 4 ? m0 : m1);
         }
         fence_proxy_async_smem();
         __syncwarp();
