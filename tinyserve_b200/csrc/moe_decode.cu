@@ -14,6 +14,8 @@ namespace tsb {
 constexpr int kNCW = 16;
 constexpr int kNStage = 4;
 constexpr int kStageBytes = 32768;
+constexpr int kNStageWide = 5;   // stages of whole-row single/diagonal-vector plans
+constexpr int kGroupsWide = 4;   // consumer groups of those plans
 
 __device__ __forceinline__ float load_act(const void* p, int dtype, int64_t i) {
   if (dtype == TSB_DT_F32) return static_cast<const float*>(p)[i];
@@ -387,14 +389,26 @@ static bool choose_geom(int K, int nseg, int rows_per_seg, StageGeom& G) {
 
 template <int F, int MODE, class P>
 static cudaError_t run_plan(const P& plan, int nblocks, int nv, cudaStream_t st, bool pdl) {
-  const int smem = SmemPlan<kNCW, kNStage, kStageBytes, MODE, F>::total(plan.geom.K, nv);
   const int grid = std::max(1, std::min(nblocks, num_sms()));
   if (plan.geom.KC >= plan.geom.K) {
+    // Single-vector whole-row plans: kGroupsWide consumer groups (each warp
+    // covers a longer K range of its row block) over a kNStageWide-deep ring,
+    // when that fits in shared memory.
+    using SW = SmemPlan<kNCW, kNStageWide, kStageBytes, MODE, F>;
+    if (MODE == COLS_DUP && SW::total(plan.geom.K, nv) <= 227 * 1024) {
+      const int smem = SW::total(plan.geom.K, nv);
+      auto kern = qmv_kernel<F, MODE, kNCW, kNStageWide, kStageBytes, kGroupsWide, P>;
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      return launch(kern, grid, 32 * (kNCW + 1), (size_t)smem, st, pdl, plan);
+    }
+    const int smem = SmemPlan<kNCW, kNStage, kStageBytes, MODE, F>::total(plan.geom.K, nv);
     auto kern = qmv_kernel<F, MODE, kNCW, kNStage, kStageBytes, 2, P>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     return launch(kern, grid, 32 * (kNCW + 1), (size_t)smem, st, pdl, plan);
   }
+  const int smem = SmemPlan<kNCW, kNStage, kStageBytes, MODE, F>::total(plan.geom.K, nv);
   auto kern = qmv_kernel<F, MODE, kNCW, kNStage, kStageBytes, 1, P>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;

@@ -366,12 +366,6 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&p);
 }
 
-__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
 // Four MXFP4 bytes (8 e2m1 codes, low nibble first) times 2^e as eight fp16
 // values, the fp16 rounding of tsb_dequant's exact fp32 value: e2m1 -> f16 is
 // exact and, when 2^e is itself an fp16 number (-24 <= e <= 15), one correctly
@@ -409,7 +403,7 @@ __device__ __forceinline__ uint4 mx_chunk(uint32_t q4, const MxScale& m) {
   if (!m.fast) return mx_chunk_slow(q4, m.e);
   uint32_t h[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = hmul2_bits(cvt_e2m1x2((q4 >> (8 * i)) & 0xFFu), m.s2);
+  for (int i = 0; i < 4; ++i) h[i] = h2mul(cvt_e2m1x2((q4 >> (8 * i)) & 0xFFu), m.s2);
   return make_uint4(h[0], h[1], h[2], h[3]);
 }
 
