@@ -776,6 +776,12 @@ __device__ __forceinline__ bool eng_consume(const P& plan, const SlotCache* cach
 
 template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, int NG, class P>
 __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
+  // Waits use only the parity of a stage's phase.  A group waits for its next
+  // row block only after finishing its previous one, and stages are filled in
+  // row-block order, so with NG <= NSTAGE a stage is never two fills ahead of
+  // its waiter; with more groups than stages a waiter can match an older
+  // phase of the same parity and read another row block's stage.
+  static_assert(NG <= NSTAGE, "more consumer groups than stages aliases mbarrier phases");
   using SP = SmemPlan<NCW, NSTAGE, STAGE_BYTES, MODE, F>;
   constexpr int WPG = NCW / NG;
   extern __shared__ __align__(128) uint8_t smem[];
