@@ -14,7 +14,9 @@ namespace tsb {
 constexpr int kNCW = 16;
 constexpr int kNStage = 4;
 constexpr int kStageBytes = 32768;
-constexpr int kNStageWide = 5;   // stages of whole-row single/diagonal-vector plans
+constexpr int kNStageWide = 5;
+constexpr int kWarpNW = 8;          // warps of the warp-owned variant
+constexpr int kWarpBuf = 10240;     // bytes per warp buffer (two per warp)   // stages of whole-row single/diagonal-vector plans
 constexpr int kGroupsWide = 4;   // consumer groups of those plans
 
 __device__ __forceinline__ float load_act(const void* p, int dtype, int64_t i) {
@@ -363,11 +365,11 @@ static int num_sms() {
 }
 
 template <int F>
-static bool choose_geom(int K, int nseg, int rows_per_seg, StageGeom& G) {
+static bool choose_geom(int K, int nseg, int rows_per_seg, StageGeom& G, int kData = kStageBytes - 256) {
+  // kData: stage (or warp buffer) bytes minus its RowInfo header
   int slot, scb, ssl;
   G.K = K;
   G.rps = rows_per_seg;
-  constexpr int kData = kStageBytes - 256;  // stage minus its RowInfo header
   if (host_stage_bytes<F>(K, K, nseg, rows_per_seg, slot, scb, ssl) <= kData) {
     G.KC = K;
     G.slot = slot;

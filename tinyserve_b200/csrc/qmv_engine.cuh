@@ -534,6 +534,174 @@ __device__ __forceinline__ bool eng_produce(const P& plan, const SlotCache* cach
   return true;
 }
 
+// One stage chunk of one row block for one consumer warp: steps [u_beg, u_end)
+// of the chunk (ub = its first 32-block), accumulated into acc.  Shared by the
+// stage-ring engine and the warp-owned variant.
+template <int F, int MODE, class SP>
+__device__ __forceinline__ void consume_chunk(const uint8_t* stage, int u_beg, int u_end, int ub, int nv, int vb,
+                                              int v0, int v1, int n_a, int n_b, const uint4* xq, const float4* xsx,
+                                              uint8_t* coef, float (&acc)[4], int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  constexpr bool kKQ = (F == FMT_Q4_K || F == FMT_Q5_K || F == FMT_Q6_K);
+  const uint8_t* data = stage + SP::kHdr;
+  const int4* hdr = reinterpret_cast<const int4*>(stage);
+  const int4 h0 = hdr[g], h1 = hdr[g + 8];
+  const RowInfo r0{h0.x, h0.y, h0.z, h0.w}, r1{h1.x, h1.y, h1.z, h1.w};
+
+  // Running per-row positions.  Rows outside the matrix (valid == 0) read
+  // the stage from offset 0 instead of branching: every decoded A value is
+  // finite (magic f16 <= 1279, e2m1 <= 6), and their fold coefficient is 0.
+  // Rows g and g+8 are 8 rows apart and 8*K/32 is a multiple of 8 for any
+  // K % 32 == 0, so both rows sit at the same 32-block phase within their
+  // superblocks: one sub-block counter serves both.
+  using T = FmtT<F>;
+  const uint8_t* pA = data + (r0.valid ? r0.off : 0);
+  const uint8_t* pB = data + (r1.valid ? r1.off : 0);
+  int sA = 0;
+  if (kKQ) {
+    sA = (r0.valid ? r0.sub0 : r1.sub0) + u_beg;
+    pA += (sA >> 3) * T::BB;
+    pB += (sA >> 3) * T::BB;
+    sA &= 7;
+  } else {
+    pA += u_beg * T::BB;
+    pB += u_beg * T::BB;
+  }
+  const uint8_t* scA = data + r0.soff + u_beg;  // MXFP4 scale bytes
+  const uint8_t* scB = data + r1.soff + u_beg;
+  const uint4* xqp = xq + ((size_t)(ub + u_beg) * nv + vb) * 4 + t;
+  const float4* xsp = xsx + (size_t)(ub + u_beg) * nv;
+
+  for (int uc = u_beg; uc < u_end; uc += SP::kCoefCh) {
+    const int nst = min(SP::kCoefCh, u_end - uc);
+    if (F == FMT_Q4_K || F == FMT_Q5_K) {
+      // One task per (row, superblock): decode d, dmin and the 12 scale bytes
+      // once and emit the coefficients of the sub-blocks that fall in this
+      // chunk of steps (16 steps from any phase span at most 3 superblocks).
+      __syncwarp();
+      float2* cf = reinterpret_cast<float2*>(coef);
+      for (int task = lane; task < 48; task += 32) {
+        const int m = task / 3, j = task - 3 * (task / 3);
+        const int4 q = hdr[m];
+        if (!q.w) {
+          if (j == 0)
+            for (int u = 0; u < nst; ++u) cf[m * SP::kCoefCh + u] = make_float2(0.f, 0.f);
+          continue;
+        }
+        const int sb = ((q.y + uc) >> 3) + j;  // superblock index relative to the row's first
+        const int ubase = sb * 8 - q.y - uc;   // chunk step of sub-block 0 of this superblock
+        if (ubase >= nst) continue;
+        const uint4 hw = *reinterpret_cast<const uint4*>(data + q.x + sb * FmtT<F>::BB);
+        const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&hw.x));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int u = ubase + i;
+          if (u < 0 || u >= nst) continue;
+          const int sh = 8 * (i & 3);
+          uint32_t sc, mn;
+          if (i < 4) {
+            sc = (hw.y >> sh) & 63u;
+            mn = (hw.z >> sh) & 63u;
+          } else {
+            sc = ((hw.w >> sh) & 15u) | (((hw.y >> sh) >> 2) & 0x30u);
+            mn = (((hw.w >> sh) >> 4) & 15u) | (((hw.z >> sh) >> 2) & 0x30u);
+          }
+          const float a = dd.x * small_u2f(sc);
+          cf[m * SP::kCoefCh + u] = make_float2(a, fmaf(FoldBias<F>::v, a, dd.y * small_u2f(mn)));
+        }
+      }
+      __syncwarp();
+    } else if (kKQ) {
+      __syncwarp();
+#pragma unroll
+      for (int e0 = 0; e0 < 16 * SP::kCoefCh; e0 += 32) {
+        const int e = e0 + lane;
+        const int m = e / SP::kCoefCh, s = e % SP::kCoefCh;
+        const int4 q = hdr[m];
+        const RowInfo ri{q.x, q.y, q.z, q.w};
+        float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ri.valid && s < nst) c = fold_coef<F>(row_loc<F>(data, ri, uc + s));
+        if (F == FMT_Q6_K) reinterpret_cast<float4*>(coef)[m * SP::kCoefCh + s] = c;
+        else reinterpret_cast<float2*>(coef)[m * SP::kCoefCh + s] = make_float2(c.x, c.y);
+      }
+      __syncwarp();
+    }
+#pragma unroll 2
+    for (int s = 0; s < nst; ++s) {
+      const uint4 b = *xqp;
+      xqp += nv * 4;
+      RowLoc la, lb;
+      la.blk = pA; la.sub = sA; la.mx_scale = (F == FMT_MXFP4) ? scA[0] : 0u;
+      lb.blk = pB; lb.sub = sA; lb.mx_scale = (F == FMT_MXFP4) ? scB[0] : 0u;
+      uint32_t pa[4], pb[4];
+      decode_a<F>(la, t, pa);
+      decode_a<F>(lb, t, pb);
+      float c1[4] = {0.f, 0.f, 0.f, 0.f};
+      float c2[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t a1[4] = {pa[0], pb[0], pa[1], pb[1]};
+      const uint32_t a2[4] = {pa[2], pb[2], pa[3], pb[3]};
+      mma_f16(c1, a1, b.x, b.y);
+      if (F == FMT_Q6_K) mma_f16(c2, a2, b.z, b.w);
+      else mma_f16(c1, a2, b.z, b.w);
+      float4 ka, kb;
+      if (kKQ) {
+        if (F == FMT_Q6_K) {
+          ka = reinterpret_cast<const float4*>(coef)[g * SP::kCoefCh + s];
+          kb = reinterpret_cast<const float4*>(coef)[(g + 8) * SP::kCoefCh + s];
+        } else {
+          const float2 qa = reinterpret_cast<const float2*>(coef)[g * SP::kCoefCh + s];
+          const float2 qb = reinterpret_cast<const float2*>(coef)[(g + 8) * SP::kCoefCh + s];
+          ka = make_float4(qa.x, qa.y, 0.f, 0.f);
+          kb = make_float4(qb.x, qb.y, 0.f, 0.f);
+        }
+      } else {
+        ka = fold_coef<F>(la);
+        kb = fold_coef<F>(lb);
+        ka.x = r0.valid ? ka.x : 0.f; ka.y = r0.valid ? ka.y : 0.f;
+        kb.x = r1.valid ? kb.x : 0.f; kb.y = r1.valid ? kb.y : 0.f;
+      }
+      // advance both rows by one 32-element step
+      if (kKQ) {
+        if (++sA == 8) { sA = 0; pA += T::BB; pB += T::BB; }
+      } else {
+        pA += T::BB;
+        pB += T::BB;
+      }
+      if (F == FMT_MXFP4) { ++scA; ++scB; }
+      auto fold = [&](float& a, float cv1, float cv2, const float4& k, const float4& q) {
+        if (F == FMT_Q6_K) {
+          a = fmaf(k.x, cv1 * q.x, a);
+          a = fmaf(-k.y, q.y, a);
+          a = fmaf(k.z, cv2 * q.x, a);
+          a = fmaf(-k.w, q.z, a);
+        } else if (F == FMT_MXFP4) {
+          a = fmaf(k.x * q.x, cv1, a);
+        } else {
+          a = fmaf(k.x, cv1 * q.x, a);
+          a = fmaf(-k.y, q.y, a);
+        }
+      };
+      if (MODE == COLS_DUP) {
+        const float4 q0 = xsp[0];
+        fold(acc[0], c1[0], c2[0], ka, q0);
+        fold(acc[2], c1[2], c2[2], kb, q0);
+      } else if (MODE == COLS_FULL) {
+        const float4 qv0 = xsp[v0], qv1 = xsp[v1];
+        fold(acc[0], c1[0], c2[0], ka, qv0);
+        fold(acc[1], c1[1], c2[1], ka, qv1);
+        fold(acc[2], c1[2], c2[2], kb, qv0);
+        fold(acc[3], c1[3], c2[3], kb, qv1);
+      } else {
+        const bool oa = n_a & 1, ob = n_b & 1;
+        const float4 qa_ = xsp[n_a < 0 ? 0 : n_a], qb_ = xsp[n_b < 0 ? 0 : n_b];
+        fold(acc[0], oa ? c1[1] : c1[0], oa ? c2[1] : c2[0], ka, qa_);
+        fold(acc[2], ob ? c1[3] : c1[2], ob ? c2[3] : c2[2], kb, qb_);
+      }
+      xsp += nv;
+    }
+  }
+}
+
 // Consumer warp cw: process this CTA's row blocks of `plan` (its group's share),
 // whose stage units start at ring position it0.  Returns false on a timeout.
 template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, int NG, class P>
@@ -572,163 +740,7 @@ __device__ __forceinline__ bool eng_consume(const P& plan, const SlotCache* cach
       const int u_beg = (wg * Uc) / WPG, u_end = ((wg + 1) * Uc) / WPG;
       if (!mbar_wait(&full[st], ph, err)) return false;
       const uint8_t* stage = stages + st * STAGE_BYTES;
-      const uint8_t* data = stage + SP::kHdr;
-      const int4* hdr = reinterpret_cast<const int4*>(stage);
-      const int4 h0 = hdr[g], h1 = hdr[g + 8];
-      const RowInfo r0{h0.x, h0.y, h0.z, h0.w}, r1{h1.x, h1.y, h1.z, h1.w};
-
-      // Running per-row positions.  Rows outside the matrix (valid == 0) read
-      // the stage from offset 0 instead of branching: every decoded A value is
-      // finite (magic f16 <= 1279, e2m1 <= 6), and their fold coefficient is 0.
-      // Rows g and g+8 are 8 rows apart and 8*K/32 is a multiple of 8 for any
-      // K % 32 == 0, so both rows sit at the same 32-block phase within their
-      // superblocks: one sub-block counter serves both.
-      using T = FmtT<F>;
-      const uint8_t* pA = data + (r0.valid ? r0.off : 0);
-      const uint8_t* pB = data + (r1.valid ? r1.off : 0);
-      int sA = 0;
-      if (kKQ) {
-        sA = (r0.valid ? r0.sub0 : r1.sub0) + u_beg;
-        pA += (sA >> 3) * T::BB;
-        pB += (sA >> 3) * T::BB;
-        sA &= 7;
-      } else {
-        pA += u_beg * T::BB;
-        pB += u_beg * T::BB;
-      }
-      const uint8_t* scA = data + r0.soff + u_beg;  // MXFP4 scale bytes
-      const uint8_t* scB = data + r1.soff + u_beg;
-      const uint4* xqp = xq + ((size_t)(ub + u_beg) * nv + vb) * 4 + t;
-      const float4* xsp = xsx + (size_t)(ub + u_beg) * nv;
-
-      for (int uc = u_beg; uc < u_end; uc += SP::kCoefCh) {
-        const int nst = min(SP::kCoefCh, u_end - uc);
-        if (F == FMT_Q4_K || F == FMT_Q5_K) {
-          // One task per (row, superblock): decode d, dmin and the 12 scale bytes
-          // once and emit the coefficients of the sub-blocks that fall in this
-          // chunk of steps (16 steps from any phase span at most 3 superblocks).
-          __syncwarp();
-          float2* cf = reinterpret_cast<float2*>(coef);
-          for (int task = lane; task < 48; task += 32) {
-            const int m = task / 3, j = task - 3 * (task / 3);
-            const int4 q = hdr[m];
-            if (!q.w) {
-              if (j == 0)
-                for (int u = 0; u < nst; ++u) cf[m * SP::kCoefCh + u] = make_float2(0.f, 0.f);
-              continue;
-            }
-            const int sb = ((q.y + uc) >> 3) + j;  // superblock index relative to the row's first
-            const int ubase = sb * 8 - q.y - uc;   // chunk step of sub-block 0 of this superblock
-            if (ubase >= nst) continue;
-            const uint4 hw = *reinterpret_cast<const uint4*>(data + q.x + sb * FmtT<F>::BB);
-            const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&hw.x));
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int u = ubase + i;
-              if (u < 0 || u >= nst) continue;
-              const int sh = 8 * (i & 3);
-              uint32_t sc, mn;
-              if (i < 4) {
-                sc = (hw.y >> sh) & 63u;
-                mn = (hw.z >> sh) & 63u;
-              } else {
-                sc = ((hw.w >> sh) & 15u) | (((hw.y >> sh) >> 2) & 0x30u);
-                mn = (((hw.w >> sh) >> 4) & 15u) | (((hw.z >> sh) >> 2) & 0x30u);
-              }
-              const float a = dd.x * small_u2f(sc);
-              cf[m * SP::kCoefCh + u] = make_float2(a, fmaf(FoldBias<F>::v, a, dd.y * small_u2f(mn)));
-            }
-          }
-          __syncwarp();
-        } else if (kKQ) {
-          __syncwarp();
-#pragma unroll
-          for (int e0 = 0; e0 < 16 * SP::kCoefCh; e0 += 32) {
-            const int e = e0 + lane;
-            const int m = e / SP::kCoefCh, s = e % SP::kCoefCh;
-            const int4 q = hdr[m];
-            const RowInfo ri{q.x, q.y, q.z, q.w};
-            float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (ri.valid && s < nst) c = fold_coef<F>(row_loc<F>(data, ri, uc + s));
-            if (F == FMT_Q6_K) reinterpret_cast<float4*>(coef)[m * SP::kCoefCh + s] = c;
-            else reinterpret_cast<float2*>(coef)[m * SP::kCoefCh + s] = make_float2(c.x, c.y);
-          }
-          __syncwarp();
-        }
-#pragma unroll 2
-        for (int s = 0; s < nst; ++s) {
-          const uint4 b = *xqp;
-          xqp += nv * 4;
-          RowLoc la, lb;
-          la.blk = pA; la.sub = sA; la.mx_scale = (F == FMT_MXFP4) ? scA[0] : 0u;
-          lb.blk = pB; lb.sub = sA; lb.mx_scale = (F == FMT_MXFP4) ? scB[0] : 0u;
-          uint32_t pa[4], pb[4];
-          decode_a<F>(la, t, pa);
-          decode_a<F>(lb, t, pb);
-          float c1[4] = {0.f, 0.f, 0.f, 0.f};
-          float c2[4] = {0.f, 0.f, 0.f, 0.f};
-          const uint32_t a1[4] = {pa[0], pb[0], pa[1], pb[1]};
-          const uint32_t a2[4] = {pa[2], pb[2], pa[3], pb[3]};
-          mma_f16(c1, a1, b.x, b.y);
-          if (F == FMT_Q6_K) mma_f16(c2, a2, b.z, b.w);
-          else mma_f16(c1, a2, b.z, b.w);
-          float4 ka, kb;
-          if (kKQ) {
-            if (F == FMT_Q6_K) {
-              ka = reinterpret_cast<const float4*>(coef)[g * SP::kCoefCh + s];
-              kb = reinterpret_cast<const float4*>(coef)[(g + 8) * SP::kCoefCh + s];
-            } else {
-              const float2 qa = reinterpret_cast<const float2*>(coef)[g * SP::kCoefCh + s];
-              const float2 qb = reinterpret_cast<const float2*>(coef)[(g + 8) * SP::kCoefCh + s];
-              ka = make_float4(qa.x, qa.y, 0.f, 0.f);
-              kb = make_float4(qb.x, qb.y, 0.f, 0.f);
-            }
-          } else {
-            ka = fold_coef<F>(la);
-            kb = fold_coef<F>(lb);
-            ka.x = r0.valid ? ka.x : 0.f; ka.y = r0.valid ? ka.y : 0.f;
-            kb.x = r1.valid ? kb.x : 0.f; kb.y = r1.valid ? kb.y : 0.f;
-          }
-          // advance both rows by one 32-element step
-          if (kKQ) {
-            if (++sA == 8) { sA = 0; pA += T::BB; pB += T::BB; }
-          } else {
-            pA += T::BB;
-            pB += T::BB;
-          }
-          if (F == FMT_MXFP4) { ++scA; ++scB; }
-          auto fold = [&](float& a, float cv1, float cv2, const float4& k, const float4& q) {
-            if (F == FMT_Q6_K) {
-              a = fmaf(k.x, cv1 * q.x, a);
-              a = fmaf(-k.y, q.y, a);
-              a = fmaf(k.z, cv2 * q.x, a);
-              a = fmaf(-k.w, q.z, a);
-            } else if (F == FMT_MXFP4) {
-              a = fmaf(k.x * q.x, cv1, a);
-            } else {
-              a = fmaf(k.x, cv1 * q.x, a);
-              a = fmaf(-k.y, q.y, a);
-            }
-          };
-          if (MODE == COLS_DUP) {
-            const float4 q0 = xsp[0];
-            fold(acc[0], c1[0], c2[0], ka, q0);
-            fold(acc[2], c1[2], c2[2], kb, q0);
-          } else if (MODE == COLS_FULL) {
-            const float4 qv0 = xsp[v0], qv1 = xsp[v1];
-            fold(acc[0], c1[0], c2[0], ka, qv0);
-            fold(acc[1], c1[1], c2[1], ka, qv1);
-            fold(acc[2], c1[2], c2[2], kb, qv0);
-            fold(acc[3], c1[3], c2[3], kb, qv1);
-          } else {
-            const bool oa = n_a & 1, ob = n_b & 1;
-            const float4 qa_ = xsp[n_a < 0 ? 0 : n_a], qb_ = xsp[n_b < 0 ? 0 : n_b];
-            fold(acc[0], oa ? c1[1] : c1[0], oa ? c2[1] : c2[0], ka, qa_);
-            fold(acc[2], ob ? c1[3] : c1[2], ob ? c2[3] : c2[2], kb, qb_);
-          }
-          xsp += nv;
-        }
-      }
+      consume_chunk<F, MODE, SP>(stage, u_beg, u_end, ub, nv, vb, v0, v1, n_a, n_b, xq, xsx, coef, acc, lane);
       if (kc + 1 < nkc) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
