@@ -52,7 +52,11 @@ constexpr int kATile = kBM * 128;         // 16 KB
 constexpr int kBTileMax = 256 * 128;      // 32 KB (N tile <= 256 rows)
 constexpr int kStage = kATile + kBTileMax;
 constexpr int kNS = 4;                    // pipeline depth
-constexpr int kGemmThreads = 256;         // warp 0 producer, warp 1 MMA, warps 4-7 epilogue
+// warp 0 producer, warp 1 MMA, warps 4-7 and kEpiB..kEpiB+3 epilogue (two sets
+// splitting the accumulator's columns; warp w reads tensor-memory lanes
+// 32*(w%4)..), warps 8-15 in-GEMM decode (BF variant)
+constexpr int kEpiB = 8, kEpiBFused = 16;
+constexpr int kGemmThreads = 384;
 constexpr int kTmemCols = 512;            // two accumulators of <= 256 columns
 constexpr size_t kGemmSmem = 1024 + (size_t)kNS * kStage + 256;
 
@@ -260,21 +264,26 @@ struct TileWArgs {
   int64_t estride;  // bytes per expert
 };
 
-// One CTA per (N tile, k-block) of one expert (blockIdx.y): eight threads per
-// tile row, one 16-byte chunk (8 elements) each, so a warp writes four whole
-// 128-byte rows.  For the gate/up projection a tile's first NT/2 rows are gate
-// features and the next NT/2 the same up features, whatever the source layout.
+// One CTA per (N tile, group of kTileKB k-blocks) of one expert (blockIdx.y):
+// eight threads per tile row, one 16-byte chunk (8 elements) per k-block each,
+// so a warp writes four whole 128-byte rows per k-block.  A thread decodes its
+// chunk of all kTileKB k-blocks before storing any, which keeps kTileKB
+// independent loads in flight per thread.  For the gate/up projection a tile's
+// first NT/2 rows are gate features and the next NT/2 the same up features,
+// whatever the source layout.
+constexpr int kTileKB = 4;
+
 template <int F>
 __global__ void __launch_bounds__(256) tile_weights_kernel(const TileWArgs a) {
   const int e = blockIdx.y;
   if (a.counts[e] == 0) return;
   const TsbExpert& E = a.experts[e];
-  const int nt = blockIdx.x / a.KB, kb = blockIdx.x % a.KB;
+  const int nkq = (a.KB + kTileKB - 1) / kTileKB;
+  const int nt = blockIdx.x / nkq, kb0 = (blockIdx.x % nkq) * kTileKB;
   const int half = a.NT / 2;
-  uint8_t* tile = a.out + (int64_t)e * a.estride + ((int64_t)nt * a.KB + kb) * a.NT * 128;
+  uint8_t* base = a.out + (int64_t)e * a.estride + (int64_t)nt * a.KB * a.NT * 128;
   for (int q = threadIdx.x; q < a.NT * 8; q += blockDim.x) {
     const int r = q >> 3, c = q & 7;
-    const int k0 = kb * kBK + c * 8;
     const uint8_t* w;
     const uint8_t* s;
     int64_t row;
@@ -295,19 +304,27 @@ __global__ void __launch_bounds__(256) tile_weights_kernel(const TileWArgs a) {
         row = a.layout == TSB_GU_INTERLEAVED ? 2 * j + (up ? 1 : 0) : (up ? a.I + j : j);
       }
     }
-    uint4 o = make_uint4(0, 0, 0, 0);
-    if (k0 < a.K) {
-      float v[8];
-      deq8<F>(w, s, row * a.K + k0, v);
-      uint32_t h[4];
+    uint4 o[kTileKB];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const __half2 p = __halves2half2(__float2half_rn(v[2 * i]), __float2half_rn(v[2 * i + 1]));
-        h[i] = *reinterpret_cast<const uint32_t*>(&p);
+    for (int i = 0; i < kTileKB; ++i) {
+      const int k0 = (kb0 + i) * kBK + c * 8;
+      o[i] = make_uint4(0, 0, 0, 0);
+      if (kb0 + i < a.KB && k0 < a.K) {
+        float v[8];
+        deq8<F>(w, s, row * a.K + k0, v);
+        uint32_t h[4];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const __half2 p = __halves2half2(__float2half_rn(v[2 * m]), __float2half_rn(v[2 * m + 1]));
+          h[m] = *reinterpret_cast<const uint32_t*>(&p);
+        }
+        o[i] = make_uint4(h[0], h[1], h[2], h[3]);
       }
-      o = make_uint4(h[0], h[1], h[2], h[3]);
     }
-    *reinterpret_cast<uint4*>(tile + sw128_off(r, c)) = o;
+#pragma unroll
+    for (int i = 0; i < kTileKB; ++i)
+      if (kb0 + i < a.KB)
+        *reinterpret_cast<uint4*>(base + ((int64_t)(kb0 + i) * a.NT + r) * 128 + sw128_off(0, c ^ (r & 7))) = o[i];
   }
 }
 
@@ -459,7 +476,8 @@ constexpr int kRawSlot = 256 * kRawPitch;
 constexpr size_t kGemmSmemFused = 1024 + (size_t)kNSFused * kStage + (size_t)kRawSlots * kRawSlot + 256;
 
 template <int BF>
-__global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const GemmArgs g) {
+__global__ void __launch_bounds__(BF ? 640 : 384, 1) grouped_gemm_kernel(const GemmArgs g) {
+  constexpr int EB = BF ? kEpiBFused : kEpiB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int NS = BF ? kNSFused : kNS;
@@ -482,7 +500,7 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], 8);
     }
     mbar_init(fin, 1);
     if (BF) {
@@ -544,8 +562,9 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
     // Every MMA issued above completes before tensor memory is released.
     umma_commit(fin);
     mbar_wait(fin, 0, g.err);
-  } else if (warp >= 4 && warp < 8) {
-    const int q = warp - 4;
+  } else if ((warp >= 4 && warp < 8) || (warp >= EB && warp < EB + 4)) {
+    const int q = warp & 3;
+    const bool setB = warp >= EB;
     const int m = 32 * q + lane;
     uint32_t tc = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tc) {
@@ -565,7 +584,8 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
         const float asc = pow2f(-ash);
         const float* gb = E.gate_bias;
         const float* ub = E.up_bias;
-        for (int c = 0; c < half; c += 8) {
+        const int cs = (half / 2 + 7) / 8 * 8;
+        for (int c = setB ? cs : 0; c < (setB ? half : cs); c += 8) {
           uint32_t gr[8], ur[8];
           tmem_ld8(tl + c, gr);
           tmem_ld8(tl + half + c, ur);
@@ -589,7 +609,8 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
       } else {
         const float* db = E.down_bias;
         const float dsc = pow2f(ash);
-        for (int c = 0; c < g.NT; c += 8) {
+        const int cs = (g.NT / 2 + 7) / 8 * 8;
+        for (int c = setB ? cs : 0; c < (setB ? g.NT : cs); c += 8) {
           uint32_t r[8];
           tmem_ld8(tl + c, r);
           tmem_ld_wait();
@@ -608,7 +629,7 @@ __global__ void __launch_bounds__(BF ? 512 : 256, 1) grouped_gemm_kernel(const G
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
     }
-  } else if (BF && warp >= 8) {
+  } else if (BF && warp >= 8 && warp < 16) {
     // Raw MXFP4 bytes of this thread's B row arrive kRawItems k-blocks at a
     // time (one bulk copy per row, kRawSlots groups ahead); E8M0 scales are
     // read with plain loads one group ahead.  Groups never straddle tiles.
@@ -869,7 +890,7 @@ static int num_sms() {
 
 template <int F>
 static void launch_tile_weights(const TileWArgs& a, int E, cudaStream_t st) {
-  tile_weights_kernel<F><<<dim3((a.N / a.NT) * a.KB, E), 256, 0, st>>>(a);
+  tile_weights_kernel<F><<<dim3((a.N / a.NT) * ((a.KB + kTileKB - 1) / kTileKB), E), 256, 0, st>>>(a);
 }
 
 static int tile_weights(int fmt, const TileWArgs& a, int E, cudaStream_t st) {
@@ -892,7 +913,7 @@ static int launch_gemm(const GemmArgs& g, int tiles_max, cudaStream_t st) {
   }();
   if (!attr) return set_error(TSB_ERR_CUDA, "cannot enable the grouped GEMM's shared memory");
   const int grid = std::max(1, std::min(tiles_max, num_sms()));
-  grouped_gemm_kernel<BF><<<grid, BF ? 512 : 256, BF ? kGemmSmemFused : kGemmSmem, st>>>(g);
+  grouped_gemm_kernel<BF><<<grid, BF ? 640 : kGemmThreads, BF ? kGemmSmemFused : kGemmSmem, st>>>(g);
   return TSB_OK;
 }
 
