@@ -61,82 +61,108 @@ constexpr int kTmemCols = 512;            // two accumulators of <= 256 columns
 constexpr size_t kGemmSmem = 1024 + (size_t)kNS * kStage + 256;
 
 // ------------------------------------------------------------------ routing
-// counts[e] = #(t, j) with ids[t, j] == e.  Ids outside [0, E) are reported in
-// the error word and get row_of = -1 (they contribute nothing, as in decode).
-__global__ void __launch_bounds__(256) route_count_kernel(const int32_t* __restrict__ ids, int n, int E,
-                                                          int* __restrict__ counts, int* __restrict__ row_of,
-                                                          int* err) {
-  const int e = blockIdx.x;
-  int c = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+// Grouping of the T*k (token, slot) entries by expert, in three small kernels
+// over chunks of kRouteChunk entries:
+//   route_chunk_count  per-chunk histogram (shared-memory atomics; integer
+//                      counts, so the order of the atomics does not matter)
+//   route_scan         per expert: total, exclusive prefix over chunks and the
+//                      expert's first row (experts padded to 128-row blocks);
+//                      padding rows, row-block owners and the block count
+//   route_chunk_place  one warp per chunk walks its entries in index order and
+//                      gives each the next row of its expert (warp match +
+//                      popcount), so inside an expert rows keep (token, slot)
+//                      order and the grouping is deterministic
+// Ids outside [0, E) are reported in the error word and get row_of = -1 (they
+// contribute nothing, as in decode).
+constexpr int kRouteChunk = 1024;
+
+__global__ void __launch_bounds__(256) route_chunk_count(const int32_t* __restrict__ ids, int n, int E,
+                                                         int* __restrict__ ccount, int* __restrict__ row_of, int* err) {
+  extern __shared__ int hist[];
+  const int c = blockIdx.x;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  for (int j = threadIdx.x; j < kRouteChunk; j += blockDim.x) {
+    const int i = c * kRouteChunk + j;
+    if (i >= n) break;
     const int v = ids[i];
-    c += (v == e);
-    if (e == 0 && (unsigned)v >= (unsigned)E) {
+    if ((unsigned)v < (unsigned)E) {
+      atomicAdd(&hist[v], 1);
+    } else {
       row_of[i] = -1;
       atomicExch(err, kDevBadPlan);
     }
   }
-  __shared__ int part[8];
-#pragma unroll
-  for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int s = 0;
-    for (int w = 0; w < 8; ++w) s += part[w];
-    counts[e] = s;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) ccount[(size_t)c * E + e] = hist[e];
+}
+
+__global__ void __launch_bounds__(1024) route_scan(int nchunks, int E, int* __restrict__ ccount,
+                                                   int* __restrict__ counts, int* __restrict__ row_src,
+                                                   int* __restrict__ mb_expert, int* __restrict__ total_mb) {
+  __shared__ int wsum[32];
+  const int e = threadIdx.x;
+  int tot = 0;
+  if (e < E) {
+    for (int c = 0; c < nchunks; ++c) {  // exclusive prefix over chunks, in place
+      const int v = ccount[(size_t)c * E + e];
+      ccount[(size_t)c * E + e] = tot;
+      tot += v;
+    }
+    counts[e] = tot;
+  }
+  // exclusive scan of the padded totals over experts (block-wide)
+  const int padded = (e < E) ? (tot + kBM - 1) / kBM * kBM : 0;
+  const int lane = e & 31, warp = e >> 5;
+  int inc = padded;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  if (lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const int v = wsum[lane];
+    int w = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += u;
+    }
+    wsum[lane] = w - v;
+  }
+  __syncthreads();
+  const int start = wsum[warp] + inc - padded;
+  if (e < E) {
+    for (int c = 0; c < nchunks; ++c) ccount[(size_t)c * E + e] += start;
+    for (int r = tot; r < padded; ++r) row_src[start + r] = -1;
+    for (int b = 0; b < padded / kBM; ++b) mb_expert[start / kBM + b] = e;
+    if (e == E - 1) *total_mb = (start + padded) / kBM;
   }
 }
 
-// Expert e's rows: start_e = sum over e' < e of count rounded up to 128.  The
-// rank of (t, j) inside its expert is its position in flattened (t, j) order,
-// so the grouping is deterministic.  Writes row_of[t*k+j], row_src[row] (the
-// token, -1 for padding), mb_expert[row/128] and the number of row blocks.
-__global__ void __launch_bounds__(1024) route_place_kernel(const int32_t* __restrict__ ids, int n, int top_k, int E,
-                                                           const int* __restrict__ counts, int* __restrict__ row_of,
-                                                           int* __restrict__ row_src, int* __restrict__ mb_expert,
-                                                           int* __restrict__ total_mb) {
-  const int e = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ int s_start, s_run, s_woff[32], s_tot;
-  if (threadIdx.x == 0) {
-    int st = 0;
-    for (int q = 0; q < e; ++q) st += (counts[q] + kBM - 1) / kBM * kBM;
-    s_start = st;
-    s_run = 0;
-    if (e == E - 1) *total_mb = (st + (counts[e] + kBM - 1) / kBM * kBM) / kBM;
-  }
-  __syncthreads();
-  const int start = s_start, cnt = counts[e], pad = (cnt + kBM - 1) / kBM * kBM;
-  for (int base = 0; base < n; base += 1024) {
-    const int i = base + threadIdx.x;
-    const bool f = i < n && ids[i] == e;
-    const unsigned bal = __ballot_sync(0xffffffffu, f);
-    if (lane == 0) s_woff[warp] = __popc(bal);
-    __syncthreads();
-    if (warp == 0) {
-      const int v = s_woff[lane];
-      int inc = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += u;
-      }
-      s_woff[lane] = inc - v;
-      if (lane == 31) s_tot = inc;
-    }
-    __syncthreads();
-    if (f) {
-      const int r = start + s_run + s_woff[warp] + __popc(bal & ((1u << lane) - 1u));
+__global__ void __launch_bounds__(32) route_chunk_place(const int32_t* __restrict__ ids, int n, int top_k, int E,
+                                                        const int* __restrict__ cbase, int* __restrict__ row_of,
+                                                        int* __restrict__ row_src) {
+  extern __shared__ int running[];
+  const int c = blockIdx.x, lane = threadIdx.x;
+  for (int e = lane; e < E; e += 32) running[e] = cbase[(size_t)c * E + e];
+  __syncwarp();
+  for (int j = 0; j < kRouteChunk; j += 32) {
+    const int i = c * kRouteChunk + j + lane;
+    const int v = i < n ? ids[i] : -1;
+    const bool ok = (unsigned)v < (unsigned)E;
+    const unsigned peers = __match_any_sync(0xffffffffu, ok ? v : -1 - lane);
+    if (ok) {
+      const int r = running[v] + __popc(peers & ((1u << lane) - 1u));
       row_of[i] = r;
       row_src[r] = i / top_k;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) s_run += s_tot;
-    __syncthreads();
+    __syncwarp();
+    if (ok && lane == __ffs(peers) - 1) running[v] += __popc(peers);
+    __syncwarp();
   }
-  for (int r = cnt + threadIdx.x; r < pad; r += blockDim.x) row_src[start + r] = -1;
-  for (int b = threadIdx.x; b < pad / kBM; b += blockDim.x) mb_expert[start / kBM + b] = e;
 }
 
 // One warp per permuted row: copy token row x[src] (bf16) into the fp16 A
@@ -860,6 +886,7 @@ PrefillLayout prefill_layout(const TsbMoeSpec& sp, int T) {
   L.total_mb = 4;     // int32
   o = 256;
   L.counts = o;   o = al(o + 4 * (size_t)sp.n_experts);
+  L.ccount = o;   o = al(o + 4 * (size_t)sp.n_experts * (size_t)((n + kRouteChunk - 1) / kRouteChunk));
   L.mb_expert = o; o = al(o + 4 * (size_t)L.mb_max);
   L.row_of = o;   o = al(o + 4 * (size_t)n);
   L.row_src = o;  o = al(o + 4 * (size_t)L.rows_max);
@@ -948,8 +975,11 @@ int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x,
     const int rc = launch_route(sp, x, T, rw, rb, ids, wts, st);
     if (rc) return rc;
   }
-  route_count_kernel<<<E, 256, 0, st>>>(ids, n, E, counts, row_of, err);
-  route_place_kernel<<<E, 1024, 0, st>>>(ids, n, k, E, counts, row_of, row_src, mb_expert, total_mb);
+  int* ccount = reinterpret_cast<int*>(ws + L.ccount);
+  const int nchunks = (n + kRouteChunk - 1) / kRouteChunk;
+  route_chunk_count<<<nchunks, 256, 4 * E, st>>>(ids, n, E, ccount, row_of, err);
+  route_scan<<<1, 1024, 0, st>>>(nchunks, E, ccount, counts, row_src, mb_expert, total_mb);
+  route_chunk_place<<<nchunks, 32, 4 * E, st>>>(ids, n, k, E, ccount, row_of, row_src);
   gather_rows_kernel<<<(int)((L.rows_max + 7) / 8), 256, 0, st>>>(static_cast<const uint16_t*>(x), sp.hidden, L.kbh,
                                                                   row_src, total_mb, xp, row_shift);
   if (sp.inter % kBK) {

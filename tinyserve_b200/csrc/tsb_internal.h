@@ -29,7 +29,7 @@ int launch_moe_fused(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, c
                      cudaStream_t st);
 // Workspace layout of tsb_moe_prefill (byte offsets) and its tile geometry.
 struct PrefillLayout {
-  size_t err, total_mb, counts, mb_expert, row_of, row_src, row_shift, xp, act, y, wgu, wdn, total;
+  size_t err, total_mb, counts, ccount, mb_expert, row_of, row_src, row_shift, xp, act, y, wgu, wdn, total;
   int64_t rows_max, wgu_estride, wdn_estride;
   int mb_max, kbh, kbi, nt_gu, nt_dn;
   bool fused_gu, fused_dn;  // MXFP4 decoded inside the GEMM (no fp16 weight tiles)
