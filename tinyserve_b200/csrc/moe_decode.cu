@@ -402,19 +402,19 @@ static cudaError_t run_plan(const P& plan, int nblocks, int nv, cudaStream_t st,
       auto kern = qmv_kernel<F, MODE, kNCW, kNStageWide, kStageBytes, kGroupsWide, P>;
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
-      return launch(kern, grid, 32 * (kNCW + 1), (size_t)smem, st, pdl, plan);
+      return launch(kern, grid, 32 * (kNCW + kNStageWide), (size_t)smem, st, pdl, plan);
     }
     const int smem = SmemPlan<kNCW, kNStage, kStageBytes, MODE, F>::total(plan.geom.K, nv);
     auto kern = qmv_kernel<F, MODE, kNCW, kNStage, kStageBytes, 2, P>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    return launch(kern, grid, 32 * (kNCW + 1), (size_t)smem, st, pdl, plan);
+    return launch(kern, grid, 32 * (kNCW + kNStage), (size_t)smem, st, pdl, plan);
   }
   const int smem = SmemPlan<kNCW, kNStage, kStageBytes, MODE, F>::total(plan.geom.K, nv);
   auto kern = qmv_kernel<F, MODE, kNCW, kNStage, kStageBytes, 1, P>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  return launch(kern, grid, 32 * (kNCW + 1), (size_t)smem, st, pdl, plan);
+  return launch(kern, grid, 32 * (kNCW + kNStage), (size_t)smem, st, pdl, plan);
 }
 
 int max_vectors_for(int K) {

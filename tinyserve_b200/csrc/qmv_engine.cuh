@@ -342,7 +342,7 @@ struct SmemPlan {
   static constexpr int off_red = 256;
   static constexpr int off_cache = off_red + kRed;
   static constexpr int off_ptab = off_cache + kMaxSlots * (int)sizeof(SlotCache);
-  static constexpr int off_coef = ((off_ptab + kPtabBytes + 15) / 16) * 16;
+  static constexpr int off_coef = ((off_ptab + NSTAGE * kPtabBytes + 15) / 16) * 16;  // one table per producer
   static constexpr int off_stage = ((off_coef + kCoef + 127) / 128) * 128;
   static constexpr int off_x = off_stage + NSTAGE * STAGE_BYTES;
   static __host__ __device__ constexpr int x_bytes(int K, int nv) { return (K / 32) * nv * (64 + 16); }
@@ -388,9 +388,12 @@ __device__ __forceinline__ int eng_units(const P& plan) {
 
 // Producer warp: stream every row block of this CTA for `plan` into the stage
 // ring, continuing the ring position `it`.  Returns false if a wait timed out.
+// With np producer warps, producer p fills the ring positions it with
+// it % np == p (np == NSTAGE: producer p owns stage p); every producer walks
+// the same unit sequence so the positions agree with the consumers'.
 template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, int NG, class P>
 __device__ __forceinline__ bool eng_produce(const P& plan, const SlotCache* cache, const EngSmem& S, int& it, int lane,
-                                            int* err) {
+                                            int* err, int np = 1, int pidx = 0) {
   using SP = SmemPlan<NCW, NSTAGE, STAGE_BYTES, MODE, F>;
   constexpr int WPG = NCW / NG;
   static_assert(NCW % NG == 0, "groups must split the consumer warps evenly");
@@ -414,6 +417,7 @@ __device__ __forceinline__ bool eng_produce(const P& plan, const SlotCache* cach
       for (int j = 0; j < kPtabUnits; ++j) {
         const int rb = rb0 + j * gridDim.x;
         if (rb >= nblocks) break;
+        if ((it + j) % np != pidx) continue;  // another producer's stage
         const int ns = plan.nseg(rb);
         uint32_t bytes = 0;
         if (lane < 16) {
@@ -443,6 +447,7 @@ __device__ __forceinline__ bool eng_produce(const P& plan, const SlotCache* cach
       for (int j = 0; j < kPtabUnits; ++j, ++u, ++it) {
         const int rb = rb0 + j * gridDim.x;
         if (rb >= nblocks) break;
+        if (it % np != pidx) continue;
         const int ns = plan.nseg(rb);
         const int st = it % NSTAGE;
         const uint32_t ph = ((it / NSTAGE) & 1) ^ 1;
@@ -480,6 +485,7 @@ __device__ __forceinline__ bool eng_produce(const P& plan, const SlotCache* cach
         if (rs >= 0) rseg = plan.seg(cache, rb, rs);
       }
       for (int kc = 0; kc < nkc; ++kc, ++it) {
+        if (it % np != pidx) continue;
         const int k0 = kc * KC, k1 = min(K, k0 + KC);
         const bool whole = (k0 == 0 && k1 == K);
         const int st = it % NSTAGE;
@@ -787,7 +793,7 @@ __device__ __forceinline__ bool eng_consume(const P& plan, const SlotCache* cach
 }
 
 template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, int NG, class P>
-__global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
+__global__ void __launch_bounds__(32 * (NCW + NSTAGE), 1) qmv_kernel(const P plan) {
   // Waits use only the parity of a stage's phase.  A group waits for its next
   // row block only after finishing its previous one, and stages are filled in
   // row-block order, so with NG <= NSTAGE a stage is never two fills ahead of
@@ -804,7 +810,6 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
   S.red = reinterpret_cast<float*>(smem + SP::off_red);
   S.stages = smem + SP::off_stage;
   S.coef = smem + SP::off_coef;
-  S.ptab = smem + SP::off_ptab;
   SlotCache* cache = reinterpret_cast<SlotCache*>(smem + SP::off_cache);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = plan.geom.K;
@@ -821,22 +826,24 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) qmv_kernel(const P plan) {
     fence_barrier_init();
   }
   __syncthreads();
-  if (warp == 0) {
+  // Warps 0..NSTAGE-1 are producers (producer p fills stage p); the rest consume.
+  if (warp < NSTAGE) {
     if (P::kProducerWaits) pdl_wait();
-    plan.fill_cache(cache, lane);
-    __syncwarp();
+    if (warp == 0) plan.fill_cache(cache, lane);
+    named_bar_sync(2, 32 * NSTAGE);  // slot cache ready for every producer
+    S.ptab = smem + SP::off_ptab + warp * kPtabBytes;
     int it = 0;
-    eng_produce<F, MODE, NCW, NSTAGE, STAGE_BYTES, NG>(plan, cache, S, it, lane, err);
+    eng_produce<F, MODE, NCW, NSTAGE, STAGE_BYTES, NG>(plan, cache, S, it, lane, err, NSTAGE, warp);
     return;
   }
-  const int ctid = tid - 32;
+  const int ctid = tid - 32 * NSTAGE;
   if (!P::kXIndependent) pdl_wait();
   stage_x<F>(xq_raw, xsx, K, nv, plan.xsrc(), ctid, 32 * NCW);
   named_bar_sync(1, 32 * NCW);
   if (P::kXIndependent) pdl_wait();
   pdl_launch_dependents();
   eng_consume<F, MODE, NCW, NSTAGE, STAGE_BYTES, NG>(plan, cache, S, 0, reinterpret_cast<const uint4*>(xq_raw), xsx,
-                                                     warp - 1, lane, err);
+                                                     warp - NSTAGE, lane, err);
 }
 
 // Host-side geometry (excluding the 256-B RowInfo header): stage slot size for a given chunk.
