@@ -220,7 +220,9 @@ def run_ours(args, ws, rank, local):
                    "l2": f"inputs larger than L2: {NL} layer replicas cycled ({NL * 32 * expert_b / 1e9:.2f} GB)",
                    "timing": "one CUDA graph of K steps, CUDA events, max over ranks"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": peak_kind, "traffic": None,
+                     "peak_source": peak_kind, "traffic": DECODE_TRAFFIC,
+                     "traffic_source": "ncu dram__bytes_read+write of the three launches of one token-layer "
+                                       "(profiles/moe_layer_decode_q4k.md), same workload",
                      "unit_of_work": f"one token through one layer = {step_bytes} algorithmic bytes "
                                      "(4 experts' Q4_K gate/up/down + router + activations)",
                      "kernel": "router + gate_up(SwiGLU) + down(combine), PDL-chained"},
@@ -233,6 +235,10 @@ def run_ours(args, ws, rank, local):
     }
     return res, layers, xs
 
+
+# DRAM bytes per token-layer from the committed ncu capture of this workload
+# (gate/up 37.40 MB + down 18.77 MB + router 0.19 MB read, writes < 0.1 MB).
+DECODE_TRAFFIC = 56.4e6
 
 PREFILL_T = 4096
 
@@ -280,6 +286,65 @@ def run_prefill(dev, steps: int = 10, warmup: int = 3):
                                          "(experts padded to 128-row blocks) run on the tensor cores",
                          "kernel": "whole layer: route + gather + weight tiles + 2 grouped GEMMs + combine"},
             "gpu_launches_per_layer": 8}
+
+
+SWEEP_SHAPES = [(2880, 2880), (5760, 2880), (4096, 14336), (14336, 4096)]
+
+
+def run_matvec_sweep(dev, reps: int = 6, calls: int = 24):
+    """tsb_quant_matvec on each format x shape, batch 1,
+    weights N(0, 0.02) quantised per format, bf16 N(0, 1) activations.  Each
+    timing is a CUDA graph of `calls` matvecs cycling over `reps` distinct
+    matrices (at least 26 MB apart in the cycle, so the timed reads come
+    from HBM for the large shapes), CUDA events."""
+    import torch
+    from tinyserve_b200 import ops
+    from tinyserve_b200 import quantize as Q
+    from tinyserve_b200.formats import GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_Q8_0, TSB_MXFP4
+    peak, _ = _peaks()
+    names = {GGML_Q8_0: "Q8_0", GGML_Q4_K: "Q4_K", GGML_Q5_K: "Q5_K", GGML_Q6_K: "Q6_K", TSB_MXFP4: "MXFP4"}
+    out = []
+    st = torch.cuda.Stream(dev)
+    for fmt in (GGML_Q8_0, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, TSB_MXFP4):
+        for (N, K) in SWEEP_SHAPES:
+            g = torch.Generator(device=dev).manual_seed(N * 31 + K + fmt)
+            ws = []
+            for _ in range(reps):
+                w = torch.randn(N, K, generator=g, device=dev) * 0.02
+                if fmt == TSB_MXFP4:
+                    b, sc = Q.quantize_mxfp4(w, N, K)
+                    ws.append((b.reshape(-1), sc.reshape(-1)))
+                else:
+                    ws.append((Q.quantize(fmt, w), None))
+                del w
+            x = torch.randn(1, K, generator=g, device=dev).to(torch.bfloat16)
+            nbytes = ws[0][0].numel() + (ws[0][1].numel() if ws[0][1] is not None else 0)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(st):
+                for i in range(3):
+                    ops.quant_matvec(fmt, ws[i % reps][0], ws[i % reps][1], N, K, x)
+                torch.cuda.synchronize()
+                with torch.cuda.graph(graph, stream=st):
+                    for i in range(calls):
+                        ops.quant_matvec(fmt, ws[i % reps][0], ws[i % reps][1], N, K, x)
+            graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(st):
+                e0.record(st)
+                graph.replay()
+                e1.record(st)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / calls
+            alg = nbytes + 2 * K + 2 * N  # weights + bf16 x + bf16 y
+            gbs = alg / us / 1e3
+            out.append({"format": names[fmt], "rows": N, "cols": K, "us": us, "GB/s": gbs, "frac": gbs / peak})
+            del ws, graph
+    torch.cuda.empty_cache()
+    return {"metric": "quant_matvec_hbm_gbs", "unit": "GB/s", "peak": peak, "peak_source": "measured copy",
+            "config": {"workload": "BASELINE config 2: batch-1 quantised matvec sweep (5 formats x 4 shapes)",
+                       "timing": f"CUDA graph of {calls} calls over {reps} distinct matrices, CUDA events"},
+            "results": out}
 
 
 EP_T = 4096  # tokens per rank per layer call (weak scaling)
@@ -423,6 +488,7 @@ def main():
         res["prefill"] = pf
         torch.cuda.empty_cache()
         res["expert_parallel"] = run_ep(torch.device("cuda", local), ws, rank)
+        res["matvec_sweep"] = run_matvec_sweep(torch.device("cuda", local))
     if rank == 0:
         if not args.no_cpu_baseline and ws == 1:
             threads = len(os.sched_getaffinity(0))
