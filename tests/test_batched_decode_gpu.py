@@ -82,3 +82,19 @@ def test_pipeline_batched_prefill_api(dev):
     assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
     assert pipe.execute_layer_experts_batched(x[:0].to(dev), 0, ids[:0], wts[:0]).shape == (0, H)
     assert pipe.schedule_prefetch(0, [1, 2]) is None
+
+
+def test_decode_inplace_matches_decode(dev):
+    """QuantMoE.decode_ (caller-owned buffers, prepared arguments) gives the
+    same routing and output as decode, with and without a router, T = 1 and 3."""
+    H, I, E, k = 512, 256, 8, 2
+    layer, _, _ = _build_layer(dev, GGML_Q4_K, GGML_Q4_K, H, I, E, k, "separate", seed=13)
+    for T in (1, 3):
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(T)).to(torch.bfloat16).to(dev)
+        ref, ref_ids, ref_w = layer.decode(x)
+        out = torch.empty_like(ref)
+        ids = torch.empty_like(ref_ids)
+        w = torch.empty_like(ref_w)
+        layer.decode_(x, out, ids, w)
+        torch.cuda.synchronize()
+        assert torch.equal(ids, ref_ids) and torch.equal(w, ref_w) and torch.equal(out, ref)

@@ -410,6 +410,20 @@ static cudaError_t run_plan(const P& plan, int nblocks, int nv, cudaStream_t st,
     if (e != cudaSuccess) return e;
     return launch(kern, grid, 32 * (kNCW + kNStage), (size_t)smem, st, pdl, plan);
   }
+  // K-chunked rows: two consumer groups over the deeper ring when the ring is
+  // still phase-safe for them ((groups - 1) * chunks + 1 <= stages, see
+  // qmv_kernel), so each warp covers twice as many steps of a stage.
+  {
+    using SW = SmemPlan<kNCW, kNStageWide, kStageBytes, MODE, F>;
+    const int nkc = (plan.geom.K + plan.geom.KC - 1) / plan.geom.KC;
+    if (MODE != COLS_FULL && (2 - 1) * nkc + 1 <= kNStageWide && SW::total(plan.geom.K, nv) <= 227 * 1024) {
+      const int smem = SW::total(plan.geom.K, nv);
+      auto kern = qmv_kernel<F, MODE, kNCW, kNStageWide, kStageBytes, 2, P>;
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      return launch(kern, grid, 32 * (kNCW + kNStageWide), (size_t)smem, st, pdl, plan);
+    }
+  }
   const int smem = SmemPlan<kNCW, kNStage, kStageBytes, MODE, F>::total(plan.geom.K, nv);
   auto kern = qmv_kernel<F, MODE, kNCW, kNStage, kStageBytes, 1, P>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

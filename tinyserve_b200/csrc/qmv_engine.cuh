@@ -794,11 +794,13 @@ __device__ __forceinline__ bool eng_consume(const P& plan, const SlotCache* cach
 
 template <int F, int MODE, int NCW, int NSTAGE, int STAGE_BYTES, int NG, class P>
 __global__ void __launch_bounds__(32 * (NCW + NSTAGE), 1) qmv_kernel(const P plan) {
-  // Waits use only the parity of a stage's phase.  A group waits for its next
-  // row block only after finishing its previous one, and stages are filled in
-  // row-block order, so with NG <= NSTAGE a stage is never two fills ahead of
-  // its waiter; with more groups than stages a waiter can match an older
-  // phase of the same parity and read another row block's stage.
+  // Waits use only the parity of a stage's phase, so a consumer may wait for
+  // ring position p only once position p - NSTAGE has been filled (else it
+  // matches that older phase of the same parity and reads another unit).
+  // Fills are in ring order and a group waits for p only after consuming its
+  // previous position p', so the condition holds when p - p' <= NSTAGE: the
+  // largest gap is (NG - 1) * nkc + 1 (the other groups' row blocks), which the
+  // launcher keeps <= NSTAGE (nkc = 1 for whole-row plans: NG <= NSTAGE).
   static_assert(NG <= NSTAGE, "more consumer groups than stages aliases mbarrier phases");
   using SP = SmemPlan<NCW, NSTAGE, STAGE_BYTES, MODE, F>;
   constexpr int WPG = NCW / NG;

@@ -62,6 +62,7 @@ class QuantMoE:
         self._table = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.device)
         self._ws_cache: dict[int, torch.Tensor] = {}
         self._pws_cache: dict[int, torch.Tensor] = {}
+        self._fast: dict[int, tuple] = {}
 
     def workspace(self, T: int) -> torch.Tensor:
         if T not in self._ws_cache:
@@ -99,6 +100,30 @@ class QuantMoE:
             torch.cuda.current_stream(self.device).cuda_stream)
         _lib.check(rc)
         return out, ids, weights
+
+    def decode_(self, x: torch.Tensor, out: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                stream: int | None = None) -> None:
+        """Allocation-free :meth:`decode` into caller-owned buffers (x bf16
+        [T, H], out bf16 [T, H], ids int32 [T, k], weights fp32 [T, k], all
+        contiguous on this device).  With a router the routing is written to
+        ids / weights; without one they are read.  `stream` is a raw
+        cudaStream_t (default: the current stream).  The C arguments that do not
+        change between calls are prepared once per T, so a call is one ctypes
+        call with no tensor allocation: the lean path for per-token serving."""
+        T = x.shape[0]
+        fast = self._fast.get(T)
+        if fast is None:
+            ws = self.workspace(T)
+            fn = _lib.lib().tsb_moe_decode
+            routed = self.router_w is not None
+            fast = (fn, ctypes.byref(self.spec), self._table.data_ptr(), _p(self.router_w) if routed else None,
+                    _p(self.router_b) if routed else None, ws.data_ptr(), ws.numel())
+            self._fast[T] = fast
+        fn, spec, table, rw, rb, wsp, wsn = fast
+        st = torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream
+        rc = fn(spec, table, x.data_ptr(), T, rw, rb, ids.data_ptr(), weights.data_ptr(), out.data_ptr(), wsp, wsn, st)
+        if rc:
+            _lib.check(rc)
 
     def prefill_workspace(self, T: int) -> torch.Tensor:
         if T not in self._pws_cache:
