@@ -399,7 +399,12 @@ static cudaError_t run_plan(const P& plan, int nblocks, int nv, cudaStream_t st,
     using SW = SmemPlan<kNCW, kNStageWide, kStageBytes, MODE, F>;
     if (MODE == COLS_DUP && SW::total(plan.geom.K, nv) <= 227 * 1024) {
       const int smem = SW::total(plan.geom.K, nv);
-      auto kern = qmv_kernel<F, MODE, kNCW, kNStageWide, kStageBytes, kGroupsWide, P>;
+      // With few row blocks per CTA (small matrices) fewer groups keep all
+      // consumer warps on the blocks there are.
+      const int per_cta = (nblocks + grid - 1) / grid;
+      auto kern = per_cta >= 3           ? qmv_kernel<F, MODE, kNCW, kNStageWide, kStageBytes, kGroupsWide, P>
+                  : per_cta >= 2         ? qmv_kernel<F, MODE, kNCW, kNStageWide, kStageBytes, 2, P>
+                                         : qmv_kernel<F, MODE, kNCW, kNStageWide, kStageBytes, 1, P>;
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
       return launch(kern, grid, 32 * (kNCW + kNStageWide), (size_t)smem, st, pdl, plan);
