@@ -56,7 +56,7 @@ static int check_shape(int fmt, int64_t rows, int64_t cols) {
 
 // Workspace layout of tsb_moe_decode (offsets in bytes).
 struct WsLayout {
-  size_t err, counter, gridbar, logits, act, total;
+  size_t err, counter, logits, act, total;
 };
 
 static WsLayout ws_layout(const TsbMoeSpec& sp, int T) {
@@ -64,7 +64,6 @@ static WsLayout ws_layout(const TsbMoeSpec& sp, int T) {
   auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
   L.err = 0;
   L.counter = 4;
-  L.gridbar = 8;  // two unsigned: arrivals, generation
   L.logits = 256;
   L.act = L.logits + al(sizeof(float) * (size_t)T * sp.n_experts);
   L.total = L.act + al(sizeof(float) * (size_t)T * sp.top_k * sp.inter);
@@ -200,17 +199,6 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
   float* act = reinterpret_cast<float*>(ws + L.act);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool routed = router_w != nullptr;
-  // The single-launch persistent kernel is opt-in (TSB_DECODE_FUSED=1): on the
-  // GPT-OSS-20B shape the three PDL-chained launches are currently faster.
-  static const bool fused = [] {
-    const char* v = getenv("TSB_DECODE_FUSED");
-    return v && v[0] == '1';
-  }();
-  if (routed && fused) {
-    rc = launch_moe_fused(sp, experts, x, router_w, router_b, ids, weights, out, act,
-                          reinterpret_cast<float*>(ws + L.logits), reinterpret_cast<unsigned*>(ws + L.gridbar), err, st);
-    if (rc != -1) return rc;
-  }
   if (routed) {
     rc = launch_router(x, router_w, router_b, sp.hidden, sp.n_experts, T, sp.top_k,
                        reinterpret_cast<float*>(ws + L.logits), ids, weights,

@@ -184,7 +184,7 @@ struct PlanDownT1 {
   int n_experts;
   int top_k, rpe, H, I;
   const float* act;  // [top_k, I]
-  int act_cg;        // act written by other CTAs of the same grid (fused kernel)
+  int act_cg;        // act written by other CTAs of this grid: load through L2 (0 here)
   uint16_t* out;     // bf16 [H]
   int64_t dn_bytes;
 
@@ -366,23 +366,23 @@ static int num_sms() {
 
 template <int F>
 static bool choose_geom(int K, int nseg, int rows_per_seg, StageGeom& G, int kData = kStageBytes - 256) {
-  // kData: stage (or warp buffer) bytes minus its RowInfo header
+  // kData: stage bytes minus its RowInfo header
   int slot, scb, ssl;
   G.K = K;
   G.rps = rows_per_seg;
-  if (host_stage_bytes<F>(K, K, nseg, rows_per_seg, slot, scb, ssl) <= kData) {
-    G.KC = K;
+  auto take = [&](int KC) {
+    G.KC = KC;
     G.slot = slot;
     G.sc_base = scb;
     G.sslot = ssl;
+  };
+  if (host_stage_bytes<F>(K, K, nseg, rows_per_seg, slot, scb, ssl) <= kData) {
+    take(K);
     return true;
   }
   for (int KC = (K / 256) * 256; KC >= 256; KC -= 256) {
     if (host_stage_bytes<F>(K, KC, nseg, rows_per_seg, slot, scb, ssl) <= kData) {
-      G.KC = KC;
-      G.slot = slot;
-      G.sc_base = scb;
-      G.sslot = ssl;
+      take(KC);
       return true;
     }
   }
@@ -595,334 +595,5 @@ int launch_router(const void* x, const void* W, const float* b, int H, int E, in
 // ============================================================================
 namespace tsb {
 
-struct FusedParams {
-  StageGeom gu_geom, dn_geom;
-  int* err;
-  unsigned* gridbar;  // [count, generation], zero-initialised, self-resetting
-  float* logits;      // [E] scratch for the sliced router
-  const TsbExpert* experts;
-  const uint16_t* x;  // bf16 [H]
-  const uint16_t* router_w;
-  const float* router_b;
-  int32_t* ids_out;
-  float* wts_out;
-  float* act;         // [top_k, I]
-  uint16_t* out;      // bf16 [H]
-  int H, I, E, top_k, layout, act_kind, rpe, tpe, x_vec_ok;
-  float limit, alpha;
-  int64_t gu_bytes, up_bytes, dn_bytes;
-};
-
-struct FusedSmem {
-  static constexpr int off_bars = 0;     // full[4], empty[4], ready
-  static constexpr int off_cnt = 128;
-  static constexpr int off_ids = 160;    // int[8]
-  static constexpr int off_wts = 192;    // float[8]
-  static constexpr int off_red = 256;    // 4 KB
-  static constexpr int off_cgu = off_red + kNStage * kNCW * 16 * 4;
-  static constexpr int off_cdn = off_cgu + kMaxSlots * (int)sizeof(SlotCache);
-  static constexpr int off_logit = off_cdn + kMaxSlots * (int)sizeof(SlotCache);  // float[1024]
-  static constexpr int off_ptab = off_logit + 4096;
-  static constexpr int off_coef = ((off_ptab + kPtabBytes + 15) / 16) * 16;
-  static constexpr int off_stage = ((off_coef + kNCW * 2048 + 127) / 128) * 128;
-  static constexpr int off_x = off_stage + kNStage * kStageBytes;
-  static int total(int H, int I, int k) { return off_x + (H / 32) * 80 + (I / 32) * k * 80; }
-};
-
-// Bounded grid-wide barrier for one thread per CTA (generation counting).
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void grid_barrier(unsigned* bar, int* err) {
-  __threadfence();
-  const unsigned gen = ld_acquire(bar + 1);
-  if (atomicAdd(&bar[0], 1u) == gridDim.x - 1) {
-    bar[0] = 0u;
-    __threadfence();
-    atomicAdd(&bar[1], 1u);
-    return;
-  }
-  for (uint32_t i = 0; i < (1u << 28); ++i) {
-    if (ld_acquire(bar + 1) != gen) return;
-  }
-  atomicExch(err, kDevWaitTimeout);
-}
-
-template <int FGU>
-__device__ __forceinline__ PlanGateUp<FGU> fused_gu_plan(const FusedParams& p, const int32_t* sid) {
-  PlanGateUp<FGU> q{};
-  q.geom = p.gu_geom;
-  q.err = p.err;
-  q.experts = p.experts;
-  q.ids = sid;
-  q.n_experts = p.E;
-  q.top_k = p.top_k;
-  q.I = p.I;
-  q.layout = p.layout;
-  q.act = p.act_kind;
-  q.limit = p.limit;
-  q.alpha = p.alpha;
-  q.x = p.x;
-  q.x_vec_ok = p.x_vec_ok;
-  q.act_out = p.act;
-  q.gu_bytes = p.gu_bytes;
-  q.up_bytes = p.up_bytes;
-  q.tpe = p.tpe;
-  return q;
-}
-
-template <int FDN>
-__device__ __forceinline__ PlanDownT1<FDN> fused_dn_plan(const FusedParams& p, const int32_t* sid, const float* swt) {
-  PlanDownT1<FDN> q{};
-  q.geom = p.dn_geom;
-  q.err = p.err;
-  q.experts = p.experts;
-  q.ids = sid;
-  q.wts = swt;
-  q.n_experts = p.E;
-  q.top_k = p.top_k;
-  q.rpe = p.rpe;
-  q.H = p.H;
-  q.I = p.I;
-  q.act = p.act;
-  q.act_cg = 1;
-  q.out = p.out;
-  q.dn_bytes = p.dn_bytes;
-  return q;
-}
-
-template <int FGU, int FDN>
-__global__ void __launch_bounds__(32 * (kNCW + 1), 1) moe_decode_fused(const FusedParams p) {
-  constexpr int NG = 2;
-  constexpr int WPG = kNCW / NG;
-  extern __shared__ __align__(128) uint8_t smem[];
-  using FS = FusedSmem;
-  EngSmem S;
-  S.full = reinterpret_cast<uint64_t*>(smem + FS::off_bars);
-  S.empty = S.full + kNStage;
-  uint64_t* ready = S.empty + kNStage;
-  S.cnt = reinterpret_cast<int*>(smem + FS::off_cnt);
-  S.red = reinterpret_cast<float*>(smem + FS::off_red);
-  S.stages = smem + FS::off_stage;
-  S.coef = smem + FS::off_coef;
-  S.ptab = smem + FS::off_ptab;
-  int32_t* sid = reinterpret_cast<int32_t*>(smem + FS::off_ids);
-  float* swt = reinterpret_cast<float*>(smem + FS::off_wts);
-  float* slog = reinterpret_cast<float*>(smem + FS::off_logit);
-  SlotCache* cgu = reinterpret_cast<SlotCache*>(smem + FS::off_cgu);
-  SlotCache* cdn = reinterpret_cast<SlotCache*>(smem + FS::off_cdn);
-  uint8_t* xgu = smem + FS::off_x;
-  float4* xsgu = reinterpret_cast<float4*>(xgu + (size_t)(p.H / 32) * 64);
-  uint8_t* xdn = xgu + (size_t)(p.H / 32) * 80;
-  float4* xsdn = reinterpret_cast<float4*>(xdn + (size_t)(p.I / 32) * p.top_k * 64);
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) {
-    for (int s = 0; s < kNStage; ++s) {
-      mbar_init(&S.full[s], 1);
-      mbar_init(&S.empty[s], WPG);
-      S.cnt[s] = 0;
-    }
-    mbar_init(ready, 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-
-  if (warp == 0) {
-    // ------------------------------ producer ------------------------------
-    if (!mbar_wait(ready, 0, p.err)) return;
-    const PlanGateUp<FGU> gu = fused_gu_plan<FGU>(p, sid);
-    const PlanDownT1<FDN> dn = fused_dn_plan<FDN>(p, sid, swt);
-    gu.fill_cache(cgu, lane);
-    dn.fill_cache(cdn, lane);
-    __syncwarp();
-    int it = 0;
-    if (!eng_produce<FGU, COLS_DUP, kNCW, kNStage, kStageBytes, NG>(gu, cgu, S, it, lane, p.err)) return;
-    eng_produce<FDN, COLS_DIAG, kNCW, kNStage, kStageBytes, NG>(dn, cdn, S, it, lane, p.err);
-    return;
-  }
-
-  // ------------------------------ consumers ------------------------------
-  const int ctid = tid - 32, cw = warp - 1;
-  constexpr int NCT = 32 * kNCW;
-  // x for gate/up (does not depend on routing)
-  stage_x<FGU>(xgu, xsgu, p.H, 1, XSrc{p.x, 0, TSB_DT_BF16, p.x_vec_ok, 0}, ctid, NCT);
-  // Router: expert e belongs to CTA e % grid; the CTA's consumer warps split
-  // its H range (all loads in flight at once), then a grid barrier publishes
-  // the logits and every CTA reads all of them.
-  {
-    const int n8 = p.H / 8;
-    const int per = (n8 + kNCW - 1) / kNCW;
-    const int i0 = cw * per, i1 = min(n8, i0 + per);
-    float* part = S.red;  // scratch: [kNCW] partial dots (free until the first row block)
-    for (int e = blockIdx.x; e < p.E; e += gridDim.x) {
-      const uint4* xr = reinterpret_cast<const uint4*>(p.x);
-      const uint4* wr = reinterpret_cast<const uint4*>(p.router_w + (int64_t)e * p.H);
-      float acc = 0.f;
-      for (int i = i0 + lane; i < i1; i += 32) {
-        const uint4 a = xr[i], w = __ldg(wr + i);
-        const uint32_t av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          acc = fmaf(__uint_as_float(av[q] << 16), __uint_as_float(wv[q] << 16), acc);
-          acc = fmaf(__uint_as_float(av[q] & 0xFFFF0000u), __uint_as_float(wv[q] & 0xFFFF0000u), acc);
-        }
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (lane == 0) part[cw] = acc;
-      named_bar_sync(1, NCT);
-      if (ctid == 0) {
-        float l = 0.f;
-        for (int w = 0; w < kNCW; ++w) l += part[w];
-        if (p.router_b) l += p.router_b[e];
-        p.logits[e] = bf16_bits_to_f32(f32_to_bf16_bits(l));
-      }
-      named_bar_sync(1, NCT);
-    }
-    if (ctid == 0) grid_barrier(p.gridbar, p.err);
-    named_bar_sync(1, NCT);
-    for (int e = ctid; e < p.E; e += NCT) slog[e] = __ldcg(p.logits + e);
-    named_bar_sync(1, NCT);
-  }
-  if (cw == 0) {
-    float sel[8];
-    int sidx[8];
-    uint32_t taken = 0;
-    for (int k = 0; k < p.top_k; ++k) {
-      float best = -INFINITY;
-      int bi = 0x7fffffff;
-      for (int j = 0; lane + 32 * j < p.E; ++j) {
-        if ((taken >> j) & 1u) continue;
-        const int ee = lane + 32 * j;
-        float v = slog[ee];
-        if (v != v) v = -INFINITY;
-        if (v > best || (v == best && ee < bi)) { best = v; bi = ee; }
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-      }
-      sel[k] = best;
-      sidx[k] = bi;
-      if (bi != 0x7fffffff && (bi & 31) == lane) taken |= 1u << (bi >> 5);
-    }
-    if (lane == 0) {
-      float den = 0.f, ex[8];
-      for (int k = 0; k < p.top_k; ++k) { ex[k] = __expf(sel[k] - sel[0]); den += ex[k]; }
-      for (int k = 0; k < p.top_k; ++k) {
-        sid[k] = sidx[k];
-        swt[k] = ex[k] / den;
-        if (blockIdx.x == 0) {
-          p.ids_out[k] = sidx[k];
-          p.wts_out[k] = ex[k] / den;
-        }
-      }
-      mbar_arrive(ready);  // releases sid / swt to the producer
-    }
-  }
-  named_bar_sync(1, NCT);  // sid / swt and the staged x visible to all consumers
-
-  const PlanGateUp<FGU> gu = fused_gu_plan<FGU>(p, sid);
-  // A timed-out wait only records the error: every consumer still reaches the
-  // barriers below, so no warp of the CTA is left waiting on another.
-  eng_consume<FGU, COLS_DUP, kNCW, kNStage, kStageBytes, NG>(gu, cgu, S, 0, reinterpret_cast<const uint4*>(xgu), xsgu,
-                                                             cw, lane, p.err);
-  named_bar_sync(1, NCT);
-  if (ctid == 0) grid_barrier(p.gridbar, p.err);
-  named_bar_sync(1, NCT);
-  const PlanDownT1<FDN> dn = fused_dn_plan<FDN>(p, sid, swt);
-  stage_x<FDN>(xdn, xsdn, p.I, p.top_k, dn.xsrc(), ctid, NCT);
-  named_bar_sync(1, NCT);
-  eng_consume<FDN, COLS_DIAG, kNCW, kNStage, kStageBytes, NG>(dn, cdn, S, eng_units(gu),
-                                                             reinterpret_cast<const uint4*>(xdn), xsdn, cw, lane, p.err);
-}
-
-template <int FGU, int FDN>
-static int fused_t(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, const void* rw, const float* rb,
-                   int32_t* ids, float* wts, void* out, float* act, float* logits, unsigned* gridbar, int32_t* err,
-                   cudaStream_t st) {
-  FusedParams p{};
-  const bool inter = sp.gate_up_layout == TSB_GU_INTERLEAVED;
-  int kp = 1;
-  while (kp < sp.top_k) kp <<= 1;
-  p.rpe = 16 / kp;
-  if (!choose_geom<FGU>(sp.hidden, inter ? 1 : 2, inter ? 16 : 8, p.gu_geom) || p.gu_geom.KC < p.gu_geom.K ||
-      !choose_geom<FDN>(sp.inter, sp.top_k, p.rpe, p.dn_geom) || p.dn_geom.KC < p.dn_geom.K)
-    return -1;  // rows do not fit one stage: caller uses the three-kernel path
-  const int smem = FusedSmem::total(sp.hidden, sp.inter, sp.top_k);
-  if (smem > 227 * 1024) return -1;
-  p.err = err;
-  p.gridbar = gridbar;
-  p.logits = logits;
-  p.experts = ex;
-  p.x = static_cast<const uint16_t*>(x);
-  p.router_w = static_cast<const uint16_t*>(rw);
-  p.router_b = rb;
-  p.ids_out = ids;
-  p.wts_out = wts;
-  p.act = act;
-  p.out = static_cast<uint16_t*>(out);
-  p.H = sp.hidden;
-  p.I = sp.inter;
-  p.E = sp.n_experts;
-  p.top_k = sp.top_k;
-  p.layout = sp.gate_up_layout;
-  p.act_kind = sp.activation;
-  p.limit = sp.limit;
-  p.alpha = sp.alpha;
-  p.tpe = (sp.inter + 7) / 8;
-  p.x_vec_ok = reinterpret_cast<uintptr_t>(x) % 8 == 0;
-  int64_t db, sb;
-  weight_bytes_of(FGU, (inter || sp.gate_up_layout == TSB_GU_CHUNKED ? 2 : 1) * (int64_t)sp.inter, sp.hidden, db, sb);
-  p.gu_bytes = db;
-  weight_bytes_of(FGU, sp.inter, sp.hidden, db, sb);
-  p.up_bytes = db;
-  weight_bytes_of(FDN, sp.hidden, sp.inter, db, sb);
-  p.dn_bytes = db;
-  auto kern = moe_decode_fused<FGU, FDN>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * (kNCW + 1), smem);
-  if (e != cudaSuccess || per_sm < 1) return -1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(num_sms());
-  cfg.blockDim = dim3(32 * (kNCW + 1));
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, p);
-  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
-  return TSB_OK;
-}
-
-// Returns TSB_OK, an error code, or -1 when the fused kernel does not apply.
-int launch_moe_fused(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, const void* rw, const float* rb,
-                     int32_t* ids, float* wts, void* out, float* act, float* logits, unsigned* gridbar, int32_t* err,
-                     cudaStream_t st) {
-#define TSB_FUSED(A, B)                                                                  \
-  if (sp.fmt_gate_up == A && sp.fmt_down == B)                                          \
-    return fused_t<A, B>(sp, ex, x, rw, rb, ids, wts, out, act, logits, gridbar, err, st);
-  TSB_FUSED(FMT_Q4_K, FMT_Q4_K)
-  TSB_FUSED(FMT_Q5_K, FMT_Q5_K)
-  TSB_FUSED(FMT_Q6_K, FMT_Q6_K)
-  TSB_FUSED(FMT_Q8_0, FMT_Q8_0)
-  TSB_FUSED(FMT_MXFP4, FMT_MXFP4)
-  TSB_FUSED(FMT_Q4_K, FMT_Q6_K)
-  TSB_FUSED(FMT_Q5_K, FMT_Q6_K)
-  TSB_FUSED(FMT_Q4_K, FMT_Q5_K)
-#undef TSB_FUSED
-  return -1;
-}
 
 }  // namespace tsb

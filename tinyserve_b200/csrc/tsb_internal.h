@@ -23,10 +23,6 @@ int launch_down(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* ids, c
                 void* out, int32_t* err, cudaStream_t st, bool pdl);
 int launch_router(const void* x, const void* W, const float* b, int H, int E, int T, int top_k, float* logits,
                   int32_t* ids, float* wts, unsigned* counter, cudaStream_t st);
-// Fused one-kernel batch-1 MoE layer; returns -1 when it does not apply.
-int launch_moe_fused(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, const void* rw, const float* rb,
-                     int32_t* ids, float* wts, void* out, float* act, float* logits, unsigned* gridbar, int32_t* err,
-                     cudaStream_t st);
 // Workspace layout of tsb_moe_prefill (byte offsets) and its tile geometry.
 struct PrefillLayout {
   size_t err, total_mb, counts, ccount, mb_expert, row_of, row_src, row_shift, xp, act, y, wgu, wdn, total;
