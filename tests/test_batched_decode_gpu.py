@@ -98,3 +98,23 @@ def test_decode_inplace_matches_decode(dev):
         layer.decode_(x, out, ids, w)
         torch.cuda.synchronize()
         assert torch.equal(ids, ref_ids) and torch.equal(w, ref_w) and torch.equal(out, ref)
+
+
+def test_decode_session_graph_replays_match_decode(dev):
+    """DecodeSession (one CUDA graph per token: host -> device -> layer ->
+    host) returns what decode returns for each of a stream of tokens."""
+    from tinyserve_b200.moe import DecodeSession
+    H, I, E, k = 512, 256, 8, 2
+    layer, _, _ = _build_layer(dev, GGML_Q4_K, GGML_Q4_K, H, I, E, k, "separate", seed=17)
+    sess = DecodeSession(layer, slots=3)
+    xs = torch.randn(7, H, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    got = []
+    pend = []
+    for i in range(7):
+        pend.append(sess.submit(xs[i]))
+        if len(pend) == 3:
+            got.append(sess.result(pend.pop(0)).clone())
+    got += [sess.result(s).clone() for s in pend]
+    for i in range(7):
+        ref, _, _ = layer.decode(xs[i:i + 1].to(dev))
+        assert torch.equal(got[i], ref.cpu()), i

@@ -211,3 +211,67 @@ class Router:
                                             _p(self.router_b), ids.data_ptr(), w.data_ptr(),
                                             torch.cuda.current_stream(x.device).cuda_stream))
         return ids, w
+
+
+class DecodeSession:
+    """Batch-1 decode of one layer per token as one CUDA-graph replay.
+
+    For a serving loop that feeds one token at a time from the host: each
+    slot's graph copies the token from a pinned host buffer to the device, runs
+    the layer (router, gate/up, down: three PDL-chained launches) and copies
+    the result back to a pinned host buffer, so a token costs one host row copy
+    and one graph launch instead of five separately issued operations.
+    `slots` buffers rotate so the host can fill the next token while earlier
+    ones run; a slot is reused only after its previous token finished.  Tokens
+    run in submission order on the session's stream (pass one stream to
+    several sessions to keep their tokens strictly sequential).
+
+        sess = DecodeSession(layer)
+        s = sess.submit(x_row)       # x_row: bf16 [1, H] or [H] on the host
+        y = sess.result(s)           # pinned bf16 [1, H] (valid until slot s is reused)
+    """
+
+    def __init__(self, layer: QuantMoE, slots: int = 4, stream: torch.cuda.Stream | None = None):
+        if layer.router_w is None:
+            raise ValueError("DecodeSession needs a layer with router weights")
+        dev = layer.device
+        H, k = layer.hidden, layer.top_k
+        self.layer, self.slots = layer, slots
+        self.hin = torch.zeros(slots, 1, H, dtype=torch.bfloat16).pin_memory()
+        self.hout = torch.zeros(slots, 1, H, dtype=torch.bfloat16).pin_memory()
+        self.din = torch.zeros(1, H, dtype=torch.bfloat16, device=dev)
+        self.dout = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
+        self.ids = torch.empty(1, k, dtype=torch.int32, device=dev)
+        self.wts = torch.empty(1, k, dtype=torch.float32, device=dev)
+        self.stream = stream if stream is not None else torch.cuda.Stream(dev)
+        raw = self.stream.cuda_stream
+        with torch.cuda.stream(self.stream):
+            layer.decode_(self.din, self.dout, self.ids, self.wts, raw)  # workspace and arguments before capture
+        torch.cuda.synchronize(dev)
+        self.graphs = []
+        for s in range(slots):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                self.din.copy_(self.hin[s], non_blocking=True)
+                layer.decode_(self.din, self.dout, self.ids, self.wts, raw)
+                self.hout[s].copy_(self.dout, non_blocking=True)
+            self.graphs.append(g)
+        self.done = [torch.cuda.Event() for _ in range(slots)]
+        self.used = [False] * slots
+        self.n = 0
+
+    def submit(self, x_row: torch.Tensor) -> int:
+        s = self.n % self.slots
+        self.n += 1
+        if self.used[s]:
+            self.done[s].synchronize()
+        self.hin[s].copy_(x_row.reshape(1, -1))
+        with torch.cuda.stream(self.stream):
+            self.graphs[s].replay()
+            self.done[s].record(self.stream)
+        self.used[s] = True
+        return s
+
+    def result(self, s: int) -> torch.Tensor:
+        self.done[s].synchronize()
+        return self.hout[s]
