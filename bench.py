@@ -406,7 +406,7 @@ def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
                        "timing": "CUDA events, max over ranks"}}
 
 
-def cpu_sample(layers, xs, n_tokens: int, threads: int):
+def cpu_sample(layers, xs, n_tokens: int, threads: int, warmup: int = 3):
     """Reference CPU path (oracle port of CPUExpertForward) on a bounded sample."""
     import numpy as np
     import torch
@@ -426,7 +426,7 @@ def cpu_sample(layers, xs, n_tokens: int, threads: int):
     # decodes GGUF experts once and caches the result)
     with torch.no_grad():
         cpu.prefetch(sorted({int(e) for i in range(n_tokens) for e in cpu.route(sample[i:i + 1])[0][0]}))
-    s = time_tokens(cpu, sample)
+    s = time_tokens(cpu, sample, warmup=warmup)
     return 1.0 / s, len(cpu._cache)
 
 
@@ -445,9 +445,9 @@ def run_reference(args, ws, rank, local):
         return {"impl": "reference", "unavailable": "needs a CUDA device to build the seeded Q4_K layer"}
     xs = hidden_states(args.steps + args.warmup, device=dev)
     n = min(args.steps, 40)
-    tps, nexp = cpu_sample([L], xs, n, threads)
+    tps, nexp = cpu_sample([L], xs, n, threads, warmup=args.warmup)
     return {"impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": ws, "steps": n,
-            "warmup": 2, "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "warmup": args.warmup, "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "fp32 (weights decoded once by dequant_tensor)", "data": "synthetic",
             "config": {"workload": "BASELINE config 1: GPT-OSS-20B-shaped MoE layer, batch-1 decode, Q4_K experts"},
             "cpu_baseline": {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",

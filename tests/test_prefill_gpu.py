@@ -218,3 +218,17 @@ def test_prefill_mxfp4_tiled_decode_subprocess(dev):
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", __file__, "-k", "mxfp4 and not subprocess"],
                        env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+def test_prefill_cta_pair_subprocess(dev):
+    """TSB_PREFILL_PAIR=1 runs the tiled GEMMs on CTA pairs (tcgen05
+    cta_group::2, experts padded to 256 rows); with TSB_PREFILL_FUSED=0 every
+    format takes the tiled path, so all cases of this file cover the pair
+    kernel."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, TSB_PREFILL_FUSED="0", TSB_PREFILL_PAIR="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", __file__, "-k", "not subprocess"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

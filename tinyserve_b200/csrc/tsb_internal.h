@@ -28,7 +28,9 @@ struct PrefillLayout {
   size_t err, total_mb, counts, ccount, mb_expert, row_of, row_src, row_shift, xp, act, y, wgu, wdn, total;
   int64_t rows_max, wgu_estride, wdn_estride;
   int mb_max, kbh, kbi, nt_gu, nt_dn;
-  bool fused_gu, fused_dn;  // MXFP4 decoded inside the GEMM (no fp16 weight tiles)
+  bool fused_gu, fused_dn;
+  bool pair;                // tiled GEMMs on CTA pairs (experts padded to 256 rows)
+  int pad;                  // expert row padding: 128, or 256 for CTA pairs  // MXFP4 decoded inside the GEMM (no fp16 weight tiles)
 };
 PrefillLayout prefill_layout(const TsbMoeSpec& sp, int T);
 int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, int T, const void* rw,
