@@ -181,6 +181,30 @@ int tsb_moe_decode_noalloc(const TsbMoeSpec* spec, const TsbExpert* experts, con
                            const void* router_w, const float* router_b, int32_t* ids, float* weights, void* out,
                            void* stream);
 
+/* ---- decode-packed experts (batch-1 decode of Q4_K layers) ----------------
+ * A one-time repack of all E experts' Q4_K gate/up/down streams into the
+ * order the decode kernels' tensor-core fragments read, with each 32-element
+ * sub-block's scale products d*sc and dmin*m precomputed in fp32 (768 bytes
+ * per 16 rows x 64 columns: 1.33x the Q4_K bytes).  Replaces, for HBM-resident
+ * layers, the per-call GGUF decode of ggml_mul_mat_vec
+ * (tinyserve/ggml_forward.py:40-62) inside ExpertPipeline.execute_layer_experts
+ * (tinyserve/expert_pipeline.py:140-164); results equal tsb_moe_decode's within
+ * the fp32 summation order.
+ * tsb_moe_packed_bytes: size of the packed copy, 0 when the spec has no packed
+ *   form (needs Q4_K gate/up and down, H and I multiples of 64, top_k <= 8).
+ * tsb_moe_pack: writes it (experts: device array of E TsbExpert, as for
+ *   tsb_moe_decode); stream-ordered, run once per weight set.
+ * tsb_moe_decode_packed: tsb_moe_decode's contract (T tokens, optional router,
+ *   ids/weights in or out) on the packed copy; `experts` supplies the biases
+ *   (and the raw streams for T > 16, which take the grouped path).  Workspace
+ *   from tsb_moe_decode_packed_workspace, zero-initialised once. */
+size_t tsb_moe_packed_bytes(const TsbMoeSpec* spec);
+int tsb_moe_pack(const TsbMoeSpec* spec, const TsbExpert* experts, void* packed, size_t packed_bytes, void* stream);
+size_t tsb_moe_decode_packed_workspace(const TsbMoeSpec* spec, int32_t T);
+int tsb_moe_decode_packed(const TsbMoeSpec* spec, const void* packed, const TsbExpert* experts, const void* x,
+                          int32_t T, const void* router_w, const float* router_b, int32_t* ids, float* weights,
+                          void* out, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -77,3 +77,22 @@ def test_moe_decode_argument_checks():
     assert rc == _lib.TSB_ERR_INVALID and "top_k" in _lib.last_error()
     rc = L.tsb_moe_decode(ctypes.byref(spec), 16, 16, 1, None, None, 16, 16, 16, 256, 16, None)
     assert rc == _lib.TSB_ERR_WORKSPACE
+
+
+def test_packed_bytes_query():
+    """tsb_moe_packed_bytes is host arithmetic: 768 bytes per (16 rows, 64
+    columns) unit for gate/up (8 outputs x 2 rows per block) and down, padded
+    to 256 bytes per expert; 0 for specs without a packed form."""
+    import ctypes
+    L = _lib.lib()
+    H = I = 2880
+    spec = _lib.TsbMoeSpec(12, 12, H, I, 32, 4, _lib.GU_SEPARATE, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
+    per = (I // 8) * (H // 64) * 768 + (H // 16) * (I // 64) * 768
+    per = (per + 255) // 256 * 256
+    assert L.tsb_moe_packed_bytes(ctypes.byref(spec)) == 32 * per
+    q4k = 3 * I * H // 256 * 144
+    assert abs(per / q4k - 4 / 3) < 0.01
+    mx = _lib.TsbMoeSpec(39, 39, H, I, 32, 4, _lib.GU_INTERLEAVED, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
+    assert L.tsb_moe_packed_bytes(ctypes.byref(mx)) == 0
+    odd = _lib.TsbMoeSpec(12, 12, 2880, 2880 + 32, 32, 4, _lib.GU_SEPARATE, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
+    assert L.tsb_moe_packed_bytes(ctypes.byref(odd)) == 0

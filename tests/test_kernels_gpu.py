@@ -141,7 +141,7 @@ def test_ggml_op_errors(dev):
 
 
 # ------------------------------------------------------------------ fused MoE decode layer
-def _build_layer(dev, fmt_gu, fmt_dn, H, I, E, k, layout, seed, bias=False):
+def _build_layer(dev, fmt_gu, fmt_dn, H, I, E, k, layout, seed, bias=False, pack=None, activation="swiglu_oai"):
     from tinyserve_b200.moe import ExpertWeights, QuantMoE
     experts, dense = [], []
     for e in range(E):
@@ -168,7 +168,7 @@ def _build_layer(dev, fmt_gu, fmt_dn, H, I, E, k, layout, seed, bias=False):
     gen = torch.Generator().manual_seed(seed)
     router = (torch.randn(E, H, generator=gen) * 0.02).to(torch.bfloat16)
     layer = QuantMoE(experts, fmt_gate_up=fmt_gu, fmt_down=fmt_dn, hidden=H, inter=I, top_k=k,
-                     router_w=router.to(dev), gate_up_layout=layout, activation="swiglu_oai")
+                     router_w=router.to(dev), gate_up_layout=layout, activation=activation, pack=pack)
     return layer, dense, router
 
 

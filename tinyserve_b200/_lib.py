@@ -29,6 +29,7 @@ EXPORTS = (
     "tsb_version", "tsb_last_error", "tsb_format_info", "tsb_weight_bytes", "tsb_dequant",
     "tsb_quant_matvec", "tsb_moe_decode_workspace", "tsb_moe_decode", "tsb_read_device_error",
     "tsb_moe_decode_noalloc", "tsb_moe_prefill_workspace", "tsb_moe_prefill",
+    "tsb_moe_packed_bytes", "tsb_moe_pack", "tsb_moe_decode_packed_workspace", "tsb_moe_decode_packed",
     "tsb_moe_route",
 )
 
@@ -74,6 +75,13 @@ def _declare(L: ctypes.CDLL) -> None:
     L.tsb_moe_prefill.argtypes = [ctypes.POINTER(TsbMoeSpec), _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
     L.tsb_moe_route.argtypes = [ctypes.POINTER(TsbMoeSpec), _vp, _i32, _vp, _vp, _vp, _vp, _vp]
     L.tsb_moe_decode_noalloc.argtypes = [ctypes.POINTER(TsbMoeSpec), _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp]
+    L.tsb_moe_packed_bytes.argtypes = [ctypes.POINTER(TsbMoeSpec)]
+    L.tsb_moe_packed_bytes.restype = _sz
+    L.tsb_moe_pack.argtypes = [ctypes.POINTER(TsbMoeSpec), _vp, _vp, _sz, _vp]
+    L.tsb_moe_decode_packed_workspace.argtypes = [ctypes.POINTER(TsbMoeSpec), _i32]
+    L.tsb_moe_decode_packed_workspace.restype = _sz
+    L.tsb_moe_decode_packed.argtypes = [ctypes.POINTER(TsbMoeSpec), _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
+                                        _vp, _sz, _vp]
 
 
 def lib() -> ctypes.CDLL:

@@ -147,6 +147,20 @@ int tsb_quant_matvec(int fmt, const void* w, const void* scales, int64_t N, int6
   return TSB_OK;
 }
 
+// Validation shared by the batch-1 decode entry points.
+static int check_decode_spec(const TsbMoeSpec& sp, const void* router_w) {
+  if (sp.top_k < 1 || sp.top_k > 8 || sp.top_k > sp.n_experts) return set_error(TSB_ERR_INVALID, "top_k must be in [1, min(8, E)]");
+  if (sp.n_experts < 1 || sp.n_experts > 1024) return set_error(TSB_ERR_INVALID, "n_experts must be in [1, 1024]");
+  if (sp.hidden % 32 || sp.inter % 32 || sp.hidden <= 0 || sp.inter <= 0)
+    return set_error(TSB_ERR_INVALID, "hidden and inter must be positive multiples of 32");
+  if (router_w && sp.hidden % 8) return set_error(TSB_ERR_INVALID, "hidden must be a multiple of 8 for the router");
+  if (sp.gate_up_layout < 0 || sp.gate_up_layout > 2) return set_error(TSB_ERR_INVALID, "bad gate_up_layout");
+  if (sp.activation < 0 || sp.activation > 1) return set_error(TSB_ERR_INVALID, "bad activation");
+  const int rc = check_shape(sp.fmt_gate_up, sp.inter, sp.hidden);
+  if (rc) return rc;
+  return check_shape(sp.fmt_down, sp.hidden, sp.inter);
+}
+
 // Up to this many tokens, tsb_moe_decode runs the batch-1 kernels once per
 // token: each token costs one HBM pass over its 4 experts (~45-55 us on the
 // GPT-OSS-20B shape), which beats the grouped GEMM path until the batch
@@ -180,16 +194,7 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
     }
     return TSB_OK;
   }
-  if (sp.top_k < 1 || sp.top_k > 8 || sp.top_k > sp.n_experts) return set_error(TSB_ERR_INVALID, "top_k must be in [1, min(8, E)]");
-  if (sp.n_experts < 1 || sp.n_experts > 1024) return set_error(TSB_ERR_INVALID, "n_experts must be in [1, 1024]");
-  if (sp.hidden % 32 || sp.inter % 32 || sp.hidden <= 0 || sp.inter <= 0)
-    return set_error(TSB_ERR_INVALID, "hidden and inter must be positive multiples of 32");
-  if (router_w && sp.hidden % 8) return set_error(TSB_ERR_INVALID, "hidden must be a multiple of 8 for the router");
-  if (sp.gate_up_layout < 0 || sp.gate_up_layout > 2) return set_error(TSB_ERR_INVALID, "bad gate_up_layout");
-  if (sp.activation < 0 || sp.activation > 1) return set_error(TSB_ERR_INVALID, "bad activation");
-  int rc = check_shape(sp.fmt_gate_up, sp.inter, sp.hidden);
-  if (rc) return rc;
-  rc = check_shape(sp.fmt_down, sp.hidden, sp.inter);
+  int rc = check_decode_spec(sp, router_w);
   if (rc) return rc;
   const WsLayout L = ws_layout(sp, T);
   if (workspace_bytes < L.total) return set_error(TSB_ERR_WORKSPACE, "workspace too small");
@@ -208,6 +213,68 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
   rc = launch_gate_up(sp, experts, ids, x, act, err, st, routed);
   if (rc) return rc;
   return launch_down(sp, experts, ids, weights, act, out, err, st, true);
+}
+
+size_t tsb_moe_packed_bytes(const TsbMoeSpec* spec) {
+  if (!spec || !packable(*spec)) return 0;
+  return (size_t)pack_geom(*spec).expert_bytes * (size_t)spec->n_experts;
+}
+
+int tsb_moe_pack(const TsbMoeSpec* spec, const TsbExpert* experts, void* packed, size_t packed_bytes, void* stream) {
+  if (!spec || !experts || !packed) return set_error(TSB_ERR_INVALID, "null pointer");
+  const TsbMoeSpec& sp = *spec;
+  if (!packable(sp)) return set_error(TSB_ERR_UNSUPPORTED, "no packed form: needs Q4_K gate/up and down, H and I multiples of 64");
+  int rc = check_decode_spec(sp, nullptr);
+  if (rc) return rc;
+  if (packed_bytes < tsb_moe_packed_bytes(spec)) return set_error(TSB_ERR_WORKSPACE, "packed buffer too small");
+  if (reinterpret_cast<uintptr_t>(packed) & 255) return set_error(TSB_ERR_INVALID, "packed buffer must be 256-byte aligned");
+  return launch_pack(sp, experts, packed, static_cast<cudaStream_t>(stream));
+}
+
+size_t tsb_moe_decode_packed_workspace(const TsbMoeSpec* spec, int32_t T) {
+  if (!spec || T <= 0) return 0;
+  if (T > kDecodeLoopMax) return prefill_layout(*spec, T).total;
+  return ws_layout(*spec, 1).total + ((packed_ws_bytes(*spec) + 255) & ~size_t(255));
+}
+
+int tsb_moe_decode_packed(const TsbMoeSpec* spec, const void* packed, const TsbExpert* experts, const void* x,
+                          int32_t T, const void* router_w, const float* router_b, int32_t* ids, float* weights,
+                          void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!spec || !packed || !experts || !x || !ids || !weights || !out || !workspace)
+    return set_error(TSB_ERR_INVALID, "null pointer");
+  const TsbMoeSpec& sp = *spec;
+  if (T < 1) return set_error(TSB_ERR_INVALID, "T must be >= 1");
+  if (!packable(sp)) return set_error(TSB_ERR_UNSUPPORTED, "no packed form for this spec");
+  if (T > kDecodeLoopMax)
+    return tsb_moe_prefill(spec, experts, x, T, router_w, router_b, ids, weights, out, workspace, workspace_bytes, stream);
+  if (T > 1) {
+    const int64_t H = sp.hidden, k = sp.top_k;
+    for (int t = 0; t < T; ++t) {
+      const int rc = tsb_moe_decode_packed(spec, packed, experts, static_cast<const uint16_t*>(x) + t * H, 1, router_w,
+                                           router_b, ids + t * k, weights + t * k, static_cast<uint16_t*>(out) + t * H,
+                                           workspace, workspace_bytes, stream);
+      if (rc) return rc;
+    }
+    return TSB_OK;
+  }
+  int rc = check_decode_spec(sp, router_w);
+  if (rc) return rc;
+  const WsLayout L = ws_layout(sp, 1);
+  if (workspace_bytes < tsb_moe_decode_packed_workspace(spec, 1)) return set_error(TSB_ERR_WORKSPACE, "workspace too small");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(TSB_ERR_INVALID, "workspace must be 256-byte aligned");
+  if (reinterpret_cast<uintptr_t>(packed) & 255) return set_error(TSB_ERR_INVALID, "packed buffer must be 256-byte aligned");
+  char* ws = static_cast<char*>(workspace);
+  int32_t* err = reinterpret_cast<int32_t*>(ws + L.err);
+  float* act = reinterpret_cast<float*>(ws + L.act);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool routed = router_w != nullptr;
+  if (routed) {
+    rc = launch_router(x, router_w, router_b, sp.hidden, sp.n_experts, 1, sp.top_k,
+                       reinterpret_cast<float*>(ws + L.logits), ids, weights,
+                       reinterpret_cast<unsigned*>(ws + L.counter), st);
+    if (rc) return rc;
+  }
+  return launch_packed_decode(sp, packed, experts, x, ids, weights, act, out, err, ws + L.total, st, routed);
 }
 
 int tsb_read_device_error(void* workspace, int32_t* code, void* stream) {

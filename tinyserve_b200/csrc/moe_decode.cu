@@ -140,10 +140,14 @@ struct PlanGateUp {
     if (s == 0) return Seg{C.w[0], C.s[0], (int64_t)j0, nr, gu_bytes};
     return Seg{C.w[1], C.s[1], (int64_t)j0, nr, up_bytes};
   }
+  // Fragment rows g and g+8 must be source rows 8 apart (they share one
+  // superblock-phase counter when K % 256 != 0), so interleaved rows keep
+  // their order: A row m = gate_up row 2*j0 + m, and the epilogue pairs rows
+  // 2i (gate) and 2i+1 (up).
   __device__ void rowmap(int, int m, int& sg, int& lr) const {
     if (layout == TSB_GU_INTERLEAVED) {
       sg = 0;
-      lr = m < 8 ? 2 * m : 2 * (m - 8) + 1;
+      lr = m;
     } else {
       sg = m >> 3;
       lr = m & 7;
@@ -157,10 +161,12 @@ struct PlanGateUp {
     if (lane >= 8) return;
     const int u = rb / tpe, j = 8 * (rb % tpe) + lane;
     if (j >= I) return;
+    const int rg = layout == TSB_GU_INTERLEAVED ? 2 * lane : lane;
+    const int ru = layout == TSB_GU_INTERLEAVED ? 2 * lane + 1 : lane + 8;
     float gate = 0.f, up = 0.f;
     for (int i = 0; i < nw; ++i) {
-      gate += rd[i * 16 + lane];
-      up += rd[i * 16 + lane + 8];
+      gate += rd[i * 16 + rg];
+      up += rd[i * 16 + ru];
     }
     const SlotCache& C = c[u];
     if (C.e < 0) { act_out[(int64_t)u * I + j] = 0.f; return; }

@@ -1,0 +1,611 @@
+// Batch-1 MoE decode on a decode-packed copy of 4-bit K-quant experts.
+//
+// The generic decode engine reads the GGUF block stream as stored
+// (tinyserve/gguf_dequant_torch.py:180-205): with K % 256 != 0 rows start at
+// different superblock phases and every 32-element step rebuilds its scale
+// from the 12-byte packed scales, which costs ~120 instructions per 512
+// weights.  Here the experts are repacked once (tsb_moe_pack) into the order
+// the tensor-core fragments consume, with each (row, 32-element sub-block)'s
+// fold coefficients already formed, so the inner loop is a shared-memory
+// read, a handful of bit operations, four MMAs and eight FMAs per 1024 weights.
+//
+// Packed unit: one 16-row block x one 64-element k-block = 768 bytes
+//   [0, 512)    codes: lane L (g = L/4, t = L%4) owns 16 bytes = 32 codes in
+//               mma.m16n8k16 A-fragment order (see pack_unit_kernel)
+//   [512, 768)  fold coefficients: for sub-block sb (0, 1) and row pair g,
+//               float4 (s_g, s_g+8, o_g, o_g+8) at 512 + 128 sb + 16 g
+// A row's contribution from a sub-block is s * sum(q*x) - dmin*m * sum(x);
+// the codes of sub-block 0 decode to 1024+q and those of sub-block 1 to 64+q
+// (one LOP3 per f16 pair: 0x6400|q and 0x5400|q<<4), so the MMA yields
+// C = sum(q*x) + off * X and the fold is s*C - (off*s + dmin*m)*X with
+// o = off*s + dmin*m stored.  s = d*sc and dmin*m are the products the
+// reference decoder forms (gguf_dequant_torch.py:195-203), in fp32.
+//
+// Gate/up row blocks hold 8 gate rows then the 8 up rows of the same outputs,
+// so the SwiGLU pair of output j sits in one lane's accumulators (rows g and
+// g+8 of the fragment).  Down row blocks are 16 consecutive rows.
+//
+// Work: warp tasks (slot, row block, k-range); each task writes its 16 fp32
+// partial sums, and the last task of a row block (atomic counter, reset after
+// use) reduces the partials in fixed order and runs the epilogue, so results
+// do not depend on scheduling.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "../../include/tsb_moe.h"
+#include "moe_math.cuh"
+#include "qformats.cuh"
+#include "tsb_common.cuh"
+#include "tsb_internal.h"
+
+namespace tsb {
+
+constexpr int kPkThreads = 512;
+constexpr int kPkWarps = kPkThreads / 32;
+constexpr int kUnitBytes = 768;
+constexpr int kMaxSplit = 16;
+
+bool packable(const TsbMoeSpec& sp) {
+  return sp.fmt_gate_up == FMT_Q4_K && sp.fmt_down == FMT_Q4_K && sp.hidden % 64 == 0 && sp.inter % 64 == 0 &&
+         sp.hidden > 0 && sp.inter > 0 && sp.n_experts >= 1 && sp.top_k >= 1 && sp.top_k <= 8;
+}
+
+PackGeom pack_geom(const TsbMoeSpec& sp) {
+  PackGeom G{};
+  G.rgu = (sp.inter + 7) / 8;
+  G.rdn = (sp.hidden + 15) / 16;
+  G.kbh = sp.hidden / 64;
+  G.kbi = sp.inter / 64;
+  G.gu_off = 0;
+  G.dn_off = (int64_t)G.rgu * G.kbh * kUnitBytes;
+  G.expert_bytes = (G.dn_off + (int64_t)G.rdn * G.kbi * kUnitBytes + 255) & ~int64_t(255);
+  return G;
+}
+
+// ------------------------------------------------------------------ packing
+// Q4_K element f of a flat stream: code, and the sub-block's (d*sc, dmin*m).
+__device__ __forceinline__ int q4k_code(const uint8_t* w, int64_t f) {
+  const uint8_t* b = w + (f >> 8) * 144;
+  const int i = (int)(f & 255), j = i >> 5, l = i & 31;
+  return (b[16 + 32 * (j >> 1) + l] >> (4 * (j & 1))) & 15;
+}
+__device__ __forceinline__ void q4k_coef(const uint8_t* w, int64_t f, float& s, float& o) {
+  const uint8_t* b = w + (f >> 8) * 144;
+  const int j = (int)((f & 255) >> 5);
+  const float d = half_bits_to_f32((uint16_t)(b[0] | (b[1] << 8)));
+  const float dmin = half_bits_to_f32((uint16_t)(b[2] | (b[3] << 8)));
+  int sc, m;
+  kq_scale_min(b + 4, j, sc, m);
+  s = __fmul_rn(d, (float)sc);
+  o = __fmul_rn(dmin, (float)m);
+}
+
+struct PackArgs {
+  const TsbExpert* experts;
+  uint8_t* packed;
+  PackGeom G;
+  int H, I, layout;
+  int64_t units_gu, units_per_expert;
+};
+
+// Source (stream, row) of packed row m of a row block; null when past the end.
+__device__ __forceinline__ const uint8_t* src_row(const PackArgs& a, const TsbExpert& E, bool down, int rb, int m,
+                                                  int64_t& row) {
+  if (down) {
+    row = 16 * rb + m;
+    return row < a.H ? static_cast<const uint8_t*>(E.down) : nullptr;
+  }
+  const int j = 8 * rb + (m & 7);
+  if (j >= a.I) return nullptr;
+  const bool up = m >= 8;
+  if (a.layout == TSB_GU_INTERLEAVED) {
+    row = 2 * (int64_t)j + (up ? 1 : 0);
+    return static_cast<const uint8_t*>(E.gate);
+  }
+  if (a.layout == TSB_GU_CHUNKED) {
+    row = (up ? a.I : 0) + (int64_t)j;
+    return static_cast<const uint8_t*>(E.gate);
+  }
+  row = j;
+  return static_cast<const uint8_t*>(up ? E.up : E.gate);
+}
+
+// One warp per packed unit.  Lane L's 32 codes: for family fam (0: sub-block
+// 0, decoded as 1024+q; 1: sub-block 1, decoded as 64+q), fragment register
+// m (0..7) and half h, the code of row g + 8*(r&1), column
+// 16*(2 fam + m/4) + 2t + 8*(r/2) + h (r = m%4) sits in word m/2 at bit
+// 8*(m%2) + 16h + 4 fam.
+__global__ void __launch_bounds__(256) pack_unit_kernel(const PackArgs a, int64_t nunits) {
+  const int64_t unit = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (unit >= nunits) return;
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int64_t e = unit / a.units_per_expert;
+  int64_t r = unit % a.units_per_expert;
+  const bool down = r >= a.units_gu;
+  if (down) r -= a.units_gu;
+  const int KB = down ? a.G.kbi : a.G.kbh;
+  const int rb = (int)(r / KB), kb = (int)(r % KB);
+  const int K = down ? a.I : a.H;
+  const TsbExpert E = a.experts[e];
+  uint8_t* dst = a.packed + e * a.G.expert_bytes + (down ? a.G.dn_off : a.G.gu_off) + r * kUnitBytes;
+
+  uint32_t word[4] = {0, 0, 0, 0};
+  int64_t row_lo = 0, row_hi = 0;
+  const uint8_t* w_lo = src_row(a, E, down, rb, g, row_lo);
+  const uint8_t* w_hi = src_row(a, E, down, rb, g + 8, row_hi);
+#pragma unroll
+  for (int fam = 0; fam < 2; ++fam)
+#pragma unroll
+    for (int m = 0; m < 8; ++m)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int rr = m & 3;
+        const int col = 16 * (2 * fam + (m >> 2)) + 2 * t + 8 * (rr >> 1) + h;
+        const uint8_t* w = (rr & 1) ? w_hi : w_lo;
+        const int64_t row = (rr & 1) ? row_hi : row_lo;
+        const int q = w ? q4k_code(w, row * K + 64 * (int64_t)kb + col) : 0;
+        word[m >> 1] |= (uint32_t)q << (8 * (m & 1) + 16 * h + 4 * fam);
+      }
+  *reinterpret_cast<uint4*>(dst + 16 * lane) = make_uint4(word[0], word[1], word[2], word[3]);
+
+  if (lane < 16) {
+    const int sb = lane >> 3, gg = lane & 7;
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int hi = 0; hi < 2; ++hi) {
+      int64_t row = 0;
+      const uint8_t* w = src_row(a, E, down, rb, gg + 8 * hi, row);
+      if (!w) continue;
+      float s, o;
+      q4k_coef(w, row * K + 64 * (int64_t)kb + 32 * sb, s, o);
+      c[hi] = s;
+      c[2 + hi] = fmaf(sb ? 64.f : 1024.f, s, o);
+    }
+    *reinterpret_cast<float4*>(dst + 512 + 128 * sb + 16 * gg) = make_float4(c[0], c[1], c[2], c[3]);
+  }
+}
+
+int launch_pack(const TsbMoeSpec& sp, const TsbExpert* experts, void* packed, cudaStream_t st) {
+  PackArgs a{};
+  a.experts = experts;
+  a.packed = static_cast<uint8_t*>(packed);
+  a.G = pack_geom(sp);
+  a.H = sp.hidden;
+  a.I = sp.inter;
+  a.layout = sp.gate_up_layout;
+  a.units_gu = (int64_t)a.G.rgu * a.G.kbh;
+  a.units_per_expert = a.units_gu + (int64_t)a.G.rdn * a.G.kbi;
+  const int64_t n = a.units_per_expert * sp.n_experts;
+  pack_unit_kernel<<<(unsigned)((n + 7) / 8), 256, 0, st>>>(a, n);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return TSB_OK;
+}
+
+// ------------------------------------------------------------------ decode
+struct PkArgs {
+  const uint8_t* packed;
+  int64_t expert_bytes, sec_off;
+  int R, KB, S, nkb, ntasks;
+  const int32_t* ids;
+  const float* wts;
+  const TsbExpert* experts;
+  int n_experts, top_k;
+  int* err;
+  const void* x;      // mode 0: bf16 [H]; mode 1: fp32 [top_k, I]
+  int nv;             // staged vectors: 1 (gate/up) or top_k (down)
+  float* part;        // [ntasks, 16]
+  unsigned* cnt;      // per output row block, zero between calls
+  int mode, I, H, act;
+  float limit, alpha;
+  float* act_out;     // mode 0: fp32 [top_k, I]
+  uint16_t* out;      // mode 1: bf16 [H]
+};
+
+// Each warp streams its units through a private ring of kSlots slots of
+// kSlotUnits units (one cp.async.bulk copy per slot, completing on the slot's
+// mbarrier): kSlots * kSlotUnits * 768 bytes in flight per warp.
+constexpr int kSlotUnits = 2, kSlots = 3;
+constexpr int kSlotBytes = kSlotUnits * kUnitBytes;
+
+__device__ __forceinline__ bool pk_warp_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const bool ok = mbar_wait(bar, parity, err);
+  return __all_sync(0xffffffffu, ok);
+}
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Shared memory per staged vector v: xf (KB x 128 B: for k-block kb and quad
+// lane t, the eight B-fragment registers of the four MMAs) and X (KB x 8 B:
+// the two sub-block sums); then 32 zero bytes (the B operand of lanes whose
+// fragment column is not the token's), the per-vector unscale factors and
+// the warps' rings.
+__host__ __device__ inline size_t pk_zero_off(int nv, int KB) { return ((size_t)nv * KB * 136 + 15) & ~size_t(15); }
+__host__ __device__ inline size_t pk_ring_off(int nv, int KB) { return pk_zero_off(nv, KB) + 128; }
+__host__ __device__ inline size_t pk_smem(int nv, int KB) {
+  return pk_ring_off(nv, KB) + (size_t)kPkWarps * kSlots * kSlotBytes;
+}
+
+template <int MODE>
+__device__ __forceinline__ float vec_elem(const PkArgs& a, int v, int k) {
+  return MODE == 0 ? bf16_bits_to_f32(static_cast<const uint16_t*>(a.x)[k])
+                   : __ldcg(static_cast<const float*>(a.x) + (int64_t)v * a.I + k);
+}
+
+// All staged vectors in two passes (max |x| per vector, then scale, round to
+// fp16, permute and sum per sub-block), two block barriers in total; each pass
+// issues kStageU independent loads per thread before using them.
+constexpr int kStageU = 8;
+
+template <int MODE>
+__device__ void stage_vectors(const PkArgs& a, uint8_t* sm, float* inv, int warp, int lane) {
+  __shared__ float red[8][kPkWarps];
+  __shared__ float s_scale[8];
+  const int K = 64 * a.KB, n = a.nv * K;
+  float mx[8];
+#pragma unroll
+  for (int v = 0; v < 8; ++v) mx[v] = 0.f;
+  for (int i0 = threadIdx.x; i0 < n; i0 += kStageU * kPkThreads) {
+    float xv[kStageU];
+#pragma unroll
+    for (int u = 0; u < kStageU; ++u) {
+      const int i = i0 + u * kPkThreads;
+      xv[u] = i < n ? vec_elem<MODE>(a, i / K, i % K) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kStageU; ++u) {
+      const int i = i0 + u * kPkThreads, v = i / K;
+#pragma unroll
+      for (int w = 0; w < 8; ++w)
+        if (w == v) mx[w] = fmaxf(mx[w], fabsf(xv[u]));
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < 8; ++v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx[v] = fmaxf(mx[v], __shfl_xor_sync(0xffffffffu, mx[v], o));
+    if (lane == 0) red[v][warp] = mx[v];
+  }
+  __syncthreads();
+  if (threadIdx.x < a.nv) {
+    const int v = threadIdx.x;
+    float m = red[v][0];
+    for (int i = 1; i < kPkWarps; ++i) m = fmaxf(m, red[v][i]);
+    // power-of-two scale putting max|x| in [2^14, 2^15) (exact in fp32)
+    const int ex = (int)((__float_as_uint(m) >> 23) & 255u);
+    int sx = (m > 0.f && ex != 255) ? 14 - (ex - 127) : 0;
+    sx = max(-126, min(126, sx));
+    s_scale[v] = __uint_as_float((uint32_t)(sx + 127) << 23);
+    inv[v] = __uint_as_float((uint32_t)(127 - sx) << 23);
+  }
+  __syncthreads();
+  float* X = reinterpret_cast<float*>(sm + (size_t)a.nv * a.KB * 128);
+  const int nsb = 2 * a.KB * a.nv;
+  for (int q0 = warp; q0 < nsb; q0 += kStageU * kPkWarps) {
+    float xv[kStageU];
+#pragma unroll
+    for (int u = 0; u < kStageU; ++u) {
+      const int q = q0 + u * kPkWarps;
+      const int v = q / (2 * a.KB), sb = q - v * 2 * a.KB;
+      xv[u] = q < nsb ? vec_elem<MODE>(a, v, 32 * sb + lane) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kStageU; ++u) {
+      const int q = q0 + u * kPkWarps;
+      if (q >= nsb) break;
+      const int v = q / (2 * a.KB), sb = q - v * 2 * a.KB;
+      const int k = 32 * sb + lane;
+      const __half hv = __float2half_rn(xv[u] * s_scale[v]);
+      float sum = __half2float(hv);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) X[(size_t)v * 2 * a.KB + sb] = sum;
+      const int kb = k >> 6, kk = k & 63, j = kk >> 4, w = kk & 15;
+      const int idx = ((((kb * 4 + ((w & 7) >> 1)) * 4 + j) * 2 + (w >> 3)) * 2) + (w & 1);
+      reinterpret_cast<uint16_t*>(sm + (size_t)v * a.KB * 128)[idx] = __half_as_ushort(hv);
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kPkThreads, 2) packed_matvec_kernel(const PkArgs a) {
+  extern __shared__ uint4 smem4[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(smem4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  uint8_t* zero = sm + pk_zero_off(a.nv, a.KB);
+  uint8_t* ring = sm + pk_ring_off(a.nv, a.KB) + (size_t)warp * kSlots * kSlotBytes;
+  float* inv = reinterpret_cast<float*>(zero + 32);
+  __shared__ int s_e[8];
+  __shared__ uint64_t s_bar[kPkWarps][kSlots];
+  uint64_t* bar = s_bar[warp];
+  if (threadIdx.x < 8) reinterpret_cast<uint32_t*>(zero)[threadIdx.x] = 0u;
+  if (lane < kSlots) mbar_init(&bar[lane], 1);
+  fence_barrier_init();
+
+  const int gw0 = blockIdx.x * kPkWarps + warp, nw = gridDim.x * kPkWarps;
+  auto task_ptr = [&](int task, int e, int& kb0, int& kb1) {
+    const int rem = task % (a.R * a.S), rb = rem / a.S, s = rem % a.S;
+    kb0 = s * a.nkb;
+    kb1 = min(a.KB, kb0 + a.nkb);
+    return a.packed + (int64_t)e * a.expert_bytes + a.sec_off + ((int64_t)rb * a.KB + kb0) * kUnitBytes;
+  };
+  auto expert_of = [&](int u) {
+    const int e = a.ids[u];
+    if ((unsigned)e >= (unsigned)a.n_experts) {
+      if (a.err) atomicExch(a.err, kDevBadPlan);
+      return -1;
+    }
+    return e;
+  };
+
+  if (MODE == 0) {
+    // x does not depend on the router: stage it while the router runs
+    stage_vectors<0>(a, sm, inv, warp, lane);
+    pdl_wait();
+  } else {
+    // Expert ids were written before the gate/up kernel passed its wait: pull
+    // this warp's weight ranges into L2 while gate/up finishes.
+    if (lane == 0)
+      for (int task = gw0; task < a.ntasks; task += nw) {
+        const int e = expert_of(task / (a.R * a.S));
+        if (e < 0) continue;
+        int kb0, kb1;
+        const uint8_t* p = task_ptr(task, e, kb0, kb1);
+        prefetch_l2(p, (uint32_t)(kb1 - kb0) * kUnitBytes);
+      }
+    pdl_wait();
+  }
+  if (threadIdx.x < a.top_k) s_e[threadIdx.x] = expert_of(threadIdx.x);
+  pdl_launch_dependents();
+  if (MODE == 1) stage_vectors<1>(a, sm, inv, warp, lane);
+  __syncthreads();
+
+  uint32_t issued = 0, consumed = 0;  // slot fills / drains of this warp's ring
+  bool bad = false;                   // a slot wait ran out: stop streaming
+  for (int task = gw0; task < a.ntasks; task += nw) {
+    const int u = task / (a.R * a.S), rb = (task % (a.R * a.S)) / a.S;
+    const int e = s_e[u];
+    float acc_lo = 0.f, acc_hi = 0.f;
+    if (e >= 0 && !bad) {
+      int kb0, kb1;
+      const uint8_t* p = task_ptr(task, e, kb0, kb1);
+      const int v = MODE == 0 ? 0 : u;
+      const uint8_t* xb = g == 0 ? sm + (size_t)v * a.KB * 128 + (size_t)kb0 * 128 + 32 * t : zero;
+      const int xstep = g == 0 ? 128 : 0;
+      const float2* X = reinterpret_cast<const float2*>(sm + (size_t)a.nv * a.KB * 128) + (size_t)v * a.KB + kb0;
+      const int n = kb1 - kb0, ngrp = (n + kSlotUnits - 1) / kSlotUnits;
+      auto issue = [&](int gi) {
+        uint64_t* b = &bar[issued % kSlots];
+        uint8_t* dst = ring + (issued % kSlots) * kSlotBytes;
+        ++issued;
+        if (lane == 0) {
+          const uint32_t bytes = (uint32_t)min(kSlotUnits, n - gi * kSlotUnits) * kUnitBytes;
+          mbar_arrive_expect_tx(b, bytes);
+          bulk_g2s(dst, p + (size_t)gi * kSlotBytes, bytes, b);
+        }
+      };
+      for (int gi = 0; gi < kSlots && gi < ngrp; ++gi) issue(gi);
+      for (int gi = 0; gi < ngrp; ++gi) {
+        const int sl = consumed % kSlots;
+        if (!pk_warp_wait(&bar[sl], (consumed / kSlots) & 1u, a.err)) {
+          bad = true;
+          break;
+        }
+        ++consumed;
+        const uint8_t* slot = ring + sl * kSlotBytes;
+        const int nu = min(kSlotUnits, n - gi * kSlotUnits);
+        for (int ui = 0; ui < nu; ++ui, slot += kUnitBytes) {
+          const uint4 q = *reinterpret_cast<const uint4*>(slot + 16 * lane);
+          const float4 c0 = *reinterpret_cast<const float4*>(slot + 512 + 16 * g);
+          const float4 c1 = *reinterpret_cast<const float4*>(slot + 640 + 16 * g);
+          const uint4 b01 = *reinterpret_cast<const uint4*>(xb);
+          const uint4 b23 = *reinterpret_cast<const uint4*>(xb + 16);
+          const float2 xs = *X;
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+          uint32_t lo[8], hi[8];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const uint32_t v8 = w[r] >> 8;
+            lo[2 * r] = (w[r] & 0x000F000Fu) | 0x64006400u;
+            hi[2 * r] = (w[r] & 0x00F000F0u) | 0x54005400u;
+            lo[2 * r + 1] = (v8 & 0x000F000Fu) | 0x64006400u;
+            hi[2 * r + 1] = (v8 & 0x00F000F0u) | 0x54005400u;
+          }
+          float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_f16(d0, *reinterpret_cast<const uint32_t(*)[4]>(&lo[0]), b01.x, b01.y);
+          mma_f16(d0, *reinterpret_cast<const uint32_t(*)[4]>(&lo[4]), b01.z, b01.w);
+          mma_f16(d1, *reinterpret_cast<const uint32_t(*)[4]>(&hi[0]), b23.x, b23.y);
+          mma_f16(d1, *reinterpret_cast<const uint32_t(*)[4]>(&hi[4]), b23.z, b23.w);
+          acc_lo = fmaf(c0.x, d0[0], acc_lo);
+          acc_lo = fmaf(-c0.z, xs.x, acc_lo);
+          acc_hi = fmaf(c0.y, d0[2], acc_hi);
+          acc_hi = fmaf(-c0.w, xs.x, acc_hi);
+          acc_lo = fmaf(c1.x, d1[0], acc_lo);
+          acc_lo = fmaf(-c1.z, xs.y, acc_lo);
+          acc_hi = fmaf(c1.y, d1[2], acc_hi);
+          acc_hi = fmaf(-c1.w, xs.y, acc_hi);
+          xb += xstep;
+          ++X;
+        }
+        __syncwarp();  // every lane has read the slot before it is refilled
+        if (gi + kSlots < ngrp) issue(gi + kSlots);
+      }
+    }
+    // partial sums of rows g and g+8 live in the t == 0 lanes
+    float* P = a.part + (int64_t)task * 16;
+    if (t == 0) {
+      P[g] = acc_lo;
+      P[g + 8] = acc_hi;
+      __threadfence();
+    }
+    __syncwarp();
+    const int slot = MODE == 0 ? u * a.R + rb : rb;
+    const unsigned need = MODE == 0 ? (unsigned)a.S : (unsigned)(a.top_k * a.S);
+    unsigned last = 0;
+    if (lane == 0) last = atomicAdd(a.cnt + slot, 1u) == need - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) continue;
+    __threadfence();
+    if (MODE == 0) {
+      const int j = 8 * rb + lane;
+      if (lane < 8 && j < a.I) {
+        float gate = 0.f, up = 0.f;
+        const float* Q = a.part + (int64_t)(u * a.R + rb) * a.S * 16;
+        for (int s = 0; s < a.S; ++s) {
+          gate += __ldcg(Q + 16 * s + lane);
+          up += __ldcg(Q + 16 * s + lane + 8);
+        }
+        float r = 0.f;
+        if (e >= 0) {
+          gate *= inv[0];
+          up *= inv[0];
+          const TsbExpert& E = a.experts[e];
+          if (E.gate_bias) gate += E.gate_bias[j];
+          if (E.up_bias) up += E.up_bias[j];
+          r = act_fn(a.act, gate, up, a.limit, a.alpha);
+        }
+        a.act_out[(int64_t)u * a.I + j] = r;
+      }
+    } else {
+      const int h = 16 * rb + lane;
+      if (lane < 16 && h < a.H) {
+        float o = 0.f;
+        for (int k = 0; k < a.top_k; ++k) {
+          const int ek = s_e[k];
+          if (ek < 0) continue;
+          const float* Q = a.part + (int64_t)(k * a.R + rb) * a.S * 16;
+          float v = 0.f;
+          for (int s = 0; s < a.S; ++s) v += __ldcg(Q + 16 * s + lane);
+          v *= inv[k];
+          const float* bias = a.experts[ek].down_bias;
+          if (bias) v += bias[h];
+          o = fmaf(a.wts[k], v, o);
+        }
+        a.out[h] = f32_to_bf16_bits(o);
+      }
+    }
+    if (lane == 0) a.cnt[slot] = 0u;
+  }
+  // copies still in flight after a timed-out wait land before the CTA exits
+  while (consumed < issued) {
+    if (!pk_warp_wait(&bar[consumed % kSlots], (consumed / kSlots) & 1u, a.err)) break;
+    ++consumed;
+  }
+}
+
+static int num_sms_pk() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+// K-split: the smallest makespan (k-blocks per warp, plus one k-block of
+// per-task overhead) over the resident warps of one CTA per SM.
+static int choose_split(int rows, int KB, int warps) {
+  int best = 1;
+  double best_t = 1e30;
+  for (int S = 1; S <= std::min(KB, kMaxSplit); ++S) {
+    const int nkb = (KB + S - 1) / S;
+    const int Seff = (KB + nkb - 1) / nkb;
+    const int64_t tasks = (int64_t)rows * Seff;
+    const double waves = (double)((tasks + warps - 1) / warps);
+    const double tm = waves * (nkb + 1);
+    if (tm < best_t - 1e-9) {
+      best_t = tm;
+      best = Seff;
+    }
+  }
+  return best;
+}
+
+size_t packed_ws_bytes(const TsbMoeSpec& sp) {
+  const PackGeom G = pack_geom(sp);
+  const int64_t parts =
+      (int64_t)sp.top_k * std::max<int64_t>((int64_t)G.rgu * std::min(G.kbh, kMaxSplit), (int64_t)G.rdn * std::min(G.kbi, kMaxSplit));
+  const int64_t cnts = std::max<int64_t>((int64_t)sp.top_k * G.rgu, G.rdn);
+  return (size_t)(parts * 16 * 4 + cnts * 4 + 512);
+}
+
+constexpr size_t kPkSmemMax = 160 * 1024;
+
+template <int MODE>
+static int launch_pk(PkArgs& a, int rows, cudaStream_t st, bool pdl) {
+  const int grid = num_sms_pk();
+  a.S = choose_split(rows, a.KB, grid * kPkWarps);
+  a.nkb = (a.KB + a.S - 1) / a.S;
+  a.S = (a.KB + a.nkb - 1) / a.nkb;
+  a.ntasks = rows * a.S;
+  const size_t smem = pk_smem(a.nv, a.KB);
+  static bool attr = [] {
+    return cudaFuncSetAttribute(packed_matvec_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kPkSmemMax) == cudaSuccess;
+  }();
+  if (!attr || smem > kPkSmemMax)
+    return set_error(TSB_ERR_UNSUPPORTED, "packed decode: vectors too long for shared memory");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kPkThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, packed_matvec_kernel<MODE>, a);
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return TSB_OK;
+}
+
+int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x,
+                         const int32_t* ids, const float* wts, float* act, void* out, int32_t* err, char* pws,
+                         cudaStream_t st, bool pdl_first) {
+  const PackGeom G = pack_geom(sp);
+  PkArgs a{};
+  a.packed = static_cast<const uint8_t*>(packed);
+  a.expert_bytes = G.expert_bytes;
+  a.ids = ids;
+  a.wts = wts;
+  a.experts = ex;
+  a.n_experts = sp.n_experts;
+  a.top_k = sp.top_k;
+  a.err = err;
+  a.I = sp.inter;
+  a.H = sp.hidden;
+  a.act = sp.activation;
+  a.limit = sp.limit;
+  a.alpha = sp.alpha;
+  a.act_out = act;
+  a.out = static_cast<uint16_t*>(out);
+  a.cnt = reinterpret_cast<unsigned*>(pws);
+  const int64_t cnts = std::max<int64_t>((int64_t)sp.top_k * G.rgu, G.rdn);
+  a.part = reinterpret_cast<float*>(pws + ((cnts * 4 + 255) & ~int64_t(255)));
+
+  PkArgs gu = a;
+  gu.mode = 0;
+  gu.sec_off = G.gu_off;
+  gu.R = G.rgu;
+  gu.KB = G.kbh;
+  gu.x = x;
+  gu.nv = 1;
+  int rc = launch_pk<0>(gu, sp.top_k * G.rgu, st, pdl_first);
+  if (rc) return rc;
+  PkArgs dn = a;
+  dn.mode = 1;
+  dn.sec_off = G.dn_off;
+  dn.R = G.rdn;
+  dn.KB = G.kbi;
+  dn.x = act;
+  dn.nv = sp.top_k;
+  return launch_pk<1>(dn, sp.top_k * G.rdn, st, true);
+}
+
+}  // namespace tsb

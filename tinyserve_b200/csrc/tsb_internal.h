@@ -28,9 +28,9 @@ struct PrefillLayout {
   size_t err, total_mb, counts, ccount, mb_expert, row_of, row_src, row_shift, xp, act, y, wgu, wdn, total;
   int64_t rows_max, wgu_estride, wdn_estride;
   int mb_max, kbh, kbi, nt_gu, nt_dn;
-  bool fused_gu, fused_dn;
+  bool fused_gu, fused_dn;  // MXFP4 decoded inside the GEMM (no fp16 weight tiles)
   bool pair;                // tiled GEMMs on CTA pairs (experts padded to 256 rows)
-  int pad;                  // expert row padding: 128, or 256 for CTA pairs  // MXFP4 decoded inside the GEMM (no fp16 weight tiles)
+  int pad;                  // expert row padding: 128, or 256 for CTA pairs
 };
 PrefillLayout prefill_layout(const TsbMoeSpec& sp, int T);
 int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, int T, const void* rw,
@@ -38,6 +38,18 @@ int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x,
                        cudaStream_t st);
 int launch_route(const TsbMoeSpec& sp, const void* x, int T, const void* rw, const float* rb, int32_t* ids,
                  float* wts, cudaStream_t st);
+// Decode-packed experts (batch-1 decode of 4-bit K-quant layers).
+struct PackGeom {
+  int64_t gu_off, dn_off, expert_bytes;  // per expert: gate/up units, then down units
+  int rgu, rdn, kbh, kbi;                // row blocks (8 outputs / 16 rows) and 64-wide k-blocks
+};
+bool packable(const TsbMoeSpec& sp);
+PackGeom pack_geom(const TsbMoeSpec& sp);
+int launch_pack(const TsbMoeSpec& sp, const TsbExpert* experts, void* packed, cudaStream_t st);
+size_t packed_ws_bytes(const TsbMoeSpec& sp);
+int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x,
+                         const int32_t* ids, const float* wts, float* act, void* out, int32_t* err, char* pws,
+                         cudaStream_t st, bool pdl_first);
 int launch_dequant(int fmt, const void* w, const void* s, int64_t rows, int64_t cols, void* out, int odt,
                    cudaStream_t st);
 

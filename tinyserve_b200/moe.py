@@ -42,7 +42,7 @@ class QuantMoE:
     def __init__(self, experts: list[ExpertWeights], *, fmt_gate_up: int, fmt_down: int, hidden: int, inter: int,
                  top_k: int, router_w: torch.Tensor | None = None, router_b: torch.Tensor | None = None,
                  gate_up_layout: str = "separate", activation: str = "swiglu_oai", limit: float = 7.0,
-                 alpha: float = 1.702):
+                 alpha: float = 1.702, pack: bool | None = None):
         if not experts:
             raise ValueError("no experts")
         self.device = experts[0].gate.device
@@ -63,10 +63,36 @@ class QuantMoE:
         self._ws_cache: dict[int, torch.Tensor] = {}
         self._pws_cache: dict[int, torch.Tensor] = {}
         self._fast: dict[int, tuple] = {}
+        # Batch-1 decode on a decode-packed copy of the experts (Q4_K layers):
+        # built once here, 1.33x the Q4_K bytes; pack=None packs when the
+        # spec has a packed form, pack=False keeps the generic decode engine.
+        self._packed = None
+        nbytes = _lib.lib().tsb_moe_packed_bytes(ctypes.byref(self.spec))
+        if pack and not nbytes:
+            raise ValueError("this layer has no packed form (needs Q4_K gate/up and down, H and I multiples of 64)")
+        if nbytes and pack is not False:
+            self._packed = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            _lib.check(_lib.lib().tsb_moe_pack(ctypes.byref(self.spec), self._table.data_ptr(),
+                                               self._packed.data_ptr(), nbytes,
+                                               torch.cuda.current_stream(self.device).cuda_stream))
+
+    @property
+    def packed(self) -> bool:
+        """True when batch-1 decode runs on the decode-packed expert copy."""
+        return self._packed is not None
+
+    def _decode_call(self):
+        """(C function, leading arguments) of this layer's decode entry point."""
+        L = _lib.lib()
+        if self._packed is not None:
+            return L.tsb_moe_decode_packed, (ctypes.byref(self.spec), self._packed.data_ptr(), self._table.data_ptr())
+        return L.tsb_moe_decode, (ctypes.byref(self.spec), self._table.data_ptr())
 
     def workspace(self, T: int) -> torch.Tensor:
         if T not in self._ws_cache:
-            n = _lib.lib().tsb_moe_decode_workspace(ctypes.byref(self.spec), T)
+            L = _lib.lib()
+            ws_fn = L.tsb_moe_decode_packed_workspace if self._packed is not None else L.tsb_moe_decode_workspace
+            n = ws_fn(ctypes.byref(self.spec), T)
             self._ws_cache[T] = torch.zeros(n, dtype=torch.uint8, device=self.device)
         return self._ws_cache[T]
 
@@ -93,8 +119,9 @@ class QuantMoE:
         if out is None:
             out = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=self.device)
         ws = self.workspace(T)
-        rc = _lib.lib().tsb_moe_decode(
-            ctypes.byref(self.spec), self._table.data_ptr(), x.data_ptr(), T,
+        fn, lead = self._decode_call()
+        rc = fn(
+            *lead, x.data_ptr(), T,
             None if given else _p(self.router_w), None if given else _p(self.router_b),
             ids.data_ptr(), weights.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
             torch.cuda.current_stream(self.device).cuda_stream)
@@ -114,14 +141,14 @@ class QuantMoE:
         fast = self._fast.get(T)
         if fast is None:
             ws = self.workspace(T)
-            fn = _lib.lib().tsb_moe_decode
+            fn, lead = self._decode_call()
             routed = self.router_w is not None
-            fast = (fn, ctypes.byref(self.spec), self._table.data_ptr(), _p(self.router_w) if routed else None,
-                    _p(self.router_b) if routed else None, ws.data_ptr(), ws.numel())
+            fast = (fn, lead, _p(self.router_w) if routed else None, _p(self.router_b) if routed else None,
+                    ws.data_ptr(), ws.numel())
             self._fast[T] = fast
-        fn, spec, table, rw, rb, wsp, wsn = fast
+        fn, lead, rw, rb, wsp, wsn = fast
         st = torch.cuda.current_stream(self.device).cuda_stream if stream is None else stream
-        rc = fn(spec, table, x.data_ptr(), T, rw, rb, ids.data_ptr(), weights.data_ptr(), out.data_ptr(), wsp, wsn, st)
+        rc = fn(*lead, x.data_ptr(), T, rw, rb, ids.data_ptr(), weights.data_ptr(), out.data_ptr(), wsp, wsn, st)
         if rc:
             _lib.check(rc)
 
