@@ -206,14 +206,83 @@ struct PkArgs {
 
 // Each warp streams its units through a private ring of kSlots slots of
 // kSlotUnits units (one cp.async.bulk copy per slot, completing on the slot's
-// mbarrier): kSlots * kSlotUnits * 768 bytes in flight per warp.
-constexpr int kSlotUnits = 2, kSlots = 3;
+// mbarrier): up to kSlots * kSlotUnits * 768 bytes in flight per warp.  The
+// ring is refilled across the warp's tasks, so it does not drain between them.
+constexpr int kSlotUnits = 4, kSlots = 2;
 constexpr int kSlotBytes = kSlotUnits * kUnitBytes;
 
+// Slot waits spin on mbarrier.test_wait (no suspend): a warp waits for its
+// own next slot every two units, so a sleeping wait's wake-up delay would sit
+// on the critical path.  Bounded: after kSpinPolls polls (seconds) it records
+// kDevWaitTimeout and returns false.
+constexpr uint32_t kSpinPolls = 1u << 26;
 __device__ __forceinline__ bool pk_warp_wait(uint64_t* bar, uint32_t parity, int* err) {
-  const bool ok = mbar_wait(bar, parity, err);
+  bool ok = false;
+  for (uint32_t i = 0; i < kSpinPolls && !ok; ++i) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(r)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    ok = r != 0;
+  }
+  if (!ok && err) atomicExch(err, kDevWaitTimeout);
   return __all_sync(0xffffffffu, ok);
 }
+// D = A * B with a zero accumulator input (no per-use register clearing).
+__device__ __forceinline__ void mma_f16_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+// One 768-byte unit: decode the 32 codes of this lane, four MMAs against the
+// staged vector, fold into the two row accumulators.
+__device__ __forceinline__ void unit_fma(const uint8_t* u, int oq, int oc, const uint8_t* xb, const float2 xs,
+                                         float& acc_lo, float& acc_hi) {
+  const uint4 q = *reinterpret_cast<const uint4*>(u + oq);
+  const float4 c0 = *reinterpret_cast<const float4*>(u + oc);
+  const float4 c1 = *reinterpret_cast<const float4*>(u + oc + 128);
+  const uint4 b01 = *reinterpret_cast<const uint4*>(xb);
+  const uint4 b23 = *reinterpret_cast<const uint4*>(xb + 16);
+  uint32_t l0[4], l1[4], h0[4], h1[4];
+  {
+    const uint32_t w0 = q.x, w1 = q.y, w2 = q.z, w3 = q.w;
+    const uint32_t v0 = w0 >> 8, v1 = w1 >> 8, v2 = w2 >> 8, v3 = w3 >> 8;
+    l0[0] = (w0 & 0x000F000Fu) | 0x64006400u;
+    l0[1] = (v0 & 0x000F000Fu) | 0x64006400u;
+    l0[2] = (w1 & 0x000F000Fu) | 0x64006400u;
+    l0[3] = (v1 & 0x000F000Fu) | 0x64006400u;
+    l1[0] = (w2 & 0x000F000Fu) | 0x64006400u;
+    l1[1] = (v2 & 0x000F000Fu) | 0x64006400u;
+    l1[2] = (w3 & 0x000F000Fu) | 0x64006400u;
+    l1[3] = (v3 & 0x000F000Fu) | 0x64006400u;
+    h0[0] = (w0 & 0x00F000F0u) | 0x54005400u;
+    h0[1] = (v0 & 0x00F000F0u) | 0x54005400u;
+    h0[2] = (w1 & 0x00F000F0u) | 0x54005400u;
+    h0[3] = (v1 & 0x00F000F0u) | 0x54005400u;
+    h1[0] = (w2 & 0x00F000F0u) | 0x54005400u;
+    h1[1] = (v2 & 0x00F000F0u) | 0x54005400u;
+    h1[2] = (w3 & 0x00F000F0u) | 0x54005400u;
+    h1[3] = (v3 & 0x00F000F0u) | 0x54005400u;
+  }
+  float d0[4], d1[4];
+  mma_f16_z(d0, l0, b01.x, b01.y);
+  mma_f16(d0, l1, b01.z, b01.w);
+  mma_f16_z(d1, h0, b23.x, b23.y);
+  mma_f16(d1, h1, b23.z, b23.w);
+  acc_lo = fmaf(c0.x, d0[0], acc_lo);
+  acc_lo = fmaf(-c0.z, xs.x, acc_lo);
+  acc_hi = fmaf(c0.y, d0[2], acc_hi);
+  acc_hi = fmaf(-c0.w, xs.x, acc_hi);
+  acc_lo = fmaf(c1.x, d1[0], acc_lo);
+  acc_lo = fmaf(-c1.z, xs.y, acc_lo);
+  acc_hi = fmaf(c1.y, d1[2], acc_hi);
+  acc_hi = fmaf(-c1.w, xs.y, acc_hi);
+}
+
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -229,38 +298,50 @@ __host__ __device__ inline size_t pk_smem(int nv, int KB) {
   return pk_ring_off(nv, KB) + (size_t)kPkWarps * kSlots * kSlotBytes;
 }
 
+// Four consecutive elements [k, k+4) of staged vector v as floats.
 template <int MODE>
-__device__ __forceinline__ float vec_elem(const PkArgs& a, int v, int k) {
-  return MODE == 0 ? bf16_bits_to_f32(static_cast<const uint16_t*>(a.x)[k])
-                   : __ldcg(static_cast<const float*>(a.x) + (int64_t)v * a.I + k);
+__device__ __forceinline__ float4 vec4(const PkArgs& a, int v, int k) {
+  if (MODE == 0) {
+    const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(a.x) + k);
+    return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u), __uint_as_float(r.y << 16),
+                       __uint_as_float(r.y & 0xFFFF0000u));
+  }
+  return __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + (int64_t)v * a.I + k));
 }
 
-// All staged vectors in two passes (max |x| per vector, then scale, round to
-// fp16, permute and sum per sub-block), two block barriers in total; each pass
-// issues kStageU independent loads per thread before using them.
-constexpr int kStageU = 8;
+// Staging of all vectors in two passes (max |x| per vector; then scale, round
+// to fp16, permute into fragment order and sum per sub-block), two block
+// barriers in total.  Both passes walk the vectors' float4 groups as one flat
+// range (thread i: groups i, i+512, ...; vector index carried incrementally),
+// kStageU groups per thread loaded before any is used.  The eight groups of a
+// 32-element sub-block sit on eight consecutive lanes (vector length K4 is a
+// multiple of 16 groups), so three shuffles sum it.
+constexpr int kStageU = 4;
 
 template <int MODE>
 __device__ void stage_vectors(const PkArgs& a, uint8_t* sm, float* inv, int warp, int lane) {
   __shared__ float red[8][kPkWarps];
   __shared__ float s_scale[8];
-  const int K = 64 * a.KB, n = a.nv * K;
+  const int K4 = 16 * a.KB, total = a.nv * K4;
   float mx[8];
 #pragma unroll
   for (int v = 0; v < 8; ++v) mx[v] = 0.f;
-  for (int i0 = threadIdx.x; i0 < n; i0 += kStageU * kPkThreads) {
-    float xv[kStageU];
+  for (int q0 = threadIdx.x; q0 < total; q0 += kStageU * kPkThreads) {
+    float4 f[kStageU];
+    int vv[kStageU];
 #pragma unroll
     for (int u = 0; u < kStageU; ++u) {
-      const int i = i0 + u * kPkThreads;
-      xv[u] = i < n ? vec_elem<MODE>(a, i / K, i % K) : 0.f;
+      const int q = q0 + u * kPkThreads;
+      const int v = q / K4;
+      vv[u] = q < total ? v : 8;
+      f[u] = q < total ? vec4<MODE>(a, v, 4 * (q - v * K4)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < kStageU; ++u) {
-      const int i = i0 + u * kPkThreads, v = i / K;
+      const float m = fmaxf(fmaxf(fabsf(f[u].x), fabsf(f[u].y)), fmaxf(fabsf(f[u].z), fabsf(f[u].w)));
 #pragma unroll
-      for (int w = 0; w < 8; ++w)
-        if (w == v) mx[w] = fmaxf(mx[w], fabsf(xv[u]));
+      for (int v = 0; v < 8; ++v)
+        if (vv[u] == v) mx[v] = fmaxf(mx[v], m);
     }
   }
 #pragma unroll
@@ -283,29 +364,39 @@ __device__ void stage_vectors(const PkArgs& a, uint8_t* sm, float* inv, int warp
   }
   __syncthreads();
   float* X = reinterpret_cast<float*>(sm + (size_t)a.nv * a.KB * 128);
-  const int nsb = 2 * a.KB * a.nv;
-  for (int q0 = warp; q0 < nsb; q0 += kStageU * kPkWarps) {
-    float xv[kStageU];
+  // all lanes stay in the loop for the shuffles (a sub-block's eight lanes are
+  // all in range or all out)
+  for (int q0 = threadIdx.x - lane; q0 < total; q0 += kStageU * kPkThreads) {
+    float4 f[kStageU];
 #pragma unroll
     for (int u = 0; u < kStageU; ++u) {
-      const int q = q0 + u * kPkWarps;
-      const int v = q / (2 * a.KB), sb = q - v * 2 * a.KB;
-      xv[u] = q < nsb ? vec_elem<MODE>(a, v, 32 * sb + lane) : 0.f;
+      const int q = q0 + lane + u * kPkThreads;
+      const int v = q / K4;
+      f[u] = q < total ? vec4<MODE>(a, v, 4 * (q - v * K4)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < kStageU; ++u) {
-      const int q = q0 + u * kPkWarps;
-      if (q >= nsb) break;
-      const int v = q / (2 * a.KB), sb = q - v * 2 * a.KB;
-      const int k = 32 * sb + lane;
-      const __half hv = __float2half_rn(xv[u] * s_scale[v]);
-      float sum = __half2float(hv);
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (lane == 0) X[(size_t)v * 2 * a.KB + sb] = sum;
-      const int kb = k >> 6, kk = k & 63, j = kk >> 4, w = kk & 15;
-      const int idx = ((((kb * 4 + ((w & 7) >> 1)) * 4 + j) * 2 + (w >> 3)) * 2) + (w & 1);
-      reinterpret_cast<uint16_t*>(sm + (size_t)v * a.KB * 128)[idx] = __half_as_ushort(hv);
+      const int q = q0 + lane + u * kPkThreads;
+      if (q0 + u * kPkThreads >= total) break;  // warp-uniform
+      const int v = min(q / K4, a.nv - 1), m = q - v * K4;
+      const float sc = s_scale[v];
+      const __half2 h01 = __floats2half2_rn(f[u].x * sc, f[u].y * sc);
+      const __half2 h23 = __floats2half2_rn(f[u].z * sc, f[u].w * sc);
+      const float2 g01 = __half22float2(h01), g23 = __half22float2(h23);
+      float sum = (g01.x + g01.y) + (g23.x + g23.y);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      if (q >= total) continue;
+      if ((lane & 7) == 0) X[(size_t)v * 2 * a.KB + (m >> 3)] = sum;
+      // k = 4m: k-block kb = m/16, MMA j = (m/4)%4, w0 = 4*(m%4) in [0,16):
+      // pairs (w0, w0+1) and (w0+2, w0+3) go to quad lanes tt and tt+1 of half w0/8
+      const int kb = m >> 4, j = (m >> 2) & 3, w0 = 4 * (m & 3);
+      const int tt = (w0 & 7) >> 1, hf = w0 >> 3;
+      const int i0 = ((kb * 4 + tt) * 4 + j) * 2 + hf;
+      uint32_t* xf = reinterpret_cast<uint32_t*>(sm + (size_t)v * a.KB * 128);
+      xf[i0] = *reinterpret_cast<const uint32_t*>(&h01);
+      xf[i0 + 8] = *reinterpret_cast<const uint32_t*>(&h23);
     }
   }
 }
@@ -365,73 +456,72 @@ __global__ void __launch_bounds__(kPkThreads, 2) packed_matvec_kernel(const PkAr
 
   uint32_t issued = 0, consumed = 0;  // slot fills / drains of this warp's ring
   bool bad = false;                   // a slot wait ran out: stop streaming
+  // Per-task geometry (one division chain per task, not per slot).
+  struct TaskGeo {
+    const uint8_t* p;  // first unit
+    int n, u, rb, kb0;
+  };
+  auto geo = [&](int task) {
+    TaskGeo G;
+    G.u = task / (a.R * a.S);
+    const int rem = task - G.u * (a.R * a.S);
+    G.rb = rem / a.S;
+    G.kb0 = (rem - G.rb * a.S) * a.nkb;
+    const int e = s_e[G.u];
+    G.n = e < 0 ? 0 : min(a.KB, G.kb0 + a.nkb) - G.kb0;
+    G.p = a.packed + (int64_t)(e < 0 ? 0 : e) * a.expert_bytes + a.sec_off +
+          ((int64_t)G.rb * a.KB + G.kb0) * kUnitBytes;
+    return G;
+  };
+  // issue cursor: the next (task, group) to fetch, running ahead of the consumer
+  int it_task = gw0, it_g = 0;
+  TaskGeo it_geo{};
+  if (gw0 < a.ntasks) it_geo = geo(gw0);
+  auto issue_next = [&]() {
+    while (it_task < a.ntasks && it_g * kSlotUnits >= it_geo.n) {
+      it_task += nw;
+      it_g = 0;
+      if (it_task < a.ntasks) it_geo = geo(it_task);
+    }
+    if (it_task >= a.ntasks) return;
+    const uint32_t bytes = (uint32_t)min(kSlotUnits, it_geo.n - it_g * kSlotUnits) * kUnitBytes;
+    uint64_t* b = &bar[issued & (kSlots - 1)];
+    if (lane == 0) {
+      mbar_arrive_expect_tx(b, bytes);
+      bulk_g2s(ring + (issued & (kSlots - 1)) * kSlotBytes, it_geo.p + (size_t)it_g * kSlotBytes, bytes, b);
+    }
+    ++issued;
+    ++it_g;
+  };
+#pragma unroll
+  for (int i = 0; i < kSlots; ++i) issue_next();
+  const int oq = 16 * lane, oc = 512 + 16 * g;
+
   for (int task = gw0; task < a.ntasks; task += nw) {
-    const int u = task / (a.R * a.S), rb = (task % (a.R * a.S)) / a.S;
+    const TaskGeo G = geo(task);
+    const int u = G.u, rb = G.rb, n = G.n, kb0 = G.kb0;
     const int e = s_e[u];
     float acc_lo = 0.f, acc_hi = 0.f;
-    if (e >= 0 && !bad) {
-      int kb0, kb1;
-      const uint8_t* p = task_ptr(task, e, kb0, kb1);
+    if (n > 0 && !bad) {
       const int v = MODE == 0 ? 0 : u;
       const uint8_t* xb = g == 0 ? sm + (size_t)v * a.KB * 128 + (size_t)kb0 * 128 + 32 * t : zero;
       const int xstep = g == 0 ? 128 : 0;
       const float2* X = reinterpret_cast<const float2*>(sm + (size_t)a.nv * a.KB * 128) + (size_t)v * a.KB + kb0;
-      const int n = kb1 - kb0, ngrp = (n + kSlotUnits - 1) / kSlotUnits;
-      auto issue = [&](int gi) {
-        uint64_t* b = &bar[issued % kSlots];
-        uint8_t* dst = ring + (issued % kSlots) * kSlotBytes;
-        ++issued;
-        if (lane == 0) {
-          const uint32_t bytes = (uint32_t)min(kSlotUnits, n - gi * kSlotUnits) * kUnitBytes;
-          mbar_arrive_expect_tx(b, bytes);
-          bulk_g2s(dst, p + (size_t)gi * kSlotBytes, bytes, b);
-        }
-      };
-      for (int gi = 0; gi < kSlots && gi < ngrp; ++gi) issue(gi);
-      for (int gi = 0; gi < ngrp; ++gi) {
-        const int sl = consumed % kSlots;
+      for (int u0 = 0; u0 < n; u0 += kSlotUnits) {
+        const uint32_t sl = consumed & (kSlots - 1);
         if (!pk_warp_wait(&bar[sl], (consumed / kSlots) & 1u, a.err)) {
           bad = true;
           break;
         }
         ++consumed;
         const uint8_t* slot = ring + sl * kSlotBytes;
-        const int nu = min(kSlotUnits, n - gi * kSlotUnits);
-        for (int ui = 0; ui < nu; ++ui, slot += kUnitBytes) {
-          const uint4 q = *reinterpret_cast<const uint4*>(slot + 16 * lane);
-          const float4 c0 = *reinterpret_cast<const float4*>(slot + 512 + 16 * g);
-          const float4 c1 = *reinterpret_cast<const float4*>(slot + 640 + 16 * g);
-          const uint4 b01 = *reinterpret_cast<const uint4*>(xb);
-          const uint4 b23 = *reinterpret_cast<const uint4*>(xb + 16);
-          const float2 xs = *X;
-          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-          uint32_t lo[8], hi[8];
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const uint32_t v8 = w[r] >> 8;
-            lo[2 * r] = (w[r] & 0x000F000Fu) | 0x64006400u;
-            hi[2 * r] = (w[r] & 0x00F000F0u) | 0x54005400u;
-            lo[2 * r + 1] = (v8 & 0x000F000Fu) | 0x64006400u;
-            hi[2 * r + 1] = (v8 & 0x00F000F0u) | 0x54005400u;
-          }
-          float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-          mma_f16(d0, *reinterpret_cast<const uint32_t(*)[4]>(&lo[0]), b01.x, b01.y);
-          mma_f16(d0, *reinterpret_cast<const uint32_t(*)[4]>(&lo[4]), b01.z, b01.w);
-          mma_f16(d1, *reinterpret_cast<const uint32_t(*)[4]>(&hi[0]), b23.x, b23.y);
-          mma_f16(d1, *reinterpret_cast<const uint32_t(*)[4]>(&hi[4]), b23.z, b23.w);
-          acc_lo = fmaf(c0.x, d0[0], acc_lo);
-          acc_lo = fmaf(-c0.z, xs.x, acc_lo);
-          acc_hi = fmaf(c0.y, d0[2], acc_hi);
-          acc_hi = fmaf(-c0.w, xs.x, acc_hi);
-          acc_lo = fmaf(c1.x, d1[0], acc_lo);
-          acc_lo = fmaf(-c1.z, xs.y, acc_lo);
-          acc_hi = fmaf(c1.y, d1[2], acc_hi);
-          acc_hi = fmaf(-c1.w, xs.y, acc_hi);
-          xb += xstep;
-          ++X;
-        }
+        for (int ui = 0; ui < kSlotUnits; ++ui)
+          if (ui == 0 || u0 + ui < n) unit_fma(slot + ui * kUnitBytes, oq, oc, xb + ui * xstep, X[ui], acc_lo, acc_hi);
+        xb += kSlotUnits * xstep;
+        X += kSlotUnits;
         __syncwarp();  // every lane has read the slot before it is refilled
-        if (gi + kSlots < ngrp) issue(gi + kSlots);
+        issue_next();
       }
     }
     // partial sums of rows g and g+8 live in the t == 0 lanes
@@ -470,19 +560,34 @@ __global__ void __launch_bounds__(kPkThreads, 2) packed_matvec_kernel(const PkAr
         a.act_out[(int64_t)u * a.I + j] = r;
       }
     } else {
-      const int h = 16 * rb + lane;
+      // lane = row (lane & 15) x half (lane >> 4); the halves take alternate
+      // (slot, split) partials, all loads issued before the sums, then one shuffle.
+      const int r = lane & 15, hf = lane >> 4, h = 16 * rb + r;
+      const int nks = a.top_k * a.S;
+      float o = 0.f;
+      for (int i0 = hf; i0 < nks; i0 += 16) {
+        float pv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = i0 + 2 * j;
+          const int k = i / a.S, sp = i - k * a.S;
+          pv[j] = (i < nks && s_e[min(k, 7)] >= 0) ? __ldcg(a.part + ((int64_t)(k * a.R + rb) * a.S + sp) * 16 + r) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = i0 + 2 * j;
+          if (i >= nks) break;
+          const int k = i / a.S;
+          o = fmaf(a.wts[k] * inv[k], pv[j], o);
+        }
+      }
+      o += __shfl_xor_sync(0xffffffffu, o, 16);
       if (lane < 16 && h < a.H) {
-        float o = 0.f;
         for (int k = 0; k < a.top_k; ++k) {
           const int ek = s_e[k];
           if (ek < 0) continue;
-          const float* Q = a.part + (int64_t)(k * a.R + rb) * a.S * 16;
-          float v = 0.f;
-          for (int s = 0; s < a.S; ++s) v += __ldcg(Q + 16 * s + lane);
-          v *= inv[k];
           const float* bias = a.experts[ek].down_bias;
-          if (bias) v += bias[h];
-          o = fmaf(a.wts[k], v, o);
+          if (bias) o = fmaf(a.wts[k], bias[h], o);
         }
         a.out[h] = f32_to_bf16_bits(o);
       }
