@@ -225,10 +225,13 @@ def run_ours(args, ws, rank, local):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "traffic": DECODE_TRAFFIC,
                      "traffic_source": "ncu dram__bytes_read+write of the three launches of one token-layer "
-                                       "(profiles/moe_layer_decode_q4k.md), same workload",
+                                       "(profiles/moe_layer_decode_q4k_packed.md), same workload",
                      "unit_of_work": f"one token through one layer = {step_bytes} algorithmic bytes "
-                                     "(4 experts' Q4_K gate/up/down + router + activations)",
-                     "kernel": "router + gate_up(SwiGLU) + down(combine), PDL-chained"},
+                                     "(4 experts' Q4_K gate/up/down + router + activations); the decode-packed "
+                                     "copy the kernels stream is 1.33x the Q4_K bytes (fp32 fold coefficients), "
+                                     "which the traffic figure shows",
+                     "kernel": "router + packed gate_up(SwiGLU) + packed down(combine), PDL-chained",
+                     "packed": bool(layers[0].packed)},
         "e2e": {"value": ws * E2E / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": 2880 * 2,
                 "d2h_bytes_per_step": 2880 * 2,
                 "how": "QuantMoE.decode_ (public API, allocation-free, one eager ctypes call) per token, "
@@ -239,9 +242,10 @@ def run_ours(args, ws, rank, local):
     return res, layers, xs
 
 
-# DRAM bytes per token-layer from the committed ncu capture of this workload
-# (gate/up 37.40 MB + down 18.77 MB + router 0.19 MB read, writes < 0.1 MB).
-DECODE_TRAFFIC = 56.4e6
+# DRAM bytes per token-layer from the committed ncu capture of this workload on
+# the decode-packed experts (gate/up 49.81 MB + down 24.97 MB + router 0.22 MB
+# read, writes < 0.1 MB).
+DECODE_TRAFFIC = 75.0e6
 
 PREFILL_T = 4096
 
