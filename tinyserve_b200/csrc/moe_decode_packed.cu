@@ -202,6 +202,10 @@ struct PkArgs {
   float limit, alpha;
   float* act_out;     // mode 0: fp32 [top_k, I]
   uint16_t* out;      // mode 1: bf16 [H]
+  // 0x64006400 and 0x54005400 (f16x2 1024 and 64), passed as arguments so the
+  // compiler keeps them in registers: each code decode is then one LOP3 with
+  // the mask as its immediate, (w & mask) | magic.
+  uint32_t magic1024, magic64;
 };
 
 // Each warp streams its units through a private ring of kSlots slots of
@@ -241,7 +245,7 @@ __device__ __forceinline__ void mma_f16_z(float (&d)[4], const uint32_t (&a)[4],
 // One 768-byte unit: decode the 32 codes of this lane, four MMAs against the
 // staged vector, fold into the two row accumulators.
 __device__ __forceinline__ void unit_fma(const uint8_t* u, int oq, int oc, const uint8_t* xb, const float2 xs,
-                                         float& acc_lo, float& acc_hi) {
+                                         uint32_t M1, uint32_t M2, float& acc_lo, float& acc_hi) {
   const uint4 q = *reinterpret_cast<const uint4*>(u + oq);
   const float4 c0 = *reinterpret_cast<const float4*>(u + oc);
   const float4 c1 = *reinterpret_cast<const float4*>(u + oc + 128);
@@ -251,22 +255,22 @@ __device__ __forceinline__ void unit_fma(const uint8_t* u, int oq, int oc, const
   {
     const uint32_t w0 = q.x, w1 = q.y, w2 = q.z, w3 = q.w;
     const uint32_t v0 = w0 >> 8, v1 = w1 >> 8, v2 = w2 >> 8, v3 = w3 >> 8;
-    l0[0] = (w0 & 0x000F000Fu) | 0x64006400u;
-    l0[1] = (v0 & 0x000F000Fu) | 0x64006400u;
-    l0[2] = (w1 & 0x000F000Fu) | 0x64006400u;
-    l0[3] = (v1 & 0x000F000Fu) | 0x64006400u;
-    l1[0] = (w2 & 0x000F000Fu) | 0x64006400u;
-    l1[1] = (v2 & 0x000F000Fu) | 0x64006400u;
-    l1[2] = (w3 & 0x000F000Fu) | 0x64006400u;
-    l1[3] = (v3 & 0x000F000Fu) | 0x64006400u;
-    h0[0] = (w0 & 0x00F000F0u) | 0x54005400u;
-    h0[1] = (v0 & 0x00F000F0u) | 0x54005400u;
-    h0[2] = (w1 & 0x00F000F0u) | 0x54005400u;
-    h0[3] = (v1 & 0x00F000F0u) | 0x54005400u;
-    h1[0] = (w2 & 0x00F000F0u) | 0x54005400u;
-    h1[1] = (v2 & 0x00F000F0u) | 0x54005400u;
-    h1[2] = (w3 & 0x00F000F0u) | 0x54005400u;
-    h1[3] = (v3 & 0x00F000F0u) | 0x54005400u;
+    l0[0] = (w0 & 0x000F000Fu) | M1;
+    l0[1] = (v0 & 0x000F000Fu) | M1;
+    l0[2] = (w1 & 0x000F000Fu) | M1;
+    l0[3] = (v1 & 0x000F000Fu) | M1;
+    l1[0] = (w2 & 0x000F000Fu) | M1;
+    l1[1] = (v2 & 0x000F000Fu) | M1;
+    l1[2] = (w3 & 0x000F000Fu) | M1;
+    l1[3] = (v3 & 0x000F000Fu) | M1;
+    h0[0] = (w0 & 0x00F000F0u) | M2;
+    h0[1] = (v0 & 0x00F000F0u) | M2;
+    h0[2] = (w1 & 0x00F000F0u) | M2;
+    h0[3] = (v1 & 0x00F000F0u) | M2;
+    h1[0] = (w2 & 0x00F000F0u) | M2;
+    h1[1] = (v2 & 0x00F000F0u) | M2;
+    h1[2] = (w3 & 0x00F000F0u) | M2;
+    h1[3] = (v3 & 0x00F000F0u) | M2;
   }
   float d0[4], d1[4];
   mma_f16_z(d0, l0, b01.x, b01.y);
@@ -517,7 +521,8 @@ __global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkAr
         const uint8_t* slot = ring + sl * kSlotBytes;
 #pragma unroll
         for (int ui = 0; ui < kSlotUnits; ++ui)
-          if (ui == 0 || u0 + ui < n) unit_fma(slot + ui * kUnitBytes, oq, oc, xb + ui * xstep, X[ui], acc_lo, acc_hi);
+          if (ui == 0 || u0 + ui < n) unit_fma(slot + ui * kUnitBytes, oq, oc, xb + ui * xstep, X[ui], a.magic1024, a.magic64, acc_lo,
+                   acc_hi);
         xb += kSlotUnits * xstep;
         X += kSlotUnits;
         __syncwarp();  // every lane has read the slot before it is refilled
@@ -695,6 +700,8 @@ int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpe
   a.act_out = act;
   a.out = static_cast<uint16_t*>(out);
   a.cnt = reinterpret_cast<unsigned*>(pws);
+  a.magic1024 = 0x64006400u;
+  a.magic64 = 0x54005400u;
   const int64_t cnts = std::max<int64_t>((int64_t)sp.top_k * G.rgu, G.rdn);
   a.part = reinterpret_cast<float*>(pws + ((cnts * 4 + 255) & ~int64_t(255)));
 
