@@ -505,7 +505,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkAr
     const TaskGeo G = geo(task);
     const int u = G.u, rb = G.rb, n = G.n, kb0 = G.kb0;
     const int e = s_e[u];
-    float acc_lo = 0.f, acc_hi = 0.f;
+    float acc_lo = 0.f, acc_hi = 0.f, acc_lo1 = 0.f, acc_hi1 = 0.f;
     if (n > 0 && !bad) {
       const int v = MODE == 0 ? 0 : u;
       const uint8_t* xb = g == 0 ? sm + (size_t)v * a.KB * 128 + (size_t)kb0 * 128 + 32 * t : zero;
@@ -519,16 +519,25 @@ __global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkAr
         }
         ++consumed;
         const uint8_t* slot = ring + sl * kSlotBytes;
+        if (u0 + kSlotUnits <= n) {
+          // full slot: independent units, two accumulator pairs
 #pragma unroll
-        for (int ui = 0; ui < kSlotUnits; ++ui)
-          if (ui == 0 || u0 + ui < n) unit_fma(slot + ui * kUnitBytes, oq, oc, xb + ui * xstep, X[ui], a.magic1024, a.magic64, acc_lo,
-                   acc_hi);
+          for (int ui = 0; ui < kSlotUnits; ++ui)
+            unit_fma(slot + ui * kUnitBytes, oq, oc, xb + ui * xstep, X[ui], a.magic1024, a.magic64,
+                     (ui & 1) ? acc_lo1 : acc_lo, (ui & 1) ? acc_hi1 : acc_hi);
+        } else {
+          for (int ui = 0; ui < n - u0; ++ui)
+            unit_fma(slot + ui * kUnitBytes, oq, oc, xb + ui * xstep, X[ui], a.magic1024, a.magic64, acc_lo,
+                     acc_hi);
+        }
         xb += kSlotUnits * xstep;
         X += kSlotUnits;
         __syncwarp();  // every lane has read the slot before it is refilled
         issue_next();
       }
     }
+    acc_lo += acc_lo1;
+    acc_hi += acc_hi1;
     // partial sums of rows g and g+8 live in the t == 0 lanes
     float* P = a.part + (int64_t)task * 16;
     if (t == 0) {
@@ -617,20 +626,22 @@ static int num_sms_pk() {
   return n;
 }
 
-// K-split: the smallest makespan (k-blocks per warp, plus one k-block of
-// per-task overhead) over the resident warps of one CTA per SM.
-static int choose_split(int rows, int KB, int warps) {
-  int best = 1;
+// K-split: k-blocks per task a multiple of kSlotUnits (so every slot but a
+// row's last is full), the smallest makespan (k-blocks per warp plus one of
+// per-task overhead) over the resident warps, at most kMaxSplit tasks per row.
+static int choose_nkb(int rows, int KB, int warps) {
+  int best = 0;
   double best_t = 1e30;
-  for (int S = 1; S <= std::min(KB, kMaxSplit); ++S) {
-    const int nkb = (KB + S - 1) / S;
-    const int Seff = (KB + nkb - 1) / nkb;
-    const int64_t tasks = (int64_t)rows * Seff;
+  const int top = (KB + kSlotUnits - 1) / kSlotUnits * kSlotUnits;
+  for (int nkb = kSlotUnits; nkb <= top; nkb += kSlotUnits) {
+    const int S = (KB + nkb - 1) / nkb;
+    if (S > kMaxSplit) continue;
+    const int64_t tasks = (int64_t)rows * S;
     const double waves = (double)((tasks + warps - 1) / warps);
     const double tm = waves * (nkb + 1);
     if (tm < best_t - 1e-9) {
       best_t = tm;
-      best = Seff;
+      best = nkb;
     }
   }
   return best;
@@ -653,8 +664,7 @@ constexpr int kPkCtasPerSm = 1;
 template <int MODE>
 static int launch_pk(PkArgs& a, int rows, cudaStream_t st, bool pdl) {
   const int grid = kPkCtasPerSm * num_sms_pk();
-  a.S = choose_split(rows, a.KB, grid * kPkWarps);
-  a.nkb = (a.KB + a.S - 1) / a.S;
+  a.nkb = choose_nkb(rows, a.KB, grid * kPkWarps);
   a.S = (a.KB + a.nkb - 1) / a.nkb;
   a.ntasks = rows * a.S;
   const size_t smem = pk_smem(a.nv, a.KB);
