@@ -138,17 +138,18 @@ def run_ours(args, ws, rank, local):
     st = torch.cuda.Stream(dev)
 
     def step(i, s):
+        # the layer's own decode entry point: tsb_moe_decode_packed on packed
+        # layers, tsb_moe_decode otherwise
         L = layers[i % NL]
-        rc = _lib.lib().tsb_moe_decode(
-            ctypes.byref(L.spec), L._table.data_ptr(), xs[i].data_ptr(), 1, L.router_w.data_ptr(),
-            None, ids[i].data_ptr(), wts[i].data_ptr(), outs[i].data_ptr(), L.workspace(1).data_ptr(),
-            L.workspace(1).numel(), s.cuda_stream)
+        fn, lead = L._decode_call()
+        rc = fn(*lead, xs[i].data_ptr(), 1, L.router_w.data_ptr(), None, ids[i].data_ptr(), wts[i].data_ptr(),
+                outs[i].data_ptr(), L.workspace(1).data_ptr(), L.workspace(1).numel(), s.cuda_stream)
         _lib.check(rc)
 
     with torch.cuda.stream(st):
         for i in range(W):
             step(i, st)
-        # capture the K timed steps as one CUDA graph (3 launches per step)
+        # capture the K timed steps as one CUDA graph (2 launches per step packed, 3 generic)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=st):
             for i in range(K):
@@ -230,13 +231,13 @@ def run_ours(args, ws, rank, local):
                                      "(4 experts' Q4_K gate/up/down + router + activations); the decode-packed "
                                      "copy the kernels stream is 1.33x the Q4_K bytes (fp32 fold coefficients), "
                                      "which the traffic figure shows",
-                     "kernel": "router + packed gate_up(SwiGLU) + packed down(combine), PDL-chained",
+                     "kernel": "packed gate_up with in-launch routing (SwiGLU) + packed down (combine), PDL-chained",
                      "packed": bool(layers[0].packed)},
         "e2e": {"value": ws * E2E / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": 2880 * 2,
                 "d2h_bytes_per_step": 2880 * 2,
                 "how": "QuantMoE.decode_ (public API, allocation-free, one eager ctypes call) per token, "
                        "pinned host x -> device, output -> pinned host, CUDA events"},
-        "gpu_launches": 3 * K,
+        "gpu_launches": (2 if layers[0].packed else 3) * K,
         "clocks": clk.summary(),
     }
     return res, layers, xs

@@ -29,6 +29,10 @@ def _x(H, seed, scale=1.0):
     return (torch.randn(1, H, generator=torch.Generator().manual_seed(seed)) * scale).to(torch.bfloat16)
 
 
+def _ref_w(x, router, k):
+    return OE.router_topk_softmax(x.float().numpy(), router.float().numpy(), k)[1][0]
+
+
 @pytest.mark.parametrize("layout", ["separate", "interleaved", "chunked"])
 def test_packed_layer_matches_oracle_and_engine(dev, layout):
     """GPT-OSS-20B shape (H = I = 2880, K % 256 != 0: rows start mid-superblock)."""
@@ -40,15 +44,25 @@ def test_packed_layer_matches_oracle_and_engine(dev, layout):
     for step in range(3):
         x = _x(H, 200 + step)
         out, ids, wts = packed.decode(x.to(dev))
-        out_g, ids_g, _ = generic.decode(x.to(dev))
+        out_g, ids_g, _g_w = generic.decode(x.to(dev))
         torch.cuda.synchronize()
-        assert torch.equal(ids, ids_g)
+        # routing runs inside the packed gate/up launch (its own summation
+        # order): the same experts unless two logits tie after bf16 rounding
+        ids_o, _, lg = OE.router_topk_softmax(x.float().numpy(), router.float().numpy(), k)
+        if set(ids.cpu().numpy()[0]) != set(ids_o[0]):
+            srt = np.sort(lg[0])[::-1]
+            assert abs(srt[k - 1] - srt[k]) <= 1e-2 * abs(srt[k - 1]) + 1e-6, "routing differs away from a tie"
+        else:
+            np.testing.assert_allclose(np.sort(wts.cpu().numpy()[0])[::-1], np.sort(_ref_w(x, router, k))[::-1],
+                                       rtol=1e-5, atol=1e-6)
         ref = _oracle_layer(x.float().numpy(), ids.cpu().numpy()[0], wts.cpu().numpy()[0], dense)
         assert rel_l2(out.float().cpu().numpy()[0], ref) <= TOL
         # the generic engine on the raw streams (rows start mid-superblock:
         # covers its interleaved row order)
-        assert rel_l2(out_g.float().cpu().numpy()[0], ref) <= TOL
-        assert rel_l2(out.float().cpu().numpy()[0], out_g.float().cpu().numpy()[0]) <= TOL
+        if torch.equal(ids, ids_g):
+            assert rel_l2(out.float().cpu().numpy()[0], out_g.float().cpu().numpy()[0]) <= TOL
+        ref_g = _oracle_layer(x.float().numpy(), ids_g.cpu().numpy()[0], _g_w.cpu().numpy()[0], dense)
+        assert rel_l2(out_g.float().cpu().numpy()[0], ref_g) <= TOL
         assert packed.device_error() == 0
 
 

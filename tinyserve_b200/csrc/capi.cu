@@ -267,14 +267,9 @@ int tsb_moe_decode_packed(const TsbMoeSpec* spec, const void* packed, const TsbE
   int32_t* err = reinterpret_cast<int32_t*>(ws + L.err);
   float* act = reinterpret_cast<float*>(ws + L.act);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool routed = router_w != nullptr;
-  if (routed) {
-    rc = launch_router(x, router_w, router_b, sp.hidden, sp.n_experts, 1, sp.top_k,
-                       reinterpret_cast<float*>(ws + L.logits), ids, weights,
-                       reinterpret_cast<unsigned*>(ws + L.counter), st);
-    if (rc) return rc;
-  }
-  return launch_packed_decode(sp, packed, experts, x, ids, weights, act, out, err, ws + L.total, st, routed);
+  // with router weights, routing runs inside the gate/up launch
+  return launch_packed_decode(sp, packed, experts, x, ids, weights, act, out, err, ws + L.total, st, router_w,
+                              router_b);
 }
 
 int tsb_read_device_error(void* workspace, int32_t* code, void* stream) {

@@ -202,6 +202,9 @@ struct PkArgs {
   float limit, alpha;
   float* act_out;     // mode 0: fp32 [top_k, I]
   uint16_t* out;      // mode 1: bf16 [H]
+  // routing inside the gate/up launch (null: ids and wts are inputs)
+  const uint16_t* router_w;  // bf16 [E, H]
+  const float* router_b;     // fp32 [E] or null
   // 0x64006400 and 0x54005400 (f16x2 1024 and 64), passed as arguments so the
   // compiler keeps them in registers: each code decode is then one LOP3 with
   // the mask as its immediate, (w & mask) | magic.
@@ -405,6 +408,81 @@ __device__ void stage_vectors(const PkArgs& a, uint8_t* sm, float* inv, int warp
   }
 }
 
+// Routing of one token inside every gate/up CTA (tinyserve/_model_hooks.py:466-473):
+// warp w computes the logits of experts w, w+16, ... (bf16 x . bf16 W[e] in
+// fp32, + bias, rounded to bf16 as the reference's bf16 Linear returns them)
+// into shared memory, then warp 0 selects the top-k (ties -> lower id, NaN
+// lowest) and softmaxes the k selected logits.  Every CTA reaches the same
+// result from the same arithmetic; CTA 0 publishes ids / weights.
+__device__ void route_in_cta(const PkArgs& a, float* s_logit, int* s_e, float* s_w, int warp, int lane) {
+  const int H = a.H, n8 = H / 8;
+  const uint4* xr = static_cast<const uint4*>(a.x);
+  constexpr int kU = 8;
+  for (int e = warp; e < a.n_experts; e += kPkWarps) {
+    const uint4* wr = reinterpret_cast<const uint4*>(a.router_w + (int64_t)e * H);
+    float acc = 0.f;
+    for (int base = lane; base < n8; base += 32 * kU) {
+      uint4 xv[kU], wv[kU];
+#pragma unroll
+      for (int j = 0; j < kU; ++j) {
+        const int i = base + 32 * j;
+        xv[j] = i < n8 ? __ldg(xr + i) : make_uint4(0, 0, 0, 0);
+        wv[j] = i < n8 ? __ldg(wr + i) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < kU; ++j) {
+        const uint32_t av[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w}, bv[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc = fmaf(__uint_as_float(av[q] << 16), __uint_as_float(bv[q] << 16), acc);
+          acc = fmaf(__uint_as_float(av[q] & 0xFFFF0000u), __uint_as_float(bv[q] & 0xFFFF0000u), acc);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) s_logit[e] = bf16_bits_to_f32(f32_to_bf16_bits(a.router_b ? acc + a.router_b[e] : acc));
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  float sel[8];
+  int sid[8];
+  uint32_t taken = 0;  // bit j: expert lane + 32*j already selected (E <= 1024)
+  for (int k = 0; k < a.top_k; ++k) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = 0; lane + 32 * j < a.n_experts; ++j) {
+      if ((taken >> j) & 1u) continue;
+      const int ee = lane + 32 * j;
+      float v = s_logit[ee];
+      if (v != v) v = -INFINITY;
+      if (v > best || (v == best && ee < bi)) { best = v; bi = ee; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    sel[k] = best;
+    sid[k] = bi;
+    if (bi != 0x7fffffff && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+  }
+  if (lane == 0) {
+    const float mx = sel[0];
+    float den = 0.f, ex[8];
+    for (int k = 0; k < a.top_k; ++k) { ex[k] = __expf(sel[k] - mx); den += ex[k]; }
+    for (int k = 0; k < a.top_k; ++k) {
+      s_e[k] = sid[k];
+      s_w[k] = ex[k] / den;
+      if (blockIdx.x == 0) {
+        const_cast<int32_t*>(a.ids)[k] = sid[k];
+        const_cast<float*>(a.wts)[k] = ex[k] / den;
+      }
+    }
+  }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkArgs a) {
   extern __shared__ uint4 smem4[];
@@ -427,25 +505,34 @@ __global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkAr
     kb1 = min(a.KB, kb0 + a.nkb);
     return a.packed + (int64_t)e * a.expert_bytes + a.sec_off + ((int64_t)rb * a.KB + kb0) * kUnitBytes;
   };
-  auto expert_of = [&](int u) {
+  auto expert_of = [&](int u, bool report) {
     const int e = a.ids[u];
     if ((unsigned)e >= (unsigned)a.n_experts) {
-      if (a.err) atomicExch(a.err, kDevBadPlan);
+      if (report && a.err) atomicExch(a.err, kDevBadPlan);
       return -1;
     }
     return e;
   };
 
+  __shared__ float s_logit[1024];
+  __shared__ float s_w[8];
+  bool routed_here = false;
   if (MODE == 0) {
-    // x does not depend on the router: stage it while the router runs
+    if (a.router_w) {
+      route_in_cta(a, s_logit, s_e, s_w, warp, lane);
+      routed_here = true;
+    }
+    // x does not depend on the router kernel (when there is one): stage it
+    // while that runs
     stage_vectors<0>(a, sm, inv, warp, lane);
     pdl_wait();
   } else {
-    // Expert ids were written before the gate/up kernel passed its wait: pull
-    // this warp's weight ranges into L2 while gate/up finishes.
+    // Pull this warp's weight ranges into L2 while gate/up finishes.  The ids
+    // read here are a hint only (routing inside the gate/up launch may not have
+    // published them yet); the ids used below are read after the wait.
     if (lane == 0)
       for (int task = gw0; task < a.ntasks; task += nw) {
-        const int e = expert_of(task / (a.R * a.S));
+        const int e = expert_of(task / (a.R * a.S), false);
         if (e < 0) continue;
         int kb0, kb1;
         const uint8_t* p = task_ptr(task, e, kb0, kb1);
@@ -453,7 +540,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkAr
       }
     pdl_wait();
   }
-  if (threadIdx.x < a.top_k) s_e[threadIdx.x] = expert_of(threadIdx.x);
+  if (!routed_here && threadIdx.x < a.top_k) s_e[threadIdx.x] = expert_of(threadIdx.x, true);
   pdl_launch_dependents();
   if (MODE == 1) stage_vectors<1>(a, sm, inv, warp, lane);
   __syncthreads();
@@ -691,7 +778,7 @@ static int launch_pk(PkArgs& a, int rows, cudaStream_t st, bool pdl) {
 
 int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x,
                          const int32_t* ids, const float* wts, float* act, void* out, int32_t* err, char* pws,
-                         cudaStream_t st, bool pdl_first) {
+                         cudaStream_t st, const void* router_w, const float* router_b) {
   const PackGeom G = pack_geom(sp);
   PkArgs a{};
   a.packed = static_cast<const uint8_t*>(packed);
@@ -722,7 +809,9 @@ int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpe
   gu.KB = G.kbh;
   gu.x = x;
   gu.nv = 1;
-  int rc = launch_pk<0>(gu, sp.top_k * G.rgu, st, pdl_first);
+  gu.router_w = static_cast<const uint16_t*>(router_w);
+  gu.router_b = router_b;
+  int rc = launch_pk<0>(gu, sp.top_k * G.rgu, st, false);
   if (rc) return rc;
   PkArgs dn = a;
   dn.mode = 1;

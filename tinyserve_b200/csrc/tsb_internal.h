@@ -49,7 +49,7 @@ int launch_pack(const TsbMoeSpec& sp, const TsbExpert* experts, void* packed, cu
 size_t packed_ws_bytes(const TsbMoeSpec& sp);
 int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x,
                          const int32_t* ids, const float* wts, float* act, void* out, int32_t* err, char* pws,
-                         cudaStream_t st, bool pdl_first);
+                         cudaStream_t st, const void* router_w, const float* router_b);
 int launch_dequant(int fmt, const void* w, const void* s, int64_t rows, int64_t cols, void* out, int odt,
                    cudaStream_t st);
 
