@@ -316,41 +316,45 @@ __device__ __forceinline__ float4 vec4(const PkArgs& a, int v, int k) {
   return __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + (int64_t)v * a.I + k));
 }
 
-// Staging of all vectors in two passes (max |x| per vector; then scale, round
-// to fp16, permute into fragment order and sum per sub-block), two block
-// barriers in total.  Both passes walk the vectors' float4 groups as one flat
-// range (thread i: groups i, i+512, ...; vector index carried incrementally),
-// kStageU groups per thread loaded before any is used.  The eight groups of a
-// 32-element sub-block sit on eight consecutive lanes (vector length K4 is a
-// multiple of 16 groups), so three shuffles sum it.
-constexpr int kStageU = 4;
-
+// Thread i owns float4 groups q = i + 512 u of the flat range of all staged
+// vectors; vector v = q / K4.
 template <int MODE>
-__device__ void stage_vectors(const PkArgs& a, uint8_t* sm, float* inv, int warp, int lane) {
-  __shared__ float red[8][kPkWarps];
-  __shared__ float s_scale[8];
-  const int K4 = 16 * a.KB, total = a.nv * K4;
-  float mx[8];
-#pragma unroll
-  for (int v = 0; v < 8; ++v) mx[v] = 0.f;
-  for (int q0 = threadIdx.x; q0 < total; q0 += kStageU * kPkThreads) {
-    float4 f[kStageU];
-    int vv[kStageU];
-#pragma unroll
-    for (int u = 0; u < kStageU; ++u) {
-      const int q = q0 + u * kPkThreads;
-      const int v = q / K4;
-      vv[u] = q < total ? v : 8;
-      f[u] = q < total ? vec4<MODE>(a, v, 4 * (q - v * K4)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int u = 0; u < kStageU; ++u) {
-      const float m = fmaxf(fmaxf(fabsf(f[u].x), fabsf(f[u].y)), fmaxf(fabsf(f[u].z), fabsf(f[u].w)));
-#pragma unroll
-      for (int v = 0; v < 8; ++v)
-        if (vv[u] == v) mx[v] = fmaxf(mx[v], m);
-    }
-  }
+__device__ __forceinline__ float4 stage_load(const PkArgs& a, int q, int K4, int total) {
+  const int v = q / K4;
+  return q < total ? vec4<MODE>(a, v, 4 * (q - v * K4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// Pass 2 of one group: scale, round to fp16, sub-block sum over eight lanes,
+// store into the fragment-order image.  All lanes of the warp call it.
+template <int MODE>
+__device__ __forceinline__ void stage_store(const PkArgs& a, uint8_t* sm, const float* s_scale, int q, int K4,
+                                            int total, float4 f, int lane) {
+  const int v = min(q / K4, a.nv - 1), m = q - v * K4;
+  const float sc = s_scale[v];
+  const __half2 h01 = __floats2half2_rn(f.x * sc, f.y * sc);
+  const __half2 h23 = __floats2half2_rn(f.z * sc, f.w * sc);
+  const float2 g01 = __half22float2(h01), g23 = __half22float2(h23);
+  float sum = (g01.x + g01.y) + (g23.x + g23.y);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+  if (q >= total) return;
+  float* X = reinterpret_cast<float*>(sm + (size_t)a.nv * a.KB * 128);
+  if ((lane & 7) == 0) X[(size_t)v * 2 * a.KB + (m >> 3)] = sum;
+  // k = 4m: k-block kb = m/16, MMA j = (m/4)%4, w0 = 4*(m%4) in [0,16):
+  // pairs (w0, w0+1) and (w0+2, w0+3) go to quad lanes tt and tt+1 of half w0/8
+  const int kb = m >> 4, j = (m >> 2) & 3, w0 = 4 * (m & 3);
+  const int tt = (w0 & 7) >> 1, hf = w0 >> 3;
+  const int i0 = ((kb * 4 + tt) * 4 + j) * 2 + hf;
+  uint32_t* xf = reinterpret_cast<uint32_t*>(sm + (size_t)v * a.KB * 128);
+  xf[i0] = *reinterpret_cast<const uint32_t*>(&h01);
+  xf[i0 + 8] = *reinterpret_cast<const uint32_t*>(&h23);
+}
+
+// Max |x| per vector over this thread's groups, then the block-wide
+// power-of-two scales (max|x| in [2^14, 2^15), exact in fp32).
+__device__ __forceinline__ void stage_scales(const PkArgs& a, float (&mx)[8], float* inv, float* s_scale,
+                                             float (*red)[kPkWarps], int warp, int lane) {
 #pragma unroll
   for (int v = 0; v < 8; ++v) {
 #pragma unroll
@@ -362,7 +366,6 @@ __device__ void stage_vectors(const PkArgs& a, uint8_t* sm, float* inv, int warp
     const int v = threadIdx.x;
     float m = red[v][0];
     for (int i = 1; i < kPkWarps; ++i) m = fmaxf(m, red[v][i]);
-    // power-of-two scale putting max|x| in [2^14, 2^15) (exact in fp32)
     const int ex = (int)((__float_as_uint(m) >> 23) & 255u);
     int sx = (m > 0.f && ex != 255) ? 14 - (ex - 127) : 0;
     sx = max(-126, min(126, sx));
@@ -370,40 +373,70 @@ __device__ void stage_vectors(const PkArgs& a, uint8_t* sm, float* inv, int warp
     inv[v] = __uint_as_float((uint32_t)(127 - sx) << 23);
   }
   __syncthreads();
-  float* X = reinterpret_cast<float*>(sm + (size_t)a.nv * a.KB * 128);
+}
+
+__device__ __forceinline__ void max_into(float (&mx)[8], int v, float4 f) {
+  const float m = fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w)));
+#pragma unroll
+  for (int w = 0; w < 8; ++w)
+    if (w == v) mx[w] = fmaxf(mx[w], m);
+}
+
+// Staging of all vectors: max |x| per vector, then scale, round to fp16,
+// permute into fragment order and sum per sub-block; two block barriers.  When
+// the vectors fit in kStageRegs groups per thread (the GPT-OSS shapes: 720 and
+// 2880 groups) the groups are loaded once and kept in registers for both
+// passes; otherwise each pass loads kStageU groups per thread at a time.
+// The eight groups of a 32-element sub-block sit on eight consecutive lanes
+// (vector length K4 is a multiple of 16 groups), so three shuffles sum it.
+constexpr int kStageU = 4, kStageRegs = 8;
+
+template <int MODE>
+__device__ void stage_vectors(const PkArgs& a, uint8_t* sm, float* inv, int warp, int lane) {
+  __shared__ float red[8][kPkWarps];
+  __shared__ float s_scale[8];
+  const int K4 = 16 * a.KB, total = a.nv * K4;
+  float mx[8];
+#pragma unroll
+  for (int v = 0; v < 8; ++v) mx[v] = 0.f;
+  if (total <= kStageRegs * kPkThreads) {
+    float4 f[kStageRegs];
+#pragma unroll
+    for (int u = 0; u < kStageRegs; ++u) f[u] = stage_load<MODE>(a, threadIdx.x + u * kPkThreads, K4, total);
+#pragma unroll
+    for (int u = 0; u < kStageRegs; ++u) {
+      const int q = threadIdx.x + u * kPkThreads;
+      if (q < total) max_into(mx, q / K4, f[u]);
+    }
+    stage_scales(a, mx, inv, s_scale, red, warp, lane);
+#pragma unroll
+    for (int u = 0; u < kStageRegs; ++u) {
+      if ((int)(threadIdx.x - lane) + u * kPkThreads >= total) break;  // warp-uniform
+      stage_store<MODE>(a, sm, s_scale, threadIdx.x + u * kPkThreads, K4, total, f[u], lane);
+    }
+    return;
+  }
+  for (int q0 = threadIdx.x; q0 < total; q0 += kStageU * kPkThreads) {
+    float4 f[kStageU];
+#pragma unroll
+    for (int u = 0; u < kStageU; ++u) f[u] = stage_load<MODE>(a, q0 + u * kPkThreads, K4, total);
+#pragma unroll
+    for (int u = 0; u < kStageU; ++u) {
+      const int q = q0 + u * kPkThreads;
+      if (q < total) max_into(mx, q / K4, f[u]);
+    }
+  }
+  stage_scales(a, mx, inv, s_scale, red, warp, lane);
   // all lanes stay in the loop for the shuffles (a sub-block's eight lanes are
   // all in range or all out)
   for (int q0 = threadIdx.x - lane; q0 < total; q0 += kStageU * kPkThreads) {
     float4 f[kStageU];
 #pragma unroll
-    for (int u = 0; u < kStageU; ++u) {
-      const int q = q0 + lane + u * kPkThreads;
-      const int v = q / K4;
-      f[u] = q < total ? vec4<MODE>(a, v, 4 * (q - v * K4)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    for (int u = 0; u < kStageU; ++u) f[u] = stage_load<MODE>(a, q0 + lane + u * kPkThreads, K4, total);
 #pragma unroll
     for (int u = 0; u < kStageU; ++u) {
-      const int q = q0 + lane + u * kPkThreads;
       if (q0 + u * kPkThreads >= total) break;  // warp-uniform
-      const int v = min(q / K4, a.nv - 1), m = q - v * K4;
-      const float sc = s_scale[v];
-      const __half2 h01 = __floats2half2_rn(f[u].x * sc, f[u].y * sc);
-      const __half2 h23 = __floats2half2_rn(f[u].z * sc, f[u].w * sc);
-      const float2 g01 = __half22float2(h01), g23 = __half22float2(h23);
-      float sum = (g01.x + g01.y) + (g23.x + g23.y);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-      if (q >= total) continue;
-      if ((lane & 7) == 0) X[(size_t)v * 2 * a.KB + (m >> 3)] = sum;
-      // k = 4m: k-block kb = m/16, MMA j = (m/4)%4, w0 = 4*(m%4) in [0,16):
-      // pairs (w0, w0+1) and (w0+2, w0+3) go to quad lanes tt and tt+1 of half w0/8
-      const int kb = m >> 4, j = (m >> 2) & 3, w0 = 4 * (m & 3);
-      const int tt = (w0 & 7) >> 1, hf = w0 >> 3;
-      const int i0 = ((kb * 4 + tt) * 4 + j) * 2 + hf;
-      uint32_t* xf = reinterpret_cast<uint32_t*>(sm + (size_t)v * a.KB * 128);
-      xf[i0] = *reinterpret_cast<const uint32_t*>(&h01);
-      xf[i0 + 8] = *reinterpret_cast<const uint32_t*>(&h23);
+      stage_store<MODE>(a, sm, s_scale, q0 + lane + u * kPkThreads, K4, total, f[u], lane);
     }
   }
 }
