@@ -450,7 +450,7 @@ __device__ void stage_vectors(const PkArgs& a, uint8_t* sm, float* inv, int warp
 __device__ void route_in_cta(const PkArgs& a, float* s_logit, int* s_e, float* s_w, int warp, int lane) {
   const int H = a.H, n8 = H / 8;
   const uint4* xr = static_cast<const uint4*>(a.x);
-  constexpr int kU = 8;
+  constexpr int kU = 12;  // 384 16-byte groups per pass: one pass for H <= 3072
   for (int e = warp; e < a.n_experts; e += kPkWarps) {
     const uint4* wr = reinterpret_cast<const uint4*>(a.router_w + (int64_t)e * H);
     float acc = 0.f;
@@ -513,6 +513,9 @@ __device__ void route_in_cta(const PkArgs& a, float* s_logit, int* s_e, float* s
         const_cast<float*>(a.wts)[k] = ex[k] / den;
       }
     }
+    // published before this CTA lets the down kernel launch, whose L2
+    // prefetch reads them (a hint; its real reads follow its PDL wait)
+    if (blockIdx.x == 0) __threadfence();
   }
 }
 
