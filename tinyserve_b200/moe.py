@@ -245,7 +245,7 @@ class DecodeSession:
 
     For a serving loop that feeds one token at a time from the host: each
     slot's graph copies the token from a pinned host buffer to the device, runs
-    the layer (router, gate/up, down: three PDL-chained launches) and copies
+    the layer (two or three PDL-chained launches: packed or generic decode) and copies
     the result back to a pinned host buffer, so a token costs one host row copy
     and one graph launch instead of five separately issued operations.
     `slots` buffers rotate so the host can fill the next token while earlier
