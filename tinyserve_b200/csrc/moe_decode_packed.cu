@@ -666,16 +666,21 @@ __global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkAr
     if (t == 0) {
       P[g] = acc_lo;
       P[g + 8] = acc_hi;
-      __threadfence();
     }
+    // The warp barrier orders the lanes' partial stores before lane 0's
+    // counter update; the update releases them at GPU scope (release is
+    // cumulative) and acquires the other tasks' partials for the last one.
     __syncwarp();
     const int slot = MODE == 0 ? u * a.R + rb : rb;
     const unsigned need = MODE == 0 ? (unsigned)a.S : (unsigned)(a.top_k * a.S);
     unsigned last = 0;
-    if (lane == 0) last = atomicAdd(a.cnt + slot, 1u) == need - 1;
+    if (lane == 0) {
+      unsigned old;
+      asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.cnt + slot) : "memory");
+      last = old == need - 1;
+    }
     last = __shfl_sync(0xffffffffu, last, 0);
     if (!last) continue;
-    __threadfence();
     if (MODE == 0) {
       const int j = 8 * rb + lane;
       if (lane < 8 && j < a.I) {
