@@ -577,6 +577,15 @@ __global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkAr
     pdl_wait();
   }
   if (!routed_here && threadIdx.x < a.top_k) s_e[threadIdx.x] = expert_of(threadIdx.x, true);
+  // bias pointers of the chosen experts, read once per CTA (the epilogues'
+  // only other dependent load)
+  __shared__ const float* s_bias[2][8];
+  if (threadIdx.x < a.top_k) {
+    const int e = s_e[threadIdx.x];
+    const TsbExpert* E = a.experts + (e < 0 ? 0 : e);
+    s_bias[0][threadIdx.x] = e < 0 ? nullptr : (MODE == 0 ? E->gate_bias : E->down_bias);
+    s_bias[1][threadIdx.x] = e < 0 ? nullptr : (MODE == 0 ? E->up_bias : nullptr);
+  }
   pdl_launch_dependents();
   if (MODE == 1) stage_vectors<1>(a, sm, inv, warp, lane);
   __syncthreads();
@@ -694,9 +703,8 @@ __global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkAr
         if (e >= 0) {
           gate *= inv[0];
           up *= inv[0];
-          const TsbExpert& E = a.experts[e];
-          if (E.gate_bias) gate += E.gate_bias[j];
-          if (E.up_bias) up += E.up_bias[j];
+          if (s_bias[0][u]) gate += s_bias[0][u][j];
+          if (s_bias[1][u]) up += s_bias[1][u][j];
           r = act_fn(a.act, gate, up, a.limit, a.alpha);
         }
         a.act_out[(int64_t)u * a.I + j] = r;
@@ -728,7 +736,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkAr
         for (int k = 0; k < a.top_k; ++k) {
           const int ek = s_e[k];
           if (ek < 0) continue;
-          const float* bias = a.experts[ek].down_bias;
+          const float* bias = s_bias[0][k];
           if (bias) o = fmaf(a.wts[k], bias[h], o);
         }
         a.out[h] = f32_to_bf16_bits(o);
