@@ -96,3 +96,26 @@ def test_packed_bytes_query():
     assert L.tsb_moe_packed_bytes(ctypes.byref(mx)) == 0
     odd = _lib.TsbMoeSpec(12, 12, 2880, 2880 + 32, 32, 4, _lib.GU_SEPARATE, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
     assert L.tsb_moe_packed_bytes(ctypes.byref(odd)) == 0
+
+
+def test_packed_entry_points_validate_on_the_host():
+    """tsb_moe_pack refuses specs without a packed form and short buffers
+    before touching the device; the packed decode workspace holds the generic
+    one plus the partial-sum scratch."""
+    import ctypes
+    L = _lib.lib()
+    mx = _lib.TsbMoeSpec(39, 39, 2880, 2880, 32, 4, _lib.GU_INTERLEAVED, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
+    buf = ctypes.create_string_buffer(512)
+    rc = L.tsb_moe_pack(ctypes.byref(mx), 256, 256, 1 << 20, None)
+    assert rc != 0
+    L.tsb_last_error(buf, 512)
+    assert b"no packed form" in buf.value
+    q4 = _lib.TsbMoeSpec(12, 12, 2880, 2880, 32, 4, _lib.GU_SEPARATE, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
+    need = L.tsb_moe_packed_bytes(ctypes.byref(q4))
+    rc = L.tsb_moe_pack(ctypes.byref(q4), 256, 256, need - 1, None)
+    assert rc != 0
+    L.tsb_last_error(buf, 512)
+    assert b"too small" in buf.value
+    assert L.tsb_moe_decode_packed_workspace(ctypes.byref(q4), 1) > L.tsb_moe_decode_workspace(ctypes.byref(q4), 1)
+    # T > 16 takes the grouped path: same workspace as tsb_moe_decode
+    assert L.tsb_moe_decode_packed_workspace(ctypes.byref(q4), 64) == L.tsb_moe_decode_workspace(ctypes.byref(q4), 64)
