@@ -73,6 +73,9 @@ typedef struct {
   int32_t activation;  /* TSB_ACT_* */
   float limit;         /* SwiGLU clamp (7.0 for GPT-OSS) */
   float alpha;         /* SwiGLU sigmoid slope (1.702 for GPT-OSS) */
+  int32_t out_f32;     /* 0: layer output `out` is bf16 [T, H]; 1: fp32 [T, H] (the
+                          unrounded combine, for callers that keep the residual stream
+                          in fp32 and for exact parity checks) */
 } TsbMoeSpec;
 
 /* One expert's weights (device pointers).  Weights are raw GGUF block streams
@@ -131,7 +134,8 @@ size_t tsb_moe_decode_workspace(const TsbMoeSpec* spec, int32_t T);
  *   router_b  fp32 [E] or NULL
  *   ids       int32 [T, top_k]  (output if router_w != NULL, else input)
  *   weights   fp32  [T, top_k]  (same)
- *   out       bf16 [T, H] = sum_k weights[t,k] * expert_{ids[t,k]}(x[t]) */
+ *   out       [T, H] = sum_k weights[t,k] * expert_{ids[t,k]}(x[t]), bf16, or
+ *             fp32 when spec->out_f32 is set */
 int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void* x, int32_t T,
                    const void* router_w, const float* router_b, int32_t* ids, float* weights, void* out,
                    void* workspace, size_t workspace_bytes, void* stream);
@@ -181,23 +185,30 @@ int tsb_moe_decode_noalloc(const TsbMoeSpec* spec, const TsbExpert* experts, con
                            const void* router_w, const float* router_b, int32_t* ids, float* weights, void* out,
                            void* stream);
 
-/* ---- decode-packed experts (batch-1 decode of Q4_K layers) ----------------
- * A one-time repack of all E experts' Q4_K gate/up/down streams into the
- * order the decode kernels' tensor-core fragments read, with each 32-element
- * sub-block's scale products d*sc and dmin*m precomputed in fp32 (768 bytes
- * per 16 rows x 64 columns: 1.33x the Q4_K bytes).  Replaces, for HBM-resident
- * layers, the per-call GGUF decode of ggml_mul_mat_vec
- * (tinyserve/ggml_forward.py:40-62) inside ExpertPipeline.execute_layer_experts
- * (tinyserve/expert_pipeline.py:140-164); results equal tsb_moe_decode's within
- * the fp32 summation order.
+/* ---- decode-packed experts (batch-1 decode of Q4_K and MXFP4 layers) -----
+ * A one-time repack of all E experts' gate/up/down streams into units of 16
+ * rows x 256 columns in the order the decode kernel's tensor-core fragments
+ * read them (Q4_K: rows grouped by superblock phase so every unit is one
+ * source superblock per row, scales widened to bytes, ~1.03x the Q4_K bytes
+ * plus the superblocks that straddle two rows; MXFP4: exactly the MXFP4
+ * bytes).  Replaces, for HBM-resident layers, the per-call GGUF decode of
+ * ggml_mul_mat_vec (tinyserve/ggml_forward.py:40-62) and the MXFP4 vecmat
+ * dot_scaled_vecmat (tinyserve/triton_dot_scaled.py:68-122) inside
+ * ExpertPipeline.execute_layer_experts (tinyserve/expert_pipeline.py:140-164);
+ * results equal tsb_moe_decode's within the fp32 summation order.
  * tsb_moe_packed_bytes: size of the packed copy, 0 when the spec has no packed
- *   form (needs Q4_K gate/up and down, H and I multiples of 64, top_k <= 8).
+ *   form (needs Q4_K gate/up and down, or MXFP4 gate/up and down; H and I
+ *   multiples of 32 and at most 16384; top_k <= 8).
  * tsb_moe_pack: writes it (experts: device array of E TsbExpert, as for
- *   tsb_moe_decode); stream-ordered, run once per weight set.
+ *   tsb_moe_decode); run once per weight set; returns after the row maps are
+ *   on the device (the repack itself is stream-ordered).
  * tsb_moe_decode_packed: tsb_moe_decode's contract (T tokens, optional router,
- *   ids/weights in or out) on the packed copy; `experts` supplies the biases
- *   (and the raw streams for T > 16, which take the grouped path).  Workspace
- *   from tsb_moe_decode_packed_workspace, zero-initialised once. */
+ *   ids/weights in or out, bf16 or fp32 output) on the packed copy: one
+ *   cooperative launch per token (routing, gate/up, activation, down,
+ *   combine); `experts` supplies the biases (and the raw streams for T > 16,
+ *   which take the grouped path).  Workspace from
+ *   tsb_moe_decode_packed_workspace, zero-initialised once; after a non-zero
+ *   device error (tsb_read_device_error) zero it again. */
 size_t tsb_moe_packed_bytes(const TsbMoeSpec* spec);
 int tsb_moe_pack(const TsbMoeSpec* spec, const TsbExpert* experts, void* packed, size_t packed_bytes, void* stream);
 size_t tsb_moe_decode_packed_workspace(const TsbMoeSpec* spec, int32_t T);

@@ -45,3 +45,25 @@ def bits_equal_f32(a: np.ndarray, b: np.ndarray) -> bool:
     b = np.ascontiguousarray(b, dtype=np.float32)
     same = a.view(np.uint32) == b.view(np.uint32)
     return bool((same | (np.isnan(a) & np.isnan(b))).all())
+
+
+def layer_bound(out, ref, tol: float = 1e-3) -> float:
+    """Relative-L2 bound for a layer output against float64 oracle math: the
+    north-star 1e-3 for fp32 outputs; for bf16 outputs the rounding of the
+    output itself (rel_l2(bf16(ref), ref), about 1.1e-3) plus 1e-3, so a kernel
+    with more than 1e-3 of its own error fails either way."""
+    if out.dtype == torch.bfloat16:
+        from oracle.expert import bf16_round
+        r = np.asarray(ref, dtype=np.float64)
+        return rel_l2(bf16_round(r.astype(np.float32)), r) + tol
+    return tol
+
+
+def assert_layer(out, ref, tol: float = 1e-3) -> float:
+    """Assert a layer output tensor (bf16 or fp32, any device) is within
+    layer_bound of the oracle reference; returns the measured error."""
+    got = out.float().cpu().numpy()
+    err = rel_l2(got, ref)
+    bound = layer_bound(out, ref, tol)
+    assert err <= bound, f"relative L2 {err:.3e} > {bound:.3e} ({out.dtype})"
+    return err

@@ -9,12 +9,11 @@ import pytest
 import torch
 
 from oracle import expert as OE
-from tests.helpers import rel_l2
+from tests.helpers import assert_layer, rel_l2
 from tests.test_kernels_gpu import _build_layer
 from tests.test_prefill_gpu import _oracle
 from tinyserve_b200.formats import GGML_Q4_K, GGML_Q8_0, TSB_MXFP4
 
-TOL = 1e-3 + 4e-3
 
 pytestmark = pytest.mark.gpu
 
@@ -41,7 +40,7 @@ def test_decode_several_tokens_with_router(dev, fmt, layout, T):
             srt = np.sort(lg[t])[::-1]
             assert abs(srt[k - 1] - srt[k]) <= 1e-2 * abs(srt[k - 1]) + 1e-6
     ref = _oracle(x.float().numpy(), ids_g, wts.cpu().numpy(), dense)
-    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert_layer(out, ref)
     assert layer.device_error(T) == 0
 
 
@@ -64,8 +63,8 @@ def test_batcher_matches_per_request_decode(dev):
                                             it.routing_weights.reshape(1, -1))
         ref = _oracle(it.hidden_states.float().cpu().numpy(), it.expert_indices.cpu().numpy().reshape(1, -1),
                       it.routing_weights.float().cpu().numpy().reshape(1, -1), dense)
-        assert rel_l2(o.float().cpu().numpy(), ref) <= TOL
-        assert rel_l2(single.float().cpu().numpy(), ref) <= TOL
+        assert_layer(o, ref)
+        assert_layer(single, ref)
     assert pipe.execute_batched_experts([], 3) == []
 
 
@@ -79,7 +78,7 @@ def test_pipeline_batched_prefill_api(dev):
     x = torch.randn(T, H, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
     out = pipe.execute_layer_experts_batched(x.to(dev), 0, ids.to(dev), wts.to(dev))
     ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
-    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert_layer(out, ref)
     assert pipe.execute_layer_experts_batched(x[:0].to(dev), 0, ids[:0], wts[:0]).shape == (0, H)
     assert pipe.schedule_prefetch(0, [1, 2]) is None
 

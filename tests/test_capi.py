@@ -79,23 +79,56 @@ def test_moe_decode_argument_checks():
     assert rc == _lib.TSB_ERR_WORKSPACE
 
 
+def _packed_bytes_expected(fmt, H, I, E, layout):
+    """Host restatement of the decode-packed geometry: gate/up j-groups of 16
+    outputs whose gate rows share a Q4_K superblock phase and whose up rows
+    share one (MXFP4: phase 0), down groups of 32 rows of one phase; units of
+    16 rows x 256 columns (Q4_K 2368 bytes, MXFP4 2176), C chunks per row
+    block = ceil((K/32 + max phase) / 8); row maps first, 256-byte aligned."""
+    al = lambda v: (v + 255) // 256 * 256  # noqa: E731
+    q4 = fmt == 12
+    phase = (lambda r, K: (r * K % 256) // 32) if q4 else (lambda r, K: 0)
+    gate_row = (lambda j: 2 * j) if layout == _lib.GU_INTERLEAVED else (lambda j: j)
+    up_row = {_lib.GU_INTERLEAVED: lambda j: 2 * j + 1, _lib.GU_CHUNKED: lambda j: I + j}.get(layout, lambda j: j)
+    keys = {}
+    for j in range(I):
+        keys.setdefault((phase(gate_row(j), H), phase(up_row(j), H)), []).append(j)
+    ngj = sum((len(v) + 15) // 16 for v in keys.values())
+    pmax = max(max(k) for k in keys)
+    c_gu = (H // 32 + pmax + 7) // 8
+    dk = {}
+    for h in range(H):
+        dk.setdefault(phase(h, I), []).append(h)
+    ndp = sum((len(v) + 31) // 32 for v in dk.values())
+    c_dn = (I // 32 + max(dk) + 7) // 8
+    unit = 2368 if q4 else 2176
+    maps = al(al(al(al(4 * 16 * ngj) + 4 * 2 * ngj) + 4 * 32 * ndp) + 4 * ndp)
+    expert = al((ngj * c_gu * 2 + ndp * c_dn * 2) * unit)
+    return maps + E * expert, expert
+
+
 def test_packed_bytes_query():
-    """tsb_moe_packed_bytes is host arithmetic: 768 bytes per (16 rows, 64
-    columns) unit for gate/up (8 outputs x 2 rows per block) and down, padded
-    to 256 bytes per expert; 0 for specs without a packed form."""
+    """tsb_moe_packed_bytes is host arithmetic (see _packed_bytes_expected);
+    0 for specs without a packed form."""
     import ctypes
     L = _lib.lib()
     H = I = 2880
-    spec = _lib.TsbMoeSpec(12, 12, H, I, 32, 4, _lib.GU_SEPARATE, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
-    per = (I // 8) * (H // 64) * 768 + (H // 16) * (I // 64) * 768
-    per = (per + 255) // 256 * 256
-    assert L.tsb_moe_packed_bytes(ctypes.byref(spec)) == 32 * per
-    q4k = 3 * I * H // 256 * 144
-    assert abs(per / q4k - 4 / 3) < 0.01
-    mx = _lib.TsbMoeSpec(39, 39, H, I, 32, 4, _lib.GU_INTERLEAVED, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
-    assert L.tsb_moe_packed_bytes(ctypes.byref(mx)) == 0
-    odd = _lib.TsbMoeSpec(12, 12, 2880, 2880 + 32, 32, 4, _lib.GU_SEPARATE, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
-    assert L.tsb_moe_packed_bytes(ctypes.byref(odd)) == 0
+    for fmt, layout in ((12, _lib.GU_SEPARATE), (12, _lib.GU_INTERLEAVED), (12, _lib.GU_CHUNKED),
+                        (39, _lib.GU_INTERLEAVED)):
+        spec = _lib.TsbMoeSpec(fmt, fmt, H, I, 32, 4, layout, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
+        total, expert = _packed_bytes_expected(fmt, H, I, 32, layout)
+        assert L.tsb_moe_packed_bytes(ctypes.byref(spec)) == total
+        raw = 3 * I * H // 256 * 144 if fmt == 12 else 3 * I * H * 17 // 32
+        assert 1.0 <= expert / raw < 1.11  # superblocks straddling rows, chunk and row padding
+    # K % 256 == 0: one phase, whole chunks: only the header overhead is left
+    spec = _lib.TsbMoeSpec(12, 12, 4096, 2048, 8, 2, _lib.GU_SEPARATE, _lib.ACT_SILU, 7.0, 1.702)
+    total, expert = _packed_bytes_expected(12, 4096, 2048, 8, _lib.GU_SEPARATE)
+    assert L.tsb_moe_packed_bytes(ctypes.byref(spec)) == total
+    assert abs(expert / (3 * 4096 * 2048 // 256 * 144) - 2368 / 2304) < 1e-3
+    mixed = _lib.TsbMoeSpec(12, 8, H, I, 32, 4, _lib.GU_SEPARATE, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
+    assert L.tsb_moe_packed_bytes(ctypes.byref(mixed)) == 0
+    q8 = _lib.TsbMoeSpec(8, 8, H, I, 32, 4, _lib.GU_SEPARATE, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
+    assert L.tsb_moe_packed_bytes(ctypes.byref(q8)) == 0
 
 
 def test_packed_entry_points_validate_on_the_host():
@@ -104,9 +137,9 @@ def test_packed_entry_points_validate_on_the_host():
     one plus the partial-sum scratch."""
     import ctypes
     L = _lib.lib()
-    mx = _lib.TsbMoeSpec(39, 39, 2880, 2880, 32, 4, _lib.GU_INTERLEAVED, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
+    q6 = _lib.TsbMoeSpec(14, 14, 2880, 2880, 32, 4, _lib.GU_SEPARATE, _lib.ACT_SWIGLU_OAI, 7.0, 1.702)
     buf = ctypes.create_string_buffer(512)
-    rc = L.tsb_moe_pack(ctypes.byref(mx), 256, 256, 1 << 20, None)
+    rc = L.tsb_moe_pack(ctypes.byref(q6), 256, 256, 1 << 20, None)
     assert rc != 0
     L.tsb_last_error(buf, 512)
     assert b"no packed form" in buf.value

@@ -5,8 +5,9 @@ The reference's batched path groups tokens by expert and runs one expert
 forward per group (tinyserve/expert_pipeline.py:166-239); its tests check the
 grouped result against the per-token loop (tests/test_batched_prefill.py:52-119).
 Here every case is checked against the exact per-token sum.  Products run in
-fp16 with fp32 accumulation, so the layer math stays within 1e-3 relative L2;
-the bf16 output adds its own rounding (4e-3), as for decode.
+fp16 with fp32 accumulation, so the layer math stays within 1e-3 relative L2
+(fp32 outputs); bf16 outputs may add their own rounding on top of the 1e-3
+(tests.helpers.layer_bound).
 """
 from __future__ import annotations
 
@@ -15,11 +16,9 @@ import pytest
 import torch
 
 from oracle import expert as OE
-from tests.helpers import rel_l2
+from tests.helpers import assert_layer, rel_l2
 from tests.test_kernels_gpu import _build_layer
 from tinyserve_b200.formats import GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_Q8_0, TSB_MXFP4
-
-TOL = 1e-3 + 4e-3
 
 pytestmark = pytest.mark.gpu
 
@@ -65,7 +64,7 @@ def test_prefill_layer_formats(dev, fmt_gu, fmt_dn, layout):
     out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
     torch.cuda.synchronize()
     ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
-    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert_layer(out, ref)
     assert layer.prefill_error(T) == 0
 
 
@@ -80,7 +79,7 @@ def test_prefill_gpt_oss_shape_with_bias(dev):
     out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
     torch.cuda.synchronize()
     ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
-    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert_layer(out, ref)
     per_tok = np.linalg.norm(out.float().cpu().numpy() - ref, axis=1) / np.linalg.norm(ref, axis=1)
     assert per_tok.max() <= 3e-2
 
@@ -98,7 +97,7 @@ def test_prefill_router_matches_oracle_routing(dev):
             srt = np.sort(lg[t])[::-1]
             assert abs(srt[k - 1] - srt[k]) <= 1e-2 * abs(srt[k - 1]) + 1e-6, "routing differs away from a tie"
     ref = _oracle(x.float().numpy(), ids_g, wts.cpu().numpy(), dense)
-    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert_layer(out, ref)
 
 
 def test_prefill_one_token_matches_decode(dev):
@@ -109,7 +108,7 @@ def test_prefill_one_token_matches_decode(dev):
     o2, ids2, w2 = layer.prefill(x)
     torch.cuda.synchronize()
     assert torch.equal(ids1.cpu(), ids2.cpu())
-    assert rel_l2(o2.float().cpu().numpy(), o1.float().cpu().numpy()) <= 2 * TOL
+    assert rel_l2(o2.float().cpu().numpy(), o1.float().cpu().numpy()) <= 4e-3
 
 
 def test_prefill_unused_experts_and_all_to_one(dev):
@@ -121,7 +120,7 @@ def test_prefill_unused_experts_and_all_to_one(dev):
     x = torch.randn(T, H, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16)
     out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
     ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
-    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert_layer(out, ref)
 
 
 def test_prefill_row_scaling_wide_dynamic_range(dev):
@@ -162,7 +161,7 @@ def test_prefill_bad_ids_reported(dev):
     torch.cuda.synchronize()
     assert layer.prefill_error(T) == 2
     ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
-    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert_layer(out, ref)
     assert layer.prefill_error(T) == 0
 
 
@@ -176,7 +175,7 @@ def test_prefill_mxfp4_half_k_blocks(dev, layout):
     x = torch.randn(T, H, generator=torch.Generator().manual_seed(11)).to(torch.bfloat16)
     out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
     ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
-    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert_layer(out, ref)
 
 
 def test_prefill_mxfp4_extreme_scales(dev):
@@ -203,7 +202,7 @@ def test_prefill_mxfp4_extreme_scales(dev):
     x = (torch.randn(T, H, generator=torch.Generator().manual_seed(12)) * 1e-3).to(torch.bfloat16)
     out, _, _ = layer.prefill(x.to(dev), ids=ids, weights=wts)
     ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
-    assert rel_l2(out.float().cpu().numpy(), ref) <= TOL
+    assert_layer(out, ref)
 
 
 def test_prefill_mxfp4_tiled_decode_subprocess(dev):
@@ -232,3 +231,47 @@ def test_prefill_cta_pair_subprocess(dev):
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", __file__, "-k", "not subprocess"],
                        env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("fmt_gu,layout", [(GGML_Q4_K, "separate"), (TSB_MXFP4, "interleaved")])
+def test_prefill_fp32_output(dev, fmt_gu, layout):
+    """fp32 output: the grouped layer itself within the north-star 1e-3."""
+    H, I, E, k, T = 1024, 512, 8, 4, 200
+    layer, dense, _ = _build_layer(dev, fmt_gu, fmt_gu, H, I, E, k, layout, seed=61)
+    ids, wts = _routing(T, E, k, seed=5)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(61)).to(torch.bfloat16)
+    out, _, _ = layer.prefill(x.to(dev), ids=ids.to(dev), weights=wts.to(dev), out_dtype=torch.float32)
+    assert out.dtype == torch.float32
+    ref = _oracle(x.float().numpy(), ids.numpy(), wts.numpy(), dense)
+    assert_layer(out, ref)
+
+
+def test_prefill_config4_full_shape(dev):
+    """BASELINE config 4 as bench.py runs it: the GPT-OSS-20B-shaped MXFP4
+    layer (32 experts, H = I = 2880, interleaved gate/up) from
+    workloads.build_layer, 4096 tokens with top-4 Zipf(1.1) routing, on the
+    path the bench takes (tiled weights).  The whole output is computed on the
+    GPU; the oracle checks a seeded sample of 256 tokens (fp32 output, 1e-3)."""
+    from tests.helpers import oracle_dequant
+    from tinyserve_b200.workloads import build_layer, hidden_states, zipf_routing
+    T = 4096
+    layer = build_layer(TSB_MXFP4, seed=4, device=dev)
+    ids, wts = zipf_routing(T, 32, 4, seed=0)
+    x = hidden_states(T, seed=4, device=dev)
+    out, _, _ = layer.prefill(x, ids=ids.to(dev), weights=wts.to(dev), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert layer.prefill_error(T) == 0
+    sample = np.sort(np.random.default_rng(0).choice(T, 256, replace=False))
+    xs = x.cpu().float().numpy()[sample]
+    idl, wl = ids.numpy()[sample], wts.numpy()[sample]
+    dense = {}
+    for e in np.unique(idl):
+        ex = layer.experts[int(e)]
+        gu = oracle_dequant(TSB_MXFP4, ex.gate.cpu(), ex.gate_scales.cpu(), 2 * 2880, 2880)
+        wd = oracle_dequant(TSB_MXFP4, ex.down.cpu(), ex.down_scales.cpu(), 2880, 2880)
+        dense[int(e)] = (gu[0::2], gu[1::2], wd, None, None, None)
+    ref = np.zeros_like(xs, dtype=np.float64)
+    for e, (wg, wu, wd, _, _, _) in dense.items():
+        tok, kk = np.nonzero(idl == e)
+        ref[tok] += wl[tok, kk][:, None] * OE.expert_forward(xs[tok], wg, wu, wd)
+    assert_layer(out[torch.from_numpy(sample).to(dev)], ref)

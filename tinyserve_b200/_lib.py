@@ -41,6 +41,7 @@ class TsbMoeSpec(ctypes.Structure):
         ("n_experts", ctypes.c_int32), ("top_k", ctypes.c_int32),
         ("gate_up_layout", ctypes.c_int32), ("activation", ctypes.c_int32),
         ("limit", ctypes.c_float), ("alpha", ctypes.c_float),
+        ("out_f32", ctypes.c_int32),
     ]
 
 

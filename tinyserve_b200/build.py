@@ -2,10 +2,14 @@
 
 Compiles every ``csrc/*.cu`` for sm_100a with nvcc and links one shared
 library.  Run ``python -m tinyserve_b200.build`` (or ``__graft_entry__.build()``).
-Rebuilds only when a source is newer than the library.
+Rebuild decisions are keyed on content, not timestamps: each object carries a
+hash of its source, every header it can include and the compiler flags, and the
+library a hash of its objects' keys, so an edited source is never served by a
+stale library (and an unchanged tree is not rebuilt after a checkout).
 """
 from __future__ import annotations
 
+import hashlib
 import os
 import shutil
 import subprocess
@@ -20,7 +24,7 @@ BUILD = PKG / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
-              "-Xptxas", "-v"] + ARCH
+              "-Xptxas", "-v"] + ARCH + os.environ.get("TSB_NVCC_EXTRA", "").split()
 
 
 def _nvcc() -> str:
@@ -34,22 +38,55 @@ def sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
 
+def _headers_digest() -> str:
+    h = hashlib.sha256()
+    for p in sorted(list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))):
+        h.update(p.name.encode())
+        h.update(p.read_bytes())
+    return h.hexdigest()
+
+
+def _obj_key(src: Path, headers: str) -> str:
+    h = hashlib.sha256()
+    h.update(src.read_bytes())
+    h.update(headers.encode())
+    h.update(" ".join(NVCC_FLAGS).encode())
+    return h.hexdigest()
+
+
+def _lib_key(keys: list[str]) -> str:
+    return hashlib.sha256(("|".join(keys) + " ".join(ARCH)).encode()).hexdigest()
+
+
+def _stamp(p: Path) -> Path:
+    return p.with_name(p.name + ".key")
+
+
+def _read(p: Path) -> str:
+    return p.read_text().strip() if p.exists() else ""
+
+
 def _stale() -> bool:
     if not LIB.exists():
         return True
-    t = LIB.stat().st_mtime
-    deps = list(CSRC.glob("*")) + list(INCLUDE.glob("*.h"))
-    return any(p.stat().st_mtime > t for p in deps)
+    headers = _headers_digest()
+    return _read(_stamp(LIB)) != _lib_key([_obj_key(s, headers) for s in sources()])
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not _stale():
+    headers = _headers_digest()
+    keys = [_obj_key(s, headers) for s in sources()]
+    lib_key = _lib_key(keys)
+    if not force and LIB.exists() and _read(_stamp(LIB)) == lib_key:
         return LIB
     BUILD.mkdir(exist_ok=True)
     nvcc = _nvcc()
     objs = []
-    for src in sources():
+    for src, key in zip(sources(), keys):
         obj = BUILD / (src.stem + ".o")
+        objs.append(str(obj))
+        if not force and obj.exists() and _read(_stamp(obj)) == key:
+            continue
         cmd = [nvcc, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if verbose or r.returncode:
@@ -57,7 +94,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         if r.returncode:
             raise RuntimeError(f"nvcc failed on {src.name}")
         (BUILD / (src.stem + ".ptxas.txt")).write_text(r.stderr)
-        objs.append(str(obj))
+        _stamp(obj).write_text(key)
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc, "-shared", *ARCH, "-o", str(tmp), *objs, "-lcudart"]
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -65,6 +102,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         sys.stderr.write(r.stdout + r.stderr)
         raise RuntimeError("link of libtsb_moe.so failed")
     os.replace(tmp, LIB)
+    _stamp(LIB).write_text(lib_key)
     return LIB
 
 

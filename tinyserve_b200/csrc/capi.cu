@@ -147,6 +147,9 @@ int tsb_quant_matvec(int fmt, const void* w, const void* scales, int64_t N, int6
   return TSB_OK;
 }
 
+// Bytes per element of the layer output (bf16, or fp32 with spec.out_f32).
+static int64_t out_elem(const TsbMoeSpec& sp) { return sp.out_f32 ? 4 : 2; }
+
 // Validation shared by the batch-1 decode entry points.
 static int check_decode_spec(const TsbMoeSpec& sp, const void* router_w) {
   if (sp.top_k < 1 || sp.top_k > 8 || sp.top_k > sp.n_experts) return set_error(TSB_ERR_INVALID, "top_k must be in [1, min(8, E)]");
@@ -156,6 +159,7 @@ static int check_decode_spec(const TsbMoeSpec& sp, const void* router_w) {
   if (router_w && sp.hidden % 8) return set_error(TSB_ERR_INVALID, "hidden must be a multiple of 8 for the router");
   if (sp.gate_up_layout < 0 || sp.gate_up_layout > 2) return set_error(TSB_ERR_INVALID, "bad gate_up_layout");
   if (sp.activation < 0 || sp.activation > 1) return set_error(TSB_ERR_INVALID, "bad activation");
+  if (sp.out_f32 != 0 && sp.out_f32 != 1) return set_error(TSB_ERR_INVALID, "out_f32 must be 0 or 1");
   const int rc = check_shape(sp.fmt_gate_up, sp.inter, sp.hidden);
   if (rc) return rc;
   return check_shape(sp.fmt_down, sp.hidden, sp.inter);
@@ -188,8 +192,8 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
     const int64_t H = spec->hidden, k = spec->top_k;
     for (int t = 0; t < T; ++t) {
       const int rc = tsb_moe_decode(spec, experts, static_cast<const uint16_t*>(x) + t * H, 1, router_w, router_b,
-                                    ids + t * k, weights + t * k, static_cast<uint16_t*>(out) + t * H, workspace,
-                                    workspace_bytes, stream);
+                                    ids + t * k, weights + t * k, static_cast<char*>(out) + t * H * out_elem(sp),
+                                    workspace, workspace_bytes, stream);
       if (rc) return rc;
     }
     return TSB_OK;
@@ -217,13 +221,14 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
 
 size_t tsb_moe_packed_bytes(const TsbMoeSpec* spec) {
   if (!spec || !packable(*spec)) return 0;
-  return (size_t)pack_geom(*spec).expert_bytes * (size_t)spec->n_experts;
+  return packed_total_bytes(*spec);
 }
 
 int tsb_moe_pack(const TsbMoeSpec* spec, const TsbExpert* experts, void* packed, size_t packed_bytes, void* stream) {
   if (!spec || !experts || !packed) return set_error(TSB_ERR_INVALID, "null pointer");
   const TsbMoeSpec& sp = *spec;
-  if (!packable(sp)) return set_error(TSB_ERR_UNSUPPORTED, "no packed form: needs Q4_K gate/up and down, H and I multiples of 64");
+  if (!packable(sp))
+    return set_error(TSB_ERR_UNSUPPORTED, "no packed form: needs Q4_K or MXFP4 gate/up and down, H and I multiples of 32 up to 16384");
   int rc = check_decode_spec(sp, nullptr);
   if (rc) return rc;
   if (packed_bytes < tsb_moe_packed_bytes(spec)) return set_error(TSB_ERR_WORKSPACE, "packed buffer too small");
@@ -251,8 +256,9 @@ int tsb_moe_decode_packed(const TsbMoeSpec* spec, const void* packed, const TsbE
     const int64_t H = sp.hidden, k = sp.top_k;
     for (int t = 0; t < T; ++t) {
       const int rc = tsb_moe_decode_packed(spec, packed, experts, static_cast<const uint16_t*>(x) + t * H, 1, router_w,
-                                           router_b, ids + t * k, weights + t * k, static_cast<uint16_t*>(out) + t * H,
-                                           workspace, workspace_bytes, stream);
+                                           router_b, ids + t * k, weights + t * k,
+                                           static_cast<char*>(out) + t * H * out_elem(sp), workspace,
+                                           workspace_bytes, stream);
       if (rc) return rc;
     }
     return TSB_OK;
@@ -268,8 +274,8 @@ int tsb_moe_decode_packed(const TsbMoeSpec* spec, const void* packed, const TsbE
   float* act = reinterpret_cast<float*>(ws + L.act);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // with router weights, routing runs inside the gate/up launch
-  return launch_packed_decode(sp, packed, experts, x, ids, weights, act, out, err, ws + L.total, st, router_w,
-                              router_b);
+  return launch_packed_decode(sp, packed, experts, x, ids, weights, act, out, sp.out_f32 != 0, err, ws + L.total, st,
+                              router_w, router_b);
 }
 
 int tsb_read_device_error(void* workspace, int32_t* code, void* stream) {
@@ -316,6 +322,7 @@ int tsb_moe_prefill(const TsbMoeSpec* spec, const TsbExpert* experts, const void
     return set_error(TSB_ERR_INVALID, "hidden and inter must be positive multiples of 32");
   if (sp.gate_up_layout < 0 || sp.gate_up_layout > 2) return set_error(TSB_ERR_INVALID, "bad gate_up_layout");
   if (sp.activation < 0 || sp.activation > 1) return set_error(TSB_ERR_INVALID, "bad activation");
+  if (sp.out_f32 != 0 && sp.out_f32 != 1) return set_error(TSB_ERR_INVALID, "out_f32 must be 0 or 1");
   if ((int64_t)T * sp.top_k > (int64_t)1 << 26) return set_error(TSB_ERR_UNSUPPORTED, "T * top_k too large");
   int rc = check_shape(sp.fmt_gate_up, sp.inter, sp.hidden);
   if (rc) return rc;

@@ -191,7 +191,8 @@ struct PlanDownT1 {
   int top_k, rpe, H, I;
   const float* act;  // [top_k, I]
   int act_cg;        // act written by other CTAs of this grid: load through L2 (0 here)
-  uint16_t* out;     // bf16 [H]
+  void* out;         // [H], bf16 or fp32 (out_f32)
+  int out_f32;
   int64_t dn_bytes;
 
   __device__ int num_vectors() const { return top_k; }
@@ -242,7 +243,10 @@ struct PlanDownT1 {
       if (C.b[0]) v += C.b[0][h];
       o = fmaf(wts[k], v, o);
     }
-    out[h] = f32_to_bf16_bits(o);
+    if (out_f32)
+      static_cast<float*>(out)[h] = o;
+    else
+      static_cast<uint16_t*>(out)[h] = f32_to_bf16_bits(o);
   }
 };
 
@@ -544,7 +548,8 @@ static int down_t(const TsbMoeSpec& sp, const TsbExpert* ex, const int32_t* ids,
   p.H = sp.hidden;
   p.I = sp.inter;
   p.act = act;
-  p.out = static_cast<uint16_t*>(out);
+  p.out = out;
+  p.out_f32 = sp.out_f32 != 0;
   int64_t db, sb;
   weight_bytes_of(F, sp.hidden, sp.inter, db, sb);
   p.dn_bytes = db;

@@ -1,38 +1,51 @@
-// Batch-1 MoE decode on a decode-packed copy of 4-bit K-quant experts.
+// Batch-1 MoE decode, one persistent launch per token-layer, on a decode-packed
+// copy of the experts (Q4_K or MXFP4).
 //
-// The generic decode engine reads the GGUF block stream as stored
-// (tinyserve/gguf_dequant_torch.py:180-205): with K % 256 != 0 rows start at
-// different superblock phases and every 32-element step rebuilds its scale
-// from the 12-byte packed scales, which costs ~120 instructions per 512
-// weights.  Here the experts are repacked once (tsb_moe_pack) into the order
-// the tensor-core fragments consume, with each (row, 32-element sub-block)'s
-// fold coefficients already formed, so the inner loop is a shared-memory
-// read, a handful of bit operations, four MMAs and eight FMAs per 1024 weights.
+// Packed unit = one row block (16 rows of one projection) x one chunk of 256
+// columns.  Its codes are laid out so that one 128-bit shared-memory load
+// gives a lane the A fragments of four mma.m16n8k16 (f16 in, f32 out), and the
+// eight 32-element sub-blocks of the chunk are spread over the MMA's eight N
+// columns: the B operand holds the activation vector "diagonally" (column n
+// sees only sub-block n's elements), so after the chunk's 16 MMAs the
+// accumulator holds, per row, the eight per-sub-block dot products.  The
+// per-(row, sub-block) scale fold therefore runs once per 4096 weights rather
+// than once per MMA.
 //
-// Packed unit: one 16-row block x one 64-element k-block = 768 bytes
-//   [0, 512)    codes: lane L (g = L/4, t = L%4) owns 16 bytes = 32 codes in
-//               mma.m16n8k16 A-fragment order (see pack_unit_kernel)
-//   [512, 768)  fold coefficients: for sub-block sb (0, 1) and row pair g,
-//               float4 (s_g, s_g+8, o_g, o_g+8) at 512 + 128 sb + 16 g
-// A row's contribution from a sub-block is s * sum(q*x) - dmin*m * sum(x);
-// the codes of sub-block 0 decode to 1024+q and those of sub-block 1 to 64+q
-// (one LOP3 per f16 pair: 0x6400|q and 0x5400|q<<4), so the MMA yields
-// C = sum(q*x) + off * X and the fold is s*C - (off*s + dmin*m)*X with
-// o = off*s + dmin*m stored.  s = d*sc and dmin*m are the products the
-// reference decoder forms (gguf_dequant_torch.py:195-203), in fp32.
+// Q4_K (tinyserve/gguf_dequant_torch.py:180-205): a row of length K starts at
+// superblock phase p = (row*K mod 256)/32; rows are grouped by phase (row maps)
+// so that chunk c of every row in a block is exactly one source superblock,
+// whose 144 bytes become the unit: codes (128 B per row) and a header of
+// fp16 d / dmin and the eight 6-bit (scale, min) pairs widened to bytes
+// (20 B per row).  1.03x the Q4_K bytes, plus the superblocks that straddle
+// two rows, which both rows carry.  Codes decode to 64+q (0x5400|q<<4): one
+// shift and one LOP3 per f16 pair (a 1024+q decode would save the shift but
+// makes the accumulator 16x larger across the chunk's 16 chained MMAs and
+// doubles the layer error); the offset is removed in the fold:
+//   row += s*D_n - (off*s + dmin*m) * X_n,  s = d*sc,  X_n = sum of x over n.
+// MXFP4 (tinyserve/mxfp4.py:20-44): e2m1 codes convert exactly with
+// cvt.rn.f16x2.e2m1x2; the unit header is the 8 E8M0 scale bytes per row, the
+// fold row += 2^(e_n - 127) * D_n.  Exactly the MXFP4 bytes.
 //
-// Gate/up row blocks hold 8 gate rows then the 8 up rows of the same outputs,
-// so the SwiGLU pair of output j sits in one lane's accumulators (rows g and
-// g+8 of the fragment).  Down row blocks are 16 consecutive rows.
-//
-// Work: warp tasks (slot, row block, k-range); each task writes its 16 fp32
-// partial sums, and the last task of a row block (atomic counter, reset after
-// use) reduces the partials in fixed order and runs the epilogue, so results
-// do not depend on scheduling.
+// One launch per token-layer (cooperative, one CTA per SM):
+//   1. every CTA routes the token itself (bf16 logits, top-k, softmax;
+//      tinyserve/_model_hooks.py:466-473) and stages x as the f16 B image;
+//   2. gate/up tasks (slot, j-group of 16 gate + 16 up rows, chunk range)
+//      stream their units through a per-warp cp.async.bulk ring; the last
+//      task of a j-group (counter) reduces the partial sums in fixed order,
+//      applies the bias and the activation, and publishes 16 activations;
+//   3. every CTA waits for all j-groups (a device-wide counter, bounded
+//      wait), stages the top_k activation vectors as B images, and runs its
+//      down tasks, whose weights its warps' rings and an L2 prefetch issued
+//      right after routing have been pulling in meanwhile;
+//   4. the last down task of a 32-row group combines slots and splits in
+//      fixed order: out[h] = sum_k w_k * (down_k . act_k)[h] + w_k * b_k[h].
+// Results do not depend on scheduling.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstring>
+#include <vector>
 
 #include "../../include/tsb_moe.h"
 #include "moe_math.cuh"
@@ -44,80 +57,189 @@ namespace tsb {
 
 constexpr int kPkThreads = 512;
 constexpr int kPkWarps = kPkThreads / 32;
-constexpr int kUnitBytes = 768;
-constexpr int kMaxSplit = 16;
+constexpr int kSlots = 2;            // ring slots per warp (one chunk = two units each)
+constexpr int kPadL = 8, kPadR = 16;  // zero sub-blocks before / after a B image (phase shifts, last chunk)
+constexpr int kQ4Hdr = 320, kQ4Unit = 320 + 2048;
+constexpr int kMxHdr = 128, kMxUnit = 128 + 2048;
 
 bool packable(const TsbMoeSpec& sp) {
-  return sp.fmt_gate_up == FMT_Q4_K && sp.fmt_down == FMT_Q4_K && sp.hidden % 64 == 0 && sp.inter % 64 == 0 &&
-         sp.hidden > 0 && sp.inter > 0 && sp.n_experts >= 1 && sp.top_k >= 1 && sp.top_k <= 8;
+  const bool q4 = sp.fmt_gate_up == FMT_Q4_K && sp.fmt_down == FMT_Q4_K;
+  const bool mx = sp.fmt_gate_up == FMT_MXFP4 && sp.fmt_down == FMT_MXFP4;
+  return (q4 || mx) && sp.hidden % 32 == 0 && sp.inter % 32 == 0 && sp.hidden > 0 && sp.inter > 0 &&
+         sp.hidden <= 16384 && sp.inter <= 16384 && sp.n_experts >= 1 && sp.n_experts <= 1024 && sp.top_k >= 1 &&
+         sp.top_k <= 8 && sp.top_k <= sp.n_experts && sp.gate_up_layout >= 0 && sp.gate_up_layout <= 2;
 }
 
-PackGeom pack_geom(const TsbMoeSpec& sp) {
-  PackGeom G{};
-  G.rgu = (sp.inter + 7) / 8;
-  G.rdn = (sp.hidden + 15) / 16;
-  G.kbh = sp.hidden / 64;
-  G.kbi = sp.inter / 64;
+// ------------------------------------------------------------------ geometry
+static int q4_phase(int64_t row, int K) { return (int)(((row * K) % 256) / 32); }
+
+static int64_t gate_row(const TsbMoeSpec& sp, int j) {
+  return sp.gate_up_layout == TSB_GU_INTERLEAVED ? 2 * (int64_t)j : j;
+}
+static int64_t up_row(const TsbMoeSpec& sp, int j) {
+  if (sp.gate_up_layout == TSB_GU_INTERLEAVED) return 2 * (int64_t)j + 1;
+  if (sp.gate_up_layout == TSB_GU_CHUNKED) return (int64_t)sp.inter + j;
+  return j;
+}
+
+// Row maps: gate/up j-groups of 16 outputs whose gate rows share one phase and
+// whose up rows share one phase; down groups of 32 outputs of one phase.
+struct PkMaps {
+  std::vector<int32_t> gu_j, gu_ph, dn_h, dn_ph;
+  int C_gu = 0, C_dn = 0;
+};
+
+static PkMaps pk_maps(const TsbMoeSpec& sp) {
+  PkMaps M;
+  const bool q4 = sp.fmt_gate_up == FMT_Q4_K;
+  const int H = sp.hidden, I = sp.inter;
+  // gate/up: key = gate phase * 8 + up phase
+  std::vector<std::vector<int32_t>> b(64);
+  for (int j = 0; j < I; ++j) {
+    const int pg = q4 ? q4_phase(gate_row(sp, j), H) : 0, pu = q4 ? q4_phase(up_row(sp, j), H) : 0;
+    b[pg * 8 + pu].push_back(j);
+  }
+  int pmax = 0;
+  for (int key = 0; key < 64; ++key) {
+    const auto& v = b[key];
+    if (v.empty()) continue;
+    pmax = std::max(pmax, std::max(key / 8, key % 8));
+    for (size_t i = 0; i < v.size(); i += 16) {
+      for (size_t r = 0; r < 16; ++r) M.gu_j.push_back(i + r < v.size() ? v[i + r] : -1);
+      M.gu_ph.push_back(key / 8);
+      M.gu_ph.push_back(key % 8);
+    }
+  }
+  M.C_gu = (H / 32 + pmax + 7) / 8;
+  std::vector<std::vector<int32_t>> d(8);
+  for (int h = 0; h < H; ++h) d[q4 ? q4_phase(h, I) : 0].push_back(h);
+  pmax = 0;
+  for (int p = 0; p < 8; ++p) {
+    const auto& v = d[p];
+    if (v.empty()) continue;
+    pmax = std::max(pmax, p);
+    for (size_t i = 0; i < v.size(); i += 32) {
+      for (size_t r = 0; r < 32; ++r) M.dn_h.push_back(i + r < v.size() ? v[i + r] : -1);
+      M.dn_ph.push_back(p);
+    }
+  }
+  M.C_dn = (I / 32 + pmax + 7) / 8;
+  return M;
+}
+
+struct PkGeo {
+  int q4, unit, hdr;
+  int ngj, ndp, C_gu, C_dn;
+  int64_t o_guj, o_guph, o_dnh, o_dnph, maps_bytes;
+  int64_t gu_off, dn_off, expert_bytes, total;
+};
+
+static PkGeo pk_geo(const TsbMoeSpec& sp, const PkMaps& M) {
+  PkGeo G{};
+  G.q4 = sp.fmt_gate_up == FMT_Q4_K;
+  G.unit = G.q4 ? kQ4Unit : kMxUnit;
+  G.hdr = G.q4 ? kQ4Hdr : kMxHdr;
+  G.ngj = (int)M.gu_ph.size() / 2;
+  G.ndp = (int)M.dn_ph.size();
+  G.C_gu = M.C_gu;
+  G.C_dn = M.C_dn;
+  auto al = [](int64_t v) { return (v + 255) & ~int64_t(255); };
+  G.o_guj = 0;
+  G.o_guph = al(G.o_guj + 4 * (int64_t)M.gu_j.size());
+  G.o_dnh = al(G.o_guph + 4 * (int64_t)M.gu_ph.size());
+  G.o_dnph = al(G.o_dnh + 4 * (int64_t)M.dn_h.size());
+  G.maps_bytes = al(G.o_dnph + 4 * (int64_t)M.dn_ph.size());
   G.gu_off = 0;
-  G.dn_off = (int64_t)G.rgu * G.kbh * kUnitBytes;
-  G.expert_bytes = (G.dn_off + (int64_t)G.rdn * G.kbi * kUnitBytes + 255) & ~int64_t(255);
+  G.dn_off = (int64_t)G.ngj * G.C_gu * 2 * G.unit;
+  G.expert_bytes = al(G.dn_off + (int64_t)G.ndp * G.C_dn * 2 * G.unit);
+  G.total = G.maps_bytes + G.expert_bytes * sp.n_experts;
   return G;
 }
 
-// ------------------------------------------------------------------ packing
-// Q4_K element f of a flat stream: code, and the sub-block's (d*sc, dmin*m).
-__device__ __forceinline__ int q4k_code(const uint8_t* w, int64_t f) {
-  const uint8_t* b = w + (f >> 8) * 144;
-  const int i = (int)(f & 255), j = i >> 5, l = i & 31;
-  return (b[16 + 32 * (j >> 1) + l] >> (4 * (j & 1))) & 15;
-}
-__device__ __forceinline__ void q4k_coef(const uint8_t* w, int64_t f, float& s, float& o) {
-  const uint8_t* b = w + (f >> 8) * 144;
-  const int j = (int)((f & 255) >> 5);
-  const float d = half_bits_to_f32((uint16_t)(b[0] | (b[1] << 8)));
-  const float dmin = half_bits_to_f32((uint16_t)(b[2] | (b[3] << 8)));
-  int sc, m;
-  kq_scale_min(b + 4, j, sc, m);
-  s = __fmul_rn(d, (float)sc);
-  o = __fmul_rn(dmin, (float)m);
+size_t packed_total_bytes(const TsbMoeSpec& sp) {
+  if (!packable(sp)) return 0;
+  return (size_t)pk_geo(sp, pk_maps(sp)).total;
 }
 
+// ------------------------------------------------------------------ packing
 struct PackArgs {
   const TsbExpert* experts;
-  uint8_t* packed;
-  PackGeom G;
+  uint8_t* packed;  // start of the expert sections
+  const int32_t* gu_j;
+  const int32_t* gu_ph;
+  const int32_t* dn_h;
+  const int32_t* dn_ph;
+  PkGeo G;
   int H, I, layout;
   int64_t units_gu, units_per_expert;
 };
 
-// Source (stream, row) of packed row m of a row block; null when past the end.
-__device__ __forceinline__ const uint8_t* src_row(const PackArgs& a, const TsbExpert& E, bool down, int rb, int m,
-                                                  int64_t& row) {
+struct SrcRow {
+  const uint8_t* w;  // block stream (null: padding row)
+  const uint8_t* s;  // MXFP4 scale bytes
+  int64_t row;       // row in that stream
+  int64_t nrows;     // rows of that stream
+  int K, p;          // row length, Q4_K phase
+};
+
+__device__ SrcRow pack_src(const PackArgs& a, const TsbExpert& E, bool down, int grp, int rbsel, int r) {
+  SrcRow S{};
   if (down) {
-    row = 16 * rb + m;
-    return row < a.H ? static_cast<const uint8_t*>(E.down) : nullptr;
+    const int h = a.dn_h[grp * 32 + rbsel * 16 + r];
+    S.K = a.I;
+    S.p = a.dn_ph[grp];
+    if (h < 0) return S;
+    S.w = static_cast<const uint8_t*>(E.down);
+    S.s = static_cast<const uint8_t*>(E.down_scales);
+    S.row = h;
+    S.nrows = a.H;
+    return S;
   }
-  const int j = 8 * rb + (m & 7);
-  if (j >= a.I) return nullptr;
-  const bool up = m >= 8;
-  if (a.layout == TSB_GU_INTERLEAVED) {
-    row = 2 * (int64_t)j + (up ? 1 : 0);
-    return static_cast<const uint8_t*>(E.gate);
+  const int j = a.gu_j[grp * 16 + r];
+  S.K = a.H;
+  S.p = a.gu_ph[grp * 2 + rbsel];
+  if (j < 0) return S;
+  const bool up = rbsel == 1;
+  if (a.layout == TSB_GU_SEPARATE) {
+    S.w = static_cast<const uint8_t*>(up ? E.up : E.gate);
+    S.s = static_cast<const uint8_t*>(up ? E.up_scales : E.gate_scales);
+    S.row = j;
+    S.nrows = a.I;
+  } else {
+    S.w = static_cast<const uint8_t*>(E.gate);
+    S.s = static_cast<const uint8_t*>(E.gate_scales);
+    S.row = a.layout == TSB_GU_INTERLEAVED ? 2 * (int64_t)j + (up ? 1 : 0) : (up ? (int64_t)a.I : 0) + j;
+    S.nrows = 2 * (int64_t)a.I;
   }
-  if (a.layout == TSB_GU_CHUNKED) {
-    row = (up ? a.I : 0) + (int64_t)j;
-    return static_cast<const uint8_t*>(E.gate);
-  }
-  row = j;
-  return static_cast<const uint8_t*>(up ? E.up : E.gate);
+  return S;
 }
 
-// One warp per packed unit.  Lane L's 32 codes: for family fam (0: sub-block
-// 0, decoded as 1024+q; 1: sub-block 1, decoded as 64+q), fragment register
-// m (0..7) and half h, the code of row g + 8*(r&1), column
-// 16*(2 fam + m/4) + 2t + 8*(r/2) + h (r = m%4) sits in word m/2 at bit
-// 8*(m%2) + 16h + 4 fam.
-__global__ void __launch_bounds__(256) pack_unit_kernel(const PackArgs a, int64_t nunits) {
+// Q4_K superblock of chunk c of a row (null when past the stream).
+__device__ __forceinline__ const uint8_t* q4_block(const SrcRow& S, int c) {
+  if (!S.w) return nullptr;
+  const int64_t sbi = (S.row * S.K - 32 * S.p) / 256 + c;
+  if (sbi < 0 || sbi >= S.nrows * S.K / 256) return nullptr;
+  return S.w + sbi * 144;
+}
+__device__ __forceinline__ uint32_t q4_code(const uint8_t* b, int n, int e) {
+  return b ? (b[16 + 32 * (n >> 1) + e] >> (4 * (n & 1))) & 15u : 0u;
+}
+__device__ __forceinline__ uint32_t mx_byte(const SrcRow& S, int c, int n, int bi) {
+  const int blk = 8 * c + n;
+  if (!S.w || blk >= S.K / 32) return 0u;
+  return S.w[S.row * (S.K / 2) + (int64_t)blk * 16 + bi];
+}
+
+// One warp per unit.  Lane L = (g, t) owns sub-blocks t and 4 + t of rows g
+// and g + 8: 16 code words W[h][rho][i'] (half h: sub-block 4h + t; row
+// rho: g, g + 8; i' = 0..3: elements 8i'..8i'+7).  Q4_K (int8 MMA): byte k
+// of the word holds elements 8i'+k (low nibble) and 8i'+4+k (high nibble),
+// so W & 0x0F0F0F0F and (W >> 4) & 0x0F0F0F0F are the two u8 A registers.
+// MXFP4 (f16 MMA): the word is bytes 4i'..4i'+3 of the source block (low
+// nibble first), so the e2m1 conversions give the pairs (e0,e1) .. (e6,e7).  Plane j (16 B per
+// lane; h = j / 2, i' in {2(j%2), 2(j%2)+1}) holds W[h][0][i'0],
+// W[h][1][i'0], W[h][0][i'1], W[h][1][i'1].
+__global__ void __launch_bounds__(256) pk_pack_kernel(const PackArgs a, int64_t nunits) {
   const int64_t unit = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (unit >= nunits) return;
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -125,333 +247,438 @@ __global__ void __launch_bounds__(256) pack_unit_kernel(const PackArgs a, int64_
   int64_t r = unit % a.units_per_expert;
   const bool down = r >= a.units_gu;
   if (down) r -= a.units_gu;
-  const int KB = down ? a.G.kbi : a.G.kbh;
-  const int rb = (int)(r / KB), kb = (int)(r % KB);
-  const int K = down ? a.I : a.H;
+  const int C = down ? a.G.C_dn : a.G.C_gu;
+  const int rbsel = (int)(r & 1);
+  const int c = (int)((r >> 1) % C);
+  const int grp = (int)((r >> 1) / C);
   const TsbExpert E = a.experts[e];
-  uint8_t* dst = a.packed + e * a.G.expert_bytes + (down ? a.G.dn_off : a.G.gu_off) + r * kUnitBytes;
+  uint8_t* dst = a.packed + e * a.G.expert_bytes + (down ? a.G.dn_off : a.G.gu_off) + r * a.G.unit;
 
-  uint32_t word[4] = {0, 0, 0, 0};
-  int64_t row_lo = 0, row_hi = 0;
-  const uint8_t* w_lo = src_row(a, E, down, rb, g, row_lo);
-  const uint8_t* w_hi = src_row(a, E, down, rb, g + 8, row_hi);
+  uint32_t w[2][2][4];  // [h][rho][i']
+  const SrcRow S0 = pack_src(a, E, down, grp, rbsel, g), S1 = pack_src(a, E, down, grp, rbsel, g + 8);
+  if (a.G.q4) {
+    const uint8_t* blk[2] = {q4_block(S0, c), q4_block(S1, c)};
+    const int sh[8] = {0, 8, 16, 24, 4, 12, 20, 28};
 #pragma unroll
-  for (int fam = 0; fam < 2; ++fam)
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-    for (int m = 0; m < 8; ++m)
+      for (int rho = 0; rho < 2; ++rho)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int rr = m & 3;
-        const int col = 16 * (2 * fam + (m >> 2)) + 2 * t + 8 * (rr >> 1) + h;
-        const uint8_t* w = (rr & 1) ? w_hi : w_lo;
-        const int64_t row = (rr & 1) ? row_hi : row_lo;
-        const int q = w ? q4k_code(w, row * K + 64 * (int64_t)kb + col) : 0;
-        word[m >> 1] |= (uint32_t)q << (8 * (m & 1) + 16 * h + 4 * fam);
+        for (int ip = 0; ip < 4; ++ip) {
+          uint32_t v = 0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v |= q4_code(blk[rho], 4 * h + t, 8 * ip + q) << sh[q];
+          w[h][rho][ip] = v;
+        }
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int rho = 0; rho < 2; ++rho) {
+        const SrcRow& S = rho ? S1 : S0;
+#pragma unroll
+        for (int ip = 0; ip < 4; ++ip)
+          w[h][rho][ip] = mx_byte(S, c, 4 * h + t, 4 * ip) | mx_byte(S, c, 4 * h + t, 4 * ip + 1) << 8 |
+                          mx_byte(S, c, 4 * h + t, 4 * ip + 2) << 16 | mx_byte(S, c, 4 * h + t, 4 * ip + 3) << 24;
       }
-  *reinterpret_cast<uint4*>(dst + 16 * lane) = make_uint4(word[0], word[1], word[2], word[3]);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int h = j >> 1, i0 = 2 * (j & 1);
+    *reinterpret_cast<uint4*>(dst + a.G.hdr + (32 * j + lane) * 16) =
+        make_uint4(w[h][0][i0], w[h][1][i0], w[h][0][i0 + 1], w[h][1][i0 + 1]);
+  }
 
   if (lane < 16) {
-    const int sb = lane >> 3, gg = lane & 7;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int hi = 0; hi < 2; ++hi) {
-      int64_t row = 0;
-      const uint8_t* w = src_row(a, E, down, rb, gg + 8 * hi, row);
-      if (!w) continue;
-      float s, o;
-      q4k_coef(w, row * K + 64 * (int64_t)kb + 32 * sb, s, o);
-      c[hi] = s;
-      c[2 + hi] = fmaf(sb ? 64.f : 1024.f, s, o);
+    const SrcRow S = pack_src(a, E, down, grp, rbsel, lane);
+    if (a.G.q4) {
+      const uint8_t* b = q4_block(S, c);
+      uint32_t dd = 0, pw[4] = {0, 0, 0, 0};
+      if (b) {
+        dd = (uint32_t)b[0] | (uint32_t)b[1] << 8 | (uint32_t)b[2] << 16 | (uint32_t)b[3] << 24;
+        for (int q = 0; q < 4; ++q) {
+          int sa, ma, sb, mb;
+          kq_scale_min(b + 4, 2 * q, sa, ma);
+          kq_scale_min(b + 4, 2 * q + 1, sb, mb);
+          pw[q] = (uint32_t)sa | (uint32_t)sb << 8 | (uint32_t)ma << 16 | (uint32_t)mb << 24;
+        }
+      }
+      *reinterpret_cast<uint32_t*>(dst + 4 * lane) = dd;
+      *reinterpret_cast<uint4*>(dst + 64 + 16 * lane) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+    } else {
+      uint32_t s[2] = {0, 0};
+      if (S.w)
+        for (int n = 0; n < 8; ++n) {
+          const int blk = 8 * c + n;
+          if (blk < S.K / 32) s[n >> 2] |= (uint32_t)S.s[S.row * (S.K / 32) + blk] << (8 * (n & 3));
+        }
+      *reinterpret_cast<uint2*>(dst + 8 * lane) = make_uint2(s[0], s[1]);
     }
-    *reinterpret_cast<float4*>(dst + 512 + 128 * sb + 16 * gg) = make_float4(c[0], c[1], c[2], c[3]);
   }
 }
 
 int launch_pack(const TsbMoeSpec& sp, const TsbExpert* experts, void* packed, cudaStream_t st) {
+  const PkMaps M = pk_maps(sp);
+  const PkGeo G = pk_geo(sp, M);
+  uint8_t* base = static_cast<uint8_t*>(packed);
+  // the row maps: small, copied once from host memory (stream-ordered)
+  std::vector<uint8_t> maps((size_t)G.maps_bytes, 0);
+  memcpy(maps.data() + G.o_guj, M.gu_j.data(), 4 * M.gu_j.size());
+  memcpy(maps.data() + G.o_guph, M.gu_ph.data(), 4 * M.gu_ph.size());
+  memcpy(maps.data() + G.o_dnh, M.dn_h.data(), 4 * M.dn_h.size());
+  memcpy(maps.data() + G.o_dnph, M.dn_ph.data(), 4 * M.dn_ph.size());
+  cudaError_t e = cudaMemcpyAsync(base, maps.data(), maps.size(), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);  // host vector dies on return
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   PackArgs a{};
   a.experts = experts;
-  a.packed = static_cast<uint8_t*>(packed);
-  a.G = pack_geom(sp);
+  a.packed = base + G.maps_bytes;
+  a.gu_j = reinterpret_cast<const int32_t*>(base + G.o_guj);
+  a.gu_ph = reinterpret_cast<const int32_t*>(base + G.o_guph);
+  a.dn_h = reinterpret_cast<const int32_t*>(base + G.o_dnh);
+  a.dn_ph = reinterpret_cast<const int32_t*>(base + G.o_dnph);
+  a.G = G;
   a.H = sp.hidden;
   a.I = sp.inter;
   a.layout = sp.gate_up_layout;
-  a.units_gu = (int64_t)a.G.rgu * a.G.kbh;
-  a.units_per_expert = a.units_gu + (int64_t)a.G.rdn * a.G.kbi;
+  a.units_gu = (int64_t)G.ngj * G.C_gu * 2;
+  a.units_per_expert = a.units_gu + (int64_t)G.ndp * G.C_dn * 2;
   const int64_t n = a.units_per_expert * sp.n_experts;
-  pack_unit_kernel<<<(unsigned)((n + 7) / 8), 256, 0, st>>>(a, n);
-  const cudaError_t e = cudaGetLastError();
+  pk_pack_kernel<<<(unsigned)((n + 7) / 8), 256, 0, st>>>(a, n);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   return TSB_OK;
 }
 
 // ------------------------------------------------------------------ decode
+// Phase timing (development builds only, -DTSB_PK_TIMING=1): per-CTA
+// globaltimer stamps at the phase boundaries and per-warp cycle counts of
+// waiting, computing, issuing copies and epilogues, read back with
+// tsb_pk_timing_read.  Compiled out of the default build.
+#ifndef TSB_PK_TIMING
+#define TSB_PK_TIMING 0
+#endif
+#if TSB_PK_TIMING
+#define PK_T(...) __VA_ARGS__
+__device__ unsigned long long g_pk_trace[160 * 16];
+__device__ unsigned long long g_pk_wtrace[160 * 16 * 8];
+#else
+#define PK_T(...)
+#endif
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
 struct PkArgs {
-  const uint8_t* packed;
-  int64_t expert_bytes, sec_off;
-  int R, KB, S, nkb, ntasks;
-  const int32_t* ids;
-  const float* wts;
+  const uint8_t* packed;  // expert sections
+  const int32_t* gu_j;
+  const int32_t* dn_h;
+  const int32_t* gu_ph;
+  const int32_t* dn_ph;
+  int64_t gu_off, dn_off, expert_bytes;
+  int H, I, E, top_k, ngj, ndp, C_gu, C_dn;
+  int nc_gu, S_gu, nc_dn, S_dn, n_gu, n_dn;  // chunks per task, tasks per group, task counts
+  int nsb_h, nsb_i;                          // padded sub-blocks of the x / activation images
+  const uint16_t* x;
+  const uint16_t* router_w;
+  const float* router_b;
+  int32_t* ids;
+  float* wts;
   const TsbExpert* experts;
-  int n_experts, top_k;
-  int* err;
-  const void* x;      // mode 0: bf16 [H]; mode 1: fp32 [top_k, I]
-  int nv;             // staged vectors: 1 (gate/up) or top_k (down)
-  float* part;        // [ntasks, 16]
-  unsigned* cnt;      // per output row block, zero between calls
-  int mode, I, H, act;
+  float* act;        // fp32 [top_k, I]
+  unsigned* cnt_gu;  // [top_k * ngj]
+  unsigned* cnt_dn;  // [ndp]
+  unsigned* sync;    // [0] gate/up groups done, [1] CTAs finished, [2..9] max |act| per slot (float bits),
+                     // [10] router logits published
+  float* part_gu;    // [n_gu, 32]
+  float* part_dn;    // [n_dn, 32]
+  void* out;
+  int out_f32, act_kind;
   float limit, alpha;
-  float* act_out;     // mode 0: fp32 [top_k, I]
-  uint16_t* out;      // mode 1: bf16 [H]
-  // routing inside the gate/up launch (null: ids and wts are inputs)
-  const uint16_t* router_w;  // bf16 [E, H]
-  const float* router_b;     // fp32 [E] or null
-  // 0x64006400 and 0x54005400 (f16x2 1024 and 64), passed as arguments so the
-  // compiler keeps them in registers: each code decode is then one LOP3 with
-  // the mask as its immediate, (w & mask) | magic.
-  uint32_t magic1024, magic64;
+  int* err;
+  float* logits;  // [E] router logits of this token
 };
 
-// Each warp streams its units through a private ring of kSlots slots of
-// kSlotUnits units (one cp.async.bulk copy per slot, completing on the slot's
-// mbarrier): up to kSlots * kSlotUnits * 768 bytes in flight per warp.  The
-// ring is refilled across the warp's tasks, so it does not drain between them.
-constexpr int kSlotUnits = 4, kSlots = 2;
-constexpr int kSlotBytes = kSlotUnits * kUnitBytes;
-
-// Slot waits spin on mbarrier.test_wait (no suspend): a warp waits for its
-// own next slot every two units, so a sleeping wait's wake-up delay would sit
-// on the critical path.  Bounded: after kSpinPolls polls (seconds) it records
-// kDevWaitTimeout and returns false.
-constexpr uint32_t kSpinPolls = 1u << 26;
-__device__ __forceinline__ bool pk_warp_wait(uint64_t* bar, uint32_t parity, int* err) {
+// Slot waits use mbarrier.try_wait: a waiting warp is suspended in hardware
+// until the phase completes (or a time limit passes), so it takes no issue
+// slots from the warps that compute.  Bounded: after kWaitPolls polls of up
+// to kWaitNs each (seconds in all) it records kDevWaitTimeout and gives up.
+constexpr uint32_t kSpinPolls = 1u << 26;  // polls of the device-wide counters (with a short sleep)
+constexpr uint32_t kWaitPolls = 1u << 16, kWaitNs = 100000;
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err) {
   bool ok = false;
-  for (uint32_t i = 0; i < kSpinPolls && !ok; ++i) {
+  for (uint32_t i = 0; i < kWaitPolls && !ok; ++i) {
     uint32_t r;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
         : "=r"(r)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kWaitNs)
         : "memory");
     ok = r != 0;
   }
   if (!ok && err) atomicExch(err, kDevWaitTimeout);
   return __all_sync(0xffffffffu, ok);
 }
-// D = A * B with a zero accumulator input (no per-use register clearing).
-__device__ __forceinline__ void mma_f16_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+
+__device__ __forceinline__ void mma_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                      uint32_t b1) {
   asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%10,%10,%10};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
-
-// One 768-byte unit: decode the 32 codes of this lane, four MMAs against the
-// staged vector, fold into the two row accumulators.
-__device__ __forceinline__ void unit_fma(const uint8_t* u, int oq, int oc, const uint8_t* xb, const float2 xs,
-                                         uint32_t M1, uint32_t M2, float& acc_lo, float& acc_hi) {
-  const uint4 q = *reinterpret_cast<const uint4*>(u + oq);
-  const float4 c0 = *reinterpret_cast<const float4*>(u + oc);
-  const float4 c1 = *reinterpret_cast<const float4*>(u + oc + 128);
-  const uint4 b01 = *reinterpret_cast<const uint4*>(xb);
-  const uint4 b23 = *reinterpret_cast<const uint4*>(xb + 16);
-  uint32_t l0[4], l1[4], h0[4], h1[4];
-  {
-    const uint32_t w0 = q.x, w1 = q.y, w2 = q.z, w3 = q.w;
-    const uint32_t v0 = w0 >> 8, v1 = w1 >> 8, v2 = w2 >> 8, v3 = w3 >> 8;
-    l0[0] = (w0 & 0x000F000Fu) | M1;
-    l0[1] = (v0 & 0x000F000Fu) | M1;
-    l0[2] = (w1 & 0x000F000Fu) | M1;
-    l0[3] = (v1 & 0x000F000Fu) | M1;
-    l1[0] = (w2 & 0x000F000Fu) | M1;
-    l1[1] = (v2 & 0x000F000Fu) | M1;
-    l1[2] = (w3 & 0x000F000Fu) | M1;
-    l1[3] = (v3 & 0x000F000Fu) | M1;
-    h0[0] = (w0 & 0x00F000F0u) | M2;
-    h0[1] = (v0 & 0x00F000F0u) | M2;
-    h0[2] = (w1 & 0x00F000F0u) | M2;
-    h0[3] = (v1 & 0x00F000F0u) | M2;
-    h1[0] = (w2 & 0x00F000F0u) | M2;
-    h1[1] = (v2 & 0x00F000F0u) | M2;
-    h1[2] = (w3 & 0x00F000F0u) | M2;
-    h1[3] = (v3 & 0x00F000F0u) | M2;
-  }
-  float d0[4], d1[4];
-  mma_f16_z(d0, l0, b01.x, b01.y);
-  mma_f16(d0, l1, b01.z, b01.w);
-  mma_f16_z(d1, h0, b23.x, b23.y);
-  mma_f16(d1, h1, b23.z, b23.w);
-  acc_lo = fmaf(c0.x, d0[0], acc_lo);
-  acc_lo = fmaf(-c0.z, xs.x, acc_lo);
-  acc_hi = fmaf(c0.y, d0[2], acc_hi);
-  acc_hi = fmaf(-c0.w, xs.x, acc_hi);
-  acc_lo = fmaf(c1.x, d1[0], acc_lo);
-  acc_lo = fmaf(-c1.z, xs.y, acc_lo);
-  acc_hi = fmaf(c1.y, d1[2], acc_hi);
-  acc_hi = fmaf(-c1.w, xs.y, acc_hi);
+__device__ __forceinline__ void mma_acc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint32_t u4c(const uint4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-// Shared memory per staged vector v: xf (KB x 128 B: for k-block kb and quad
-// lane t, the eight B-fragment registers of the four MMAs) and X (KB x 8 B:
-// the two sub-block sums); then 32 zero bytes (the B operand of lanes whose
-// fragment column is not the token's), the per-vector unscale factors and
-// the warps' rings.
-__host__ __device__ inline size_t pk_zero_off(int nv, int KB) { return ((size_t)nv * KB * 136 + 15) & ~size_t(15); }
-__host__ __device__ inline size_t pk_ring_off(int nv, int KB) { return pk_zero_off(nv, KB) + 128; }
-__host__ __device__ inline size_t pk_smem(int nv, int KB) {
-  return pk_ring_off(nv, KB) + (size_t)kPkWarps * kSlots * kSlotBytes;
-}
-
-// Four consecutive elements [k, k+4) of staged vector v as floats.
-template <int MODE>
-__device__ __forceinline__ float4 vec4(const PkArgs& a, int v, int k) {
-  if (MODE == 0) {
-    const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(a.x) + k);
-    return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u), __uint_as_float(r.y << 16),
-                       __uint_as_float(r.y & 0xFFFF0000u));
+// Four f16x2 A registers from one code word (see pk_pack_kernel): element
+// pairs (e0,e1), (e2,e3), (e4,e5), (e6,e7).
+template <bool Q4>
+__device__ __forceinline__ void decode_word(uint32_t w, uint32_t m64, uint32_t (&r)[4]) {
+  if (Q4) {
+    // every code decodes to 64 + q (0x5400 | q << 4): nibble pairs are moved
+    // to bits [7:4] / [23:20] of each half first
+    r[0] = ((w << 4) & 0x00F000F0u) | m64;
+    r[1] = (w & 0x00F000F0u) | m64;
+    r[2] = ((w >> 4) & 0x00F000F0u) | m64;
+    r[3] = ((w >> 8) & 0x00F000F0u) | m64;
+  } else {
+    // the word unpacked into its four bytes in PTX: the conversions read the
+    // bytes in place (a shift and a mask per byte otherwise)
+    asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n cvt.rn.f16x2.e2m1x2 %0, b0;\n"
+        " cvt.rn.f16x2.e2m1x2 %1, b1;\n cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+        : "r"(w));
   }
-  return __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + (int64_t)v * a.I + k));
 }
 
-// Thread i owns float4 groups q = i + 512 u of the flat range of all staged
-// vectors; vector v = q / K4.
-template <int MODE>
-__device__ __forceinline__ float4 stage_load(const PkArgs& a, int q, int K4, int total) {
-  const int v = q / K4;
-  return q < total ? vec4<MODE>(a, v, 4 * (q - v * K4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+// The four MMAs of plane j of one unit.  q: the lane's plane word group
+// (rows g, g+8 x two element octets); b0, b1: the B registers of the four
+// MMAs, (b01, b23) adjacent.  MMA m covers elements 4m..4m+3 of the lane's
+// sub-block: a01 (row g) / a23 (row g+8) elements 4m, 4m+1; a45 / a67
+// elements 4m+2, 4m+3.
+template <bool Q4, bool FIRST>
+__device__ __forceinline__ void plane_mma(const uint4& q, const uint4& b0, const uint4& b1, uint32_t m64,
+                                          float (&d)[4]) {
+  uint32_t r0[4], r1[4], r2[4], r3[4];
+  decode_word<Q4>(q.x, m64, r0);  // row g,   elements 8i'0 .. 8i'0+7
+  decode_word<Q4>(q.y, m64, r1);  // row g+8
+  decode_word<Q4>(q.z, m64, r2);  // row g,   elements 8i'1 .. 8i'1+7
+  decode_word<Q4>(q.w, m64, r3);  // row g+8
+  if (FIRST)
+    mma_z(d, r0[0], r1[0], r0[1], r1[1], b0.x, b0.y);
+  else
+    mma_acc(d, r0[0], r1[0], r0[1], r1[1], b0.x, b0.y);
+  mma_acc(d, r0[2], r1[2], r0[3], r1[3], b0.z, b0.w);
+  mma_acc(d, r2[0], r3[0], r2[1], r3[1], b1.x, b1.y);
+  mma_acc(d, r2[2], r3[2], r2[3], r3[3], b1.z, b1.w);
 }
 
-// Pass 2 of one group: scale, round to fp16, sub-block sum over eight lanes,
-// store into the fragment-order image.  All lanes of the warp call it.
-template <int MODE>
-__device__ __forceinline__ void stage_store(const PkArgs& a, uint8_t* sm, const float* s_scale, int q, int K4,
-                                            int total, float4 f, int lane) {
-  const int v = min(q / K4, a.nv - 1), m = q - v * K4;
-  const float sc = s_scale[v];
-  const __half2 h01 = __floats2half2_rn(f.x * sc, f.y * sc);
-  const __half2 h23 = __floats2half2_rn(f.z * sc, f.w * sc);
-  const float2 g01 = __half22float2(h01), g23 = __half22float2(h23);
-  float sum = (g01.x + g01.y) + (g23.x + g23.y);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-  if (q >= total) return;
-  float* X = reinterpret_cast<float*>(sm + (size_t)a.nv * a.KB * 128);
-  if ((lane & 7) == 0) X[(size_t)v * 2 * a.KB + (m >> 3)] = sum;
-  // k = 4m: k-block kb = m/16, MMA j = (m/4)%4, w0 = 4*(m%4) in [0,16):
-  // pairs (w0, w0+1) and (w0+2, w0+3) go to quad lanes tt and tt+1 of half w0/8
-  const int kb = m >> 4, j = (m >> 2) & 3, w0 = 4 * (m & 3);
-  const int tt = (w0 & 7) >> 1, hf = w0 >> 3;
-  const int i0 = ((kb * 4 + tt) * 4 + j) * 2 + hf;
-  uint32_t* xf = reinterpret_cast<uint32_t*>(sm + (size_t)v * a.KB * 128);
-  xf[i0] = *reinterpret_cast<const uint32_t*>(&h01);
-  xf[i0 + 8] = *reinterpret_cast<const uint32_t*>(&h23);
-}
-
-// Max |x| per vector over this thread's groups, then the block-wide
-// power-of-two scales (max|x| in [2^14, 2^15), exact in fp32).
-__device__ __forceinline__ void stage_scales(const PkArgs& a, float (&mx)[8], float* inv, float* s_scale,
-                                             float (*red)[kPkWarps], int warp, int lane) {
+// Scale fold of one unit: lane (g, t) holds rows g, g+8 x sub-blocks 2t,
+// 2t+1 of the chunk.  Q4_K (codes decoded as 64 + q):
+//   row += d * sum_n sc_n * (D_n - 64 X_n) - dmin * sum_n m_n X_n
+// MXFP4: row += sum_n 2^(e_n - 127) * D_n.
+template <bool Q4>
+__device__ __forceinline__ void unit_fold(const uint8_t* u, const float (&d)[4], float xa, float xb, int g, int t,
+                                          float& acc0, float& acc1) {
+  // MXFP4: xa, xb are the x scales 2^-e of the lane's two sub-blocks
+  if (Q4) {
 #pragma unroll
-  for (int v = 0; v < 8; ++v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx[v] = fmaxf(mx[v], __shfl_xor_sync(0xffffffffu, mx[v], o));
-    if (lane == 0) red[v][warp] = mx[v];
-  }
-  __syncthreads();
-  if (threadIdx.x < a.nv) {
-    const int v = threadIdx.x;
-    float m = red[v][0];
-    for (int i = 1; i < kPkWarps; ++i) m = fmaxf(m, red[v][i]);
-    const int ex = (int)((__float_as_uint(m) >> 23) & 255u);
-    int sx = (m > 0.f && ex != 255) ? 14 - (ex - 127) : 0;
-    sx = max(-126, min(126, sx));
-    s_scale[v] = __uint_as_float((uint32_t)(sx + 127) << 23);
-    inv[v] = __uint_as_float((uint32_t)(127 - sx) << 23);
-  }
-  __syncthreads();
-}
-
-__device__ __forceinline__ void max_into(float (&mx)[8], int v, float4 f) {
-  const float m = fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w)));
-#pragma unroll
-  for (int w = 0; w < 8; ++w)
-    if (w == v) mx[w] = fmaxf(mx[w], m);
-}
-
-// Staging of all vectors: max |x| per vector, then scale, round to fp16,
-// permute into fragment order and sum per sub-block; two block barriers.  When
-// the vectors fit in kStageRegs groups per thread (the GPT-OSS shapes: 720 and
-// 2880 groups) the groups are loaded once and kept in registers for both
-// passes; otherwise each pass loads kStageU groups per thread at a time.
-// The eight groups of a 32-element sub-block sit on eight consecutive lanes
-// (vector length K4 is a multiple of 16 groups), so three shuffles sum it.
-constexpr int kStageU = 4, kStageRegs = 8;
-
-template <int MODE>
-__device__ void stage_vectors(const PkArgs& a, uint8_t* sm, float* inv, int warp, int lane) {
-  __shared__ float red[8][kPkWarps];
-  __shared__ float s_scale[8];
-  const int K4 = 16 * a.KB, total = a.nv * K4;
-  float mx[8];
-#pragma unroll
-  for (int v = 0; v < 8; ++v) mx[v] = 0.f;
-  if (total <= kStageRegs * kPkThreads) {
-    float4 f[kStageRegs];
-#pragma unroll
-    for (int u = 0; u < kStageRegs; ++u) f[u] = stage_load<MODE>(a, threadIdx.x + u * kPkThreads, K4, total);
-#pragma unroll
-    for (int u = 0; u < kStageRegs; ++u) {
-      const int q = threadIdx.x + u * kPkThreads;
-      if (q < total) max_into(mx, q / K4, f[u]);
+    for (int rho = 0; rho < 2; ++rho) {
+      const int row = g + 8 * rho;
+      const uint32_t dd = *reinterpret_cast<const uint32_t*>(u + 4 * row);
+      const uint32_t sm = *reinterpret_cast<const uint32_t*>(u + 64 + 16 * row + 4 * t);
+      const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dd));
+      const float ya = fmaf(-64.f, xa, d[2 * rho]), yb = fmaf(-64.f, xb, d[2 * rho + 1]);
+      const float uu = fmaf((float)((sm >> 8) & 255u), yb, (float)(sm & 255u) * ya);
+      const float vv = fmaf((float)(sm >> 24), xb, (float)((sm >> 16) & 255u) * xa);
+      float acc = rho ? acc1 : acc0;
+      acc = fmaf(dm.x, uu, acc);
+      acc = fmaf(-dm.y, vv, acc);
+      if (rho) acc1 = acc; else acc0 = acc;
     }
-    stage_scales(a, mx, inv, s_scale, red, warp, lane);
+  } else {
 #pragma unroll
-    for (int u = 0; u < kStageRegs; ++u) {
-      if ((int)(threadIdx.x - lane) + u * kPkThreads >= total) break;  // warp-uniform
-      stage_store<MODE>(a, sm, s_scale, threadIdx.x + u * kPkThreads, K4, total, f[u], lane);
-    }
-    return;
-  }
-  for (int q0 = threadIdx.x; q0 < total; q0 += kStageU * kPkThreads) {
-    float4 f[kStageU];
-#pragma unroll
-    for (int u = 0; u < kStageU; ++u) f[u] = stage_load<MODE>(a, q0 + u * kPkThreads, K4, total);
-#pragma unroll
-    for (int u = 0; u < kStageU; ++u) {
-      const int q = q0 + u * kPkThreads;
-      if (q < total) max_into(mx, q / K4, f[u]);
-    }
-  }
-  stage_scales(a, mx, inv, s_scale, red, warp, lane);
-  // all lanes stay in the loop for the shuffles (a sub-block's eight lanes are
-  // all in range or all out)
-  for (int q0 = threadIdx.x - lane; q0 < total; q0 += kStageU * kPkThreads) {
-    float4 f[kStageU];
-#pragma unroll
-    for (int u = 0; u < kStageU; ++u) f[u] = stage_load<MODE>(a, q0 + lane + u * kPkThreads, K4, total);
-#pragma unroll
-    for (int u = 0; u < kStageU; ++u) {
-      if (q0 + u * kPkThreads >= total) break;  // warp-uniform
-      stage_store<MODE>(a, sm, s_scale, q0 + lane + u * kPkThreads, K4, total, f[u], lane);
+    for (int rho = 0; rho < 2; ++rho) {
+      const int row = g + 8 * rho;
+      const uint32_t e2 = *reinterpret_cast<const uint16_t*>(u + 8 * row + 2 * t);
+      const uint32_t ea = e2 & 255u, eb = e2 >> 8;
+      const float fa = __uint_as_float(ea ? ea << 23 : 0x00400000u) * xa;
+      const float fb = __uint_as_float(eb ? eb << 23 : 0x00400000u) * xb;
+      float acc = rho ? acc1 : acc0;
+      acc = fmaf(fa, d[2 * rho], acc);
+      acc = fmaf(fb, d[2 * rho + 1], acc);
+      if (rho) acc1 = acc; else acc0 = acc;
     }
   }
 }
 
-// Routing of one token inside every gate/up CTA (tinyserve/_model_hooks.py:466-473):
-// warp w computes the logits of experts w, w+16, ... (bf16 x . bf16 W[e] in
-// fp32, + bias, rounded to bf16 as the reference's bf16 Linear returns them)
-// into shared memory, then warp 0 selects the top-k (ties -> lower id, NaN
-// lowest) and softmaxes the k selected logits.  Every CTA reaches the same
-// result from the same arithmetic; CTA 0 publishes ids / weights.
-__device__ void route_in_cta(const PkArgs& a, float* s_logit, int* s_e, float* s_w, int warp, int lane) {
+// One chunk (two units, A and B, of the same 256 columns).  B operands: lanes
+// g == t hold sub-block 8c - p + t for the half-0 MMAs, lanes g == t + 4
+// sub-block 8c - p + 4 + t for the half-1 MMAs (element pairs 2m, 2m+1 of MMA
+// m as one (b01, b23) register pair); every other lane reads zeros.  Half 0
+// fills accumulator columns 0-3, half 1 columns 4-7, so the lane's columns
+// 2t, 2t+1 are sub-blocks 2t, 2t+1.  SHARED: both units have the same phase
+// (one set of B loads).
+template <bool Q4, bool SHARED>
+__device__ __forceinline__ void chunk_mma(const uint8_t* uA, const uint8_t* uB, const uint8_t* srcA0,
+                                          const uint8_t* srcA1, const uint8_t* srcB0, const uint8_t* srcB1,
+                                          size_t strA0, size_t strA1, size_t strB0, size_t strB1, uint32_t m64,
+                                          int lane, float (&dA)[4], float (&dB)[4]) {
+  float eA[4], eB[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int h = j >> 1, G = 2 * (j & 1);
+    const uint8_t* sa = h ? srcA1 : srcA0;
+    const size_t za = h ? strA1 : strA0;
+    const uint4 qa = lds128(uA + (32 * j + lane) * 16);
+    const uint4 qb = lds128(uB + (32 * j + lane) * 16);
+    const uint4 ba0 = lds128(sa + G * za), ba1 = lds128(sa + (G + 1) * za);
+    uint4 bb0 = ba0, bb1 = ba1;
+    if (!SHARED) {
+      const uint8_t* sb = h ? srcB1 : srcB0;
+      const size_t zb = h ? strB1 : strB0;
+      bb0 = lds128(sb + G * zb);
+      bb1 = lds128(sb + (G + 1) * zb);
+    }
+    if (j == 0) {
+      plane_mma<Q4, true>(qa, ba0, ba1, m64, dA);
+      plane_mma<Q4, true>(qb, bb0, bb1, m64, dB);
+    } else if (j == 2) {
+      plane_mma<Q4, true>(qa, ba0, ba1, m64, eA);
+      plane_mma<Q4, true>(qb, bb0, bb1, m64, eB);
+    } else if (j == 1) {
+      plane_mma<Q4, false>(qa, ba0, ba1, m64, dA);
+      plane_mma<Q4, false>(qb, bb0, bb1, m64, dB);
+    } else {
+      plane_mma<Q4, false>(qa, ba0, ba1, m64, eA);
+      plane_mma<Q4, false>(qb, bb0, bb1, m64, eB);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    dA[i] += eA[i];
+    dB[i] += eB[i];
+  }
+}
+
+// ---- Q4_K on the int8 tensor path (mma.m16n8k32, u8 codes x s8/u8 x bytes)
+__device__ __forceinline__ void imma_hi(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma_lo(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One chunk (two units) of Q4_K: MMA (h, i) covers elements 8i..8i+7 of the
+// lane's sub-block 4h + t (k-quad t: 8i..8i+3, k-quad t+4: 8i+4..8i+7); the B
+// operand of the lane g == 4h + t holds the hi (or lo) bytes of the same
+// elements of the x sub-block, every other lane zeros.  Half 0 fills columns
+// 0-3, half 1 columns 4-7.  Accumulators: hi and lo sums of each unit, exact
+// in int32.
+template <bool SHARED>
+__device__ __forceinline__ void chunk_imma(const uint8_t* uA, const uint8_t* uB, const uint8_t* srcA0,
+                                           const uint8_t* srcA1, const uint8_t* srcB0, const uint8_t* srcB1,
+                                           size_t strA0, size_t strA1, size_t strB0, size_t strB1, int lane,
+                                           int (&hA)[4], int (&lA)[4], int (&hB)[4], int (&lB)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) hA[i] = lA[i] = hB[i] = lB[i] = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int h = j >> 1, G = j & 1;  // plane j: MMAs (h, 2G), (h, 2G + 1)
+    const uint8_t* sa = h ? srcA1 : srcA0;
+    const size_t za = h ? strA1 : strA0;
+    const uint4 qa = lds128(uA + (32 * j + lane) * 16);
+    const uint4 qb = lds128(uB + (32 * j + lane) * 16);
+    const uint4 xha = lds128(sa + G * za), xla = lds128(sa + (2 + G) * za);
+    uint4 xhb = xha, xlb = xla;
+    if (!SHARED) {
+      const uint8_t* sb = h ? srcB1 : srcB0;
+      const size_t zb = h ? strB1 : strB0;
+      xhb = lds128(sb + G * zb);
+      xlb = lds128(sb + (2 + G) * zb);
+    }
+    // unit A: words x (row g) / y (row g+8) -> MMA 2G, z / w -> MMA 2G+1
+    const uint32_t a0 = qa.x & 0x0F0F0F0Fu, a1 = qa.y & 0x0F0F0F0Fu;
+    const uint32_t a2 = (qa.x >> 4) & 0x0F0F0F0Fu, a3 = (qa.y >> 4) & 0x0F0F0F0Fu;
+    const uint32_t a4 = qa.z & 0x0F0F0F0Fu, a5 = qa.w & 0x0F0F0F0Fu;
+    const uint32_t a6 = (qa.z >> 4) & 0x0F0F0F0Fu, a7 = (qa.w >> 4) & 0x0F0F0F0Fu;
+    imma_hi(hA, a0, a1, a2, a3, xha.x, xha.y);
+    imma_lo(lA, a0, a1, a2, a3, xla.x, xla.y);
+    imma_hi(hA, a4, a5, a6, a7, xha.z, xha.w);
+    imma_lo(lA, a4, a5, a6, a7, xla.z, xla.w);
+    const uint32_t c0 = qb.x & 0x0F0F0F0Fu, c1 = qb.y & 0x0F0F0F0Fu;
+    const uint32_t c2 = (qb.x >> 4) & 0x0F0F0F0Fu, c3 = (qb.y >> 4) & 0x0F0F0F0Fu;
+    const uint32_t c4 = qb.z & 0x0F0F0F0Fu, c5 = qb.w & 0x0F0F0F0Fu;
+    const uint32_t c6 = (qb.z >> 4) & 0x0F0F0F0Fu, c7 = (qb.w >> 4) & 0x0F0F0F0Fu;
+    imma_hi(hB, c0, c1, c2, c3, xhb.x, xhb.y);
+    imma_lo(lB, c0, c1, c2, c3, xlb.x, xlb.y);
+    imma_hi(hB, c4, c5, c6, c7, xhb.z, xhb.w);
+    imma_lo(lB, c4, c5, c6, c7, xlb.z, xlb.w);
+  }
+}
+
+// Q4_K fold of one unit: sub-block n's dot product is
+//   2^-e_n * (d * sc_n * (256*hi_n + lo_n)) - dmin * m_n * X_n
+// with X_n = 2^-e_n * sum x_int (the image's float2 per sub-block).
+__device__ __forceinline__ void fold_q4(const uint8_t* u, const int (&hi)[4], const int (&lo)[4], float2 xa, float2 xb,
+                                        int g, int t, float& acc0, float& acc1) {
+#pragma unroll
+  for (int rho = 0; rho < 2; ++rho) {
+    const int row = g + 8 * rho;
+    const uint32_t dd = *reinterpret_cast<const uint32_t*>(u + 4 * row);
+    const uint32_t sm = *reinterpret_cast<const uint32_t*>(u + 64 + 16 * row + 4 * t);
+    const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dd));
+    const float fa = (float)(hi[2 * rho] * 256 + lo[2 * rho]) * xa.x;
+    const float fb = (float)(hi[2 * rho + 1] * 256 + lo[2 * rho + 1]) * xb.x;
+    const float uu = fmaf((float)((sm >> 8) & 255u), fb, (float)(sm & 255u) * fa);
+    const float vv = fmaf((float)(sm >> 24), xb.y, (float)((sm >> 16) & 255u) * xa.y);
+    float acc = rho ? acc1 : acc0;
+    acc = fmaf(dm.x, uu, acc);
+    acc = fmaf(-dm.y, vv, acc);
+    if (rho) acc1 = acc; else acc0 = acc;
+  }
+}
+
+// Shared memory: per-warp rings, then the B images and their sub-block sums.
+// Image of vector v: plane j (MMAs 4j..4j+3) of padded sub-block s at
+// img + v*nsb*64 + (j*nsb + s)*16; X at X + v*nsb + s.  Padded sub-block s
+// is row-local sub-block s - kPadL.
+__host__ __device__ inline size_t pk_ring_bytes(int unit) { return (size_t)kPkWarps * kSlots * 2 * unit; }
+__host__ __device__ inline size_t pk_img_bytes(int nvec, int nsb) { return (size_t)nvec * nsb * 64; }
+__host__ __device__ inline size_t pk_x_bytes(int nvec, int nsb) { return ((size_t)nvec * nsb * 8 + 15) & ~size_t(15); }
+__host__ __device__ inline size_t pk_smem(int unit, int nsb_max, int top_k) {
+  const int nv = top_k > 1 ? top_k : 1;
+  return pk_ring_bytes(unit) + pk_img_bytes(nv, nsb_max) + pk_x_bytes(nv, nsb_max) + 64;
+}
+
+// Router logits (tinyserve/_model_hooks.py:466-473), spread over the grid:
+// expert e is computed by warp e / grid of CTA e % grid (bf16 x . bf16 W[e] in
+// fp32, + bias, rounded to bf16 as the reference's bf16 Linear returns them),
+// published to global memory and counted (release) in sync[10].
+__device__ void pk_logits(const PkArgs& a, int warp, int lane) {
   const int H = a.H, n8 = H / 8;
-  const uint4* xr = static_cast<const uint4*>(a.x);
-  constexpr int kU = 12;  // 384 16-byte groups per pass: one pass for H <= 3072
-  for (int e = warp; e < a.n_experts; e += kPkWarps) {
+  const uint4* xr = reinterpret_cast<const uint4*>(a.x);
+  constexpr int kU = 12;
+  int mine = 0;
+  for (int e = blockIdx.x + gridDim.x * warp; e < a.E; e += gridDim.x * kPkWarps) {
     const uint4* wr = reinterpret_cast<const uint4*>(a.router_w + (int64_t)e * H);
     float acc = 0.f;
     for (int base = lane; base < n8; base += 32 * kU) {
@@ -474,17 +701,31 @@ __device__ void route_in_cta(const PkArgs& a, float* s_logit, int* s_e, float* s
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) s_logit[e] = bf16_bits_to_f32(f32_to_bf16_bits(a.router_b ? acc + a.router_b[e] : acc));
+    if (lane == 0) a.logits[e] = bf16_bits_to_f32(f32_to_bf16_bits(a.router_b ? acc + a.router_b[e] : acc));
+    ++mine;
   }
-  __syncthreads();
-  if (warp != 0) return;
+  if (mine && lane == 0) {
+    __threadfence();
+    atomicAdd(a.sync + 10, (unsigned)mine);
+  }
+}
+
+// Top-k of the published logits (ties -> lower id, NaN lowest) and softmax
+// over the k selected logits; warp 0 of every CTA reaches the same result,
+// CTA 0 publishes ids / weights.
+__device__ void pk_select(const PkArgs& a, float* s_logit, int* s_e, float* s_w, int lane) {
+  for (int e = lane; e < a.E; e += 32) s_logit[e] = __ldcg(a.logits + e);
+  __syncwarp();
   float sel[8];
   int sid[8];
   uint32_t taken = 0;  // bit j: expert lane + 32*j already selected (E <= 1024)
-  for (int k = 0; k < a.top_k; ++k) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    if (k >= a.top_k) break;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int j = 0; lane + 32 * j < a.n_experts; ++j) {
+#pragma unroll 1
+    for (int j = 0; lane + 32 * j < a.E; ++j) {
       if ((taken >> j) & 1u) continue;
       const int ee = lane + 32 * j;
       float v = s_logit[ee];
@@ -504,254 +745,515 @@ __device__ void route_in_cta(const PkArgs& a, float* s_logit, int* s_e, float* s
   if (lane == 0) {
     const float mx = sel[0];
     float den = 0.f, ex[8];
-    for (int k = 0; k < a.top_k; ++k) { ex[k] = __expf(sel[k] - mx); den += ex[k]; }
-    for (int k = 0; k < a.top_k; ++k) {
-      s_e[k] = sid[k];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k < a.top_k) { ex[k] = __expf(sel[k] - mx); den += ex[k]; }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k >= a.top_k) break;
+      const bool ok = (unsigned)sid[k] < (unsigned)a.E;
+      s_e[k] = ok ? sid[k] : -1;
       s_w[k] = ex[k] / den;
       if (blockIdx.x == 0) {
-        const_cast<int32_t*>(a.ids)[k] = sid[k];
-        const_cast<float*>(a.wts)[k] = ex[k] / den;
+        a.ids[k] = sid[k];
+        a.wts[k] = ex[k] / den;
       }
     }
-    // published before this CTA lets the down kernel launch, whose L2
-    // prefetch reads them (a hint; its real reads follow its PDL wait)
-    if (blockIdx.x == 0) __threadfence();
   }
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(kPkThreads, 1) packed_matvec_kernel(const PkArgs a) {
+// Power-of-two scale putting max |v| in [2^14, 2^15) (exact in fp32).
+__device__ __forceinline__ void pow2_scale(float m, float& scale, float& inv) {
+  const int ex = (int)((__float_as_uint(m) >> 23) & 255u);
+  int sx = (m > 0.f && ex != 255) ? 14 - (ex - 127) : 0;
+  sx = max(-126, min(126, sx));
+  scale = __uint_as_float((uint32_t)(sx + 127) << 23);
+  inv = __uint_as_float((uint32_t)(127 - sx) << 23);
+}
+
+// B image of one vector of length K (multiple of 32), 64 bytes per 32-element
+// sub-block in four 16-byte groups; group G of padded sub-block s sits at
+// img + (G*nsb + s)*16, the sub-block's float2 (x scale, scaled sum) at X[s].
+//   MXFP4 (f16 MMA): group G = element pairs 4G..4G+3 as f16x2, x scaled by
+//     a power of two per sub-block (max |x| in [2^14, 2^15)); X[s] = (2^-e, 0).
+//   Q4_K (int8 MMA): x_int = rint(x * 2^e) with e per sub-block (max |x_int|
+//     in [2^13, 2^14)), split x_int = 256*hi + lo (hi signed, lo unsigned):
+//     groups 0, 1 = hi bytes of elements 0-15, 16-31, groups 2, 3 = lo bytes;
+//     X[s] = (2^-e, 2^-e * sum x_int).
+// stage_group writes the 8 elements 8q..8q+7 of sub-block sb; the four groups
+// of a sub-block sit on four consecutive lanes (two shuffles combine them).
+template <bool Q4>
+__device__ __forceinline__ void stage_group(uint8_t* img, float2* X, int nsb, int sb, int q, const float (&v)[8],
+                                            bool valid) {
+  const int sp = sb + kPadL;
+  if (Q4) {
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, valid ? fabsf(v[i]) : 0.f);
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const int ex = (int)((__float_as_uint(m) >> 23) & 255u);
+    int sx = (m > 0.f && ex != 255) ? 13 - (ex - 127) : 0;
+    sx = max(-126, min(126, sx));
+    const float sc = __uint_as_float((uint32_t)(sx + 127) << 23);
+    uint32_t hi[2] = {0, 0}, lo[2] = {0, 0};
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int xi = valid ? __float2int_rn(v[i] * sc) : 0;
+      sum += xi;
+      hi[i >> 2] |= (uint32_t)((xi >> 8) & 255) << (8 * (i & 3));
+      lo[i >> 2] |= (uint32_t)(xi & 255) << (8 * (i & 3));
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (!valid) return;
+    *reinterpret_cast<uint2*>(img + ((size_t)(q >> 1) * nsb + sp) * 16 + 8 * (q & 1)) = make_uint2(hi[0], hi[1]);
+    *reinterpret_cast<uint2*>(img + ((size_t)(2 + (q >> 1)) * nsb + sp) * 16 + 8 * (q & 1)) = make_uint2(lo[0], lo[1]);
+    const float inv = __uint_as_float((uint32_t)(127 - sx) << 23);
+    if (q == 0) X[sp] = make_float2(inv, (float)sum * inv);
+  } else {
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, valid ? fabsf(v[i]) : 0.f);
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    float sc, inv;
+    pow2_scale(m, sc, inv);
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = __floats2half2_rn(v[2 * i] * sc, v[2 * i + 1] * sc);
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    if (!valid) return;
+    *reinterpret_cast<uint4*>(img + ((size_t)q * nsb + sp) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    if (q == 0) X[sp] = make_float2(inv, 0.f);
+  }
+}
+
+__device__ __forceinline__ void zero_pads(uint8_t* img, float2* X, int nsb, int K) {
+  const int real = K / 32;
+  constexpr int kPad = kPadL + kPadR;
+  // 4 planes x (kPadL + kPadR) padded sub-blocks of 16 bytes, plus their sums
+  for (int i = threadIdx.x; i < 4 * kPad; i += blockDim.x) {
+    const int j = i / kPad, s = i % kPad;
+    const int sp = s < kPadL ? s : real + s;  // [0, kPadL) and [kPadL + real, nsb)
+    *reinterpret_cast<uint4*>(img + ((size_t)j * nsb + sp) * 16) = make_uint4(0, 0, 0, 0);
+    if (j == 0) X[sp] = make_float2(0.f, 0.f);
+  }
+}
+
+// sum_{s < S} Q[32 s + lane] in order, with up to 8 loads in flight.
+__device__ __forceinline__ float sum_parts(const float* Q, int S, int lane) {
+  float sum = 0.f;
+  for (int s0 = 0; s0 < S; s0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = s0 + i < S ? __ldcg(Q + 32 * (s0 + i) + lane) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sum += v[i];
+  }
+  return sum;
+}
+
+template <int F>
+__global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a) {
+  constexpr bool Q4 = F == FMT_Q4_K;
+  constexpr int UNIT = Q4 ? kQ4Unit : kMxUnit, HDR = Q4 ? kQ4Hdr : kMxHdr;
   extern __shared__ uint4 smem4[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(smem4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  uint8_t* zero = sm + pk_zero_off(a.nv, a.KB);
-  uint8_t* ring = sm + pk_ring_off(a.nv, a.KB) + (size_t)warp * kSlots * kSlotBytes;
-  float* inv = reinterpret_cast<float*>(zero + 32);
-  __shared__ int s_e[8];
-  __shared__ uint64_t s_bar[kPkWarps][kSlots];
-  uint64_t* bar = s_bar[warp];
-  if (threadIdx.x < 8) reinterpret_cast<uint32_t*>(zero)[threadIdx.x] = 0u;
-  if (lane < kSlots) mbar_init(&bar[lane], 1);
-  fence_barrier_init();
-
-  const int gw0 = blockIdx.x * kPkWarps + warp, nw = gridDim.x * kPkWarps;
-  auto task_ptr = [&](int task, int e, int& kb0, int& kb1) {
-    const int rem = task % (a.R * a.S), rb = rem / a.S, s = rem % a.S;
-    kb0 = s * a.nkb;
-    kb1 = min(a.KB, kb0 + a.nkb);
-    return a.packed + (int64_t)e * a.expert_bytes + a.sec_off + ((int64_t)rb * a.KB + kb0) * kUnitBytes;
-  };
-  auto expert_of = [&](int u, bool report) {
-    const int e = a.ids[u];
-    if ((unsigned)e >= (unsigned)a.n_experts) {
-      if (report && a.err) atomicExch(a.err, kDevBadPlan);
-      return -1;
-    }
-    return e;
-  };
+  const int nsb_max = max(a.nsb_h, a.nsb_i);
+  const int nv_max = max(a.top_k, 1);
+  uint8_t* ring = sm + (size_t)warp * kSlots * 2 * UNIT;
+  uint8_t* img = sm + pk_ring_bytes(UNIT);
+  float2* Xs = reinterpret_cast<float2*>(img + pk_img_bytes(nv_max, nsb_max));
+  uint8_t* zero = reinterpret_cast<uint8_t*>(Xs) + pk_x_bytes(nv_max, nsb_max);  // 16-byte aligned
 
   __shared__ float s_logit[1024];
+  __shared__ int s_e[8];
   __shared__ float s_w[8];
-  bool routed_here = false;
-  if (MODE == 0) {
-    if (a.router_w) {
-      route_in_cta(a, s_logit, s_e, s_w, warp, lane);
-      routed_here = true;
+  __shared__ const float* s_bias[3][8];  // gate, up, down bias of each slot's expert
+  __shared__ float s_red[8][kPkWarps];
+  __shared__ uint64_t s_bar[kPkWarps][kSlots];
+  __shared__ int s_bad;
+  uint64_t* bar = s_bar[warp];
+  auto stamp = [&](int i) {
+    PK_T(if (threadIdx.x == 0 && blockIdx.x < 160) g_pk_trace[blockIdx.x * 16 + i] = gtimer();)
+    (void)i;
+  };
+  stamp(0);
+  if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(zero)[threadIdx.x] = 0u;
+  if (lane < kSlots) mbar_init(&bar[lane], 1);
+  if (threadIdx.x == 0) s_bad = 0;
+  fence_barrier_init();
+
+  // ---- router logits, spread over the grid (ids given: validated below)
+  if (a.router_w) pk_logits(a, warp, lane);
+
+  // ---- B image of x (one vector), its scale and sub-block sums, while the
+  // other CTAs' logits arrive.  Thread i owns 8-element groups i + 512u.
+  {
+    constexpr int kXR = 4;  // H <= 16384: at most 2048 groups
+    const int ng = a.H / 8;
+    uint4 xv[kXR];
+#pragma unroll
+    for (int u = 0; u < kXR; ++u) {
+      const int q = threadIdx.x + u * kPkThreads;
+      xv[u] = q < ng ? __ldg(reinterpret_cast<const uint4*>(a.x) + q) : make_uint4(0, 0, 0, 0);
     }
-    // x does not depend on the router kernel (when there is one): stage it
-    // while that runs
-    stage_vectors<0>(a, sm, inv, warp, lane);
-    pdl_wait();
-  } else {
-    // Pull this warp's weight ranges into L2 while gate/up finishes.  The ids
-    // read here are a hint only (routing inside the gate/up launch may not have
-    // published them yet); the ids used below are read after the wait.
-    if (lane == 0)
-      for (int task = gw0; task < a.ntasks; task += nw) {
-        const int e = expert_of(task / (a.R * a.S), false);
-        if (e < 0) continue;
-        int kb0, kb1;
-        const uint8_t* p = task_ptr(task, e, kb0, kb1);
-        prefetch_l2(p, (uint32_t)(kb1 - kb0) * kUnitBytes);
+    zero_pads(img, Xs, a.nsb_h, a.H);
+#pragma unroll
+    for (int u = 0; u < kXR; ++u) {
+      const int q0 = threadIdx.x - lane + u * kPkThreads;
+      if (q0 >= ng) break;  // warp-uniform
+      const int q = q0 + lane;
+      const uint32_t wv[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(wv[i] << 16);
+        v[2 * i + 1] = __uint_as_float(wv[i] & 0xFFFF0000u);
       }
-    pdl_wait();
+      stage_group<Q4>(img, Xs, a.nsb_h, q >> 2, q & 3, v, q < ng);
+    }
   }
-  if (!routed_here && threadIdx.x < a.top_k) s_e[threadIdx.x] = expert_of(threadIdx.x, true);
-  // bias pointers of the chosen experts, read once per CTA (the epilogues'
-  // only other dependent load)
-  __shared__ const float* s_bias[2][8];
+
+  // ---- routing: wait for every expert's logit, then top-k in each CTA
+  if (a.router_w) {
+    if (threadIdx.x == 0) {
+      bool ok = false;
+      for (uint32_t i = 0; i < kSpinPolls && !ok; ++i) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 10) : "memory");
+        ok = v >= (unsigned)a.E;
+        if (!ok) __nanosleep(32);
+      }
+      if (!ok) {
+        if (a.err) atomicExch(a.err, kDevWaitTimeout);
+        s_bad = 1;
+      }
+    }
+    __syncthreads();
+    if (warp == 0) pk_select(a, s_logit, s_e, s_w, lane);
+  } else if (threadIdx.x < a.top_k) {
+    const int e = a.ids[threadIdx.x];
+    const bool ok = (unsigned)e < (unsigned)a.E;
+    if (!ok && blockIdx.x == 0 && a.err) atomicExch(a.err, kDevBadPlan);
+    s_e[threadIdx.x] = ok ? e : -1;
+    s_w[threadIdx.x] = a.wts[threadIdx.x];
+  }
+  __syncthreads();
   if (threadIdx.x < a.top_k) {
     const int e = s_e[threadIdx.x];
     const TsbExpert* E = a.experts + (e < 0 ? 0 : e);
-    s_bias[0][threadIdx.x] = e < 0 ? nullptr : (MODE == 0 ? E->gate_bias : E->down_bias);
-    s_bias[1][threadIdx.x] = e < 0 ? nullptr : (MODE == 0 ? E->up_bias : nullptr);
+    s_bias[0][threadIdx.x] = e < 0 ? nullptr : E->gate_bias;
+    s_bias[1][threadIdx.x] = e < 0 ? nullptr : E->up_bias;
+    s_bias[2][threadIdx.x] = e < 0 ? nullptr : E->down_bias;
   }
-  pdl_launch_dependents();
-  if (MODE == 1) stage_vectors<1>(a, sm, inv, warp, lane);
-  __syncthreads();
 
-  uint32_t issued = 0, consumed = 0;  // slot fills / drains of this warp's ring
-  bool bad = false;                   // a slot wait ran out: stop streaming
-  // Per-task geometry (one division chain per task, not per slot).
-  struct TaskGeo {
+  stamp(1);
+  // ---- task geometry.  Global task list: gate/up tasks [0, n_gu), then down
+  // tasks; warp gw takes gw, gw + nw, ...  A task yields 2 units per chunk.
+  const int gw = blockIdx.x * kPkWarps + warp, nw = gridDim.x * kPkWarps, ntask = a.n_gu + a.n_dn;
+  struct Task {
     const uint8_t* p;  // first unit
-    int n, u, rb, kb0;
+    int n;             // units
+    int k, grp, s, c0, down;
   };
-  auto geo = [&](int task) {
-    TaskGeo G;
-    G.u = task / (a.R * a.S);
-    const int rem = task - G.u * (a.R * a.S);
-    G.rb = rem / a.S;
-    G.kb0 = (rem - G.rb * a.S) * a.nkb;
-    const int e = s_e[G.u];
-    G.n = e < 0 ? 0 : min(a.KB, G.kb0 + a.nkb) - G.kb0;
-    G.p = a.packed + (int64_t)(e < 0 ? 0 : e) * a.expert_bytes + a.sec_off +
-          ((int64_t)G.rb * a.KB + G.kb0) * kUnitBytes;
-    return G;
+  auto task_of = [&](int id) {
+    Task T;
+    T.down = id >= a.n_gu;
+    const int lid = T.down ? id - a.n_gu : id;
+    const int S = T.down ? a.S_dn : a.S_gu, G = T.down ? a.ndp : a.ngj, C = T.down ? a.C_dn : a.C_gu;
+    const int nc = T.down ? a.nc_dn : a.nc_gu;
+    T.s = lid % S;
+    T.grp = (lid / S) % G;
+    T.k = lid / (S * G);
+    T.c0 = T.s * nc;
+    const int e = s_e[T.k];
+    T.n = e < 0 ? 0 : 2 * (min(C, T.c0 + nc) - T.c0);
+    T.p = a.packed + (int64_t)(e < 0 ? 0 : e) * a.expert_bytes + (T.down ? a.dn_off : a.gu_off) +
+          ((int64_t)T.grp * C + T.c0) * 2 * UNIT;
+    return T;
   };
-  // issue cursor: the next (task, group) to fetch, running ahead of the consumer
-  int it_task = gw0, it_g = 0;
-  TaskGeo it_geo{};
-  if (gw0 < a.ntasks) it_geo = geo(gw0);
+  // issue cursor, running ahead of the consumer through the warp's tasks
+  uint32_t issued = 0, consumed = 0;
+  int it_id = gw, it_u = 0;
+  Task it{};
+  if (it_id < ntask) it = task_of(it_id);
   auto issue_next = [&]() {
-    while (it_task < a.ntasks && it_g * kSlotUnits >= it_geo.n) {
-      it_task += nw;
-      it_g = 0;
-      if (it_task < a.ntasks) it_geo = geo(it_task);
+    while (it_id < ntask && it_u >= it.n) {
+      it_id += nw;
+      it_u = 0;
+      if (it_id < ntask) it = task_of(it_id);
     }
-    if (it_task >= a.ntasks) return;
-    const uint32_t bytes = (uint32_t)min(kSlotUnits, it_geo.n - it_g * kSlotUnits) * kUnitBytes;
-    uint64_t* b = &bar[issued & (kSlots - 1)];
+    if (it_id >= ntask) return;
+    // one chunk: its two units are adjacent in the packed layout
+    uint64_t* b = &bar[issued % kSlots];
     if (lane == 0) {
-      mbar_arrive_expect_tx(b, bytes);
-      bulk_g2s(ring + (issued & (kSlots - 1)) * kSlotBytes, it_geo.p + (size_t)it_g * kSlotBytes, bytes, b);
+      mbar_arrive_expect_tx(b, 2 * UNIT);
+      bulk_g2s(ring + (issued % kSlots) * 2 * UNIT, it.p + (size_t)it_u * UNIT, 2 * UNIT, b);
     }
     ++issued;
-    ++it_g;
+    it_u += 2;
   };
 #pragma unroll
   for (int i = 0; i < kSlots; ++i) issue_next();
-  const int oq = 16 * lane, oc = 512 + 16 * g;
-
-  for (int task = gw0; task < a.ntasks; task += nw) {
-    const TaskGeo G = geo(task);
-    const int u = G.u, rb = G.rb, n = G.n, kb0 = G.kb0;
-    const int e = s_e[u];
-    float acc_lo = 0.f, acc_hi = 0.f, acc_lo1 = 0.f, acc_hi1 = 0.f;
-    if (n > 0 && !bad) {
-      const int v = MODE == 0 ? 0 : u;
-      const uint8_t* xb = g == 0 ? sm + (size_t)v * a.KB * 128 + (size_t)kb0 * 128 + 32 * t : zero;
-      const int xstep = g == 0 ? 128 : 0;
-      const float2* X = reinterpret_cast<const float2*>(sm + (size_t)a.nv * a.KB * 128) + (size_t)v * a.KB + kb0;
-      for (int u0 = 0; u0 < n; u0 += kSlotUnits) {
-        const uint32_t sl = consumed & (kSlots - 1);
-        if (!pk_warp_wait(&bar[sl], (consumed / kSlots) & 1u, a.err)) {
-          bad = true;
-          break;
-        }
-        ++consumed;
-        const uint8_t* slot = ring + sl * kSlotBytes;
-        if (u0 + kSlotUnits <= n) {
-          // full slot: independent units, two accumulator pairs
-#pragma unroll
-          for (int ui = 0; ui < kSlotUnits; ++ui)
-            unit_fma(slot + ui * kUnitBytes, oq, oc, xb + ui * xstep, X[ui], a.magic1024, a.magic64,
-                     (ui & 1) ? acc_lo1 : acc_lo, (ui & 1) ? acc_hi1 : acc_hi);
-        } else {
-          for (int ui = 0; ui < n - u0; ++ui)
-            unit_fma(slot + ui * kUnitBytes, oq, oc, xb + ui * xstep, X[ui], a.magic1024, a.magic64, acc_lo,
-                     acc_hi);
-        }
-        xb += kSlotUnits * xstep;
-        X += kSlotUnits;
-        __syncwarp();  // every lane has read the slot before it is refilled
-        issue_next();
-      }
+  // down weights beyond the ring: into L2 while gate/up streams
+  if (lane == 0)
+    for (int id = gw; id < ntask; id += nw) {
+      if (id < a.n_gu) continue;
+      const Task T = task_of(id);
+      if (T.n) prefetch_l2(T.p, (uint32_t)T.n * UNIT);
     }
-    acc_lo += acc_lo1;
-    acc_hi += acc_hi1;
-    // partial sums of rows g and g+8 live in the t == 0 lanes
-    float* P = a.part + (int64_t)task * 16;
+
+  __syncthreads();  // the x image is complete
+
+  // 0x54005400 (f16x2 64.0) as a register operand: each decode is one LOP3
+  const uint32_t m64 = 0x54005400u;
+  stamp(2);
+  bool bad = false;
+  PK_T(long long cy_wait = 0, cy_comp = 0, n_units = 0, cy_epi = 0, cy_issue = 0, cy_task = 0;)
+
+  // One task: stream its units, fold, publish 32 partial sums; the last task
+  // of a group runs the group's epilogue.
+  auto run_task = [&](int id) {
+    PK_T(const long long ct0 = clock64();)
+    const Task T = task_of(id);
+    const int nsb = T.down ? a.nsb_i : a.nsb_h;
+    const int v = T.down ? T.k : 0;
+    const uint8_t* im = img + pk_img_bytes(v, nsb);
+    const float2* X = Xs + (size_t)v * nsb;
+    int p0, p1;
+    if (T.down) {
+      p0 = p1 = a.dn_ph[T.grp];
+    } else {
+      p0 = a.gu_ph[2 * T.grp];
+      p1 = a.gu_ph[2 * T.grp + 1];
+    }
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    const int nchunks = T.n / 2;
+    for (int ci = 0; ci < nchunks && !bad; ++ci) {
+      const int c = T.c0 + ci;
+      const uint32_t sl = consumed % kSlots;
+      PK_T(const long long c0 = clock64();)
+      if (!warp_wait(&bar[sl], (consumed / kSlots) & 1u, a.err)) {
+        bad = true;
+        break;
+      }
+      PK_T(const long long c1 = clock64(); cy_wait += c1 - c0; n_units += 2;)
+      consumed += 1;
+      const uint8_t* uA = ring + sl * 2 * UNIT;
+      const uint8_t* uB = uA + UNIT;
+      // B sources (see chunk_mma): half 0 from lanes g == t, half 1 from g == t + 4
+      const size_t pst = (size_t)nsb * 16;
+      const int sA = 8 * c - p0 + t + kPadL, sB = 8 * c - p1 + t + kPadL;
+      const bool h0 = g == t, h1 = g == t + 4;
+      const int xa = 8 * c - p0 + 2 * t + kPadL, xb = 8 * c - p1 + 2 * t + kPadL;
+      const uint8_t* a0s = h0 ? im + (size_t)sA * 16 : zero;
+      const uint8_t* a1s = h1 ? im + (size_t)(sA + 4) * 16 : zero;
+      const size_t z0 = h0 ? pst : 0, z1 = h1 ? pst : 0;
+      if (Q4) {
+        int hA[4], lA[4], hB[4], lB[4];
+        if (p0 == p1)
+          chunk_imma<true>(uA + HDR, uB + HDR, a0s, a1s, nullptr, nullptr, z0, z1, 0, 0, lane, hA, lA, hB, lB);
+        else
+          chunk_imma<false>(uA + HDR, uB + HDR, a0s, a1s, h0 ? im + (size_t)sB * 16 : zero,
+                            h1 ? im + (size_t)(sB + 4) * 16 : zero, z0, z1, z0, z1, lane, hA, lA, hB, lB);
+        fold_q4(uA, hA, lA, X[xa], X[xa + 1], g, t, acc[0][0], acc[0][1]);
+        fold_q4(uB, hB, lB, X[xb], X[xb + 1], g, t, acc[1][0], acc[1][1]);
+      } else {
+        float dA[4], dB[4];
+        chunk_mma<false, true>(uA + HDR, uB + HDR, a0s, a1s, nullptr, nullptr, z0, z1, 0, 0, m64, lane, dA, dB);
+        unit_fold<false>(uA, dA, X[xa].x, X[xa + 1].x, g, t, acc[0][0], acc[0][1]);
+        unit_fold<false>(uB, dB, X[xb].x, X[xb + 1].x, g, t, acc[1][0], acc[1][1]);
+      }
+      __syncwarp();  // every lane has read both slots before they are refilled
+      PK_T(const long long c2 = clock64(); cy_comp += c2 - c1;)
+      issue_next();
+      PK_T(cy_issue += clock64() - c2;)
+    }
+    // partial sums of the task's 32 rows (rb, row): reduce over the quad
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        float s = acc[rb][r];
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        acc[rb][r] = s;
+      }
+    float* P = (T.down ? a.part_dn : a.part_gu) + (int64_t)(T.down ? id - a.n_gu : id) * 32;
     if (t == 0) {
-      P[g] = acc_lo;
-      P[g + 8] = acc_hi;
+      P[g] = acc[0][0];
+      P[g + 8] = acc[0][1];
+      P[16 + g] = acc[1][0];
+      P[24 + g] = acc[1][1];
     }
     // The warp barrier orders the lanes' partial stores before lane 0's
     // counter update; the update releases them at GPU scope (release is
     // cumulative) and acquires the other tasks' partials for the last one.
     __syncwarp();
-    const int slot = MODE == 0 ? u * a.R + rb : rb;
-    const unsigned need = MODE == 0 ? (unsigned)a.S : (unsigned)(a.top_k * a.S);
+    unsigned* cnt = T.down ? a.cnt_dn + T.grp : a.cnt_gu + T.k * a.ngj + T.grp;
+    const unsigned need = T.down ? (unsigned)(a.top_k * a.S_dn) : (unsigned)a.S_gu;
     unsigned last = 0;
     if (lane == 0) {
       unsigned old;
-      asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.cnt + slot) : "memory");
+      asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(cnt) : "memory");
       last = old == need - 1;
     }
     last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) continue;
-    if (MODE == 0) {
-      const int j = 8 * rb + lane;
-      if (lane < 8 && j < a.I) {
-        float gate = 0.f, up = 0.f;
-        const float* Q = a.part + (int64_t)(u * a.R + rb) * a.S * 16;
-        for (int s = 0; s < a.S; ++s) {
-          gate += __ldcg(Q + 16 * s + lane);
-          up += __ldcg(Q + 16 * s + lane + 8);
-        }
-        float r = 0.f;
-        if (e >= 0) {
-          gate *= inv[0];
-          up *= inv[0];
-          if (s_bias[0][u]) gate += s_bias[0][u][j];
-          if (s_bias[1][u]) up += s_bias[1][u][j];
-          r = act_fn(a.act, gate, up, a.limit, a.alpha);
-        }
-        a.act_out[(int64_t)u * a.I + j] = r;
+    PK_T(cy_task += clock64() - ct0;)
+    if (!last) return;
+    PK_T(const long long ce = clock64();)
+    if (!T.down) {
+      // gate/up epilogue: rows [0,16) gate, [16,32) up of the group's 16 outputs
+      const int k = T.k;
+      const float* Q = a.part_gu + (int64_t)(k * a.ngj + T.grp) * a.S_gu * 32;
+      // lanes 0-15 sum the gate rows, 16-31 the up rows; swap halves
+      const float sum = sum_parts(Q, a.S_gu, lane);
+      const float other = __shfl_xor_sync(0xffffffffu, sum, 16);
+      const float gate = sum, up = other;
+      const int j = lane < 16 ? a.gu_j[T.grp * 16 + lane] : -1;
+      float r = 0.f;
+      if (j >= 0 && s_e[k] >= 0) {
+        const float gb = s_bias[0][k] ? gate + s_bias[0][k][j] : gate;
+        const float ub = s_bias[1][k] ? up + s_bias[1][k][j] : up;
+        r = act_fn(a.act_kind, gb, ub, a.limit, a.alpha);
       }
+      if (j >= 0) a.act[(int64_t)k * a.I + j] = r;
+      __syncwarp();
+      if (lane == 0) a.cnt_gu[k * a.ngj + T.grp] = 0u;
     } else {
-      // lane = row (lane & 15) x half (lane >> 4); the halves take alternate
-      // (slot, split) partials, all loads issued before the sums, then one shuffle.
-      const int r = lane & 15, hf = lane >> 4, h = 16 * rb + r;
-      const int nks = a.top_k * a.S;
+      // down epilogue: 32 outputs, slots and splits combined in fixed order
+      const int h = a.dn_h[T.grp * 32 + lane];
       float o = 0.f;
-      for (int i0 = hf; i0 < nks; i0 += 16) {
-        float pv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int i = i0 + 2 * j;
-          const int k = i / a.S, sp = i - k * a.S;
-          pv[j] = (i < nks && s_e[min(k, 7)] >= 0) ? __ldcg(a.part + ((int64_t)(k * a.R + rb) * a.S + sp) * 16 + r) : 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int i = i0 + 2 * j;
-          if (i >= nks) break;
-          const int k = i / a.S;
-          o = fmaf(a.wts[k] * inv[k], pv[j], o);
-        }
+      for (int k = 0; k < a.top_k; ++k) {
+        if (s_e[k] < 0) continue;
+        const float* Q = a.part_dn + (int64_t)(k * a.ndp + T.grp) * a.S_dn * 32;
+        o = fmaf(s_w[k], sum_parts(Q, a.S_dn, lane), o);
       }
-      o += __shfl_xor_sync(0xffffffffu, o, 16);
-      if (lane < 16 && h < a.H) {
-        for (int k = 0; k < a.top_k; ++k) {
-          const int ek = s_e[k];
-          if (ek < 0) continue;
-          const float* bias = s_bias[0][k];
-          if (bias) o = fmaf(a.wts[k], bias[h], o);
-        }
-        a.out[h] = f32_to_bf16_bits(o);
+      if (h >= 0) {
+        for (int k = 0; k < a.top_k; ++k)
+          if (s_e[k] >= 0 && s_bias[2][k]) o = fmaf(s_w[k], s_bias[2][k][h], o);
+        if (a.out_f32)
+          static_cast<float*>(a.out)[h] = o;
+        else
+          static_cast<uint16_t*>(a.out)[h] = f32_to_bf16_bits(o);
+      }
+      __syncwarp();
+      if (lane == 0) a.cnt_dn[T.grp] = 0u;
+    }
+    PK_T(cy_epi += clock64() - ce;)
+  };
+
+  // ---- phase 0: gate/up tasks of this warp; phase 1: its down tasks.  One
+  // loop, so the task body exists once in the code (instruction cache).
+  int id = gw;
+  PK_T(if (lane == 0 && blockIdx.x < 160) g_pk_wtrace[(blockIdx.x * 16 + warp) * 8 + 7] = gtimer();)
+#pragma unroll 1
+  for (int phase = 0; phase < 2; ++phase) {
+  const int end = phase == 0 ? a.n_gu : ntask;
+#pragma unroll 1
+  for (; id < end; id += nw) run_task(id);
+  PK_T(if (lane == 0 && blockIdx.x < 160 && phase == 0) {
+    unsigned long long* W = g_pk_wtrace + (blockIdx.x * 16 + warp) * 8;
+    W[0] = gtimer();
+    W[1] = cy_wait;
+    W[2] = cy_comp;
+    W[3] = n_units;
+    W[4] = cy_issue;
+    W[5] = cy_epi;
+    W[6] = cy_task;
+  })
+  if (phase == 1) break;
+
+  // ---- all gate/up groups of every CTA done: stage the activations (CTA-wide).
+  // Each CTA arrives once its own tasks and epilogues are done (the barrier
+  // makes its warps' activation stores visible to thread 0, whose release
+  // publishes them), then waits for every CTA.
+  __syncthreads();
+  stamp(3);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(a.sync, 1u);
+    const unsigned need = gridDim.x;
+    bool ok = false;
+    for (uint32_t i = 0; i < kSpinPolls && !ok; ++i) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync) : "memory");
+      ok = v >= need;
+      if (!ok) __nanosleep(32);
+    }
+    if (!ok) {
+      if (a.err) atomicExch(a.err, kDevWaitTimeout);
+      s_bad = 1;
+    }
+  }
+  __syncthreads();
+  stamp(4);
+  if (s_bad) bad = true;
+  for (int vv = 0; vv < a.top_k; ++vv) zero_pads(img + pk_img_bytes(vv, a.nsb_i), Xs + (size_t)vv * a.nsb_i, a.nsb_i, a.I);
+  {
+    // every slot's activation groups (8 elements) as one flat range, 4 groups
+    // (8 loads of 16 B) in flight per thread: one L2 round trip for the
+    // GPT-OSS shapes.  The 4 groups of a sub-block are consecutive lanes of
+    // one slot (I % 32 == 0).
+    const int ngv = a.I / 8, total = a.top_k * ngv;
+    for (int q0 = threadIdx.x - lane; q0 < total; q0 += 4 * kPkThreads) {
+      float v[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int q = q0 + lane + u * kPkThreads;
+        const float4* src = reinterpret_cast<const float4*>(a.act) + 2 * (size_t)q;  // slots are contiguous
+        const float4 f0 = q < total ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 f1 = q < total ? __ldcg(src + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[u][0] = f0.x; v[u][1] = f0.y; v[u][2] = f0.z; v[u][3] = f0.w;
+        v[u][4] = f1.x; v[u][5] = f1.y; v[u][6] = f1.z; v[u][7] = f1.w;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int qw = q0 + u * kPkThreads;
+        if (qw >= total) break;  // warp-uniform
+        const int q = qw + lane;
+        const int vv = min(q / ngv, a.top_k - 1), qi = q - vv * ngv;
+        stage_group<Q4>(img + pk_img_bytes(vv, a.nsb_i), Xs + (size_t)vv * a.nsb_i, a.nsb_i, qi >> 2, qi & 3, v[u],
+                        q < total);
       }
     }
-    if (lane == 0) a.cnt[slot] = 0u;
   }
-  // copies still in flight after a timed-out wait land before the CTA exits
-  while (consumed < issued) {
-    if (!pk_warp_wait(&bar[consumed % kSlots], (consumed / kSlots) & 1u, a.err)) break;
-    ++consumed;
+  __syncthreads();
+  stamp(5);
+  }
+  __syncthreads();
+  stamp(6);
+
+
+  // copies still in flight land before the CTA exits (bounded: after a
+  // timed-out wait, keep waiting on later slots until none is left or the
+  // total budget runs out)
+  {
+    int misses = 0;
+    while (consumed < issued && misses < 4) {
+      if (!warp_wait(&bar[consumed % kSlots], (consumed / kSlots) & 1u, a.err)) ++misses;
+      ++consumed;
+    }
+  }
+  // the last CTA to finish resets the device-wide words for the next call
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.sync + 1) : "memory");
+    if (old == gridDim.x - 1) {
+      for (int i = 0; i < 11; ++i) a.sync[i] = 0u;
+      __threadfence();
+    }
   }
 }
 
-static int num_sms_pk() {
+static int num_sms() {
   static int n = 0;
   if (!n) {
     int dev = 0;
@@ -762,114 +1264,145 @@ static int num_sms_pk() {
   return n;
 }
 
-// K-split: k-blocks per task a multiple of kSlotUnits (so every slot but a
-// row's last is full), the smallest makespan (k-blocks per warp plus one of
-// per-task overhead) over the resident warps, at most kMaxSplit tasks per row.
-static int choose_nkb(int rows, int KB, int warps) {
-  int best = 0;
+// Chunks per task: the smallest makespan (units per warp, plus one unit of
+// per-task overhead) over the resident warps.
+static int choose_nc(int groups, int C, int warps) {
+  int best = 1;
   double best_t = 1e30;
-  const int top = (KB + kSlotUnits - 1) / kSlotUnits * kSlotUnits;
-  for (int nkb = kSlotUnits; nkb <= top; nkb += kSlotUnits) {
-    const int S = (KB + nkb - 1) / nkb;
-    if (S > kMaxSplit) continue;
-    const int64_t tasks = (int64_t)rows * S;
+  for (int nc = 1; nc <= C; ++nc) {
+    const int S = (C + nc - 1) / nc;
+    const int64_t tasks = (int64_t)groups * S;
     const double waves = (double)((tasks + warps - 1) / warps);
-    const double tm = waves * (nkb + 1);
+    const double tm = waves * (2.0 * nc + 1.0);
     if (tm < best_t - 1e-9) {
       best_t = tm;
-      best = nkb;
+      best = nc;
     }
   }
   return best;
 }
 
-size_t packed_ws_bytes(const TsbMoeSpec& sp) {
-  const PackGeom G = pack_geom(sp);
-  const int64_t parts =
-      (int64_t)sp.top_k * std::max<int64_t>((int64_t)G.rgu * std::min(G.kbh, kMaxSplit), (int64_t)G.rdn * std::min(G.kbi, kMaxSplit));
-  const int64_t cnts = std::max<int64_t>((int64_t)sp.top_k * G.rgu, G.rdn);
-  return (size_t)(parts * 16 * 4 + cnts * 4 + 512);
+// Workspace after the generic layer workspace: counters, device-wide words,
+// gate/up and down partial sums (sized for one chunk per task, the most).
+struct PkWs {
+  size_t cnt_gu, cnt_dn, sync, logits, part_gu, part_dn, total;
+};
+static PkWs pk_ws(const TsbMoeSpec& sp, const PkGeo& G) {
+  auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
+  PkWs W;
+  W.cnt_gu = 0;
+  W.cnt_dn = al(W.cnt_gu + 4 * (size_t)sp.top_k * G.ngj);
+  W.sync = al(W.cnt_dn + 4 * (size_t)G.ndp);
+  W.logits = al(W.sync + 64);
+  W.part_gu = al(W.logits + 4 * (size_t)sp.n_experts);
+  W.part_dn = al(W.part_gu + 4 * 32 * (size_t)sp.top_k * G.ngj * G.C_gu);
+  W.total = al(W.part_dn + 4 * 32 * (size_t)sp.top_k * G.ndp * G.C_dn);
+  return W;
 }
 
-constexpr size_t kPkSmemMax = 160 * 1024;
+size_t packed_ws_bytes(const TsbMoeSpec& sp) {
+  if (!packable(sp)) return 0;
+  return pk_ws(sp, pk_geo(sp, pk_maps(sp))).total;
+}
 
-// One CTA per SM (measured: two per SM, one task per warp, ran the layer in
-// 51 us against 43 us).
-constexpr int kPkCtasPerSm = 1;
+constexpr int kPkSmemMax = 220 * 1024;
 
-template <int MODE>
-static int launch_pk(PkArgs& a, int rows, cudaStream_t st, bool pdl) {
-  const int grid = kPkCtasPerSm * num_sms_pk();
-  a.nkb = choose_nkb(rows, a.KB, grid * kPkWarps);
-  a.S = (a.KB + a.nkb - 1) / a.nkb;
-  a.ntasks = rows * a.S;
-  const size_t smem = pk_smem(a.nv, a.KB);
+template <int F>
+static int launch_pk(PkArgs& a, size_t smem, cudaStream_t st) {
   static bool attr = [] {
-    return cudaFuncSetAttribute(packed_matvec_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)kPkSmemMax) == cudaSuccess;
+    return cudaFuncSetAttribute(pk_layer_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPkSmemMax) ==
+           cudaSuccess;
   }();
-  if (!attr || smem > kPkSmemMax)
-    return set_error(TSB_ERR_UNSUPPORTED, "packed decode: vectors too long for shared memory");
+  if (!attr || smem > kPkSmemMax) return set_error(TSB_ERR_UNSUPPORTED, "packed decode: layer too large for shared memory");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(num_sms());
   cfg.blockDim = dim3(kPkThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
   cfg.attrs = at;
-  cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, packed_matvec_kernel<MODE>, a);
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, pk_layer_kernel<F>, a);
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   return TSB_OK;
 }
 
-int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x,
-                         const int32_t* ids, const float* wts, float* act, void* out, int32_t* err, char* pws,
-                         cudaStream_t st, const void* router_w, const float* router_b) {
-  const PackGeom G = pack_geom(sp);
+int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x, int32_t* ids,
+                         float* wts, float* act, void* out, int out_f32, int32_t* err, char* pws, cudaStream_t st,
+                         const void* router_w, const float* router_b) {
+  // geometry depends only on the spec: cache the last one
+  static thread_local TsbMoeSpec last_sp{};
+  static thread_local PkGeo last_G{};
+  static thread_local bool have = false;
+  if (!have || memcmp(&last_sp, &sp, sizeof sp) != 0) {
+    last_G = pk_geo(sp, pk_maps(sp));
+    last_sp = sp;
+    have = true;
+  }
+  const PkGeo& G = last_G;
+  const PkWs W = pk_ws(sp, G);
+  const uint8_t* base = static_cast<const uint8_t*>(packed);
   PkArgs a{};
-  a.packed = static_cast<const uint8_t*>(packed);
+  a.packed = base + G.maps_bytes;
+  a.gu_j = reinterpret_cast<const int32_t*>(base + G.o_guj);
+  a.gu_ph = reinterpret_cast<const int32_t*>(base + G.o_guph);
+  a.dn_h = reinterpret_cast<const int32_t*>(base + G.o_dnh);
+  a.dn_ph = reinterpret_cast<const int32_t*>(base + G.o_dnph);
+  a.gu_off = G.gu_off;
+  a.dn_off = G.dn_off;
   a.expert_bytes = G.expert_bytes;
+  a.H = sp.hidden;
+  a.I = sp.inter;
+  a.E = sp.n_experts;
+  a.top_k = sp.top_k;
+  a.ngj = G.ngj;
+  a.ndp = G.ndp;
+  a.C_gu = G.C_gu;
+  a.C_dn = G.C_dn;
+  const int warps = num_sms() * kPkWarps;
+  a.nc_gu = choose_nc(sp.top_k * G.ngj, G.C_gu, warps);
+  a.S_gu = (G.C_gu + a.nc_gu - 1) / a.nc_gu;
+  a.nc_dn = choose_nc(sp.top_k * G.ndp, G.C_dn, warps);
+  a.S_dn = (G.C_dn + a.nc_dn - 1) / a.nc_dn;
+  a.n_gu = sp.top_k * G.ngj * a.S_gu;
+  a.n_dn = sp.top_k * G.ndp * a.S_dn;
+  a.nsb_h = sp.hidden / 32 + kPadL + kPadR;
+  a.nsb_i = sp.inter / 32 + kPadL + kPadR;
+  a.x = static_cast<const uint16_t*>(x);
+  a.router_w = static_cast<const uint16_t*>(router_w);
+  a.router_b = router_b;
   a.ids = ids;
   a.wts = wts;
   a.experts = ex;
-  a.n_experts = sp.n_experts;
-  a.top_k = sp.top_k;
-  a.err = err;
-  a.I = sp.inter;
-  a.H = sp.hidden;
-  a.act = sp.activation;
+  a.act = act;
+  a.cnt_gu = reinterpret_cast<unsigned*>(pws + W.cnt_gu);
+  a.cnt_dn = reinterpret_cast<unsigned*>(pws + W.cnt_dn);
+  a.sync = reinterpret_cast<unsigned*>(pws + W.sync);
+  a.part_gu = reinterpret_cast<float*>(pws + W.part_gu);
+  a.part_dn = reinterpret_cast<float*>(pws + W.part_dn);
+  a.logits = reinterpret_cast<float*>(pws + W.logits);
+
+  a.out = out;
+  a.out_f32 = out_f32;
+  a.act_kind = sp.activation;
   a.limit = sp.limit;
   a.alpha = sp.alpha;
-  a.act_out = act;
-  a.out = static_cast<uint16_t*>(out);
-  a.cnt = reinterpret_cast<unsigned*>(pws);
-  a.magic1024 = 0x64006400u;
-  a.magic64 = 0x54005400u;
-  const int64_t cnts = std::max<int64_t>((int64_t)sp.top_k * G.rgu, G.rdn);
-  a.part = reinterpret_cast<float*>(pws + ((cnts * 4 + 255) & ~int64_t(255)));
-
-  PkArgs gu = a;
-  gu.mode = 0;
-  gu.sec_off = G.gu_off;
-  gu.R = G.rgu;
-  gu.KB = G.kbh;
-  gu.x = x;
-  gu.nv = 1;
-  gu.router_w = static_cast<const uint16_t*>(router_w);
-  gu.router_b = router_b;
-  int rc = launch_pk<0>(gu, sp.top_k * G.rgu, st, false);
-  if (rc) return rc;
-  PkArgs dn = a;
-  dn.mode = 1;
-  dn.sec_off = G.dn_off;
-  dn.R = G.rdn;
-  dn.KB = G.kbi;
-  dn.x = act;
-  dn.nv = sp.top_k;
-  return launch_pk<1>(dn, sp.top_k * G.rdn, st, true);
+  a.err = err;
+  const int nsb_max = std::max(a.nsb_h, a.nsb_i);
+  if (G.q4) return launch_pk<FMT_Q4_K>(a, pk_smem(kQ4Unit, nsb_max, sp.top_k), st);
+  return launch_pk<FMT_MXFP4>(a, pk_smem(kMxUnit, nsb_max, sp.top_k), st);
 }
 
 }  // namespace tsb
+
+#if TSB_PK_TIMING
+// Development builds: copy the phase stamps ([160][16]) and per-warp counts
+// ([160][16][8]) to host memory.
+extern "C" int tsb_pk_timing_read(unsigned long long* stamps, unsigned long long* warps) {
+  cudaError_t e = cudaMemcpyFromSymbol(stamps, tsb::g_pk_trace, sizeof(unsigned long long) * 160 * 16);
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(warps, tsb::g_pk_wtrace, sizeof(unsigned long long) * 160 * 16 * 8);
+  return (int)e;
+}
+#endif

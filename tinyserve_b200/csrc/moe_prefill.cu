@@ -910,7 +910,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) grouped_gemm_pair_kernel(cons
 // decode combine's order); rows of invalid experts are skipped.
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ Y, int H,
                                                       const int* __restrict__ row_of, const float* __restrict__ wts,
-                                                      int top_k, uint16_t* __restrict__ out) {
+                                                      int top_k, void* __restrict__ out, int out_f32) {
   const int t = blockIdx.x;
   for (int h4 = threadIdx.x; h4 < H / 4; h4 += blockDim.x) {
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -924,9 +924,13 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
       o.z = fmaf(w, y.z, o.z);
       o.w = fmaf(w, y.w, o.w);
     }
-    const uint32_t lo = f32_to_bf16_bits(o.x) | ((uint32_t)f32_to_bf16_bits(o.y) << 16);
-    const uint32_t hi = f32_to_bf16_bits(o.z) | ((uint32_t)f32_to_bf16_bits(o.w) << 16);
-    reinterpret_cast<uint2*>(out + (size_t)t * H)[h4] = make_uint2(lo, hi);
+    if (out_f32) {
+      reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)t * H)[h4] = o;
+    } else {
+      const uint32_t lo = f32_to_bf16_bits(o.x) | ((uint32_t)f32_to_bf16_bits(o.y) << 16);
+      const uint32_t hi = f32_to_bf16_bits(o.z) | ((uint32_t)f32_to_bf16_bits(o.w) << 16);
+      reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + (size_t)t * H)[h4] = make_uint2(lo, hi);
+    }
   }
 }
 
@@ -1239,7 +1243,7 @@ int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x,
       : L.pair ? launch_gemm_pair(d, L.mb_max * d.ntiles, st)
                : launch_gemm<0>(d, L.mb_max * d.ntiles, st);
   if (rc) return rc;
-  combine_kernel<<<T, 256, 0, st>>>(Y, sp.hidden, row_of, wts, k, static_cast<uint16_t*>(out));
+  combine_kernel<<<T, 256, 0, st>>>(Y, sp.hidden, row_of, wts, k, out, sp.out_f32 != 0);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   return TSB_OK;

@@ -38,18 +38,14 @@ int launch_moe_prefill(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x,
                        cudaStream_t st);
 int launch_route(const TsbMoeSpec& sp, const void* x, int T, const void* rw, const float* rb, int32_t* ids,
                  float* wts, cudaStream_t st);
-// Decode-packed experts (batch-1 decode of 4-bit K-quant layers).
-struct PackGeom {
-  int64_t gu_off, dn_off, expert_bytes;  // per expert: gate/up units, then down units
-  int rgu, rdn, kbh, kbi;                // row blocks (8 outputs / 16 rows) and 64-wide k-blocks
-};
+// Decode-packed experts (batch-1 decode of Q4_K and MXFP4 layers).
 bool packable(const TsbMoeSpec& sp);
-PackGeom pack_geom(const TsbMoeSpec& sp);
+size_t packed_total_bytes(const TsbMoeSpec& sp);
 int launch_pack(const TsbMoeSpec& sp, const TsbExpert* experts, void* packed, cudaStream_t st);
 size_t packed_ws_bytes(const TsbMoeSpec& sp);
-int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x,
-                         const int32_t* ids, const float* wts, float* act, void* out, int32_t* err, char* pws,
-                         cudaStream_t st, const void* router_w, const float* router_b);
+int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x, int32_t* ids,
+                         float* wts, float* act, void* out, int out_f32, int32_t* err, char* pws, cudaStream_t st,
+                         const void* router_w, const float* router_b);
 int launch_dequant(int fmt, const void* w, const void* s, int64_t rows, int64_t cols, void* out, int odt,
                    cudaStream_t st);
 

@@ -50,7 +50,10 @@ class QuantMoE:
             raise RuntimeError("QuantMoE needs the expert weights on a CUDA device")
         self.experts = experts
         self.spec = _lib.TsbMoeSpec(fmt_gate_up, fmt_down, hidden, inter, len(experts), top_k,
-                                    LAYOUTS[gate_up_layout], ACTIVATIONS[activation], limit, alpha)
+                                    LAYOUTS[gate_up_layout], ACTIVATIONS[activation], limit, alpha, 0)
+        # the same layer with an fp32 output (the unrounded combine)
+        self.spec_f32 = _lib.TsbMoeSpec(fmt_gate_up, fmt_down, hidden, inter, len(experts), top_k,
+                                        LAYOUTS[gate_up_layout], ACTIVATIONS[activation], limit, alpha, 1)
         self.hidden, self.inter, self.top_k = hidden, inter, top_k
         self.router_w = router_w.contiguous() if router_w is not None else None
         self.router_b = router_b.float().contiguous() if router_b is not None else None
@@ -63,13 +66,15 @@ class QuantMoE:
         self._ws_cache: dict[int, torch.Tensor] = {}
         self._pws_cache: dict[int, torch.Tensor] = {}
         self._fast: dict[int, tuple] = {}
-        # Batch-1 decode on a decode-packed copy of the experts (Q4_K layers):
-        # built once here, 1.33x the Q4_K bytes; pack=None packs when the
-        # spec has a packed form, pack=False keeps the generic decode engine.
+        # Batch-1 decode on a decode-packed copy of the experts (Q4_K and MXFP4
+        # layers): built once here (~1.0-1.07x the quantised bytes); pack=None
+        # packs when the spec has a packed form, pack=False keeps the generic
+        # decode engine.
         self._packed = None
         nbytes = _lib.lib().tsb_moe_packed_bytes(ctypes.byref(self.spec))
         if pack and not nbytes:
-            raise ValueError("this layer has no packed form (needs Q4_K gate/up and down, H and I multiples of 64)")
+            raise ValueError("this layer has no packed form (needs Q4_K or MXFP4 gate/up and down, H and I "
+                             "multiples of 32)")
         if nbytes and pack is not False:
             self._packed = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
             _lib.check(_lib.lib().tsb_moe_pack(ctypes.byref(self.spec), self._table.data_ptr(),
@@ -81,12 +86,14 @@ class QuantMoE:
         """True when batch-1 decode runs on the decode-packed expert copy."""
         return self._packed is not None
 
-    def _decode_call(self):
-        """(C function, leading arguments) of this layer's decode entry point."""
+    def _decode_call(self, f32: bool = False):
+        """(C function, leading arguments) of this layer's decode entry point
+        (fp32 output when `f32`)."""
         L = _lib.lib()
+        spec = ctypes.byref(self.spec_f32 if f32 else self.spec)
         if self._packed is not None:
-            return L.tsb_moe_decode_packed, (ctypes.byref(self.spec), self._packed.data_ptr(), self._table.data_ptr())
-        return L.tsb_moe_decode, (ctypes.byref(self.spec), self._table.data_ptr())
+            return L.tsb_moe_decode_packed, (spec, self._packed.data_ptr(), self._table.data_ptr())
+        return L.tsb_moe_decode, (spec, self._table.data_ptr())
 
     def workspace(self, T: int) -> torch.Tensor:
         if T not in self._ws_cache:
@@ -97,12 +104,14 @@ class QuantMoE:
         return self._ws_cache[T]
 
     def decode(self, x: torch.Tensor, ids: torch.Tensor | None = None, weights: torch.Tensor | None = None,
-               out: torch.Tensor | None = None):
+               out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16):
         """T tokens through the layer.  x: bf16 [T, H] ([1, H] for batch-1
-        decode; T > 1 runs the grouped path, each routed expert read once for
-        all its tokens).  With a router, returns (out, ids, weights) where ids /
-        weights are the routing it chose; without one, ``ids`` (int32 [T, k])
-        and ``weights`` (fp32 [T, k]) are inputs."""
+        decode; up to 16 tokens run the batch-1 path per token, more the
+        grouped path, each routed expert read once for all its tokens).  With a
+        router, returns (out, ids, weights) where ids / weights are the routing
+        it chose; without one, ``ids`` (int32 [T, k]) and ``weights`` (fp32
+        [T, k]) are inputs.  ``out_dtype`` bf16 (default) or float32 (the
+        unrounded combine; a given ``out`` decides by its own dtype)."""
         if x.dtype != torch.bfloat16:
             raise TypeError("x must be bfloat16")
         x = x.contiguous()
@@ -117,9 +126,11 @@ class QuantMoE:
             ids = ids.to(device=self.device, dtype=torch.int32).contiguous()
             weights = weights.to(device=self.device, dtype=torch.float32).contiguous()
         if out is None:
-            out = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=self.device)
+            out = torch.empty(T, self.hidden, dtype=out_dtype, device=self.device)
+        if out.dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError("out must be bfloat16 or float32")
         ws = self.workspace(T)
-        fn, lead = self._decode_call()
+        fn, lead = self._decode_call(out.dtype == torch.float32)
         rc = fn(
             *lead, x.data_ptr(), T,
             None if given else _p(self.router_w), None if given else _p(self.router_b),
@@ -159,7 +170,7 @@ class QuantMoE:
         return self._pws_cache[T]
 
     def prefill(self, x: torch.Tensor, ids: torch.Tensor | None = None, weights: torch.Tensor | None = None,
-                out: torch.Tensor | None = None):
+                out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16):
         """T tokens through the layer as grouped GEMMs (the reference's batched
         path, ``ExpertPipeline.execute_layer_experts_batched``,
         tinyserve/expert_pipeline.py:166-239).  x: bf16 [T, H]; routing as in
@@ -182,12 +193,14 @@ class QuantMoE:
             if ids.shape != (T, self.top_k) or weights.shape != (T, self.top_k):
                 raise ValueError(f"ids and weights must be [T, {self.top_k}]")
         if out is None:
-            out = torch.empty(T, self.hidden, dtype=torch.bfloat16, device=self.device)
+            out = torch.empty(T, self.hidden, dtype=out_dtype, device=self.device)
+        if out.dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError("out must be bfloat16 or float32")
         if T == 0:
             return out, ids, weights
         ws = self.prefill_workspace(T)
         rc = _lib.lib().tsb_moe_prefill(
-            ctypes.byref(self.spec), self._table.data_ptr(), x.data_ptr(), T,
+            ctypes.byref(self.spec_f32 if out.dtype == torch.float32 else self.spec), self._table.data_ptr(), x.data_ptr(), T,
             None if given else _p(self.router_w), None if given else _p(self.router_b),
             ids.data_ptr(), weights.data_ptr(), out.data_ptr(), ws.data_ptr(), ws.numel(),
             torch.cuda.current_stream(self.device).cuda_stream)
