@@ -13,7 +13,6 @@ import torch
 
 from . import quantize as Q
 from .formats import GGML_Q4_K, TSB_MXFP4
-from .moe import ExpertWeights, QuantMoE
 
 H20, I20, E20, K20 = 2880, 2880, 32, 4
 
@@ -23,12 +22,12 @@ def gen_normal(shape, seed: int, std: float, device) -> torch.Tensor:
     return torch.randn(*shape, generator=g, device=device) * std
 
 
-def build_layer(fmt: int = GGML_Q4_K, *, hidden: int = H20, inter: int = I20, n_experts: int = E20,
-                top_k: int = K20, seed: int = 0, device="cuda", layout: str | None = None,
-                activation: str = "swiglu_oai") -> QuantMoE:
-    """One MoE layer with every expert HBM-resident.  GGUF formats use separate
-    gate/up matrices (GGUF stores, mmap_store.py:86-91); MXFP4 uses the
-    interleaved gate_up [2I, H] of the HF GPT-OSS checkpoint."""
+def layer_weights(fmt: int = GGML_Q4_K, *, hidden: int = H20, inter: int = I20, n_experts: int = E20,
+                  seed: int = 0, device="cuda", layout: str | None = None):
+    """The seeded expert weights and router of one layer as plain tensors
+    (no library call): a list of per-expert dicts of uint8 block streams
+    (GGUF formats: gate, up, down; MXFP4: gate = interleaved gate_up [2I, H]
+    blocks, gate_scales, down, down_scales) and the bf16 router [E, H]."""
     device = torch.device(device)
     layout = layout or ("interleaved" if fmt == TSB_MXFP4 else "separate")
     experts = []
@@ -39,17 +38,30 @@ def build_layer(fmt: int = GGML_Q4_K, *, hidden: int = H20, inter: int = I20, n_
             gb, gs = Q.quantize_mxfp4(gu, 2 * inter, hidden)
             dn = gen_normal((hidden, inter), s + 2, 0.02, device)
             db, ds = Q.quantize_mxfp4(dn, hidden, inter)
-            experts.append(ExpertWeights(gate=gb.reshape(-1), down=db.reshape(-1), gate_scales=gs.reshape(-1),
-                                         down_scales=ds.reshape(-1)))
+            experts.append(dict(gate=gb.reshape(-1), down=db.reshape(-1), gate_scales=gs.reshape(-1),
+                                down_scales=ds.reshape(-1)))
             del gu, dn
         else:
             g = Q.quantize(fmt, gen_normal((inter, hidden), s, 0.02, device))
             u = Q.quantize(fmt, gen_normal((inter, hidden), s + 1, 0.02, device))
             d = Q.quantize(fmt, gen_normal((hidden, inter), s + 2, 0.02, device))
-            experts.append(ExpertWeights(gate=g, up=u, down=d))
+            experts.append(dict(gate=g, up=u, down=d))
     router = gen_normal((n_experts, hidden), seed * 100003 + 99991, 0.02, device).to(torch.bfloat16)
-    return QuantMoE(experts, fmt_gate_up=fmt, fmt_down=fmt, hidden=hidden, inter=inter, top_k=top_k,
-                    router_w=router, gate_up_layout=layout, activation=activation)
+    return experts, router, layout
+
+
+def build_layer(fmt: int = GGML_Q4_K, *, hidden: int = H20, inter: int = I20, n_experts: int = E20,
+                top_k: int = K20, seed: int = 0, device="cuda", layout: str | None = None,
+                activation: str = "swiglu_oai", pack: bool | None = None):
+    """One MoE layer with every expert HBM-resident.  GGUF formats use separate
+    gate/up matrices (GGUF stores, mmap_store.py:86-91); MXFP4 uses the
+    interleaved gate_up [2I, H] of the HF GPT-OSS checkpoint."""
+    from .moe import ExpertWeights, QuantMoE
+    experts, router, layout = layer_weights(fmt, hidden=hidden, inter=inter, n_experts=n_experts, seed=seed,
+                                            device=device, layout=layout)
+    return QuantMoE([ExpertWeights(**e) for e in experts], fmt_gate_up=fmt, fmt_down=fmt, hidden=hidden,
+                    inter=inter, top_k=top_k, router_w=router, gate_up_layout=layout, activation=activation,
+                    pack=pack)
 
 
 def hidden_states(steps: int, hidden: int = H20, seed: int = 0, device="cuda") -> torch.Tensor:
@@ -57,7 +69,7 @@ def hidden_states(steps: int, hidden: int = H20, seed: int = 0, device="cuda") -
     return gen_normal((steps, hidden), 10_000_019 + seed, 1.0, device).to(torch.bfloat16)
 
 
-def layer_bytes(layer: QuantMoE) -> tuple[int, int]:
+def layer_bytes(layer) -> tuple[int, int]:
     """(bytes of one expert's weights, router bytes)."""
     e = layer.experts[0]
     n = sum(t.numel() for t in (e.gate, e.up, e.down, e.gate_scales, e.up_scales, e.down_scales) if t is not None)
