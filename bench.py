@@ -7,12 +7,14 @@ layer (router -> top-4 -> gate/up -> SwiGLU -> down -> weighted combine).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-The same JSON line carries secondary measurements inside objects the driver
-record keeps: roofline.decode_mxfp4 (the config-1 shape with MXFP4 experts),
-prefill (4096-token MXFP4 layer as grouped tcgen05 GEMMs,
-TFLOP/s against the measured tensor peak), prefill.expert_parallel_config5
-(the GPT-OSS-120B-shaped layer sharded over the ranks) and, on rank 0,
-prefill.matvec_sweep.
+The same JSON line carries secondary measurements as flat scalar keys of
+objects the driver record keeps: roofline.mxfp4_* (the config-1 shape with
+MXFP4 experts), prefill (4096-token MXFP4 layer as grouped
+tcgen05 GEMMs, TFLOP/s against the measured tensor peak), prefill.matvec_*
+(rank 0: fraction of HBM peak per format and shape) and
+prefill.ep_* (the GPT-OSS-120B-shaped layer sharded
+expert-parallel over the ranks; decode T=1, T=64 and 4096-token prefill
+tok/s, with the collectives and the local layer timed alone beside each).
 
 N > 1 runs under torchrun, one process per GPU; every rank decodes its own
 token stream through its own HBM-resident copy of the layer (the batch-1
@@ -406,40 +408,19 @@ def run_matvec_sweep(dev, reps: int = 6, calls: int = 24):
             "results": out}
 
 
-EP_T = 4096  # tokens per rank per layer call (weak scaling)
+EP_T = 4096  # prefill tokens per rank per layer call (weak scaling)
+EP_DECODE_T = (1, 64)  # decode tokens per rank per layer call
 
 
-def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
-    """BASELINE config 5: GPT-OSS-120B-shaped MXFP4 layer (128 experts, top-4,
-    H = I = 2880) sharded expert-parallel over the ranks (128/N experts each),
-    every rank routing its own 4096 tokens (seeded N(0,1), router bf16
-    N(0,0.02)); dispatch and combine over NCCL (all-to-all-v), local experts as
-    grouped tcgen05 GEMMs.  value = tokens of all ranks / max-over-ranks time."""
+def _ep_time(call, steps: int, warmup: int, ws: int, dev) -> float:
+    """ms per call: CUDA events on the current stream around `steps` calls
+    after a barrier, max over ranks."""
     import torch
-    from tinyserve_b200.formats import TSB_MXFP4
-    from tinyserve_b200.moe import QuantMoE, Router
-    from tinyserve_b200.workloads import build_layer, gen_normal, hidden_states
-    E, k = 128, 4
-    el = E // ws
-    # only this rank's experts are built (seeded per rank)
-    full = build_layer(TSB_MXFP4, n_experts=el, top_k=1, seed=5000 + rank, device=dev)
-    local = QuantMoE(full.experts, fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=2880, inter=2880, top_k=1,
-                     gate_up_layout="interleaved")
-    router = Router(gen_normal((E, 2880), 77, 0.02, dev).to(torch.bfloat16), k)
-    x = hidden_states(EP_T, seed=100 + rank, device=dev)
-    if ws > 1:
-        import torch.distributed as dist
-        from tinyserve_b200.ep import ExpertParallelMoE, quant_local_forward
-        layer = ExpertParallelMoE(E, k, 2880, quant_local_forward(local), router=router)
-        call = lambda: layer(x)  # noqa: E731
-    else:
-        whole = QuantMoE(full.experts, fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=2880, inter=2880, top_k=k,
-                         router_w=router.router_w, gate_up_layout="interleaved")
-        call = lambda: whole.decode(x)  # noqa: E731
     for _ in range(warmup):
         call()
     torch.cuda.synchronize()
     if ws > 1:
+        import torch.distributed as dist
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -450,16 +431,87 @@ def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     if ws > 1:
+        import torch.distributed as dist
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    return {"metric": "moe_layer_ep_prefill_tok_s", "value": ws * EP_T / (ms * 1e-3), "unit": "tok/s",
-            "ms_per_layer": ms, "n_gpus": ws, "steps": steps, "warmup": warmup, "scaling": "weak",
-            "config": {"workload": "BASELINE config 5: GPT-OSS-120B-shaped MXFP4 MoE layer (128 experts, top-4), "
-                                   f"{EP_T} tokens per rank, experts sharded {el} per GPU",
-                       "parallelism": f"ep{ws}" if ws > 1 else "single GPU (all 128 experts local)",
-                       "exchange": "NCCL all_to_all_single (uneven splits) for rows, expert ids and outputs",
-                       "timing": "CUDA events, max over ranks"}}
+    return ms
+
+
+def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
+    """BASELINE config 5: GPT-OSS-120B-shaped MXFP4 layer (128 experts, top-4,
+    H = I = 2880) sharded expert-parallel over the ranks (128/N experts each),
+    every rank routing its own tokens (seeded N(0,1), router bf16 N(0,0.02)).
+
+    Legs (each: tokens of all ranks / max-over-ranks time of one layer call):
+    decode T=1 and T=64 per rank through ``forward_gather`` (all-gather of
+    tokens and routing, local experts with other ranks' slots skipped, fp32
+    reduce-scatter; no host synchronisation), and the 4096-token prefill
+    through both schemes (``forward_gather`` and the all-to-all ``forward``).
+    Beside each EP leg: the same collectives alone (``comm_ms``) and the local
+    layer alone on the gathered rows (``local_ms``), which name the limiter.
+    At N = 1 the whole layer runs on one GPU with no exchange."""
+    import torch
+    from tinyserve_b200.formats import TSB_MXFP4
+    from tinyserve_b200.moe import QuantMoE, Router
+    from tinyserve_b200.workloads import build_layer, gen_normal, hidden_states
+    E, k, H = 128, 4, 2880
+    el = E // ws
+    # only this rank's experts are built (seeded per rank)
+    part = build_layer(TSB_MXFP4, n_experts=el, top_k=k, seed=5000 + rank, device=dev)
+    router = Router(gen_normal((E, H), 77, 0.02, dev).to(torch.bfloat16), k)
+    res = {"n_gpus": ws, "experts_per_gpu": el, "timing": "CUDA events around eager layer calls, max over ranks"}
+    legs = [("decode_t1", 1, 50), ("decode_t64", 64, 30), ("prefill", EP_T, steps)]
+    if ws == 1:
+        whole = QuantMoE(part.experts, fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=H, inter=H, top_k=k,
+                         router_w=router.router_w, gate_up_layout="interleaved")
+        for name, T, n in legs:
+            x = hidden_states(T, seed=100 + rank, device=dev)
+            ms = _ep_time(lambda: whole.decode(x), n, warmup, ws, dev)
+            res[f"{name}_tok_s"] = T / (ms * 1e-3)
+            res[f"{name}_ms"] = ms
+        res["exchange"] = "none (all 128 experts on one GPU)"
+        return res
+    import torch.distributed as dist
+    from tinyserve_b200.ep import ExpertParallelMoE, quant_layer_forward, quant_local_forward
+    local1 = QuantMoE(part.experts, fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=H, inter=H, top_k=1,
+                      gate_up_layout="interleaved", pack=False)
+    lf = quant_layer_forward(part)
+    gather = ExpertParallelMoE(E, k, H, router=router, layer_forward=lf)
+    a2a = ExpertParallelMoE(E, k, H, quant_local_forward(local1), router=router)
+    for name, T, n in legs:
+        x = hidden_states(T, seed=100 + rank, device=dev)
+        ms = _ep_time(lambda: gather.forward_gather(x), n, warmup, ws, dev)
+        res[f"{name}_tok_s"] = ws * T / (ms * 1e-3)
+        res[f"{name}_ms"] = ms
+        # the collectives alone, same sizes
+        xa = torch.empty(ws * T, H, dtype=torch.bfloat16, device=dev)
+        ma = torch.empty(ws * T, 2 * k, dtype=torch.float32, device=dev)
+        meta = torch.zeros(T, 2 * k, dtype=torch.float32, device=dev)
+        pa = torch.zeros(ws * T, H, dtype=torch.float32, device=dev)
+        o = torch.empty(T, H, dtype=torch.float32, device=dev)
+
+        def comm():
+            dist.all_gather_into_tensor(xa, x)
+            dist.all_gather_into_tensor(ma, meta)
+            dist.reduce_scatter_tensor(o, pa)
+        res[f"{name}_comm_ms"] = _ep_time(comm, n, warmup, ws, dev)
+        res[f"{name}_comm_mb"] = (xa.numel() * 2 + ma.numel() * 4 + pa.numel() * 4) * (ws - 1) / ws / 1e6
+        # the local layer alone on gathered rows with this rank's share of slots
+        ids, w = router(hidden_states(ws * T, seed=900 + rank, device=dev))
+        lid = ids - rank * el
+        lid = torch.where((lid >= 0) & (lid < el), lid, torch.full_like(lid, -1))
+        xg = hidden_states(ws * T, seed=901, device=dev)
+        res[f"{name}_local_ms"] = _ep_time(lambda: lf(xg, lid, w), n, warmup, 1, dev)
+        if name == "prefill":
+            ms = _ep_time(lambda: a2a(x), n, warmup, ws, dev)
+            res["prefill_a2a_tok_s"] = ws * T / (ms * 1e-3)
+            res["prefill_a2a_ms"] = ms
+        del xa, ma, pa
+        torch.cuda.empty_cache()
+    res["exchange"] = ("forward_gather: NCCL all_gather_into_tensor (bf16 tokens + routing) and reduce_scatter_tensor "
+                       "(fp32 partials); prefill_a2a: NCCL all_to_all_single with uneven splits")
+    return res
 
 
 def cpu_model() -> str:
@@ -579,15 +631,21 @@ def main():
     del layers
     torch.cuda.empty_cache()
     if not args.no_prefill:
-        # secondary measurements sit inside objects the driver record keeps
-        res["roofline"]["decode_mxfp4"] = run_decode_mxfp4(dev, min(args.steps, 200), args.warmup, ws, rank)
+        # secondary measurements ride as flat scalar keys of objects the
+        # driver record keeps (nested objects are dropped from it)
+        mx = run_decode_mxfp4(dev, min(args.steps, 200), args.warmup, ws, rank)
+        res["roofline"].update({"mxfp4_tok_s": mx["value"], "mxfp4_us_per_step": mx["ms_per_step"] * 1e3,
+                                "mxfp4_achieved": mx["achieved"], "mxfp4_frac": mx["frac"]})
         torch.cuda.empty_cache()
         pf = run_prefill(dev)
         torch.cuda.empty_cache()
-        pf["expert_parallel_config5"] = run_ep(dev, ws, rank)
-        torch.cuda.empty_cache()
         if rank == 0:
-            pf["matvec_sweep"] = run_matvec_sweep(dev)
+            for r in run_matvec_sweep(dev)["results"]:
+                pf[f"matvec_{r['format']}_{r['rows']}x{r['cols']}_frac"] = round(r["frac"], 4)
+        torch.cuda.empty_cache()
+        ep = run_ep(dev, ws, rank)
+        torch.cuda.empty_cache()
+        pf.update({f"ep_{k}": (round(v, 4) if isinstance(v, float) else v) for k, v in ep.items()})
         res["prefill"] = pf
     if host is not None:
         threads = len(os.sched_getaffinity(0))

@@ -132,7 +132,10 @@ size_t tsb_moe_decode_workspace(const TsbMoeSpec* spec, int32_t T);
  *   x         bf16 [T, H]
  *   router_w  bf16 [E, H] (NULL: ids/weights are inputs)
  *   router_b  fp32 [E] or NULL
- *   ids       int32 [T, top_k]  (output if router_w != NULL, else input)
+ *   ids       int32 [T, top_k]  (output if router_w != NULL, else input; as
+ *             an input, a negative id marks a slot this call skips, e.g. an
+ *             expert another rank owns, and an id >= n_experts is an error
+ *             reported through the device error word)
  *   weights   fp32  [T, top_k]  (same)
  *   out       [T, H] = sum_k weights[t,k] * expert_{ids[t,k]}(x[t]), bf16, or
  *             fp32 when spec->out_f32 is set */

@@ -99,3 +99,51 @@ def _bad_worker(rank, world, port):
     else:
         raise AssertionError("5 experts over 2 ranks must be rejected")
     dist.destroy_process_group()
+
+
+def _gather_worker(rank, world, port, T, mode, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from tinyserve_b200.ep import ExpertParallelMoE
+    experts = _experts()
+    el = E // world
+    mine = experts[rank * el:(rank + 1) * el]
+    seen = []
+
+    def layer_forward(xa, lid, wa):
+        # the weighted local layer: rows routed elsewhere carry -1 and add nothing
+        seen.append((int(xa.shape[0]), int((lid >= 0).sum())))
+        assert lid.dtype == torch.int32 and int(lid.max()) < el
+        out = torch.zeros(xa.shape[0], H, dtype=torch.float64)
+        for t in range(xa.shape[0]):
+            for j in range(lid.shape[1]):
+                if int(lid[t, j]) >= 0:
+                    out[t] += float(wa[t, j]) * torch.tanh(xa[t] @ mine[int(lid[t, j])].T)
+        return out
+
+    ep = ExpertParallelMoE(E, K, H, layer_forward=layer_forward)
+    x, ids, w = _tokens(rank, T, mode)
+    out = ep.forward_gather(x, ids, w)
+    ref = _reference(x, ids, w, experts)
+    torch.save({"err": float((out - ref).abs().max()) if out.numel() else 0.0, "seen": seen,
+                "shape": tuple(out.shape), "dtype": str(out.dtype)}, os.path.join(outdir, f"g{rank}.pt"))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("T,mode", [(1, "random"), (5, "random"), (3, "one_owner")])
+def test_ep_gather_two_ranks_matches_single_process(tmp_path, T, mode):
+    """The decode scheme: all-gathered tokens and routing, local layer with
+    skipped rows, fp32 reduce-scatter back to each rank's own T rows."""
+    mp.spawn(_gather_worker, args=(2, _port(), T, mode, str(tmp_path)), nprocs=2, join=True)
+    total = 0
+    for r in range(2):
+        res = torch.load(tmp_path / f"g{r}.pt")
+        assert res["shape"] == (T, H) and res["dtype"] == "torch.float64"
+        assert res["err"] < 1e-5  # partial outputs travel in fp32
+        rows, active = res["seen"][0]
+        assert rows == 2 * T
+        total += active
+    assert total == 2 * T * K  # every (token, slot) pair computed exactly once
+    if mode == "one_owner":
+        assert torch.load(tmp_path / "g1.pt")["seen"][0][1] == 0

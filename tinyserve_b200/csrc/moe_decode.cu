@@ -37,7 +37,7 @@ __device__ __forceinline__ void store_out(void* p, int dtype, int64_t i, float v
 __device__ __forceinline__ int safe_expert(const int32_t* ids, int i, int E, int* err) {
   const int e = ids[i];
   if ((unsigned)e >= (unsigned)E) {
-    if (err) atomicExch(err, kDevBadPlan);
+    if (err && e >= 0) atomicExch(err, kDevBadPlan);  // negative: a skipped slot
     return -1;
   }
   return e;

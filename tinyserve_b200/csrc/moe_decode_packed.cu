@@ -57,6 +57,7 @@ namespace tsb {
 
 constexpr int kPkThreads = 512;
 constexpr int kPkWarps = kPkThreads / 32;
+constexpr int kCopyLane = 31;        // the lane that issues bulk copies and L2 prefetches
 constexpr int kSlots = 2;            // ring slots per warp (one chunk = two units each)
 constexpr int kPadL = 8, kPadR = 16;  // zero sub-blocks before / after a B image (phase shifts, last chunk)
 constexpr int kQ4Hdr = 320, kQ4Unit = 320 + 2048;
@@ -390,15 +391,13 @@ struct PkArgs {
   float* act;        // fp32 [top_k, I]
   unsigned* cnt_gu;  // [top_k * ngj]
   unsigned* cnt_dn;  // [ndp]
-  unsigned* sync;    // [0] gate/up groups done, [1] CTAs finished, [2..9] max |act| per slot (float bits),
-                     // [10] router logits published
+  unsigned* sync;    // [0] CTAs done with gate/up, [1] CTAs finished
   float* part_gu;    // [n_gu, 32]
   float* part_dn;    // [n_dn, 32]
   void* out;
   int out_f32, act_kind;
   float limit, alpha;
   int* err;
-  float* logits;  // [E] router logits of this token
 };
 
 // Slot waits use mbarrier.try_wait: a waiting warp is suspended in hardware
@@ -437,6 +436,44 @@ __device__ __forceinline__ void mma_acc(float (&d)[4], uint32_t a0, uint32_t a1,
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// L2 eviction policies: the expert weights are streamed once per token and go
+// in as evict-first, so the small data every token re-reads (router
+// weights, the row maps, the activations and partial sums) stays in L2.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint4 ldg_hint(const uint4* p, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ int ldg_hint_i32(const int32_t* p, uint64_t pol) {
+  int v;
+  asm volatile("ld.global.nc.L2::cache_hint.b32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_l2_hint(const void* p, uint32_t bytes, uint64_t pol) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p), "r"(bytes), "l"(pol)
+               : "memory");
+}
 __device__ __forceinline__ uint32_t u4c(const uint4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -669,85 +706,133 @@ __host__ __device__ inline size_t pk_smem(int unit, int nsb_max, int top_k) {
   return pk_ring_bytes(unit) + pk_img_bytes(nv, nsb_max) + pk_x_bytes(nv, nsb_max) + 64;
 }
 
-// Router logits (tinyserve/_model_hooks.py:466-473), spread over the grid:
-// expert e is computed by warp e / grid of CTA e % grid (bf16 x . bf16 W[e] in
-// fp32, + bias, rounded to bf16 as the reference's bf16 Linear returns them),
-// published to global memory and counted (release) in sync[10].
-__device__ void pk_logits(const PkArgs& a, int warp, int lane) {
+// Thread-block cluster helpers (distributed shared memory).
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// Store v into the same shared-memory location of cluster CTA `rank`.
+__device__ __forceinline__ void st_cluster(float* local, uint32_t rank, float v) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+// Every thread of every CTA of the cluster: prior (remote) shared-memory
+// stores are visible to all of them afterwards.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Split form used at kernel start: every CTA arrives once it is running; a
+// CTA waits before its first store into another CTA's shared memory.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+// Router logits (tinyserve/_model_hooks.py:466-473), split over the CTAs of
+// a thread-block cluster: CTA r of n computes experts r, r + n, ... (one warp
+// each: bf16 x . bf16 W[e] in fp32, + bias, rounded to bf16 as the
+// reference's bf16 Linear returns them) into its own s_logit, then, once
+// every CTA of the cluster is running (the arrive at kernel start), copies
+// them into the s_logit of the other CTAs; a cluster barrier follows.
+// Called by every thread of the CTA.
+__device__ void pk_logits(const PkArgs& a, float* s_logit, int warp, int lane) {
   const int H = a.H, n8 = H / 8;
   const uint4* xr = reinterpret_cast<const uint4*>(a.x);
+  const int r = (int)cluster_rank(), n = (int)cluster_size();
+  const uint64_t keep = policy_evict_last();
   constexpr int kU = 12;
-  int mine = 0;
-  for (int e = blockIdx.x + gridDim.x * warp; e < a.E; e += gridDim.x * kPkWarps) {
+  for (int e = r + n * warp; e < a.E; e += n * kPkWarps) {
     const uint4* wr = reinterpret_cast<const uint4*>(a.router_w + (int64_t)e * H);
-    float acc = 0.f;
+    float acc4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent FMA chains
     for (int base = lane; base < n8; base += 32 * kU) {
       uint4 xv[kU], wv[kU];
 #pragma unroll
       for (int j = 0; j < kU; ++j) {
         const int i = base + 32 * j;
         xv[j] = i < n8 ? __ldg(xr + i) : make_uint4(0, 0, 0, 0);
-        wv[j] = i < n8 ? __ldg(wr + i) : make_uint4(0, 0, 0, 0);
+        wv[j] = i < n8 ? ldg_hint(wr + i, keep) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
       for (int j = 0; j < kU; ++j) {
         const uint32_t av[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w}, bv[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          acc = fmaf(__uint_as_float(av[q] << 16), __uint_as_float(bv[q] << 16), acc);
-          acc = fmaf(__uint_as_float(av[q] & 0xFFFF0000u), __uint_as_float(bv[q] & 0xFFFF0000u), acc);
+          acc4[q] = fmaf(__uint_as_float(av[q] << 16), __uint_as_float(bv[q] << 16), acc4[q]);
+          acc4[q] = fmaf(__uint_as_float(av[q] & 0xFFFF0000u), __uint_as_float(bv[q] & 0xFFFF0000u), acc4[q]);
         }
       }
     }
+    float acc = (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
 #pragma unroll
     for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) a.logits[e] = bf16_bits_to_f32(f32_to_bf16_bits(a.router_b ? acc + a.router_b[e] : acc));
-    ++mine;
+    if (lane == 0) s_logit[e] = bf16_bits_to_f32(f32_to_bf16_bits(a.router_b ? acc + a.router_b[e] : acc));
   }
-  if (mine && lane == 0) {
-    __threadfence();
-    atomicAdd(a.sync + 10, (unsigned)mine);
-  }
+  __syncwarp();
+  PK_T(if (threadIdx.x == 0 && blockIdx.x < 160) g_pk_trace[blockIdx.x * 16 + 8] = gtimer();)
+  cluster_wait();
+  PK_T(if (threadIdx.x == 0 && blockIdx.x < 160) g_pk_trace[blockIdx.x * 16 + 9] = gtimer();)
+  for (int e = r + n * warp; e < a.E; e += n * kPkWarps)
+    if (lane < n && lane != r) st_cluster(s_logit + e, (uint32_t)lane, s_logit[e]);
 }
 
-// Top-k of the published logits (ties -> lower id, NaN lowest) and softmax
+// Top-k of the logits in s_logit (ties -> lower id, NaN lowest) and softmax
 // over the k selected logits; warp 0 of every CTA reaches the same result,
 // CTA 0 publishes ids / weights.
-__device__ void pk_select(const PkArgs& a, float* s_logit, int* s_e, float* s_w, int lane) {
-  for (int e = lane; e < a.E; e += 32) s_logit[e] = __ldcg(a.logits + e);
-  __syncwarp();
+// Order-preserving map of a float to an unsigned key (NaN lowest).
+__device__ __forceinline__ uint32_t sort_key(float f) {
+  if (f != f) return 0u;
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ uint32_t redux_max(uint32_t v) {
+  uint32_t r;
+  asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return r;
+}
+__device__ __forceinline__ uint32_t redux_min(uint32_t v) {
+  uint32_t r;
+  asm volatile("redux.sync.min.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return r;
+}
+
+__device__ void pk_select(const PkArgs& a, const float* s_logit, int* s_e, float* s_w, int lane) {
+  // Each pick: every lane's best remaining (key, lowest id) over its experts
+  // lane, lane + 32, ...; the warp's largest key (redux.max), then the lowest
+  // id holding it (redux.min): ties go to the lower id, NaN ranks lowest.
+  uint32_t taken = 0;  // bit j: expert lane + 32*j already selected (E <= 1024)
   float sel[8];
   int sid[8];
-  uint32_t taken = 0;  // bit j: expert lane + 32*j already selected (E <= 1024)
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     if (k >= a.top_k) break;
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll 1
+    uint32_t bk = 0u, bid = 0xFFFFFFFFu;
     for (int j = 0; lane + 32 * j < a.E; ++j) {
       if ((taken >> j) & 1u) continue;
-      const int ee = lane + 32 * j;
-      float v = s_logit[ee];
-      if (v != v) v = -INFINITY;
-      if (v > best || (v == best && ee < bi)) { best = v; bi = ee; }
+      const uint32_t key = sort_key(s_logit[lane + 32 * j]);
+      if (bid == 0xFFFFFFFFu || key > bk) { bk = key; bid = lane + 32 * j; }
     }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-    }
-    sel[k] = best;
-    sid[k] = bi;
-    if (bi != 0x7fffffff && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+    const uint32_t mk = redux_max(bid == 0xFFFFFFFFu ? 0u : bk);
+    const uint32_t id = redux_min(bid != 0xFFFFFFFFu && bk == mk ? bid : 0xFFFFFFFFu);
+    sid[k] = (int)id;
+    sel[k] = id < (uint32_t)a.E ? s_logit[id] : -INFINITY;
+    if (id < (uint32_t)a.E && (int)(id & 31) == lane) taken |= 1u << (id >> 5);
   }
   if (lane == 0) {
     const float mx = sel[0];
-    float den = 0.f, ex[8];
+    float ex[8], den = 0.f;
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-      if (k < a.top_k) { ex[k] = __expf(sel[k] - mx); den += ex[k]; }
+      if (k < a.top_k) {
+        ex[k] = __expf((sel[k] != sel[k] ? -INFINITY : sel[k]) - mx);
+        den += ex[k];
+      }
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       if (k >= a.top_k) break;
@@ -884,18 +969,44 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
     (void)i;
   };
   stamp(0);
+  PK_T(if (threadIdx.x == 0 && blockIdx.x == 0) g_pk_trace[15] = gridDim.x;)
   if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(zero)[threadIdx.x] = 0u;
   if (lane < kSlots) mbar_init(&bar[lane], 1);
   if (threadIdx.x == 0) s_bad = 0;
   fence_barrier_init();
+  if (a.router_w) cluster_arrive_relaxed();
 
-  // ---- router logits, spread over the grid (ids given: validated below)
-  if (a.router_w) pk_logits(a, warp, lane);
+  // ---- row-block phases and this lane's row-map entry of a task (L2
+  // evict-last: every token re-reads them)
+  struct Meta {
+    int id, p0, p1, map;
+  };
+  const uint64_t keep_meta = policy_evict_last();
+  auto meta_of = [&](int id) {
+    Meta m{id, 0, 0, -1};
+    if (id < 0) return m;
+    const bool down = id >= a.n_gu;
+    const int lid = down ? id - a.n_gu : id;
+    const int S = down ? a.S_dn : a.S_gu, G = down ? a.ndp : a.ngj;
+    const int grp = (lid / S) % G;
+    if (down) {
+      m.p0 = m.p1 = ldg_hint_i32(a.dn_ph + grp, keep_meta);
+      m.map = ldg_hint_i32(a.dn_h + grp * 32 + lane, keep_meta);
+    } else {
+      m.p0 = ldg_hint_i32(a.gu_ph + 2 * grp, keep_meta);
+      m.p1 = ldg_hint_i32(a.gu_ph + 2 * grp + 1, keep_meta);
+      m.map = lane < 16 ? ldg_hint_i32(a.gu_j + grp * 16 + lane, keep_meta) : -1;
+    }
+    return m;
+  };
+
+  // ---- router logits, split over the cluster (ids given: validated below)
+  if (a.router_w) pk_logits(a, s_logit, warp, lane);
 
   // ---- B image of x (one vector), its scale and sub-block sums, while the
   // other CTAs' logits arrive.  Thread i owns 8-element groups i + 512u.
   {
-    constexpr int kXR = 4;  // H <= 16384: at most 2048 groups
+    constexpr int kXR = 2048 / kPkThreads;  // H <= 16384: at most 2048 groups
     const int ng = a.H / 8;
     uint4 xv[kXR];
 #pragma unroll
@@ -920,38 +1031,23 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
     }
   }
 
-  // ---- routing: wait for every expert's logit, then top-k in each CTA
+  // ---- routing: every CTA of the cluster has written its logits into all
+  // of them; then top-k in each CTA
   if (a.router_w) {
-    if (threadIdx.x == 0) {
-      bool ok = false;
-      for (uint32_t i = 0; i < kSpinPolls && !ok; ++i) {
-        unsigned v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 10) : "memory");
-        ok = v >= (unsigned)a.E;
-        if (!ok) __nanosleep(32);
-      }
-      if (!ok) {
-        if (a.err) atomicExch(a.err, kDevWaitTimeout);
-        s_bad = 1;
-      }
-    }
-    __syncthreads();
+    PK_T(if (threadIdx.x == 0 && blockIdx.x < 160) g_pk_trace[blockIdx.x * 16 + 10] = gtimer();)
+    cluster_sync_all();
+    PK_T(if (threadIdx.x == 0 && blockIdx.x < 160) g_pk_trace[blockIdx.x * 16 + 11] = gtimer();)
     if (warp == 0) pk_select(a, s_logit, s_e, s_w, lane);
+    PK_T(if (threadIdx.x == 0 && blockIdx.x < 160) g_pk_trace[blockIdx.x * 16 + 12] = gtimer();)
   } else if (threadIdx.x < a.top_k) {
     const int e = a.ids[threadIdx.x];
     const bool ok = (unsigned)e < (unsigned)a.E;
-    if (!ok && blockIdx.x == 0 && a.err) atomicExch(a.err, kDevBadPlan);
+    if (!ok && e >= 0 && blockIdx.x == 0 && a.err) atomicExch(a.err, kDevBadPlan);  // negative: skipped slot
     s_e[threadIdx.x] = ok ? e : -1;
     s_w[threadIdx.x] = a.wts[threadIdx.x];
   }
   __syncthreads();
-  if (threadIdx.x < a.top_k) {
-    const int e = s_e[threadIdx.x];
-    const TsbExpert* E = a.experts + (e < 0 ? 0 : e);
-    s_bias[0][threadIdx.x] = e < 0 ? nullptr : E->gate_bias;
-    s_bias[1][threadIdx.x] = e < 0 ? nullptr : E->up_bias;
-    s_bias[2][threadIdx.x] = e < 0 ? nullptr : E->down_bias;
-  }
+  PK_T(if (threadIdx.x == 0 && blockIdx.x < 160) g_pk_trace[blockIdx.x * 16 + 13] = gtimer();)
 
   stamp(1);
   // ---- task geometry.  Global task list: gate/up tasks [0, n_gu), then down
@@ -978,6 +1074,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
           ((int64_t)T.grp * C + T.c0) * 2 * UNIT;
     return T;
   };
+  const uint64_t stream_pol = policy_evict_first();
   // issue cursor, running ahead of the consumer through the warp's tasks
   uint32_t issued = 0, consumed = 0;
   int it_id = gw, it_u = 0;
@@ -990,24 +1087,42 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
       if (it_id < ntask) it = task_of(it_id);
     }
     if (it_id >= ntask) return;
-    // one chunk: its two units are adjacent in the packed layout
+    // one chunk: its two units are adjacent in the packed layout.  Lane 31
+    // issues every bulk copy and prefetch; lane 0 does the fences and
+    // release atomics, so those never wait behind this warp's copies.
     uint64_t* b = &bar[issued % kSlots];
-    if (lane == 0) {
+    if (lane == kCopyLane) {
       mbar_arrive_expect_tx(b, 2 * UNIT);
-      bulk_g2s(ring + (issued % kSlots) * 2 * UNIT, it.p + (size_t)it_u * UNIT, 2 * UNIT, b);
+      bulk_g2s_hint(ring + (issued % kSlots) * 2 * UNIT, it.p + (size_t)it_u * UNIT, 2 * UNIT, b, stream_pol);
     }
     ++issued;
     it_u += 2;
   };
 #pragma unroll
   for (int i = 0; i < kSlots; ++i) issue_next();
-  // down weights beyond the ring: into L2 while gate/up streams
-  if (lane == 0)
+  // bias pointers of the chosen experts (read by the epilogues only; visible
+  // to them through the barriers that precede every epilogue)
+  if (threadIdx.x < a.top_k) {
+    const int e = s_e[threadIdx.x];
+    const TsbExpert* E = a.experts + (e < 0 ? 0 : e);
+    s_bias[0][threadIdx.x] = e < 0 ? nullptr : E->gate_bias;
+    s_bias[1][threadIdx.x] = e < 0 ? nullptr : E->up_bias;
+    s_bias[2][threadIdx.x] = e < 0 ? nullptr : E->down_bias;
+  }
+  // Down weights beyond what the ring holds: into L2 while gate/up streams.
+  // The ring requests the warp's first kSlots down chunks itself as its last
+  // gate/up chunks are consumed; prefetching those too would only take HBM
+  // bandwidth from gate/up, which the barrier waits for.
+  if (lane == kCopyLane) {
+    int skip = kSlots;  // chunks
     for (int id = gw; id < ntask; id += nw) {
       if (id < a.n_gu) continue;
       const Task T = task_of(id);
-      if (T.n) prefetch_l2(T.p, (uint32_t)T.n * UNIT);
+      const int nch = T.n / 2;
+      if (nch > skip) prefetch_l2_hint(T.p + (size_t)skip * 2 * UNIT, (uint32_t)(nch - skip) * 2 * UNIT, stream_pol);
+      skip = max(0, skip - nch);
     }
+  }
 
   __syncthreads();  // the x image is complete
 
@@ -1026,13 +1141,8 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
     const int v = T.down ? T.k : 0;
     const uint8_t* im = img + pk_img_bytes(v, nsb);
     const float2* X = Xs + (size_t)v * nsb;
-    int p0, p1;
-    if (T.down) {
-      p0 = p1 = a.dn_ph[T.grp];
-    } else {
-      p0 = a.gu_ph[2 * T.grp];
-      p1 = a.gu_ph[2 * T.grp + 1];
-    }
+    const Meta M = meta_of(id);
+    const int p0 = M.p0, p1 = M.p1;
     float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
     const int nchunks = T.n / 2;
     for (int ci = 0; ci < nchunks && !bad; ++ci) {
@@ -1116,7 +1226,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
       const float sum = sum_parts(Q, a.S_gu, lane);
       const float other = __shfl_xor_sync(0xffffffffu, sum, 16);
       const float gate = sum, up = other;
-      const int j = lane < 16 ? a.gu_j[T.grp * 16 + lane] : -1;
+      const int j = lane < 16 ? M.map : -1;
       float r = 0.f;
       if (j >= 0 && s_e[k] >= 0) {
         const float gb = s_bias[0][k] ? gate + s_bias[0][k][j] : gate;
@@ -1128,7 +1238,7 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
       if (lane == 0) a.cnt_gu[k * a.ngj + T.grp] = 0u;
     } else {
       // down epilogue: 32 outputs, slots and splits combined in fixed order
-      const int h = a.dn_h[T.grp * 32 + lane];
+      const int h = M.map;
       float o = 0.f;
       for (int k = 0; k < a.top_k; ++k) {
         if (s_e[k] < 0) continue;
@@ -1247,7 +1357,8 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
     unsigned old;
     asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.sync + 1) : "memory");
     if (old == gridDim.x - 1) {
-      for (int i = 0; i < 11; ++i) a.sync[i] = 0u;
+      a.sync[0] = 0u;
+      a.sync[1] = 0u;
       __threadfence();
     }
   }
@@ -1307,21 +1418,55 @@ size_t packed_ws_bytes(const TsbMoeSpec& sp) {
 
 constexpr int kPkSmemMax = 220 * 1024;
 
+// Launch shape: clusters of kPkCluster CTAs (the router split), as many as fit
+// co-resident with one CTA per SM (the device-wide barrier between gate/up and
+// down needs every CTA resident; its waits are bounded all the same).
+constexpr int kPkCluster = 2;
+
+// CTAs of one launch: as many clusters of kPkCluster as the device keeps
+// co-resident with one CTA per SM (cudaOccupancyMaxActiveClusters); the
+// device-wide barrier between gate/up and down needs every CTA resident.
 template <int F>
-static int launch_pk(PkArgs& a, size_t smem, cudaStream_t st) {
-  static bool attr = [] {
-    return cudaFuncSetAttribute(pk_layer_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPkSmemMax) ==
-           cudaSuccess;
+static int pk_grid(int& grid) {
+  static int g = 0;
+  static cudaError_t init = [] {
+    cudaError_t e = cudaFuncSetAttribute(pk_layer_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPkSmemMax);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(num_sms() / kPkCluster * kPkCluster));
+    cfg.blockDim = dim3(kPkThreads);
+    cfg.dynamicSmemBytes = kPkSmemMax;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = kPkCluster;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, pk_layer_kernel<F>, &cfg);
+    if (e != cudaSuccess) return e;
+    g = std::min(clusters, num_sms() / kPkCluster) * kPkCluster;
+    return g > 0 ? cudaSuccess : cudaErrorInvalidConfiguration;
   }();
-  if (!attr || smem > kPkSmemMax) return set_error(TSB_ERR_UNSUPPORTED, "packed decode: layer too large for shared memory");
+  if (init != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(init));
+  grid = g;
+  return TSB_OK;
+}
+
+template <int F>
+static int launch_pk(PkArgs& a, int grid, size_t smem, cudaStream_t st) {
+  if (smem > kPkSmemMax) return set_error(TSB_ERR_UNSUPPORTED, "packed decode: layer too large for shared memory");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(num_sms());
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kPkThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeCooperative;
-  at[0].val.cooperative = 1;
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = kPkCluster;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, pk_layer_kernel<F>, a);
@@ -1361,7 +1506,10 @@ int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpe
   a.ndp = G.ndp;
   a.C_gu = G.C_gu;
   a.C_dn = G.C_dn;
-  const int warps = num_sms() * kPkWarps;
+  int grid = 0;
+  const int rc = G.q4 ? pk_grid<FMT_Q4_K>(grid) : pk_grid<FMT_MXFP4>(grid);
+  if (rc) return rc;
+  const int warps = grid * kPkWarps;
   a.nc_gu = choose_nc(sp.top_k * G.ngj, G.C_gu, warps);
   a.S_gu = (G.C_gu + a.nc_gu - 1) / a.nc_gu;
   a.nc_dn = choose_nc(sp.top_k * G.ndp, G.C_dn, warps);
@@ -1382,7 +1530,6 @@ int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpe
   a.sync = reinterpret_cast<unsigned*>(pws + W.sync);
   a.part_gu = reinterpret_cast<float*>(pws + W.part_gu);
   a.part_dn = reinterpret_cast<float*>(pws + W.part_dn);
-  a.logits = reinterpret_cast<float*>(pws + W.logits);
 
   a.out = out;
   a.out_f32 = out_f32;
@@ -1391,8 +1538,8 @@ int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpe
   a.alpha = sp.alpha;
   a.err = err;
   const int nsb_max = std::max(a.nsb_h, a.nsb_i);
-  if (G.q4) return launch_pk<FMT_Q4_K>(a, pk_smem(kQ4Unit, nsb_max, sp.top_k), st);
-  return launch_pk<FMT_MXFP4>(a, pk_smem(kMxUnit, nsb_max, sp.top_k), st);
+  if (G.q4) return launch_pk<FMT_Q4_K>(a, grid, pk_smem(kQ4Unit, nsb_max, sp.top_k), st);
+  return launch_pk<FMT_MXFP4>(a, grid, pk_smem(kMxUnit, nsb_max, sp.top_k), st);
 }
 
 }  // namespace tsb

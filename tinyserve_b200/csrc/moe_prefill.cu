@@ -89,8 +89,10 @@ __global__ void __launch_bounds__(256) route_chunk_count(const int32_t* __restri
     if ((unsigned)v < (unsigned)E) {
       atomicAdd(&hist[v], 1);
     } else {
+      // negative ids: slots this call skips (another rank's experts);
+      // ids >= E: a routing error
       row_of[i] = -1;
-      atomicExch(err, kDevBadPlan);
+      if (v >= 0) atomicExch(err, kDevBadPlan);
     }
   }
   __syncthreads();

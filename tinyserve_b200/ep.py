@@ -2,7 +2,21 @@
 process group (one process per GPU), token dispatch and combine over NCCL.
 
 Rank r owns experts [r*E/G, (r+1)*E/G) (contiguous ranges) and brings its own
-tokens.  One layer call on every rank:
+tokens.  Two exchange schemes:
+
+* ``forward_gather`` (decode-sized batches, the same T on every rank): the
+  tokens and their routing are all-gathered (G*T rows), every rank runs its
+  local experts on the (token, slot) pairs routed to them (the other ranks'
+  pairs carry a negative id, which the kernels skip), and the fp32 partial
+  outputs are summed across ranks by one reduce-scatter that hands each rank
+  its own T rows.  Shapes are static and no count ever goes to the host, so a
+  step can be captured in a CUDA graph; the combine is the reduce-scatter.
+* ``forward`` (prefill-sized batches, any T per rank): all-to-all dispatch of
+  only the routed rows, as below.  The row counts per rank pair are exchanged
+  first and read on the host to size the uneven splits (one synchronisation
+  per layer call, small next to a prefill layer).
+
+``forward`` on every rank:
 
 1. route its tokens (router weights are replicated; ``Router``);
 2. order its (token, slot) rows by owning rank (stable, so the order is
@@ -28,18 +42,20 @@ import torch
 import torch.distributed as dist
 
 LocalForward = Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
+LayerForward = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
 
 
 class ExpertParallelMoE:
     """One MoE layer sharded expert-parallel over ``group``.
 
     ``local_forward(x_rows [R, H], local_ids [R] int32) -> [R, H]`` runs each
-    row through local expert ``local_ids[i]`` (unweighted).  ``router(x) ->
-    (ids [T,k] int32 global, weights [T,k] fp32)`` is used when the caller does
-    not pass routing."""
+    row through local expert ``local_ids[i]`` (unweighted; the ``forward``
+    scheme); ``layer_forward`` is the weighted local layer of the
+    ``forward_gather`` scheme.  ``router(x) -> (ids [T,k] int32 global,
+    weights [T,k] fp32)`` is used when the caller does not pass routing."""
 
-    def __init__(self, n_experts: int, top_k: int, hidden: int, local_forward: LocalForward, *,
-                 router: Callable | None = None, group=None):
+    def __init__(self, n_experts: int, top_k: int, hidden: int, local_forward: LocalForward | None = None, *,
+                 router: Callable | None = None, group=None, layer_forward: LayerForward | None = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -49,6 +65,7 @@ class ExpertParallelMoE:
         self.e_local = n_experts // self.world
         self.base = self.rank * self.e_local
         self.local_forward = local_forward
+        self.layer_forward = layer_forward
         self.router = router
 
     def owner(self, ids: torch.Tensor) -> torch.Tensor:
@@ -88,14 +105,46 @@ class ExpertParallelMoE:
 
         y = torch.empty(T * k, H, dtype=torch.float32, device=dev)
         y[order] = y_send.float()
-        y = y.view(T, k, H)
-        w = weights.to(torch.float32).reshape(T, k)
-        out = torch.zeros(T, H, dtype=torch.float32, device=dev)
-        for j in range(k):
-            out += w[:, j:j + 1] * y[:, j]
+        # weighted combine in one batched product: out[t] = sum_j w[t,j] y[t,j]
+        w = weights.to(torch.float32).reshape(T, 1, k)
+        out = torch.bmm(w, y.view(T, k, H)).view(T, H)
         return out.to(x.dtype)
 
     __call__ = forward
+
+    def forward_gather(self, x: torch.Tensor, ids: torch.Tensor | None = None,
+                       weights: torch.Tensor | None = None, layer_forward: LayerForward | None = None,
+                       out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        """Decode step of T tokens per rank (T equal on every rank): all-gather
+        tokens and routing, local experts on the rows routed here (other
+        ranks' rows skipped), reduce-scatter of the fp32 partial outputs.
+        ``layer_forward(x_all [G*T, H], local_ids [G*T, k] int32 (negative =
+        skip), weights [G*T, k] fp32) -> fp32 [G*T, H]`` runs this rank's
+        experts (default: the one given at construction as ``layer_forward``)."""
+        fwd = layer_forward or self.layer_forward
+        if fwd is None:
+            raise ValueError("no layer_forward for the gather scheme")
+        if ids is None:
+            if self.router is None:
+                raise ValueError("no router: pass ids and weights")
+            ids, weights = self.router(x)
+        T, H = x.shape
+        k = ids.shape[1]
+        G = self.world
+        x_all = torch.empty(G * T, H, dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(x_all, x.contiguous(), group=self.group)
+        meta = torch.cat([ids.to(torch.int32).view(torch.float32).reshape(T, k),
+                          weights.to(torch.float32).reshape(T, k)], dim=1).contiguous()
+        meta_all = torch.empty(G * T, 2 * k, dtype=torch.float32, device=x.device)
+        dist.all_gather_into_tensor(meta_all, meta, group=self.group)
+        ids_all = meta_all[:, :k].contiguous().view(torch.int32)
+        w_all = meta_all[:, k:].contiguous()
+        lid = ids_all - self.base
+        lid = torch.where((lid >= 0) & (lid < self.e_local), lid, torch.full_like(lid, -1))
+        part = fwd(x_all, lid, w_all).to(torch.float32).contiguous()
+        out = torch.empty(T, H, dtype=torch.float32, device=x.device)
+        dist.reduce_scatter_tensor(out, part, group=self.group)
+        return out.to(out_dtype or x.dtype)
 
 
 def quant_local_forward(layer) -> LocalForward:
@@ -108,6 +157,19 @@ def quant_local_forward(layer) -> LocalForward:
     def f(rows: torch.Tensor, lid: torch.Tensor) -> torch.Tensor:
         ones = torch.ones(rows.shape[0], 1, dtype=torch.float32, device=rows.device)
         out, _, _ = layer.decode(rows.contiguous(), ids=lid.reshape(-1, 1), weights=ones)
+        return out
+
+    return f
+
+
+def quant_layer_forward(layer) -> LayerForward:
+    """``layer_forward`` backed by a :class:`tinyserve_b200.moe.QuantMoE`
+    holding this rank's experts with the model's top_k: one decode call over
+    the gathered tokens (per-token packed path up to 16 tokens, grouped path
+    above), the (token, slot) pairs of other ranks' experts skipped through
+    their negative ids, fp32 output."""
+    def f(x: torch.Tensor, lid: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        out, _, _ = layer.decode(x.contiguous(), ids=lid, weights=w, out_dtype=torch.float32)
         return out
 
     return f
