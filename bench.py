@@ -603,6 +603,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the config-4 prefill leg (--steps layers after --warmup) and print its object")
+    ap.add_argument("--ep-only", action="store_true",
+                    help="run only the config-5 expert-parallel legs and print their object")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -611,6 +613,16 @@ def main():
         res = run_reference(args, ws, rank, local)
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
+        return
+    if args.ep_only:
+        import torch
+        ep = run_ep(torch.device("cuda", local), ws, rank)
+        if rank == 0:
+            print(json.dumps(ep), flush=True)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
         return
     if args.prefill_only:
         import torch

@@ -173,14 +173,16 @@ int tsb_moe_prefill(const TsbMoeSpec* spec, const TsbExpert* experts, const void
 int tsb_read_device_error(void* workspace, int32_t* code, void* stream);
 
 /* tsb_moe_decode without a caller-provided workspace (no counterpart in the
- * reference).  For callers that cannot allocate device memory (for example
- * while their stream is being captured into a CUDA graph, or inside a host
- * with a fixed memory plan): the scratch is a 1 MiB array inside the library,
+ * reference).  For callers that have no device scratch memory to hand over
+ * (for example a host with a fixed memory plan, or a binding that only sees
+ * the tensors it passes): the scratch is a 1 MiB array inside the library,
  * which every GPU that loads the library keeps until the process exits.
  * Layers needing more scratch than that (tsb_moe_decode_workspace) are
- * rejected with TSB_ERR_WORKSPACE.  Allocates nothing.  The first call on a
- * device looks up the array's device address; make that first call before
- * any stream capture on that device.  All calls share the one array: calls
+ * rejected with TSB_ERR_WORKSPACE.  Calls neither cudaMalloc nor cudaFree.
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and keeps it for later calls; after
+ * cudaDeviceReset that cached address is stale, so the process must not
+ * call this entry point again on that device.  All calls share the one array: calls
  * that overlap on the GPU (other streams, other threads) race and must be
  * serialised by the caller.  Kernel-side errors of this variant are not
  * reported (there is no workspace to read them from). */
@@ -218,6 +220,32 @@ size_t tsb_moe_decode_packed_workspace(const TsbMoeSpec* spec, int32_t T);
 int tsb_moe_decode_packed(const TsbMoeSpec* spec, const void* packed, const TsbExpert* experts, const void* x,
                           int32_t T, const void* router_w, const float* router_b, int32_t* ids, float* weights,
                           void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Expert-parallel decode over NCCL (the multi-GPU form of one
+ * tsb_moe_decode call; the reference runs all experts of a layer on one GPU,
+ * tinyserve/expert_pipeline.py:140-164).  The n_experts * world experts of
+ * the layer are split evenly: rank r holds experts [r * n, (r + 1) * n), n =
+ * local_spec->n_experts, in local_experts (and, optionally, their
+ * tsb_moe_pack copy in `packed`, else NULL).  Every rank of the communicator
+ * calls it with the same T and passes its own tokens x (bf16 [T, H]) and their
+ * routing over the GLOBAL expert ids (ids int32 [T, top_k], weights fp32, e.g.
+ * from tsb_moe_route).  On `stream`, with no host synchronisation:
+ * all-gather of the tokens and routing, this rank's experts over all world*T
+ * rows (other ranks' (token, slot) pairs skipped), reduce-scatter (sum) of the
+ * fp32 partial outputs; out [T, H] receives this rank's rows (bf16, or fp32
+ * when local_spec->out_f32 is set).
+ *   nccl_comm  the caller's ncclComm_t (rank, world as in it); NCCL is found
+ *              at run time (libnccl.so.2 already loaded by the process, else
+ *              loaded by name); TSB_ERR_UNSUPPORTED when it is absent.
+ *   workspace  tsb_ep_decode_workspace(local_spec, T, world, packed != NULL)
+ *              bytes, 256-byte aligned, zero-initialised once and used with
+ *              the same T on every call (re-zero it before changing T);
+ *              tsb_read_device_error(workspace, ...) reads its error word. */
+size_t tsb_ep_decode_workspace(const TsbMoeSpec* local_spec, int32_t T, int32_t world, int32_t packed);
+int tsb_ep_moe_decode(const TsbMoeSpec* local_spec, const TsbExpert* local_experts, const void* packed,
+                      const void* x, int32_t T, const int32_t* ids, const float* weights, void* out,
+                      void* nccl_comm, int32_t rank, int32_t world, void* workspace, size_t workspace_bytes,
+                      void* stream);
 
 #ifdef __cplusplus
 }

@@ -18,7 +18,8 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from tests.helpers import assert_layer, make_weight, oracle_dequant, rel_l2  # noqa: E402
 from tests.test_kernels_gpu import _oracle_layer  # noqa: E402
-from tinyserve_b200.ep import ExpertParallelMoE, quant_layer_forward, quant_local_forward  # noqa: E402
+from tinyserve_b200.ep import (ExpertParallelMoE, NativeEPDecode, NcclComm, quant_layer_forward,  # noqa: E402
+                               quant_local_forward)
 from tinyserve_b200.formats import TSB_MXFP4  # noqa: E402
 from tinyserve_b200.moe import ExpertWeights, QuantMoE, Router  # noqa: E402
 
@@ -77,6 +78,26 @@ def main():
         for t in range(min(T, 4)):
             assert_layer(out[t], _oracle_layer(x[t:t + 1].float().cpu().numpy(), list(idn[t]), list(wn[t]), dense))
     assert mine_k.device_error(1) == 0
+    # the same scheme through the C-ABI (tsb_ep_moe_decode on an NCCL communicator)
+    comm = NcclComm()
+    for T in (1, 4, 24):
+        nat = NativeEPDecode(mine_k, comm, T)
+        for step in range(2):
+            x = torch.randn(T, H, generator=torch.Generator().manual_seed(7000 + 100 * rank + 10 * T + step))
+            x = x.to(torch.bfloat16).to(dev)
+            ids, w = Router(router_w, k)(x)
+            out = nat(x, ids, w, out_dtype=torch.float32)
+            out_b = nat(x, ids, w)
+            ref, _, _ = full.decode(x, ids=ids, weights=w, out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            err = rel_l2(out.cpu().numpy(), ref.cpu().numpy())
+            worst = max(worst, err)
+            assert err <= 1e-4, ("native", rank, T, err)
+            assert torch.equal(out_b, out.to(torch.bfloat16))
+            idn, wn = ids.cpu().numpy(), w.cpu().numpy()
+            assert_layer(out[0], _oracle_layer(x[0:1].float().cpu().numpy(), list(idn[0]), list(wn[0]), dense))
+        assert nat.device_error() == 0
+    comm.close()
     dist.barrier()
     print(f"EP_OK rank={rank} world={world} worst_rel_l2={worst:.2e}", flush=True)
     dist.destroy_process_group()

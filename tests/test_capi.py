@@ -152,3 +152,19 @@ def test_packed_entry_points_validate_on_the_host():
     assert L.tsb_moe_decode_packed_workspace(ctypes.byref(q4), 1) > L.tsb_moe_decode_workspace(ctypes.byref(q4), 1)
     # T > 16 takes the grouped path: same workspace as tsb_moe_decode
     assert L.tsb_moe_decode_packed_workspace(ctypes.byref(q4), 64) == L.tsb_moe_decode_workspace(ctypes.byref(q4), 64)
+
+
+def test_ep_decode_workspace_and_argument_checks():
+    """tsb_ep_decode_workspace grows with world * T; tsb_ep_moe_decode rejects
+    null pointers and a rank outside the communicator before any GPU work."""
+    spec = _lib.TsbMoeSpec(39, 39, 2880, 2880, 16, 4, 0, 1, 7.0, 1.702)
+    L = _lib.lib()
+    w1 = L.tsb_ep_decode_workspace(ctypes.byref(spec), 1, 2, 0)
+    w8 = L.tsb_ep_decode_workspace(ctypes.byref(spec), 1, 8, 0)
+    assert 0 < w1 < w8
+    assert L.tsb_ep_decode_workspace(ctypes.byref(spec), 0, 2, 0) == 0
+    assert L.tsb_ep_decode_workspace(ctypes.byref(spec), 1, 0, 0) == 0
+    rc = L.tsb_ep_moe_decode(ctypes.byref(spec), None, None, 16, 1, 16, 16, 16, 16, 0, 2, 256, w1, None)
+    assert rc == _lib.TSB_ERR_INVALID
+    rc = L.tsb_ep_moe_decode(ctypes.byref(spec), 16, None, 16, 1, 16, 16, 16, 16, 2, 2, 256, w1, None)
+    assert rc == _lib.TSB_ERR_INVALID and "rank" in _lib.last_error()

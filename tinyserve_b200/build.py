@@ -96,7 +96,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         (BUILD / (src.stem + ".ptxas.txt")).write_text(r.stderr)
         _stamp(obj).write_text(key)
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc, "-shared", *ARCH, "-o", str(tmp), *objs, "-lcudart"]
+    cmd = [nvcc, "-shared", *ARCH, "-o", str(tmp), *objs, "-lcudart", "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode:
         sys.stderr.write(r.stdout + r.stderr)

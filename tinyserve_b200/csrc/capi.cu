@@ -271,10 +271,9 @@ int tsb_moe_decode_packed(const TsbMoeSpec* spec, const void* packed, const TsbE
   if (reinterpret_cast<uintptr_t>(packed) & 255) return set_error(TSB_ERR_INVALID, "packed buffer must be 256-byte aligned");
   char* ws = static_cast<char*>(workspace);
   int32_t* err = reinterpret_cast<int32_t*>(ws + L.err);
-  float* act = reinterpret_cast<float*>(ws + L.act);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // with router weights, routing runs inside the gate/up launch
-  return launch_packed_decode(sp, packed, experts, x, ids, weights, act, out, sp.out_f32 != 0, err, ws + L.total, st,
+  return launch_packed_decode(sp, packed, experts, x, ids, weights, out, sp.out_f32 != 0, err, ws + L.total, st,
                               router_w, router_b);
 }
 
@@ -341,12 +340,12 @@ int tsb_moe_prefill(const TsbMoeSpec* spec, const TsbExpert* experts, const void
 // ---------------------------------------------------------------------------
 // Allocation-free variant of tsb_moe_decode.
 //
-// Some callers have no way to hand us device scratch memory: code that runs
-// while its stream is being captured into a CUDA graph (cudaMalloc is not
-// allowed there), hosts whose memory is planned ahead and that forbid any
-// allocation behind their back, or language bindings that only ever see the
-// tensors they pass in.  For them the workspace lives in this file-scope
-// device array, sized for one layer of up to kNoAllocBytes of scratch.
+// Some callers have no device scratch memory to hand over: hosts whose
+// memory is planned ahead and that forbid any allocation behind their back,
+// or language bindings that only ever see the tensors they pass in.  For them
+// the workspace lives in this file-scope device array, sized for one layer of
+// up to kNoAllocBytes of scratch; the entry point calls neither cudaMalloc
+// nor cudaFree.
 // ---------------------------------------------------------------------------
 namespace tsb {
 constexpr size_t kNoAllocBytes = size_t(1) << 20;  // 1 MiB, held on every GPU that loads the library

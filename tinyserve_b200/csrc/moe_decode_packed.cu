@@ -380,20 +380,22 @@ struct PkArgs {
   const int32_t* dn_ph;
   int64_t gu_off, dn_off, expert_bytes;
   int H, I, E, top_k, ngj, ndp, C_gu, C_dn;
-  int nc_gu, S_gu, nc_dn, S_dn, n_gu, n_dn;  // chunks per task, tasks per group, task counts
-  int nsb_h, nsb_i;                          // padded sub-blocks of the x / activation images
+  int Q_gu, Q_dn;          // chunks of one warp's range (gate/up, down)
+  int N_gu, N_dn;          // chunks of the whole layer call (gate/up, down)
+  int slots_gu, slots_dn;  // partial-sum slots per group (workspace stride)
+  int nsb_h;  // padded sub-blocks of the x image
   const uint16_t* x;
   const uint16_t* router_w;
   const float* router_b;
   int32_t* ids;
   float* wts;
   const TsbExpert* experts;
-  float* act;        // fp32 [top_k, I]
   unsigned* cnt_gu;  // [top_k * ngj]
   unsigned* cnt_dn;  // [ndp]
-  unsigned* sync;    // [0] CTAs done with gate/up, [1] CTAs finished
-  float* part_gu;    // [n_gu, 32]
-  float* part_dn;    // [n_dn, 32]
+  unsigned* sync;    // [1] CTAs finished
+  float* dact;       // [top_k, I] activations; bit pattern 0 (+0.0) = not yet written
+  float* part_gu;    // [top_k * ngj, slots_gu, 32]
+  float* part_dn;    // [ndp, slots_dn, 32]
   void* out;
   int out_f32, act_kind;
   float limit, alpha;
@@ -456,6 +458,14 @@ __device__ __forceinline__ uint4 ldg_hint(const uint4* p, uint64_t pol) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p), "l"(pol));
   return v;
+}
+// 8 floats (32-byte aligned) with relaxed GPU-scope loads: re-read from L2
+// on every call, never served by a stale L1 line.
+__device__ __forceinline__ void ld_relaxed_f32x8(const float* p, float (&v)[8]) {
+  asm volatile("ld.relaxed.gpu.global.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7]) : "l"(p + 4) : "memory");
 }
 __device__ __forceinline__ int ldg_hint_i32(const int32_t* p, uint64_t pol) {
   int v;
@@ -701,9 +711,14 @@ __device__ __forceinline__ void fold_q4(const uint8_t* u, const int (&hi)[4], co
 __host__ __device__ inline size_t pk_ring_bytes(int unit) { return (size_t)kPkWarps * kSlots * 2 * unit; }
 __host__ __device__ inline size_t pk_img_bytes(int nvec, int nsb) { return (size_t)nvec * nsb * 64; }
 __host__ __device__ inline size_t pk_x_bytes(int nvec, int nsb) { return ((size_t)nvec * nsb * 8 + 15) & ~size_t(15); }
-__host__ __device__ inline size_t pk_smem(int unit, int nsb_max, int top_k) {
-  const int nv = top_k > 1 ? top_k : 1;
-  return pk_ring_bytes(unit) + pk_img_bytes(nv, nsb_max) + pk_x_bytes(nv, nsb_max) + 64;
+// Down-phase images: each warp stages the 8 activation sub-blocks of one
+// down chunk into a small image of its own (kMiniNsb padded sub-blocks, the
+// 8 real ones at [kPadL, kPadL + 8)), two buffers per warp.
+constexpr int kMiniNsb = kPadL + 8, kMiniBufs = 2;
+__host__ __device__ inline size_t pk_mini_bytes() { return pk_img_bytes(1, kMiniNsb) + pk_x_bytes(1, kMiniNsb); }
+__host__ __device__ inline size_t pk_smem(int unit, int nsb_h) {
+  return pk_ring_bytes(unit) + pk_img_bytes(1, nsb_h) + pk_x_bytes(1, nsb_h) + 64 +
+         (size_t)kPkWarps * kMiniBufs * pk_mini_bytes();
 }
 
 // Thread-block cluster helpers (distributed shared memory).
@@ -949,20 +964,18 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
   extern __shared__ uint4 smem4[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(smem4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int nsb_max = max(a.nsb_h, a.nsb_i);
-  const int nv_max = max(a.top_k, 1);
   uint8_t* ring = sm + (size_t)warp * kSlots * 2 * UNIT;
-  uint8_t* img = sm + pk_ring_bytes(UNIT);
-  float2* Xs = reinterpret_cast<float2*>(img + pk_img_bytes(nv_max, nsb_max));
-  uint8_t* zero = reinterpret_cast<uint8_t*>(Xs) + pk_x_bytes(nv_max, nsb_max);  // 16-byte aligned
+  uint8_t* img = sm + pk_ring_bytes(UNIT);  // image of x
+  float2* Xs = reinterpret_cast<float2*>(img + pk_img_bytes(1, a.nsb_h));
+  uint8_t* zero = reinterpret_cast<uint8_t*>(Xs) + pk_x_bytes(1, a.nsb_h);  // 16-byte aligned
+  uint8_t* mini = zero + 64 + (size_t)warp * kMiniBufs * pk_mini_bytes();  // this warp's down images
 
   __shared__ float s_logit[1024];
   __shared__ int s_e[8];
   __shared__ float s_w[8];
   __shared__ const float* s_bias[3][8];  // gate, up, down bias of each slot's expert
-  __shared__ float s_red[8][kPkWarps];
   __shared__ uint64_t s_bar[kPkWarps][kSlots];
-  __shared__ int s_bad;
+  __shared__ int s_last;  // this CTA is the last to finish
   uint64_t* bar = s_bar[warp];
   auto stamp = [&](int i) {
     PK_T(if (threadIdx.x == 0 && blockIdx.x < 160) g_pk_trace[blockIdx.x * 16 + i] = gtimer();)
@@ -972,33 +985,8 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
   PK_T(if (threadIdx.x == 0 && blockIdx.x == 0) g_pk_trace[15] = gridDim.x;)
   if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(zero)[threadIdx.x] = 0u;
   if (lane < kSlots) mbar_init(&bar[lane], 1);
-  if (threadIdx.x == 0) s_bad = 0;
   fence_barrier_init();
   if (a.router_w) cluster_arrive_relaxed();
-
-  // ---- row-block phases and this lane's row-map entry of a task (L2
-  // evict-last: every token re-reads them)
-  struct Meta {
-    int id, p0, p1, map;
-  };
-  const uint64_t keep_meta = policy_evict_last();
-  auto meta_of = [&](int id) {
-    Meta m{id, 0, 0, -1};
-    if (id < 0) return m;
-    const bool down = id >= a.n_gu;
-    const int lid = down ? id - a.n_gu : id;
-    const int S = down ? a.S_dn : a.S_gu, G = down ? a.ndp : a.ngj;
-    const int grp = (lid / S) % G;
-    if (down) {
-      m.p0 = m.p1 = ldg_hint_i32(a.dn_ph + grp, keep_meta);
-      m.map = ldg_hint_i32(a.dn_h + grp * 32 + lane, keep_meta);
-    } else {
-      m.p0 = ldg_hint_i32(a.gu_ph + 2 * grp, keep_meta);
-      m.p1 = ldg_hint_i32(a.gu_ph + 2 * grp + 1, keep_meta);
-      m.map = lane < 16 ? ldg_hint_i32(a.gu_j + grp * 16 + lane, keep_meta) : -1;
-    }
-    return m;
-  };
 
   // ---- router logits, split over the cluster (ids given: validated below)
   if (a.router_w) pk_logits(a, s_logit, warp, lane);
@@ -1050,53 +1038,65 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
   PK_T(if (threadIdx.x == 0 && blockIdx.x < 160) g_pk_trace[blockIdx.x * 16 + 13] = gtimer();)
 
   stamp(1);
-  // ---- task geometry.  Global task list: gate/up tasks [0, n_gu), then down
-  // tasks; warp gw takes gw, gw + nw, ...  A task yields 2 units per chunk.
-  const int gw = blockIdx.x * kPkWarps + warp, nw = gridDim.x * kPkWarps, ntask = a.n_gu + a.n_dn;
-  struct Task {
-    const uint8_t* p;  // first unit
-    int n;             // units
-    int k, grp, s, c0, down;
-  };
-  auto task_of = [&](int id) {
-    Task T;
-    T.down = id >= a.n_gu;
-    const int lid = T.down ? id - a.n_gu : id;
-    const int S = T.down ? a.S_dn : a.S_gu, G = T.down ? a.ndp : a.ngj, C = T.down ? a.C_dn : a.C_gu;
-    const int nc = T.down ? a.nc_dn : a.nc_gu;
-    T.s = lid % S;
-    T.grp = (lid / S) % G;
-    T.k = lid / (S * G);
-    T.c0 = T.s * nc;
-    const int e = s_e[T.k];
-    T.n = e < 0 ? 0 : 2 * (min(C, T.c0 + nc) - T.c0);
-    T.p = a.packed + (int64_t)(e < 0 ? 0 : e) * a.expert_bytes + (T.down ? a.dn_off : a.gu_off) +
-          ((int64_t)T.grp * C + T.c0) * 2 * UNIT;
-    return T;
+  // ---- work split.  The chunks of a phase form one flat list: gate/up
+  // chunk i is chunk i % C_gu of j-group (i / C_gu) % ngj of slot
+  // i / (C_gu * ngj); down chunk i is chunk r % C_dn of slot r / C_dn of
+  // down group i / (top_k * C_dn), r = i % (top_k * C_dn).  Warp gw owns the
+  // contiguous range [gw * Q, (gw + 1) * Q) of each list, so no warp streams
+  // more than Q chunks.  A group (a gate/up j-group of one slot, or a down
+  // group over all slots) is a contiguous run of Cg chunks; the warps whose
+  // ranges meet it each publish one partial sum into slot (warp - first
+  // warp), and the last to arrive combines them in slot order.
+  const int gw = blockIdx.x * kPkWarps + warp;
+  const int Cg_gu = a.C_gu, Cg_dn = a.top_k * a.C_dn;
+  const int r0_gu = min(a.N_gu, gw * a.Q_gu), r1_gu = min(a.N_gu, r0_gu + a.Q_gu);
+  const int r0_dn = min(a.N_dn, gw * a.Q_dn), r1_dn = min(a.N_dn, r0_dn + a.Q_dn);
+  // first byte of a chunk (nullptr: the slot is skipped)
+  auto chunk_ptr = [&](int down, int i) -> const uint8_t* {
+    int k, grp, c;
+    if (!down) {
+      const int G = i / Cg_gu;
+      c = i - G * Cg_gu;
+      k = G / a.ngj;
+      grp = G - k * a.ngj;
+    } else {
+      grp = i / Cg_dn;
+      const int r = i - grp * Cg_dn;
+      k = r / a.C_dn;
+      c = r - k * a.C_dn;
+    }
+    const int e = s_e[k];
+    if (e < 0) return nullptr;
+    return a.packed + (int64_t)e * a.expert_bytes + (down ? a.dn_off : a.gu_off) +
+           ((int64_t)grp * (down ? a.C_dn : a.C_gu) + c) * 2 * UNIT;
   };
   const uint64_t stream_pol = policy_evict_first();
-  // issue cursor, running ahead of the consumer through the warp's tasks
+  // issue cursor, running ahead of the consumer through the warp's gate/up
+  // range, then its down range
   uint32_t issued = 0, consumed = 0;
-  int it_id = gw, it_u = 0;
-  Task it{};
-  if (it_id < ntask) it = task_of(it_id);
+  int it_ph = 0, it_i = r0_gu, it_e = r1_gu;
   auto issue_next = [&]() {
-    while (it_id < ntask && it_u >= it.n) {
-      it_id += nw;
-      it_u = 0;
-      if (it_id < ntask) it = task_of(it_id);
+    for (;;) {
+      if (it_i >= it_e) {
+        if (it_ph == 1) return;
+        it_ph = 1;
+        it_i = r0_dn;
+        it_e = r1_dn;
+        continue;
+      }
+      const uint8_t* p = chunk_ptr(it_ph, it_i++);
+      if (!p) continue;
+      // one chunk: its two units are adjacent in the packed layout.  Lane 31
+      // issues every bulk copy; lane 0 does the fences and release atomics,
+      // so those never wait behind this warp's copies.
+      uint64_t* b = &bar[issued % kSlots];
+      if (lane == kCopyLane) {
+        mbar_arrive_expect_tx(b, 2 * UNIT);
+        bulk_g2s_hint(ring + (issued % kSlots) * 2 * UNIT, p, 2 * UNIT, b, stream_pol);
+      }
+      ++issued;
+      return;
     }
-    if (it_id >= ntask) return;
-    // one chunk: its two units are adjacent in the packed layout.  Lane 31
-    // issues every bulk copy and prefetch; lane 0 does the fences and
-    // release atomics, so those never wait behind this warp's copies.
-    uint64_t* b = &bar[issued % kSlots];
-    if (lane == kCopyLane) {
-      mbar_arrive_expect_tx(b, 2 * UNIT);
-      bulk_g2s_hint(ring + (issued % kSlots) * 2 * UNIT, it.p + (size_t)it_u * UNIT, 2 * UNIT, b, stream_pol);
-    }
-    ++issued;
-    it_u += 2;
   };
 #pragma unroll
   for (int i = 0; i < kSlots; ++i) issue_next();
@@ -1109,18 +1109,20 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
     s_bias[1][threadIdx.x] = e < 0 ? nullptr : E->up_bias;
     s_bias[2][threadIdx.x] = e < 0 ? nullptr : E->down_bias;
   }
-  // Down weights beyond what the ring holds: into L2 while gate/up streams.
+  // Down chunks beyond what the ring holds: into L2 while gate/up streams.
   // The ring requests the warp's first kSlots down chunks itself as its last
   // gate/up chunks are consumed; prefetching those too would only take HBM
   // bandwidth from gate/up, which the barrier waits for.
   if (lane == kCopyLane) {
-    int skip = kSlots;  // chunks
-    for (int id = gw; id < ntask; id += nw) {
-      if (id < a.n_gu) continue;
-      const Task T = task_of(id);
-      const int nch = T.n / 2;
-      if (nch > skip) prefetch_l2_hint(T.p + (size_t)skip * 2 * UNIT, (uint32_t)(nch - skip) * 2 * UNIT, stream_pol);
-      skip = max(0, skip - nch);
+    int skip = kSlots;
+    for (int i = r0_dn; i < r1_dn; ++i) {
+      const uint8_t* p = chunk_ptr(1, i);
+      if (!p) continue;
+      if (skip > 0) {
+        --skip;
+        continue;
+      }
+      prefetch_l2_hint(p, 2 * UNIT, stream_pol);
     }
   }
 
@@ -1131,143 +1133,256 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
   stamp(2);
   bool bad = false;
   PK_T(long long cy_wait = 0, cy_comp = 0, n_units = 0, cy_epi = 0, cy_issue = 0, cy_task = 0;)
+  const uint64_t keep_meta = policy_evict_last();
 
-  // One task: stream its units, fold, publish 32 partial sums; the last task
-  // of a group runs the group's epilogue.
-  auto run_task = [&](int id) {
-    PK_T(const long long ct0 = clock64();)
-    const Task T = task_of(id);
-    const int nsb = T.down ? a.nsb_i : a.nsb_h;
-    const int v = T.down ? T.k : 0;
-    const uint8_t* im = img + pk_img_bytes(v, nsb);
-    const float2* X = Xs + (size_t)v * nsb;
-    const Meta M = meta_of(id);
-    const int p0 = M.p0, p1 = M.p1;
-    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-    const int nchunks = T.n / 2;
-    for (int ci = 0; ci < nchunks && !bad; ++ci) {
-      const int c = T.c0 + ci;
-      const uint32_t sl = consumed % kSlots;
-      PK_T(const long long c0 = clock64();)
-      if (!warp_wait(&bar[sl], (consumed / kSlots) & 1u, a.err)) {
-        bad = true;
-        break;
-      }
-      PK_T(const long long c1 = clock64(); cy_wait += c1 - c0; n_units += 2;)
-      consumed += 1;
-      const uint8_t* uA = ring + sl * 2 * UNIT;
-      const uint8_t* uB = uA + UNIT;
-      // B sources (see chunk_mma): half 0 from lanes g == t, half 1 from g == t + 4
-      const size_t pst = (size_t)nsb * 16;
-      const int sA = 8 * c - p0 + t + kPadL, sB = 8 * c - p1 + t + kPadL;
-      const bool h0 = g == t, h1 = g == t + 4;
-      const int xa = 8 * c - p0 + 2 * t + kPadL, xb = 8 * c - p1 + 2 * t + kPadL;
-      const uint8_t* a0s = h0 ? im + (size_t)sA * 16 : zero;
-      const uint8_t* a1s = h1 ? im + (size_t)(sA + 4) * 16 : zero;
-      const size_t z0 = h0 ? pst : 0, z1 = h1 ? pst : 0;
-      if (Q4) {
-        int hA[4], lA[4], hB[4], lB[4];
-        if (p0 == p1)
-          chunk_imma<true>(uA + HDR, uB + HDR, a0s, a1s, nullptr, nullptr, z0, z1, 0, 0, lane, hA, lA, hB, lB);
-        else
-          chunk_imma<false>(uA + HDR, uB + HDR, a0s, a1s, h0 ? im + (size_t)sB * 16 : zero,
-                            h1 ? im + (size_t)(sB + 4) * 16 : zero, z0, z1, z0, z1, lane, hA, lA, hB, lB);
-        fold_q4(uA, hA, lA, X[xa], X[xa + 1], g, t, acc[0][0], acc[0][1]);
-        fold_q4(uB, hB, lB, X[xb], X[xb + 1], g, t, acc[1][0], acc[1][1]);
-      } else {
-        float dA[4], dB[4];
-        chunk_mma<false, true>(uA + HDR, uB + HDR, a0s, a1s, nullptr, nullptr, z0, z1, 0, 0, m64, lane, dA, dB);
-        unit_fold<false>(uA, dA, X[xa].x, X[xa + 1].x, g, t, acc[0][0], acc[0][1]);
-        unit_fold<false>(uB, dB, X[xb].x, X[xb + 1].x, g, t, acc[1][0], acc[1][1]);
-      }
-      __syncwarp();  // every lane has read both slots before they are refilled
-      PK_T(const long long c2 = clock64(); cy_comp += c2 - c1;)
-      issue_next();
-      PK_T(cy_issue += clock64() - c2;)
+  // One chunk (chunk c of a row group whose first rows start at superblock
+  // phases p0 / p1) against the image (im, X, nsb padded sub-blocks): the
+  // next ring slot, folded into acc.
+  auto run_chunk = [&](const uint8_t* im, const float2* X, int nsb, int c, int p0, int p1, float (&acc)[2][2]) {
+    const uint32_t sl = consumed % kSlots;
+    PK_T(const long long c0 = clock64();)
+    if (!warp_wait(&bar[sl], (consumed / kSlots) & 1u, a.err)) {
+      bad = true;
+      return;
     }
-    // partial sums of the task's 32 rows (rb, row): reduce over the quad
-#pragma unroll
-    for (int rb = 0; rb < 2; ++rb)
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        float s = acc[rb][r];
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        acc[rb][r] = s;
-      }
-    float* P = (T.down ? a.part_dn : a.part_gu) + (int64_t)(T.down ? id - a.n_gu : id) * 32;
-    if (t == 0) {
-      P[g] = acc[0][0];
-      P[g + 8] = acc[0][1];
-      P[16 + g] = acc[1][0];
-      P[24 + g] = acc[1][1];
-    }
-    // The warp barrier orders the lanes' partial stores before lane 0's
-    // counter update; the update releases them at GPU scope (release is
-    // cumulative) and acquires the other tasks' partials for the last one.
-    __syncwarp();
-    unsigned* cnt = T.down ? a.cnt_dn + T.grp : a.cnt_gu + T.k * a.ngj + T.grp;
-    const unsigned need = T.down ? (unsigned)(a.top_k * a.S_dn) : (unsigned)a.S_gu;
-    unsigned last = 0;
-    if (lane == 0) {
-      unsigned old;
-      asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(cnt) : "memory");
-      last = old == need - 1;
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    PK_T(cy_task += clock64() - ct0;)
-    if (!last) return;
-    PK_T(const long long ce = clock64();)
-    if (!T.down) {
-      // gate/up epilogue: rows [0,16) gate, [16,32) up of the group's 16 outputs
-      const int k = T.k;
-      const float* Q = a.part_gu + (int64_t)(k * a.ngj + T.grp) * a.S_gu * 32;
-      // lanes 0-15 sum the gate rows, 16-31 the up rows; swap halves
-      const float sum = sum_parts(Q, a.S_gu, lane);
-      const float other = __shfl_xor_sync(0xffffffffu, sum, 16);
-      const float gate = sum, up = other;
-      const int j = lane < 16 ? M.map : -1;
-      float r = 0.f;
-      if (j >= 0 && s_e[k] >= 0) {
-        const float gb = s_bias[0][k] ? gate + s_bias[0][k][j] : gate;
-        const float ub = s_bias[1][k] ? up + s_bias[1][k][j] : up;
-        r = act_fn(a.act_kind, gb, ub, a.limit, a.alpha);
-      }
-      if (j >= 0) a.act[(int64_t)k * a.I + j] = r;
-      __syncwarp();
-      if (lane == 0) a.cnt_gu[k * a.ngj + T.grp] = 0u;
+    PK_T(const long long c1 = clock64(); cy_wait += c1 - c0; n_units += 2;)
+    consumed += 1;
+    const uint8_t* uA = ring + sl * 2 * UNIT;
+    const uint8_t* uB = uA + UNIT;
+    // B sources (see chunk_mma): half 0 from lanes g == t, half 1 from g == t + 4
+    const size_t pst = (size_t)nsb * 16;
+    const int sA = 8 * c - p0 + t + kPadL, sB = 8 * c - p1 + t + kPadL;
+    const bool h0 = g == t, h1 = g == t + 4;
+    const int xa = 8 * c - p0 + 2 * t + kPadL, xb = 8 * c - p1 + 2 * t + kPadL;
+    const uint8_t* a0s = h0 ? im + (size_t)sA * 16 : zero;
+    const uint8_t* a1s = h1 ? im + (size_t)(sA + 4) * 16 : zero;
+    const size_t z0 = h0 ? pst : 0, z1 = h1 ? pst : 0;
+    if (Q4) {
+      int hA[4], lA[4], hB[4], lB[4];
+      if (p0 == p1)
+        chunk_imma<true>(uA + HDR, uB + HDR, a0s, a1s, nullptr, nullptr, z0, z1, 0, 0, lane, hA, lA, hB, lB);
+      else
+        chunk_imma<false>(uA + HDR, uB + HDR, a0s, a1s, h0 ? im + (size_t)sB * 16 : zero,
+                          h1 ? im + (size_t)(sB + 4) * 16 : zero, z0, z1, z0, z1, lane, hA, lA, hB, lB);
+      fold_q4(uA, hA, lA, X[xa], X[xa + 1], g, t, acc[0][0], acc[0][1]);
+      fold_q4(uB, hB, lB, X[xb], X[xb + 1], g, t, acc[1][0], acc[1][1]);
     } else {
-      // down epilogue: 32 outputs, slots and splits combined in fixed order
-      const int h = M.map;
-      float o = 0.f;
-      for (int k = 0; k < a.top_k; ++k) {
-        if (s_e[k] < 0) continue;
-        const float* Q = a.part_dn + (int64_t)(k * a.ndp + T.grp) * a.S_dn * 32;
-        o = fmaf(s_w[k], sum_parts(Q, a.S_dn, lane), o);
-      }
-      if (h >= 0) {
-        for (int k = 0; k < a.top_k; ++k)
-          if (s_e[k] >= 0 && s_bias[2][k]) o = fmaf(s_w[k], s_bias[2][k][h], o);
-        if (a.out_f32)
-          static_cast<float*>(a.out)[h] = o;
-        else
-          static_cast<uint16_t*>(a.out)[h] = f32_to_bf16_bits(o);
-      }
-      __syncwarp();
-      if (lane == 0) a.cnt_dn[T.grp] = 0u;
+      float dA[4], dB[4];
+      chunk_mma<false, true>(uA + HDR, uB + HDR, a0s, a1s, nullptr, nullptr, z0, z1, 0, 0, m64, lane, dA, dB);
+      unit_fold<false>(uA, dA, X[xa].x, X[xa + 1].x, g, t, acc[0][0], acc[0][1]);
+      unit_fold<false>(uB, dB, X[xb].x, X[xb + 1].x, g, t, acc[1][0], acc[1][1]);
     }
-    PK_T(cy_epi += clock64() - ce;)
+    __syncwarp();  // every lane has read both slots before they are refilled
+    PK_T(const long long c2 = clock64(); cy_comp += c2 - c1;)
+    issue_next();
+    PK_T(cy_issue += clock64() - c2;)
   };
 
-  // ---- phase 0: gate/up tasks of this warp; phase 1: its down tasks.  One
-  // loop, so the task body exists once in the code (instruction cache).
-  int id = gw;
+  // Down images of up to two chunks (slot k[u], activation sub-blocks
+  // sb0[u] .. sb0[u] + 7, zero outside [0, I/32); u < n) into this warp's
+  // buffers (buf0 + u) % 2.  An activation is ready once its word is not +0.0 (the gate/up
+  // epilogue never stores that pattern); the loads repeat until every word
+  // the warp needs is ready, so one L2 round trip suffices when they are.
+  // Bounded: records kDevWaitTimeout and returns false.
+  auto stage_down = [&](int n, int buf0, const int (&k)[2], const int (&sb0)[2]) -> bool {
+    const int nsbI = a.I / 32, q = lane & 3;
+    float v[2][8];
+    bool ok = false;
+    for (uint32_t it = 0; it < kSpinPolls && !ok; ++it) {
+      ok = true;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int sb = sb0[u] + (lane >> 2);
+        if (u < n && sb >= 0 && sb < nsbI) {
+          const float* src = a.dact + (int64_t)k[u] * a.I + sb * 32 + 8 * q;
+          ld_relaxed_f32x8(src, v[u]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ok = ok && __float_as_uint(v[u][i]) != 0u;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
+        }
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) __nanosleep(32);
+    }
+    if (!ok) {
+      if (lane == 0 && a.err) atomicExch(a.err, kDevWaitTimeout);
+      return false;
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (u >= n) break;
+      uint8_t* mim = mini + (size_t)((buf0 + u) & 1) * pk_mini_bytes();
+      stage_group<Q4>(mim, reinterpret_cast<float2*>(mim + pk_img_bytes(1, kMiniNsb)), kMiniNsb, lane >> 2, q, v[u],
+                      true);
+    }
+    __syncwarp();
+    return true;
+  };
+
+  // The warp's range of one phase, one group at a time: stream, fold,
+  // publish the group's partial sums; the last contributor of a group runs
+  // its epilogue.
+  // Down chunk i of the flat list: its slot and first activation sub-block;
+  // false when the slot is skipped.
+  auto dn_chunk = [&](int i, int& k, int& sb0) -> bool {
+    const int grp = i / Cg_dn, r = i - grp * Cg_dn;
+    k = r / a.C_dn;
+    if (s_e[k] < 0) return false;
+    sb0 = 8 * (r - k * a.C_dn) - ldg_hint_i32(a.dn_ph + grp, keep_meta);
+    return true;
+  };
+  int dn_m = 0;  // down chunks of this warp consumed so far (buffer dn_m % 2)
+  auto run_range = [&](int down) {
+    const int Cg = down ? Cg_dn : Cg_gu, Q = down ? a.Q_dn : a.Q_gu;
+    const int r1 = down ? r1_dn : r1_gu;
+    if (down) {
+      // the images of the warp's first two down chunks, in one pass
+      int kk[2] = {0, 0}, sb[2] = {0, 0}, n = 0;
+      for (int i = r0_dn; i < r1_dn && n < 2; ++i) {
+        int k1, s1;
+        if (!dn_chunk(i, k1, s1)) continue;
+        if (n == 0) {
+          kk[0] = k1;
+          sb[0] = s1;
+        } else {
+          kk[1] = k1;
+          sb[1] = s1;
+        }
+        ++n;
+      }
+      if (n && !stage_down(n, 0, kk, sb)) bad = true;
+    }
+    for (int i = down ? r0_dn : r0_gu; i < r1 && !bad;) {
+      PK_T(const long long ct0 = clock64();)
+      const int G = i / Cg, gend = min(r1, (G + 1) * Cg);
+      const int grp = down ? G : G % a.ngj;
+      // row-block phases and this lane's row-map entry (L2 evict-last:
+      // every token re-reads them)
+      int p0, p1, map;
+      if (down) {
+        p0 = p1 = ldg_hint_i32(a.dn_ph + grp, keep_meta);
+        map = ldg_hint_i32(a.dn_h + grp * 32 + lane, keep_meta);
+      } else {
+        p0 = ldg_hint_i32(a.gu_ph + 2 * grp, keep_meta);
+        p1 = ldg_hint_i32(a.gu_ph + 2 * grp + 1, keep_meta);
+        map = lane < 16 ? ldg_hint_i32(a.gu_j + grp * 16 + lane, keep_meta) : -1;
+      }
+      float accg[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+      if (!down) {
+        const int k = G / a.ngj;
+        if (s_e[k] >= 0)
+          for (int j = i; j < gend && !bad; ++j) run_chunk(img, Xs, a.nsb_h, j - G * Cg, p0, p1, accg);
+      } else {
+        // runs of one slot; each weighted by its routing weight
+        for (int j = i; j < gend && !bad;) {
+          const int r = j - G * Cg, k = r / a.C_dn, kend = min(gend, G * Cg + (k + 1) * a.C_dn);
+          if (s_e[k] >= 0) {
+            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+            for (int jj = j; jj < kend && !bad; ++jj, ++dn_m) {
+              // the chunk's 8 activation sub-blocks, in this warp's image
+              // (the first two staged before the loop)
+              if (dn_m >= 2) {
+                int kk[2] = {k, 0}, sb[2] = {8 * (jj - G * Cg - k * a.C_dn) - p0, 0};
+                if (!stage_down(1, dn_m & 1, kk, sb)) {
+                  bad = true;
+                  break;
+                }
+              }
+              uint8_t* mim = mini + (size_t)(dn_m & 1) * pk_mini_bytes();
+              run_chunk(mim, reinterpret_cast<float2*>(mim + pk_img_bytes(1, kMiniNsb)), kMiniNsb, 0, 0, 0, acc);
+            }
+            const float w = s_w[k];
+#pragma unroll
+            for (int rb = 0; rb < 2; ++rb)
+#pragma unroll
+              for (int q = 0; q < 2; ++q) accg[rb][q] = fmaf(w, acc[rb][q], accg[rb][q]);
+          }
+          j = kend;
+        }
+      }
+      // partial sums of the group's 32 rows (rb, row): reduce over the quad
+#pragma unroll
+      for (int rb = 0; rb < 2; ++rb)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          float v = accg[rb][q];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          accg[rb][q] = v;
+        }
+      const int first = G * Cg / Q, count = ((G + 1) * Cg - 1) / Q - first + 1;
+      const int slots = down ? a.slots_dn : a.slots_gu;
+      float* Pg = (down ? a.part_dn : a.part_gu) + (int64_t)G * slots * 32;
+      float* P = Pg + (gw - first) * 32;
+      if (t == 0) {
+        P[g] = accg[0][0];
+        P[g + 8] = accg[0][1];
+        P[16 + g] = accg[1][0];
+        P[24 + g] = accg[1][1];
+      }
+      // The warp barrier orders the lanes' partial stores before lane 0's
+      // counter update; the update releases them at GPU scope (release is
+      // cumulative) and acquires the other contributors' partials for the
+      // last one.
+      __syncwarp();
+      unsigned* cnt = down ? a.cnt_dn + G : a.cnt_gu + G;
+      unsigned last = 0;
+      if (lane == 0) {
+        unsigned old;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(cnt) : "memory");
+        last = old == (unsigned)count - 1;
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      PK_T(cy_task += clock64() - ct0;)
+      i = gend;
+      if (!last) continue;
+      PK_T(const long long ce = clock64();)
+      const float sum = sum_parts(Pg, count, lane);
+      if (!down) {
+        // gate/up epilogue: rows [0,16) gate, [16,32) up of the group's 16
+        // outputs; lanes 0-15 hold the gate sums, 16-31 the up sums
+        const int k = G / a.ngj;
+        const float other = __shfl_xor_sync(0xffffffffu, sum, 16);
+        const float gate = sum, up = other;
+        const int jo = map;
+        float r = 0.f;
+        if (jo >= 0 && s_e[k] >= 0) {
+          const float gb = s_bias[0][k] ? gate + s_bias[0][k][jo] : gate;
+          const float ub = s_bias[1][k] ? up + s_bias[1][k][jo] : up;
+          r = act_fn(a.act_kind, gb, ub, a.limit, a.alpha);
+        }
+        // +0.0 marks "not written": store it as -0.0 (the same number)
+        if (jo >= 0) a.dact[(int64_t)k * a.I + jo] = __float_as_uint(r) == 0u ? -0.f : r;
+      } else {
+        // down epilogue: 32 outputs, the slots already weighted
+        const int h = map;
+        if (h >= 0) {
+          float o = sum;
+          for (int k = 0; k < a.top_k; ++k)
+            if (s_e[k] >= 0 && s_bias[2][k]) o = fmaf(s_w[k], s_bias[2][k][h], o);
+          if (a.out_f32)
+            static_cast<float*>(a.out)[h] = o;
+          else
+            static_cast<uint16_t*>(a.out)[h] = f32_to_bf16_bits(o);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) *cnt = 0u;
+      PK_T(cy_epi += clock64() - ce;)
+    }
+  };
+
+  // ---- phase 0: the warp's gate/up range; phase 1: its down range.  One
+  // loop, so the range body exists once in the code (instruction cache).
+  // No barrier between them: a down chunk waits only for the activation
+  // sub-blocks it reads (stage_down), so down work starts where gate/up is
+  // complete while other groups still stream.
   PK_T(if (lane == 0 && blockIdx.x < 160) g_pk_wtrace[(blockIdx.x * 16 + warp) * 8 + 7] = gtimer();)
 #pragma unroll 1
   for (int phase = 0; phase < 2; ++phase) {
-  const int end = phase == 0 ? a.n_gu : ntask;
-#pragma unroll 1
-  for (; id < end; id += nw) run_task(id);
+  run_range(phase);
   PK_T(if (lane == 0 && blockIdx.x < 160 && phase == 0) {
     unsigned long long* W = g_pk_wtrace + (blockIdx.x * 16 + warp) * 8;
     W[0] = gtimer();
@@ -1278,64 +1393,6 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
     W[5] = cy_epi;
     W[6] = cy_task;
   })
-  if (phase == 1) break;
-
-  // ---- all gate/up groups of every CTA done: stage the activations (CTA-wide).
-  // Each CTA arrives once its own tasks and epilogues are done (the barrier
-  // makes its warps' activation stores visible to thread 0, whose release
-  // publishes them), then waits for every CTA.
-  __syncthreads();
-  stamp(3);
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(a.sync, 1u);
-    const unsigned need = gridDim.x;
-    bool ok = false;
-    for (uint32_t i = 0; i < kSpinPolls && !ok; ++i) {
-      unsigned v;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync) : "memory");
-      ok = v >= need;
-      if (!ok) __nanosleep(32);
-    }
-    if (!ok) {
-      if (a.err) atomicExch(a.err, kDevWaitTimeout);
-      s_bad = 1;
-    }
-  }
-  __syncthreads();
-  stamp(4);
-  if (s_bad) bad = true;
-  for (int vv = 0; vv < a.top_k; ++vv) zero_pads(img + pk_img_bytes(vv, a.nsb_i), Xs + (size_t)vv * a.nsb_i, a.nsb_i, a.I);
-  {
-    // every slot's activation groups (8 elements) as one flat range, 4 groups
-    // (8 loads of 16 B) in flight per thread: one L2 round trip for the
-    // GPT-OSS shapes.  The 4 groups of a sub-block are consecutive lanes of
-    // one slot (I % 32 == 0).
-    const int ngv = a.I / 8, total = a.top_k * ngv;
-    for (int q0 = threadIdx.x - lane; q0 < total; q0 += 4 * kPkThreads) {
-      float v[4][8];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int q = q0 + lane + u * kPkThreads;
-        const float4* src = reinterpret_cast<const float4*>(a.act) + 2 * (size_t)q;  // slots are contiguous
-        const float4 f0 = q < total ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 f1 = q < total ? __ldcg(src + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[u][0] = f0.x; v[u][1] = f0.y; v[u][2] = f0.z; v[u][3] = f0.w;
-        v[u][4] = f1.x; v[u][5] = f1.y; v[u][6] = f1.z; v[u][7] = f1.w;
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int qw = q0 + u * kPkThreads;
-        if (qw >= total) break;  // warp-uniform
-        const int q = qw + lane;
-        const int vv = min(q / ngv, a.top_k - 1), qi = q - vv * ngv;
-        stage_group<Q4>(img + pk_img_bytes(vv, a.nsb_i), Xs + (size_t)vv * a.nsb_i, a.nsb_i, qi >> 2, qi & 3, v[u],
-                        q < total);
-      }
-    }
-  }
-  __syncthreads();
-  stamp(5);
   }
   __syncthreads();
   stamp(6);
@@ -1356,11 +1413,14 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
   if (threadIdx.x == 0) {
     unsigned old;
     asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.sync + 1) : "memory");
-    if (old == gridDim.x - 1) {
-      a.sync[0] = 0u;
-      a.sync[1] = 0u;
-      __threadfence();
-    }
+    s_last = old == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    for (int i = threadIdx.x; i < a.top_k * a.I / 4; i += kPkThreads)
+      reinterpret_cast<float4*>(a.dact)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (threadIdx.x == 0) a.sync[1] = 0u;
+    __threadfence();
   }
 }
 
@@ -1375,28 +1435,21 @@ static int num_sms() {
   return n;
 }
 
-// Chunks per task: the smallest makespan (units per warp, plus one unit of
-// per-task overhead) over the resident warps.
-static int choose_nc(int groups, int C, int warps) {
-  int best = 1;
-  double best_t = 1e30;
-  for (int nc = 1; nc <= C; ++nc) {
-    const int S = (C + nc - 1) / nc;
-    const int64_t tasks = (int64_t)groups * S;
-    const double waves = (double)((tasks + warps - 1) / warps);
-    const double tm = waves * (2.0 * nc + 1.0);
-    if (tm < best_t - 1e-9) {
-      best_t = tm;
-      best = nc;
-    }
-  }
-  return best;
+// Partial-sum slots per group: the most warps whose ranges can meet one
+// group, for the smallest range length Q any launch uses (the full device's
+// warps; a smaller grid only lengthens Q and lowers the count).
+static void pk_slots(const TsbMoeSpec& sp, const PkGeo& G, int& sg, int& sd) {
+  const int64_t warps = (int64_t)num_sms() * kPkWarps;
+  const int64_t Ng = (int64_t)sp.top_k * G.ngj * G.C_gu, Nd = (int64_t)sp.top_k * G.ndp * G.C_dn;
+  const int64_t Qg = std::max<int64_t>(1, (Ng + warps - 1) / warps), Qd = std::max<int64_t>(1, (Nd + warps - 1) / warps);
+  sg = (int)((G.C_gu + Qg - 1) / Qg + 1);
+  sd = (int)(((int64_t)sp.top_k * G.C_dn + Qd - 1) / Qd + 1);
 }
 
 // Workspace after the generic layer workspace: counters, device-wide words,
-// gate/up and down partial sums (sized for one chunk per task, the most).
+// gate/up and down partial sums.
 struct PkWs {
-  size_t cnt_gu, cnt_dn, sync, logits, part_gu, part_dn, total;
+  size_t cnt_gu, cnt_dn, sync, dact, part_gu, part_dn, total;
 };
 static PkWs pk_ws(const TsbMoeSpec& sp, const PkGeo& G) {
   auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
@@ -1404,10 +1457,12 @@ static PkWs pk_ws(const TsbMoeSpec& sp, const PkGeo& G) {
   W.cnt_gu = 0;
   W.cnt_dn = al(W.cnt_gu + 4 * (size_t)sp.top_k * G.ngj);
   W.sync = al(W.cnt_dn + 4 * (size_t)G.ndp);
-  W.logits = al(W.sync + 64);
-  W.part_gu = al(W.logits + 4 * (size_t)sp.n_experts);
-  W.part_dn = al(W.part_gu + 4 * 32 * (size_t)sp.top_k * G.ngj * G.C_gu);
-  W.total = al(W.part_dn + 4 * 32 * (size_t)sp.top_k * G.ndp * G.C_dn);
+  W.dact = al(W.sync + 64);
+  W.part_gu = al(W.dact + 4 * (size_t)sp.top_k * sp.inter);
+  int sg = 0, sd = 0;
+  pk_slots(sp, G, sg, sd);
+  W.part_dn = al(W.part_gu + 4 * 32 * (size_t)sp.top_k * G.ngj * sg);
+  W.total = al(W.part_dn + 4 * 32 * (size_t)G.ndp * sd);
   return W;
 }
 
@@ -1475,7 +1530,7 @@ static int launch_pk(PkArgs& a, int grid, size_t smem, cudaStream_t st) {
 }
 
 int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x, int32_t* ids,
-                         float* wts, float* act, void* out, int out_f32, int32_t* err, char* pws, cudaStream_t st,
+                         float* wts, void* out, int out_f32, int32_t* err, char* pws, cudaStream_t st,
                          const void* router_w, const float* router_b) {
   // geometry depends only on the spec: cache the last one
   static thread_local TsbMoeSpec last_sp{};
@@ -1510,24 +1565,22 @@ int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpe
   const int rc = G.q4 ? pk_grid<FMT_Q4_K>(grid) : pk_grid<FMT_MXFP4>(grid);
   if (rc) return rc;
   const int warps = grid * kPkWarps;
-  a.nc_gu = choose_nc(sp.top_k * G.ngj, G.C_gu, warps);
-  a.S_gu = (G.C_gu + a.nc_gu - 1) / a.nc_gu;
-  a.nc_dn = choose_nc(sp.top_k * G.ndp, G.C_dn, warps);
-  a.S_dn = (G.C_dn + a.nc_dn - 1) / a.nc_dn;
-  a.n_gu = sp.top_k * G.ngj * a.S_gu;
-  a.n_dn = sp.top_k * G.ndp * a.S_dn;
+  a.N_gu = sp.top_k * G.ngj * G.C_gu;
+  a.N_dn = sp.top_k * G.ndp * G.C_dn;
+  a.Q_gu = std::max(1, (a.N_gu + warps - 1) / warps);
+  a.Q_dn = std::max(1, (a.N_dn + warps - 1) / warps);
+  pk_slots(sp, G, a.slots_gu, a.slots_dn);
   a.nsb_h = sp.hidden / 32 + kPadL + kPadR;
-  a.nsb_i = sp.inter / 32 + kPadL + kPadR;
   a.x = static_cast<const uint16_t*>(x);
   a.router_w = static_cast<const uint16_t*>(router_w);
   a.router_b = router_b;
   a.ids = ids;
   a.wts = wts;
   a.experts = ex;
-  a.act = act;
   a.cnt_gu = reinterpret_cast<unsigned*>(pws + W.cnt_gu);
   a.cnt_dn = reinterpret_cast<unsigned*>(pws + W.cnt_dn);
   a.sync = reinterpret_cast<unsigned*>(pws + W.sync);
+  a.dact = reinterpret_cast<float*>(pws + W.dact);
   a.part_gu = reinterpret_cast<float*>(pws + W.part_gu);
   a.part_dn = reinterpret_cast<float*>(pws + W.part_dn);
 
@@ -1537,9 +1590,8 @@ int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpe
   a.limit = sp.limit;
   a.alpha = sp.alpha;
   a.err = err;
-  const int nsb_max = std::max(a.nsb_h, a.nsb_i);
-  if (G.q4) return launch_pk<FMT_Q4_K>(a, grid, pk_smem(kQ4Unit, nsb_max, sp.top_k), st);
-  return launch_pk<FMT_MXFP4>(a, grid, pk_smem(kMxUnit, nsb_max, sp.top_k), st);
+  if (G.q4) return launch_pk<FMT_Q4_K>(a, grid, pk_smem(kQ4Unit, a.nsb_h), st);
+  return launch_pk<FMT_MXFP4>(a, grid, pk_smem(kMxUnit, a.nsb_h), st);
 }
 
 }  // namespace tsb

@@ -44,7 +44,7 @@ size_t packed_total_bytes(const TsbMoeSpec& sp);
 int launch_pack(const TsbMoeSpec& sp, const TsbExpert* experts, void* packed, cudaStream_t st);
 size_t packed_ws_bytes(const TsbMoeSpec& sp);
 int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x, int32_t* ids,
-                         float* wts, float* act, void* out, int out_f32, int32_t* err, char* pws, cudaStream_t st,
+                         float* wts, void* out, int out_f32, int32_t* err, char* pws, cudaStream_t st,
                          const void* router_w, const float* router_b);
 int launch_dequant(int fmt, const void* w, const void* s, int64_t rows, int64_t cols, void* out, int odt,
                    cudaStream_t st);

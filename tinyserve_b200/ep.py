@@ -173,3 +173,85 @@ def quant_layer_forward(layer) -> LayerForward:
         return out
 
     return f
+
+
+class NcclComm:
+    """An NCCL communicator for the C-ABI's expert-parallel entry point
+    (tsb_ep_moe_decode takes a raw ``ncclComm_t``).  Built with NCCL's public
+    API through the process's libnccl.so.2 (the one PyTorch loaded): rank 0
+    makes the unique id and the ranks of ``group`` (a torch.distributed
+    process group, any backend) share it; this GPU must be current."""
+
+    def __init__(self, group=None):
+        import ctypes
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self._nccl = ctypes.CDLL("libnccl.so.2", mode=ctypes.RTLD_GLOBAL)
+        uid = ctypes.create_string_buffer(128)  # ncclUniqueId: 128 opaque bytes
+        if self.rank == 0:
+            rc = self._nccl.ncclGetUniqueId(uid)
+            if rc:
+                raise RuntimeError(f"ncclGetUniqueId failed ({rc})")
+        box = [bytes(uid.raw)]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        uid = ctypes.create_string_buffer(box[0], 128)
+
+        class _Uid(ctypes.Structure):
+            _fields_ = [("internal", ctypes.c_char * 128)]
+
+        u = _Uid()
+        ctypes.memmove(ctypes.addressof(u), uid, 128)
+        self.comm = ctypes.c_void_p()
+        self._nccl.ncclCommInitRank.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _Uid, ctypes.c_int]
+        rc = self._nccl.ncclCommInitRank(ctypes.byref(self.comm), self.world, u, self.rank)
+        if rc:
+            raise RuntimeError(f"ncclCommInitRank failed ({rc})")
+
+    def close(self) -> None:
+        import ctypes
+        if self.comm:
+            self._nccl.ncclCommDestroy.argtypes = [ctypes.c_void_p]
+            self._nccl.ncclCommDestroy(self.comm)
+            self.comm = ctypes.c_void_p()
+
+
+class NativeEPDecode:
+    """The gather scheme of :meth:`ExpertParallelMoE.forward_gather` as one
+    C-ABI call (tsb_ep_moe_decode): all-gather, local experts, reduce-scatter,
+    all on the current stream inside the library.  ``local`` is a
+    :class:`tinyserve_b200.moe.QuantMoE` holding this rank's experts (top_k =
+    the model's); T is fixed per instance (the workspace is sized for it)."""
+
+    def __init__(self, local, comm: NcclComm, T: int):
+        import ctypes
+        from . import _lib
+        self.local, self.comm, self.T = local, comm, T
+        self._spec = {False: local.spec, True: local.spec_f32}
+        n = _lib.lib().tsb_ep_decode_workspace(ctypes.byref(local.spec), T, comm.world, int(local.packed))
+        self.ws = torch.zeros(n, dtype=torch.uint8, device=local.device)
+
+    def __call__(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                 out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        import ctypes
+        from . import _lib
+        if x.shape != (self.T, self.local.hidden) or x.dtype != torch.bfloat16:
+            raise ValueError(f"x must be bf16 [{self.T}, {self.local.hidden}]")
+        ids = ids.to(torch.int32).contiguous()
+        weights = weights.to(torch.float32).contiguous()
+        out = torch.empty(self.T, self.local.hidden, dtype=out_dtype, device=x.device)
+        L = self.local
+        rc = _lib.lib().tsb_ep_moe_decode(
+            ctypes.byref(self._spec[out_dtype == torch.float32]), L._table.data_ptr(),
+            L._packed.data_ptr() if L.packed else None, x.contiguous().data_ptr(), self.T, ids.data_ptr(),
+            weights.data_ptr(), out.data_ptr(), self.comm.comm, self.comm.rank, self.comm.world, self.ws.data_ptr(),
+            self.ws.numel(), torch.cuda.current_stream(x.device).cuda_stream)
+        _lib.check(rc)
+        return out
+
+    def device_error(self) -> int:
+        import ctypes
+        from . import _lib
+        code = ctypes.c_int32()
+        _lib.check(_lib.lib().tsb_read_device_error(self.ws.data_ptr(), ctypes.byref(code),
+                                                    torch.cuda.current_stream(self.local.device).cuda_stream))
+        return code.value
