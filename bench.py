@@ -438,6 +438,28 @@ def _ep_time(call, steps: int, warmup: int, ws: int, dev) -> float:
     return ms
 
 
+def _ep_graphed(call, dev):
+    """`call` captured once into a CUDA graph (a decode-sized layer call is
+    launch-bound when issued eagerly from Python); returns (replay, "graph"),
+    or (call, "eager") when capture is refused."""
+    import torch
+    try:
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            call()
+        torch.cuda.current_stream(dev).wait_stream(st)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            call()
+        torch.cuda.synchronize()
+        return g.replay, "graph"
+    except Exception as e:  # noqa: BLE001 - reported in the bench line
+        torch.cuda.synchronize()
+        return call, f"eager ({type(e).__name__})"
+
+
 def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
     """GPT-OSS-120B-shaped MXFP4 layer (128 experts, top-4,
     H = I = 2880) sharded expert-parallel over the ranks (128/N experts each),
@@ -450,7 +472,10 @@ def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
     through both schemes (``forward_gather`` and the all-to-all ``forward``).
     Beside each EP leg: the same collectives alone (``comm_ms``) and the local
     layer alone on the gathered rows (``local_ms``), which name the limiter.
-    At N = 1 the whole layer runs on one GPU with no exchange."""
+    The decode legs also run through the C-ABI (``native_*``:
+    tsb_ep_moe_decode on an NCCL communicator, router included) captured in
+    a CUDA graph.  At N = 1 the whole layer runs on one GPU with no exchange
+    (decode legs graph-captured too)."""
     import torch
     from tinyserve_b200.formats import TSB_MXFP4
     from tinyserve_b200.moe import QuantMoE, Router
@@ -467,18 +492,24 @@ def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
                          router_w=router.router_w, gate_up_layout="interleaved")
         for name, T, n in legs:
             x = hidden_states(T, seed=100 + rank, device=dev)
-            ms = _ep_time(lambda: whole.decode(x), n, warmup, ws, dev)
+            fn, how = (lambda: whole.decode(x)), "eager"
+            if T <= 64:
+                fn, how = _ep_graphed(fn, dev)
+            ms = _ep_time(fn, n, warmup, ws, dev)
             res[f"{name}_tok_s"] = T / (ms * 1e-3)
             res[f"{name}_ms"] = ms
+            res[f"{name}_launch"] = how
         res["exchange"] = "none (all 128 experts on one GPU)"
         return res
     import torch.distributed as dist
-    from tinyserve_b200.ep import ExpertParallelMoE, quant_layer_forward, quant_local_forward
+    from tinyserve_b200.ep import ExpertParallelMoE, NativeEPDecode, NcclComm, quant_layer_forward, quant_local_forward
     local1 = QuantMoE(part.experts, fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=H, inter=H, top_k=1,
                       gate_up_layout="interleaved", pack=False)
     lf = quant_layer_forward(part)
     gather = ExpertParallelMoE(E, k, H, router=router, layer_forward=lf)
     a2a = ExpertParallelMoE(E, k, H, quant_local_forward(local1), router=router)
+    nccl = NcclComm()
+    keep = []
     for name, T, n in legs:
         x = hidden_states(T, seed=100 + rank, device=dev)
         ms = _ep_time(lambda: gather.forward_gather(x), n, warmup, ws, dev)
@@ -491,11 +522,11 @@ def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
         pa = torch.zeros(ws * T, H, dtype=torch.float32, device=dev)
         o = torch.empty(T, H, dtype=torch.float32, device=dev)
 
-        def comm():
+        def coll():
             dist.all_gather_into_tensor(xa, x)
             dist.all_gather_into_tensor(ma, meta)
             dist.reduce_scatter_tensor(o, pa)
-        res[f"{name}_comm_ms"] = _ep_time(comm, n, warmup, ws, dev)
+        res[f"{name}_comm_ms"] = _ep_time(coll, n, warmup, ws, dev)
         res[f"{name}_comm_mb"] = (xa.numel() * 2 + ma.numel() * 4 + pa.numel() * 4) * (ws - 1) / ws / 1e6
         # the local layer alone on gathered rows with this rank's share of slots
         ids, w = router(hidden_states(ws * T, seed=900 + rank, device=dev))
@@ -503,12 +534,25 @@ def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
         lid = torch.where((lid >= 0) & (lid < el), lid, torch.full_like(lid, -1))
         xg = hidden_states(ws * T, seed=901, device=dev)
         res[f"{name}_local_ms"] = _ep_time(lambda: lf(xg, lid, w), n, warmup, 1, dev)
+        if name != "prefill":
+            nat = NativeEPDecode(part, nccl, T)
+            fn, how = _ep_graphed(lambda: nat(x, *router(x)), dev)
+            ms = _ep_time(fn, n, warmup, ws, dev)
+            res[f"native_{name}_tok_s"] = ws * T / (ms * 1e-3)
+            res[f"native_{name}_ms"] = ms
+            res[f"native_{name}_launch"] = how
+            keep.append((fn, nat))  # graphs released before the communicator
         if name == "prefill":
             ms = _ep_time(lambda: a2a(x), n, warmup, ws, dev)
             res["prefill_a2a_tok_s"] = ws * T / (ms * 1e-3)
             res["prefill_a2a_ms"] = ms
         del xa, ma, pa
         torch.cuda.empty_cache()
+    torch.cuda.synchronize()
+    keep.clear()
+    import gc
+    gc.collect()
+    nccl.close()
     res["exchange"] = ("forward_gather: NCCL all_gather_into_tensor (bf16 tokens + routing) and reduce_scatter_tensor "
                        "(fp32 partials); prefill_a2a: NCCL all_to_all_single with uneven splits")
     return res

@@ -57,7 +57,8 @@ namespace tsb {
 
 constexpr int kPkThreads = 512;
 constexpr int kPkWarps = kPkThreads / 32;
-constexpr int kCopyLane = 31;        // the lane that issues bulk copies and L2 prefetches
+constexpr int kCopyLane = 31;
+constexpr bool kPfGateUp = false, kPfDown = false;  // L2 prefetch of the chunks the ring does not hold yet        // the lane that issues bulk copies and L2 prefetches
 constexpr int kSlots = 2;            // ring slots per warp (one chunk = two units each)
 constexpr int kPadL = 8, kPadR = 16;  // zero sub-blocks before / after a B image (phase shifts, last chunk)
 constexpr int kQ4Hdr = 320, kQ4Unit = 320 + 2048;
@@ -620,81 +621,76 @@ __device__ __forceinline__ void chunk_mma(const uint8_t* uA, const uint8_t* uB, 
   }
 }
 
-// ---- Q4_K on the int8 tensor path (mma.m16n8k32, u8 codes x s8/u8 x bytes)
-__device__ __forceinline__ void imma_hi(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                        uint32_t b1) {
+// ---- Q4_K on the int8 tensor path (mma.m16n8k32, u8 codes x s8 x bytes)
+__device__ __forceinline__ void imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                     uint32_t b1) {
   asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void imma_lo(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                        uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 // One chunk (two units) of Q4_K: MMA (h, i) covers elements 8i..8i+7 of the
-// lane's sub-block 4h + t (k-quad t: 8i..8i+3, k-quad t+4: 8i+4..8i+7); the B
-// operand of the lane g == 4h + t holds the hi (or lo) bytes of the same
-// elements of the x sub-block, every other lane zeros.  Half 0 fills columns
-// 0-3, half 1 columns 4-7.  Accumulators: hi and lo sums of each unit, exact
-// in int32.
-template <bool SHARED>
-__device__ __forceinline__ void chunk_imma(const uint8_t* uA, const uint8_t* uB, const uint8_t* srcA0,
-                                           const uint8_t* srcA1, const uint8_t* srcB0, const uint8_t* srcB1,
-                                           size_t strA0, size_t strA1, size_t strB0, size_t strB1, int lane,
-                                           int (&hA)[4], int (&lA)[4], int (&hB)[4], int (&lB)[4]) {
+// lane's sub-block 4h + t (k-quad t: 8i..8i+3, k-quad t+4: 8i+4..8i+7).  The
+// 14-bit x of a sub-block is split x = 256*hi + lo, both signed bytes; in
+// MMA (h, i) column 4h + t carries the hi bytes of sub-block 4h + t and
+// column 4(1-h) + t its lo bytes (the B operand of lanes g == t and g == t+4;
+// every other lane supplies zeros), so one MMA yields both partial dots and a
+// unit takes 8 MMAs.  bX0 / bX1: this lane's B source for half 0 / 1 (its
+// plane 0 for the hi or lo pair), zX the plane stride (0 for a zero lane);
+// shared: unit B reads unit A's x (both row blocks at the same phase).
+// Result per unit and lane: c[r] = 256*hi + lo dot of rows g (r < 2) / g+8,
+// sub-blocks 2t, 2t+1 (r & 1); exact in int32.
+__device__ __forceinline__ void chunk_imma(const uint8_t* uA, const uint8_t* uB, const uint8_t* bA0,
+                                           const uint8_t* bA1, const uint8_t* bB0, const uint8_t* bB1, size_t zA,
+                                           size_t zB, bool shared, int lane, int (&cA)[4], int (&cB)[4]) {
+  int dA[2][4], dB[2][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) hA[i] = lA[i] = hB[i] = lB[i] = 0;
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dA[h][i] = dB[h][i] = 0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int h = j >> 1, G = j & 1;  // plane j: MMAs (h, 2G), (h, 2G + 1)
-    const uint8_t* sa = h ? srcA1 : srcA0;
-    const size_t za = h ? strA1 : strA0;
     const uint4 qa = lds128(uA + (32 * j + lane) * 16);
     const uint4 qb = lds128(uB + (32 * j + lane) * 16);
-    const uint4 xha = lds128(sa + G * za), xla = lds128(sa + (2 + G) * za);
-    uint4 xhb = xha, xlb = xla;
-    if (!SHARED) {
-      const uint8_t* sb = h ? srcB1 : srcB0;
-      const size_t zb = h ? strB1 : strB0;
-      xhb = lds128(sb + G * zb);
-      xlb = lds128(sb + (2 + G) * zb);
-    }
+    const uint4 xa = lds128((h ? bA1 : bA0) + G * zA);
+    const uint4 xb = shared ? xa : lds128((h ? bB1 : bB0) + G * zB);
     // unit A: words x (row g) / y (row g+8) -> MMA 2G, z / w -> MMA 2G+1
-    const uint32_t a0 = qa.x & 0x0F0F0F0Fu, a1 = qa.y & 0x0F0F0F0Fu;
-    const uint32_t a2 = (qa.x >> 4) & 0x0F0F0F0Fu, a3 = (qa.y >> 4) & 0x0F0F0F0Fu;
-    const uint32_t a4 = qa.z & 0x0F0F0F0Fu, a5 = qa.w & 0x0F0F0F0Fu;
-    const uint32_t a6 = (qa.z >> 4) & 0x0F0F0F0Fu, a7 = (qa.w >> 4) & 0x0F0F0F0Fu;
-    imma_hi(hA, a0, a1, a2, a3, xha.x, xha.y);
-    imma_lo(lA, a0, a1, a2, a3, xla.x, xla.y);
-    imma_hi(hA, a4, a5, a6, a7, xha.z, xha.w);
-    imma_lo(lA, a4, a5, a6, a7, xla.z, xla.w);
-    const uint32_t c0 = qb.x & 0x0F0F0F0Fu, c1 = qb.y & 0x0F0F0F0Fu;
-    const uint32_t c2 = (qb.x >> 4) & 0x0F0F0F0Fu, c3 = (qb.y >> 4) & 0x0F0F0F0Fu;
-    const uint32_t c4 = qb.z & 0x0F0F0F0Fu, c5 = qb.w & 0x0F0F0F0Fu;
-    const uint32_t c6 = (qb.z >> 4) & 0x0F0F0F0Fu, c7 = (qb.w >> 4) & 0x0F0F0F0Fu;
-    imma_hi(hB, c0, c1, c2, c3, xhb.x, xhb.y);
-    imma_lo(lB, c0, c1, c2, c3, xlb.x, xlb.y);
-    imma_hi(hB, c4, c5, c6, c7, xhb.z, xhb.w);
-    imma_lo(lB, c4, c5, c6, c7, xlb.z, xlb.w);
+    imma(dA[h], qa.x & 0x0F0F0F0Fu, qa.y & 0x0F0F0F0Fu, (qa.x >> 4) & 0x0F0F0F0Fu, (qa.y >> 4) & 0x0F0F0F0Fu, xa.x,
+         xa.y);
+    imma(dA[h], qa.z & 0x0F0F0F0Fu, qa.w & 0x0F0F0F0Fu, (qa.z >> 4) & 0x0F0F0F0Fu, (qa.w >> 4) & 0x0F0F0F0Fu, xa.z,
+         xa.w);
+    imma(dB[h], qb.x & 0x0F0F0F0Fu, qb.y & 0x0F0F0F0Fu, (qb.x >> 4) & 0x0F0F0F0Fu, (qb.y >> 4) & 0x0F0F0F0Fu, xb.x,
+         xb.y);
+    imma(dB[h], qb.z & 0x0F0F0F0Fu, qb.w & 0x0F0F0F0Fu, (qb.z >> 4) & 0x0F0F0F0Fu, (qb.w >> 4) & 0x0F0F0F0Fu, xb.z,
+         xb.w);
+  }
+  // Lane t < 2 holds the hi dots of sub-blocks 2t, 2t+1 in its half-0
+  // columns and the lo dots of sub-blocks 4+2t, 5+2t in its half-1 columns;
+  // lane t ^ 2 the reverse.  Swap the lo halves across the pair.
+  const bool lowq = (lane & 3) < 2;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int ka = lowq ? dA[0][i] : dA[1][i], sa = lowq ? dA[1][i] : dA[0][i];
+    const int kb = lowq ? dB[0][i] : dB[1][i], sb = lowq ? dB[1][i] : dB[0][i];
+    cA[i] = ka * 256 + __shfl_xor_sync(0xffffffffu, sa, 2);
+    cB[i] = kb * 256 + __shfl_xor_sync(0xffffffffu, sb, 2);
   }
 }
 
 // Q4_K fold of one unit: sub-block n's dot product is
-//   2^-e_n * (d * sc_n * (256*hi_n + lo_n)) - dmin * m_n * X_n
+//   2^-e_n * (d * sc_n * c_n) - dmin * m_n * X_n,  c_n = 256*hi_n + lo_n
 // with X_n = 2^-e_n * sum x_int (the image's float2 per sub-block).
-__device__ __forceinline__ void fold_q4(const uint8_t* u, const int (&hi)[4], const int (&lo)[4], float2 xa, float2 xb,
-                                        int g, int t, float& acc0, float& acc1) {
+__device__ __forceinline__ void fold_q4(const uint8_t* u, const int (&c)[4], float2 xa, float2 xb, int g, int t,
+                                        float& acc0, float& acc1) {
 #pragma unroll
   for (int rho = 0; rho < 2; ++rho) {
     const int row = g + 8 * rho;
     const uint32_t dd = *reinterpret_cast<const uint32_t*>(u + 4 * row);
     const uint32_t sm = *reinterpret_cast<const uint32_t*>(u + 64 + 16 * row + 4 * t);
     const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&dd));
-    const float fa = (float)(hi[2 * rho] * 256 + lo[2 * rho]) * xa.x;
-    const float fb = (float)(hi[2 * rho + 1] * 256 + lo[2 * rho + 1]) * xb.x;
+    const float fa = (float)c[2 * rho] * xa.x;
+    const float fb = (float)c[2 * rho + 1] * xb.x;
     const float uu = fmaf((float)((sm >> 8) & 255u), fb, (float)(sm & 255u) * fa);
     const float vv = fmaf((float)(sm >> 24), xb.y, (float)((sm >> 16) & 255u) * xa.y);
     float acc = rho ? acc1 : acc0;
@@ -877,7 +873,7 @@ __device__ __forceinline__ void pow2_scale(float m, float& scale, float& inv) {
 //   MXFP4 (f16 MMA): group G = element pairs 4G..4G+3 as f16x2, x scaled by
 //     a power of two per sub-block (max |x| in [2^14, 2^15)); X[s] = (2^-e, 0).
 //   Q4_K (int8 MMA): x_int = rint(x * 2^e) with e per sub-block (max |x_int|
-//     in [2^13, 2^14)), split x_int = 256*hi + lo (hi signed, lo unsigned):
+//     in [2^13, 2^14)), split x_int = 256*hi + lo (both signed bytes):
 //     groups 0, 1 = hi bytes of elements 0-15, 16-31, groups 2, 3 = lo bytes;
 //     X[s] = (2^-e, 2^-e * sum x_int).
 // stage_group writes the 8 elements 8q..8q+7 of sub-block sb; the four groups
@@ -902,7 +898,7 @@ __device__ __forceinline__ void stage_group(uint8_t* img, float2* X, int nsb, in
     for (int i = 0; i < 8; ++i) {
       const int xi = valid ? __float2int_rn(v[i] * sc) : 0;
       sum += xi;
-      hi[i >> 2] |= (uint32_t)((xi >> 8) & 255) << (8 * (i & 3));
+      hi[i >> 2] |= (uint32_t)(((xi + 128) >> 8) & 255) << (8 * (i & 3));  // x = 256*hi + lo, lo in [-128, 128)
       lo[i >> 2] |= (uint32_t)(xi & 255) << (8 * (i & 3));
     }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
@@ -987,6 +983,13 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
   if (lane < kSlots) mbar_init(&bar[lane], 1);
   fence_barrier_init();
   if (a.router_w) cluster_arrive_relaxed();
+  // Programmatic dependent launch: the next launch on the stream may start
+  // its CTAs (and this prologue) as SMs free up; everything above touches
+  // only shared memory.  Before the first global read of data an earlier
+  // launch may write (x, ids, the workspace words), wait for that launch to
+  // complete.  Without a programmatic predecessor the wait returns at once.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- router logits, split over the cluster (ids given: validated below)
   if (a.router_w) pk_logits(a, s_logit, warp, lane);
@@ -1111,8 +1114,8 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
   }
   // Down chunks beyond what the ring holds: into L2 while gate/up streams.
   // The ring requests the warp's first kSlots down chunks itself as its last
-  // gate/up chunks are consumed; prefetching those too would only take HBM
-  // bandwidth from gate/up, which the barrier waits for.
+  // gate/up chunks are consumed.  (Prefetching those, or the gate/up chunks
+  // past the ring, measured slower: the extra requests delay the ring's.)
   if (lane == kCopyLane) {
     int skip = kSlots;
     for (int i = r0_dn; i < r1_dn; ++i) {
@@ -1158,14 +1161,17 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
     const uint8_t* a1s = h1 ? im + (size_t)(sA + 4) * 16 : zero;
     const size_t z0 = h0 ? pst : 0, z1 = h1 ? pst : 0;
     if (Q4) {
-      int hA[4], lA[4], hB[4], lB[4];
-      if (p0 == p1)
-        chunk_imma<true>(uA + HDR, uB + HDR, a0s, a1s, nullptr, nullptr, z0, z1, 0, 0, lane, hA, lA, hB, lB);
-      else
-        chunk_imma<false>(uA + HDR, uB + HDR, a0s, a1s, h0 ? im + (size_t)sB * 16 : zero,
-                          h1 ? im + (size_t)(sB + 4) * 16 : zero, z0, z1, z0, z1, lane, hA, lA, hB, lB);
-      fold_q4(uA, hA, lA, X[xa], X[xa + 1], g, t, acc[0][0], acc[0][1]);
-      fold_q4(uB, hB, lB, X[xb], X[xb + 1], g, t, acc[1][0], acc[1][1]);
+      // hi bytes: lanes g == 4h + t; lo bytes (planes 2, 3): lanes g == 4(1-h) + t
+      const bool on = h0 || h1;
+      const size_t lo = 2 * pst, zq = on ? pst : 0;
+      const uint8_t* qA0 = on ? im + (size_t)sA * 16 + (h1 ? lo : 0) : zero;
+      const uint8_t* qA1 = on ? im + (size_t)(sA + 4) * 16 + (h0 ? lo : 0) : zero;
+      int cA[4], cB[4];
+      const uint8_t* qB0 = on ? im + (size_t)sB * 16 + (h1 ? lo : 0) : zero;
+      const uint8_t* qB1 = on ? im + (size_t)(sB + 4) * 16 + (h0 ? lo : 0) : zero;
+      chunk_imma(uA + HDR, uB + HDR, qA0, qA1, qB0, qB1, zq, zq, p0 == p1, lane, cA, cB);
+      fold_q4(uA, cA, X[xa], X[xa + 1], g, t, acc[0][0], acc[0][1]);
+      fold_q4(uB, cB, X[xb], X[xb + 1], g, t, acc[1][0], acc[1][1]);
     } else {
       float dA[4], dB[4];
       chunk_mma<false, true>(uA + HDR, uB + HDR, a0s, a1s, nullptr, nullptr, z0, z1, 0, 0, m64, lane, dA, dB);
@@ -1270,17 +1276,19 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
         map = lane < 16 ? ldg_hint_i32(a.gu_j + grp * 16 + lane, keep_meta) : -1;
       }
       float accg[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-      if (!down) {
-        const int k = G / a.ngj;
-        if (s_e[k] >= 0)
-          for (int j = i; j < gend && !bad; ++j) run_chunk(img, Xs, a.nsb_h, j - G * Cg, p0, p1, accg);
-      } else {
-        // runs of one slot; each weighted by its routing weight
-        for (int j = i; j < gend && !bad;) {
-          const int r = j - G * Cg, k = r / a.C_dn, kend = min(gend, G * Cg + (k + 1) * a.C_dn);
-          if (s_e[k] >= 0) {
-            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-            for (int jj = j; jj < kend && !bad; ++jj, ++dn_m) {
+      // runs of one slot (a gate/up group is one run), each weighted by its
+      // routing weight (1 for gate/up).  One chunk call site for both phases
+      // keeps the unrolled chunk body once in the code (instruction cache).
+      for (int j = i; j < gend && !bad;) {
+        const int r = j - G * Cg, k = down ? r / a.C_dn : G / a.ngj;
+        const int kend = down ? min(gend, G * Cg + (k + 1) * a.C_dn) : gend;
+        if (s_e[k] >= 0) {
+          float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+          for (int jj = j; jj < kend && !bad; ++jj) {
+            const uint8_t* im = img;
+            const float2* X = Xs;
+            int nsb = a.nsb_h, cc = jj - G * Cg, q0 = p0, q1 = p1;
+            if (down) {
               // the chunk's 8 activation sub-blocks, in this warp's image
               // (the first two staged before the loop)
               if (dn_m >= 2) {
@@ -1290,17 +1298,21 @@ __global__ void __launch_bounds__(kPkThreads, 1) pk_layer_kernel(const PkArgs a)
                   break;
                 }
               }
-              uint8_t* mim = mini + (size_t)(dn_m & 1) * pk_mini_bytes();
-              run_chunk(mim, reinterpret_cast<float2*>(mim + pk_img_bytes(1, kMiniNsb)), kMiniNsb, 0, 0, 0, acc);
+              im = mini + (size_t)(dn_m & 1) * pk_mini_bytes();
+              X = reinterpret_cast<const float2*>(im + pk_img_bytes(1, kMiniNsb));
+              nsb = kMiniNsb;
+              cc = q0 = q1 = 0;
+              ++dn_m;
             }
-            const float w = s_w[k];
-#pragma unroll
-            for (int rb = 0; rb < 2; ++rb)
-#pragma unroll
-              for (int q = 0; q < 2; ++q) accg[rb][q] = fmaf(w, acc[rb][q], accg[rb][q]);
+            run_chunk(im, X, nsb, cc, q0, q1, acc);
           }
-          j = kend;
+          const float w = down ? s_w[k] : 1.f;
+#pragma unroll
+          for (int rb = 0; rb < 2; ++rb)
+#pragma unroll
+            for (int q = 0; q < 2; ++q) accg[rb][q] = fmaf(w, acc[rb][q], accg[rb][q]);
         }
+        j = kend;
       }
       // partial sums of the group's 32 rows (rb, row): reduce over the quad
 #pragma unroll
@@ -1517,13 +1529,15 @@ static int launch_pk(PkArgs& a, int grid, size_t smem, cudaStream_t st) {
   cfg.blockDim = dim3(kPkThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = kPkCluster;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, pk_layer_kernel<F>, a);
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   return TSB_OK;
