@@ -298,8 +298,11 @@ def run_decode_mxfp4(dev, K: int, W: int, ws: int, rank: int):
 
 
 # DRAM bytes per launch of pk_layer_kernel<Q4_K> on this workload (ncu
-# dram__bytes_read.sum + dram__bytes_write.sum).
-DECODE_TRAFFIC = None
+# dram__bytes_read.sum + dram__bytes_write.sum, mean of 3 launches on the
+# config-1 layer, captured with -k regex:pk_layer -s 10 -c 3):
+# 62.2 MB read (the packed copy of 4 experts, 1.10x their Q4_K bytes), 0.15 MB
+# written.
+DECODE_TRAFFIC = 62.28e6
 
 PREFILL_T = 4096
 
@@ -543,6 +546,11 @@ def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
             res[f"native_{name}_launch"] = how
             keep.append((fn, nat))  # graphs released before the communicator
         if name == "prefill":
+            nat = NativeEPDecode(part, nccl, T, prefill=True)
+            ms = _ep_time(lambda: nat(x, *router(x)), n, warmup, ws, dev)
+            res["native_prefill_tok_s"] = ws * T / (ms * 1e-3)
+            res["native_prefill_ms"] = ms
+            keep.append(nat)
             ms = _ep_time(lambda: a2a(x), n, warmup, ws, dev)
             res["prefill_a2a_tok_s"] = ws * T / (ms * 1e-3)
             res["prefill_a2a_ms"] = ms

@@ -247,6 +247,18 @@ int tsb_ep_moe_decode(const TsbMoeSpec* local_spec, const TsbExpert* local_exper
                       void* nccl_comm, int32_t rank, int32_t world, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* The same exchange around tsb_moe_prefill (grouped tensor-core GEMMs over
+ * all world*T gathered rows, the multi-GPU form of
+ * ExpertPipeline.execute_layer_experts_batched,
+ * tinyserve/expert_pipeline.py:166-239), for prefill-sized T (the same on
+ * every rank).  Workspace: tsb_ep_prefill_workspace(local_spec, T, world),
+ * 256-byte aligned; tsb_read_device_error(workspace, ...) reads its error
+ * word. */
+size_t tsb_ep_prefill_workspace(const TsbMoeSpec* local_spec, int32_t T, int32_t world);
+int tsb_ep_moe_prefill(const TsbMoeSpec* local_spec, const TsbExpert* local_experts, const void* x, int32_t T,
+                       const int32_t* ids, const float* weights, void* out, void* nccl_comm, int32_t rank,
+                       int32_t world, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

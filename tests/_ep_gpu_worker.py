@@ -97,6 +97,21 @@ def main():
             idn, wn = ids.cpu().numpy(), w.cpu().numpy()
             assert_layer(out[0], _oracle_layer(x[0:1].float().cpu().numpy(), list(idn[0]), list(wn[0]), dense))
         assert nat.device_error() == 0
+    # the grouped-GEMM form (tsb_ep_moe_prefill), a prefill-sized batch
+    T = 300
+    nat = NativeEPDecode(mine_k, comm, T, prefill=True)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(9000 + rank)).to(torch.bfloat16).to(dev)
+    ids, w = Router(router_w, k)(x)
+    out = nat(x, ids, w, out_dtype=torch.float32)
+    ref, _, _ = full.prefill(x, ids=ids, weights=w, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    err = rel_l2(out.cpu().numpy(), ref.cpu().numpy())
+    worst = max(worst, err)
+    assert err <= 1e-4, ("native prefill", rank, err)
+    idn, wn = ids.cpu().numpy(), w.cpu().numpy()
+    for t in (0, T - 1):
+        assert_layer(out[t], _oracle_layer(x[t:t + 1].float().cpu().numpy(), list(idn[t]), list(wn[t]), dense))
+    assert nat.device_error() == 0
     comm.close()
     dist.barrier()
     print(f"EP_OK rank={rank} world={world} worst_rel_l2={worst:.2e}", flush=True)

@@ -91,7 +91,8 @@ struct EpLayout {
   size_t x_all, meta, meta_all, lid, w, part, red, inner, total, inner_bytes;
 };
 
-EpLayout ep_layout(const TsbMoeSpec& sp, int T, int world, bool packed) {
+// inner layer call: 0 tsb_moe_decode, 1 tsb_moe_decode_packed, 2 tsb_moe_prefill
+EpLayout ep_layout(const TsbMoeSpec& sp, int T, int world, int mode) {
   auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
   const size_t R = (size_t)world * T, H = sp.hidden, k = sp.top_k;
   TsbMoeSpec f = sp;
@@ -100,7 +101,9 @@ EpLayout ep_layout(const TsbMoeSpec& sp, int T, int world, bool packed) {
   // the layer's own workspace first, so its device error word sits at the
   // start of the whole (tsb_read_device_error(workspace) reads it)
   L.inner = 0;
-  L.inner_bytes = packed ? tsb_moe_decode_packed_workspace(&f, (int32_t)R) : tsb_moe_decode_workspace(&f, (int32_t)R);
+  L.inner_bytes = mode == 2   ? tsb_moe_prefill_workspace(&f, (int32_t)R)
+                  : mode == 1 ? tsb_moe_decode_packed_workspace(&f, (int32_t)R)
+                              : tsb_moe_decode_workspace(&f, (int32_t)R);
   L.x_all = al(L.inner + L.inner_bytes);
   L.meta = al(L.x_all + R * H * 2);
   L.meta_all = al(L.meta + (size_t)T * 2 * k * 4);
@@ -119,21 +122,28 @@ extern "C" {
 
 size_t tsb_ep_decode_workspace(const TsbMoeSpec* local_spec, int32_t T, int32_t world, int32_t packed) {
   if (!local_spec || T <= 0 || world <= 0) return 0;
-  return tsb::ep_layout(*local_spec, T, world, packed != 0).total;
+  return tsb::ep_layout(*local_spec, T, world, packed != 0 ? 1 : 0).total;
 }
 
-int tsb_ep_moe_decode(const TsbMoeSpec* local_spec, const TsbExpert* local_experts, const void* packed,
-                      const void* x, int32_t T, const int32_t* ids, const float* weights, void* out,
-                      void* nccl_comm, int32_t rank, int32_t world, void* workspace, size_t workspace_bytes,
-                      void* stream) {
-  using namespace tsb;
+size_t tsb_ep_prefill_workspace(const TsbMoeSpec* local_spec, int32_t T, int32_t world) {
+  if (!local_spec || T <= 0 || world <= 0) return 0;
+  return tsb::ep_layout(*local_spec, T, world, 2).total;
+}
+
+}  // extern "C"
+
+namespace tsb {
+namespace {
+int ep_call(int mode, const TsbMoeSpec* local_spec, const TsbExpert* local_experts, const void* packed,
+            const void* x, int32_t T, const int32_t* ids, const float* weights, void* out, void* nccl_comm,
+            int32_t rank, int32_t world, void* workspace, size_t workspace_bytes, void* stream) {
   if (!local_spec || !local_experts || !x || !ids || !weights || !out || !nccl_comm || !workspace)
     return set_error(TSB_ERR_INVALID, "null pointer");
   if (T < 1) return set_error(TSB_ERR_INVALID, "T must be >= 1");
   if (world < 1 || rank < 0 || rank >= world) return set_error(TSB_ERR_INVALID, "rank out of range");
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(TSB_ERR_INVALID, "workspace must be 256-byte aligned");
   const TsbMoeSpec& sp = *local_spec;
-  const EpLayout L = ep_layout(sp, T, world, packed != nullptr);
+  const EpLayout L = ep_layout(sp, T, world, mode);
   if (workspace_bytes < L.total) return set_error(TSB_ERR_WORKSPACE, "workspace too small");
   const Nccl& n = nccl();
   if (!n.ok) return set_error(TSB_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) not found");
@@ -161,10 +171,12 @@ int tsb_ep_moe_decode(const TsbMoeSpec* local_spec, const TsbExpert* local_exper
 
   TsbMoeSpec f = sp;
   f.out_f32 = 1;
-  const int rc = packed ? tsb_moe_decode_packed(&f, packed, local_experts, x_all, R, nullptr, nullptr, lid, w, part,
+  const int rc = mode == 2   ? tsb_moe_prefill(&f, local_experts, x_all, R, nullptr, nullptr, lid, w, part,
                                                 ws + L.inner, L.inner_bytes, stream)
-                        : tsb_moe_decode(&f, local_experts, x_all, R, nullptr, nullptr, lid, w, part, ws + L.inner,
-                                         L.inner_bytes, stream);
+                 : mode == 1 ? tsb_moe_decode_packed(&f, packed, local_experts, x_all, R, nullptr, nullptr, lid, w,
+                                                     part, ws + L.inner, L.inner_bytes, stream)
+                             : tsb_moe_decode(&f, local_experts, x_all, R, nullptr, nullptr, lid, w, part,
+                                              ws + L.inner, L.inner_bytes, stream);
   if (rc) return rc;
   void* dst = sp.out_f32 ? out : red;
   r = n.reduce_scatter(part, dst, (size_t)T * H, kNcclFloat32, kNcclSum, nccl_comm, st);
@@ -176,6 +188,25 @@ int tsb_ep_moe_decode(const TsbMoeSpec* local_spec, const TsbExpert* local_exper
     if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   }
   return TSB_OK;
+}
+}  // namespace
+}  // namespace tsb
+
+extern "C" {
+
+int tsb_ep_moe_decode(const TsbMoeSpec* local_spec, const TsbExpert* local_experts, const void* packed,
+                      const void* x, int32_t T, const int32_t* ids, const float* weights, void* out,
+                      void* nccl_comm, int32_t rank, int32_t world, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  return tsb::ep_call(packed ? 1 : 0, local_spec, local_experts, packed, x, T, ids, weights, out, nccl_comm, rank,
+                      world, workspace, workspace_bytes, stream);
+}
+
+int tsb_ep_moe_prefill(const TsbMoeSpec* local_spec, const TsbExpert* local_experts, const void* x, int32_t T,
+                       const int32_t* ids, const float* weights, void* out, void* nccl_comm, int32_t rank,
+                       int32_t world, void* workspace, size_t workspace_bytes, void* stream) {
+  return tsb::ep_call(2, local_spec, local_experts, nullptr, x, T, ids, weights, out, nccl_comm, rank, world,
+                      workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -217,17 +217,21 @@ class NcclComm:
 
 class NativeEPDecode:
     """The gather scheme of :meth:`ExpertParallelMoE.forward_gather` as one
-    C-ABI call (tsb_ep_moe_decode): all-gather, local experts, reduce-scatter,
-    all on the current stream inside the library.  ``local`` is a
-    :class:`tinyserve_b200.moe.QuantMoE` holding this rank's experts (top_k =
-    the model's); T is fixed per instance (the workspace is sized for it)."""
+    C-ABI call: all-gather, local experts, reduce-scatter, all on the current
+    stream inside the library (tsb_ep_moe_decode; with ``prefill`` the local
+    experts run as grouped tensor-core GEMMs, tsb_ep_moe_prefill).  ``local``
+    is a :class:`tinyserve_b200.moe.QuantMoE` holding this rank's experts
+    (top_k = the model's); T is fixed per instance (the workspace is sized
+    for it)."""
 
-    def __init__(self, local, comm: NcclComm, T: int):
+    def __init__(self, local, comm: NcclComm, T: int, prefill: bool = False):
         import ctypes
         from . import _lib
-        self.local, self.comm, self.T = local, comm, T
+        self.local, self.comm, self.T, self.prefill = local, comm, T, prefill
         self._spec = {False: local.spec, True: local.spec_f32}
-        n = _lib.lib().tsb_ep_decode_workspace(ctypes.byref(local.spec), T, comm.world, int(local.packed))
+        L = _lib.lib()
+        n = (L.tsb_ep_prefill_workspace(ctypes.byref(local.spec), T, comm.world) if prefill else
+             L.tsb_ep_decode_workspace(ctypes.byref(local.spec), T, comm.world, int(local.packed)))
         self.ws = torch.zeros(n, dtype=torch.uint8, device=local.device)
 
     def __call__(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
@@ -240,11 +244,18 @@ class NativeEPDecode:
         weights = weights.to(torch.float32).contiguous()
         out = torch.empty(self.T, self.local.hidden, dtype=out_dtype, device=x.device)
         L = self.local
-        rc = _lib.lib().tsb_ep_moe_decode(
-            ctypes.byref(self._spec[out_dtype == torch.float32]), L._table.data_ptr(),
-            L._packed.data_ptr() if L.packed else None, x.contiguous().data_ptr(), self.T, ids.data_ptr(),
-            weights.data_ptr(), out.data_ptr(), self.comm.comm, self.comm.rank, self.comm.world, self.ws.data_ptr(),
-            self.ws.numel(), torch.cuda.current_stream(x.device).cuda_stream)
+        spec = ctypes.byref(self._spec[out_dtype == torch.float32])
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        if self.prefill:
+            rc = _lib.lib().tsb_ep_moe_prefill(
+                spec, L._table.data_ptr(), x.contiguous().data_ptr(), self.T, ids.data_ptr(), weights.data_ptr(),
+                out.data_ptr(), self.comm.comm, self.comm.rank, self.comm.world, self.ws.data_ptr(), self.ws.numel(),
+                stream)
+        else:
+            rc = _lib.lib().tsb_ep_moe_decode(
+                spec, L._table.data_ptr(), L._packed.data_ptr() if L.packed else None, x.contiguous().data_ptr(),
+                self.T, ids.data_ptr(), weights.data_ptr(), out.data_ptr(), self.comm.comm, self.comm.rank,
+                self.comm.world, self.ws.data_ptr(), self.ws.numel(), stream)
         _lib.check(rc)
         return out
 
