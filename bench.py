@@ -475,10 +475,10 @@ def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
     through both schemes (``forward_gather`` and the all-to-all ``forward``).
     Beside each EP leg: the same collectives alone (``comm_ms``) and the local
     layer alone on the gathered rows (``local_ms``), which name the limiter.
-    The decode legs also run through the C-ABI (``native_*``:
-    tsb_ep_moe_decode on an NCCL communicator, router included) captured in
-    a CUDA graph.  At N = 1 the whole layer runs on one GPU with no exchange
-    (decode legs graph-captured too)."""
+    Every leg also runs through the C-ABI (``native_*``: tsb_ep_moe_decode /
+    tsb_ep_moe_prefill on an NCCL communicator, router included), issued
+    eagerly.  At N = 1 the whole layer runs on one GPU with no exchange (its
+    decode legs captured in a CUDA graph)."""
     import torch
     from tinyserve_b200.formats import TSB_MXFP4
     from tinyserve_b200.moe import QuantMoE, Router
@@ -539,7 +539,7 @@ def run_ep(dev, ws: int, rank: int, steps: int = 5, warmup: int = 3):
         res[f"{name}_local_ms"] = _ep_time(lambda: lf(xg, lid, w), n, warmup, 1, dev)
         if name != "prefill":
             nat = NativeEPDecode(part, nccl, T)
-            fn, how = _ep_graphed(lambda: nat(x, *router(x)), dev)
+            fn, how = (lambda: nat(x, *router(x))), "eager"
             ms = _ep_time(fn, n, warmup, ws, dev)
             res[f"native_{name}_tok_s"] = ws * T / (ms * 1e-3)
             res[f"native_{name}_ms"] = ms
