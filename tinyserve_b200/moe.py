@@ -288,13 +288,21 @@ class DecodeSession:
         with torch.cuda.stream(self.stream):
             layer.decode_(self.din, self.dout, self.ids, self.wts, raw)  # workspace and arguments before capture
         torch.cuda.synchronize(dev)
+        # The layer writes its output straight into the pinned host slot when
+        # that memory is mapped at the same address on the device (unified
+        # addressing): one device->host copy less per token.
+        self._cu = ctypes.CDLL("libcuda.so.1")
+        self.direct_out = all(self._mapped(self.hout[s].data_ptr()) for s in range(slots))
         self.graphs = []
         for s in range(slots):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=self.stream):
                 self.din.copy_(self.hin[s], non_blocking=True)
-                layer.decode_(self.din, self.dout, self.ids, self.wts, raw)
-                self.hout[s].copy_(self.dout, non_blocking=True)
+                if self.direct_out:
+                    layer.decode_(self.din, self.hout[s], self.ids, self.wts, raw)
+                else:
+                    layer.decode_(self.din, self.dout, self.ids, self.wts, raw)
+                    self.hout[s].copy_(self.dout, non_blocking=True)
             self.graphs.append(g)
         self.done = [torch.cuda.Event() for _ in range(slots)]
         for e in self.done:
@@ -306,12 +314,17 @@ class DecodeSession:
         # record / wait) and copies the row with one memmove: a token is
         # host-bound otherwise.  Runtime graph-exec, stream and event handles
         # are the driver's handles.
-        self._cu = ctypes.CDLL("libcuda.so.1")
         self._exec = [ctypes.c_void_p(g.raw_cuda_graph_exec()) for g in self.graphs]
         self._ev = [ctypes.c_void_p(e.cuda_event) for e in self.done]
         self._st = ctypes.c_void_p(raw)
         self._hin = [self.hin[s].data_ptr() for s in range(slots)]
         self._row_bytes = H * 2
+
+    def _mapped(self, host_ptr: int) -> bool:
+        """Pinned host memory the device reaches at the same address."""
+        dptr = ctypes.c_uint64()
+        rc = self._cu.cuMemHostGetDevicePointer_v2(ctypes.byref(dptr), ctypes.c_void_p(host_ptr), 0)
+        return rc == 0 and dptr.value == host_ptr
 
     def _drv(self, rc: int, what: str) -> None:
         if rc:
