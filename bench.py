@@ -273,7 +273,8 @@ def run_ours(args, ws, rank, local):
         "e2e": {"value": ws * E2E / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": 2880 * 2,
                 "d2h_bytes_per_step": 2880 * 2,
                 "how": "tinyserve_b200.moe.DecodeSession.submit per token (public API: host row -> pinned "
-                       "buffer, one CUDA-graph replay of pinned host x -> device, layer, output -> pinned host), "
+                       "buffer, one CUDA-graph replay of pinned host x -> device and the layer, which writes its "
+                       "output into mapped pinned host memory), "
                        "4 layer replicas cycled, CUDA events on the session stream"},
         "gpu_launches": (1 if layers[0].packed else 3) * K,
         "clocks": clocks,
