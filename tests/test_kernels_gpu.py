@@ -87,6 +87,14 @@ def test_matvec_long_rows_chunked(dev, fmt):
 
 
 @pytest.mark.parametrize("fmt", ALL_FMTS, ids=FMT_NAMES.get)
+@pytest.mark.parametrize("N,K", [(4096, 14336), (14336, 4096)])
+def test_matvec_sweep_full_shapes(dev, fmt, N, K):
+    """The two large BASELINE config-2 sweep shapes, whole matrices."""
+    y, ref = _matvec_case(dev, fmt, N, K, 1, seed=N // 7 + K)
+    assert rel_l2(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("fmt", ALL_FMTS, ids=FMT_NAMES.get)
 @pytest.mark.parametrize("M", [2, 5, 8, 11])
 def test_matvec_multi_vector(dev, fmt, M):
     y, ref = _matvec_case(dev, fmt, 200, 2880, M, seed=M)
