@@ -47,6 +47,12 @@ extern "C" {
 #define TSB_FMT_Q5_K 13
 #define TSB_FMT_Q6_K 14
 #define TSB_FMT_MXFP4 39 /* no ggml id in the reference; HF *_blocks / *_scales */
+/* dense experts (GGUF ids of the float types): plain [rows, cols] tensors,
+ * layer entry points only (tsb_moe_decode / tsb_moe_prefill and their
+ * workspace functions); tinyserve/expert_forward.py:109-194 */
+#define TSB_FMT_F32 0
+#define TSB_FMT_F16 1
+#define TSB_FMT_BF16 30
 
 /* element types of activations / outputs */
 #define TSB_DT_F32 0
@@ -57,6 +63,12 @@ extern "C" {
 #define TSB_GU_SEPARATE 0    /* gate [I,H] and up [I,H] (GGUF stores, ggml_forward.py:103-110) */
 #define TSB_GU_INTERLEAVED 1 /* gate_up [2I,H]: row 2j = gate j, 2j+1 = up j (expert_forward.py:239-240) */
 #define TSB_GU_CHUNKED 2     /* gate_up [2I,H]: rows [0,I) gate, [I,2I) up (expert_forward.py:171-172) */
+
+/* TsbMoeSpec.transposed bits (dense formats only): the projection is stored
+ * [in, out] instead of [out, in] and read in place (the reference transposes
+ * such weights before F.linear, tinyserve/expert_forward.py:140-149) */
+#define TSB_T_GATE_UP 1 /* gate_up [H, 2I] (separate: gate and up [H, I]) */
+#define TSB_T_DOWN 2    /* down [I, H] */
 
 /* activation between up and down */
 #define TSB_ACT_SILU 0       /* silu(gate) * up (ggml_forward.py:112) */
@@ -76,6 +88,7 @@ typedef struct {
   int32_t out_f32;     /* 0: layer output `out` is bf16 [T, H]; 1: fp32 [T, H] (the
                           unrounded combine, for callers that keep the residual stream
                           in fp32 and for exact parity checks) */
+  int32_t transposed;  /* TSB_T_* bits; 0 for quantised formats */
 } TsbMoeSpec;
 
 /* One expert's weights (device pointers).  Weights are raw GGUF block streams
@@ -121,6 +134,16 @@ int tsb_quant_matvec(int fmt, const void* w, const void* scales, int64_t N, int6
 
 /* workspace bytes tsb_moe_decode needs for T tokens */
 size_t tsb_moe_decode_workspace(const TsbMoeSpec* spec, int32_t T);
+
+/* Dense experts (fmt_gate_up and fmt_down both TSB_FMT_F32 / F16 / BF16, any
+ * mix of the three; replaces the dense inline forward
+ * tinyserve/expert_forward.py:109-194 and the C++ expert loop
+ * tinyserve/csrc/expert_loop.cpp:41-123): tsb_moe_decode and tsb_moe_prefill
+ * run every (token, slot) pair of a call in one launch per projection with
+ * fp32 accumulation, weights in either orientation (spec->transposed), each
+ * weight pointer 16-byte aligned (an unaligned one is reported through the
+ * device error word, code 3, and skipped).  Workspace from
+ * tsb_moe_decode_workspace for any T. */
 
 /* One MoE layer for T tokens.  T = 1: router + fused gate/up + fused down
  * (three PDL-chained launches).  Several requests decoding together

@@ -23,6 +23,7 @@ TSB_ERR_DEVICE = 5
 DT_F32, DT_BF16, DT_F16 = 0, 1, 2
 GU_SEPARATE, GU_INTERLEAVED, GU_CHUNKED = 0, 1, 2
 ACT_SILU, ACT_SWIGLU_OAI = 0, 1
+T_GATE_UP, T_DOWN = 1, 2  # TsbMoeSpec.transposed bits (dense formats)
 
 # Every symbol include/tsb_moe.h declares.
 EXPORTS = (
@@ -42,7 +43,7 @@ class TsbMoeSpec(ctypes.Structure):
         ("n_experts", ctypes.c_int32), ("top_k", ctypes.c_int32),
         ("gate_up_layout", ctypes.c_int32), ("activation", ctypes.c_int32),
         ("limit", ctypes.c_float), ("alpha", ctypes.c_float),
-        ("out_f32", ctypes.c_int32),
+        ("out_f32", ctypes.c_int32), ("transposed", ctypes.c_int32),
     ]
 
 

@@ -27,6 +27,9 @@ void weight_bytes_of(int fmt, int64_t rows, int64_t cols, int64_t& data, int64_t
     case FMT_Q5_K: data = n / 256 * 176; break;
     case FMT_Q6_K: data = n / 256 * 210; break;
     case FMT_MXFP4: data = n / 2; scales = n / 32; break;
+    case TSB_FMT_F32: data = n * 4; break;
+    case TSB_FMT_F16:
+    case TSB_FMT_BF16: data = n * 2; break;
     default: data = 0;
   }
 }
@@ -70,13 +73,50 @@ static WsLayout ws_layout(const TsbMoeSpec& sp, int T) {
   return L;
 }
 
+// A spec whose experts are dense float tensors (both projections dense).
+static bool dense_spec(const TsbMoeSpec& sp) { return is_dense_fmt(sp.fmt_gate_up) && is_dense_fmt(sp.fmt_down); }
+
+// Validation of a layer spec: quantised (both projections quantised, no
+// transposition) or dense (both dense).
+static int check_layer_spec(const TsbMoeSpec& sp) {
+  if (sp.top_k < 1 || sp.top_k > 8 || sp.top_k > sp.n_experts) return set_error(TSB_ERR_INVALID, "top_k must be in [1, min(8, E)]");
+  if (sp.n_experts < 1 || sp.n_experts > 1024) return set_error(TSB_ERR_INVALID, "n_experts must be in [1, 1024]");
+  if (sp.hidden % 32 || sp.inter % 32 || sp.hidden <= 0 || sp.inter <= 0)
+    return set_error(TSB_ERR_INVALID, "hidden and inter must be positive multiples of 32");
+  if (sp.gate_up_layout < 0 || sp.gate_up_layout > 2) return set_error(TSB_ERR_INVALID, "bad gate_up_layout");
+  if (sp.activation < 0 || sp.activation > 1) return set_error(TSB_ERR_INVALID, "bad activation");
+  if (sp.out_f32 != 0 && sp.out_f32 != 1) return set_error(TSB_ERR_INVALID, "out_f32 must be 0 or 1");
+  const bool dg = is_dense_fmt(sp.fmt_gate_up), dd = is_dense_fmt(sp.fmt_down);
+  if (dg != dd) return set_error(TSB_ERR_UNSUPPORTED, "gate/up and down must both be dense or both be quantised");
+  if (sp.transposed & ~(TSB_T_GATE_UP | TSB_T_DOWN)) return set_error(TSB_ERR_INVALID, "bad transposed bits");
+  if (!dg && sp.transposed) return set_error(TSB_ERR_INVALID, "transposed applies to dense formats only");
+  if (dg && (sp.hidden > 16384 || sp.inter > 16384))
+    return set_error(TSB_ERR_UNSUPPORTED, "dense experts: hidden and inter must be <= 16384");
+  return TSB_OK;
+}
+
+// Dense layers run every token of a call in one launch per projection.
+static int dense_layer(const TsbMoeSpec& sp, const TsbExpert* experts, const void* x, int32_t T, const void* router_w,
+                       const float* router_b, int32_t* ids, float* weights, void* out, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  int rc = check_layer_spec(sp);
+  if (rc) return rc;
+  if (router_w && sp.hidden % 8) return set_error(TSB_ERR_INVALID, "hidden must be a multiple of 8 for the router");
+  if ((int64_t)T * sp.top_k > 65535) return set_error(TSB_ERR_UNSUPPORTED, "dense experts: T * top_k must be <= 65535");
+  const DenseLayout L = dense_layout(sp, T);
+  if (workspace_bytes < L.total) return set_error(TSB_ERR_WORKSPACE, "workspace too small");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(TSB_ERR_INVALID, "workspace must be 256-byte aligned");
+  return launch_dense_layer(sp, experts, x, T, router_w, router_b, ids, weights, out, static_cast<char*>(workspace), L,
+                            static_cast<cudaStream_t>(stream));
+}
+
 }  // namespace tsb
 
 using namespace tsb;
 
 extern "C" {
 
-int tsb_version(void) { return 100; }
+int tsb_version(void) { return 200; }
 
 int tsb_last_error(char* buf, size_t n) {
   const std::string& s = g_last_error;
@@ -96,6 +136,9 @@ int tsb_format_info(int fmt, int32_t* be, int32_t* bb) {
     case FMT_Q5_K: e = 256; b = 176; break;
     case FMT_Q6_K: e = 256; b = 210; break;
     case FMT_MXFP4: e = 32; b = 17; break;
+    case TSB_FMT_F32: e = 1; b = 4; break;
+    case TSB_FMT_F16:
+    case TSB_FMT_BF16: e = 1; b = 2; break;
     default: return check_shape(fmt, 0, 32);
   }
   if (be) *be = e;
@@ -104,7 +147,8 @@ int tsb_format_info(int fmt, int32_t* be, int32_t* bb) {
 }
 
 int tsb_weight_bytes(int fmt, int64_t rows, int64_t cols, int64_t* data_bytes, int64_t* scale_bytes) {
-  int rc = check_shape(fmt, rows, cols);
+  int rc = is_dense_fmt(fmt) ? (rows < 0 || cols <= 0 ? set_error(TSB_ERR_INVALID, "bad shape") : TSB_OK)
+                             : check_shape(fmt, rows, cols);
   if (rc) return rc;
   int64_t d, s;
   weight_bytes_of(fmt, rows, cols, d, s);
@@ -173,6 +217,7 @@ constexpr int kDecodeLoopMax = 16;
 
 size_t tsb_moe_decode_workspace(const TsbMoeSpec* spec, int32_t T) {
   if (!spec || T <= 0) return 0;
+  if (dense_spec(*spec)) return dense_layout(*spec, T).total;
   if (T > kDecodeLoopMax) return prefill_layout(*spec, T).total;  // grouped GEMMs
   return ws_layout(*spec, 1).total;
 }
@@ -183,6 +228,9 @@ int tsb_moe_decode(const TsbMoeSpec* spec, const TsbExpert* experts, const void*
   if (!spec || !experts || !x || !ids || !weights || !out || !workspace) return set_error(TSB_ERR_INVALID, "null pointer");
   const TsbMoeSpec& sp = *spec;
   if (T < 1) return set_error(TSB_ERR_INVALID, "T must be >= 1");
+  if (is_dense_fmt(sp.fmt_gate_up) || is_dense_fmt(sp.fmt_down))
+    return dense_layer(sp, experts, x, T, router_w, router_b, ids, weights, out, workspace, workspace_bytes, stream);
+  if (sp.transposed) return set_error(TSB_ERR_INVALID, "transposed applies to dense formats only");
   // Larger batches (ExpertBatcher) share each expert's weight stream through
   // the grouped path; small ones run token by token (stream-ordered: the next
   // token's first kernel is launched without programmatic overlap).
@@ -304,6 +352,7 @@ int tsb_moe_route(const TsbMoeSpec* spec, const void* x, int32_t T, const void* 
 
 size_t tsb_moe_prefill_workspace(const TsbMoeSpec* spec, int32_t T) {
   if (!spec || T < 0) return 0;
+  if (dense_spec(*spec)) return T ? dense_layout(*spec, T).total : 0;
   return prefill_layout(*spec, T).total;
 }
 
@@ -315,6 +364,9 @@ int tsb_moe_prefill(const TsbMoeSpec* spec, const TsbExpert* experts, const void
   if (T == 0) return TSB_OK;
   if (!experts || !x || !ids || !weights || !out || !workspace) return set_error(TSB_ERR_INVALID, "null pointer");
   const TsbMoeSpec& sp = *spec;
+  if (is_dense_fmt(sp.fmt_gate_up) || is_dense_fmt(sp.fmt_down))
+    return dense_layer(sp, experts, x, T, router_w, router_b, ids, weights, out, workspace, workspace_bytes, stream);
+  if (sp.transposed) return set_error(TSB_ERR_INVALID, "transposed applies to dense formats only");
   if (sp.n_experts < 1 || sp.n_experts > 1024) return set_error(TSB_ERR_INVALID, "n_experts must be in [1, 1024]");
   if (sp.top_k < 1 || sp.top_k > 8 || sp.top_k > sp.n_experts) return set_error(TSB_ERR_INVALID, "top_k must be in [1, min(8, E)]");
   if (sp.hidden % 32 || sp.inter % 32 || sp.hidden <= 0 || sp.inter <= 0)

@@ -18,6 +18,7 @@ enum : int {
   kDevOk = 0,
   kDevWaitTimeout = 1,   // an mbarrier wait exceeded its poll budget
   kDevBadPlan = 2,       // routing plan inconsistent (expert id out of range)
+  kDevMisaligned = 3,    // a dense expert weight pointer is not 16-byte aligned (access skipped)
 };
 
 // Poll budget for mbarrier waits (each poll may suspend up to kSuspendNs).

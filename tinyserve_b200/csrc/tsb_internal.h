@@ -46,6 +46,16 @@ size_t packed_ws_bytes(const TsbMoeSpec& sp);
 int launch_packed_decode(const TsbMoeSpec& sp, const void* packed, const TsbExpert* ex, const void* x, int32_t* ids,
                          float* wts, void* out, int out_f32, int32_t* err, char* pws, cudaStream_t st,
                          const void* router_w, const float* router_b);
+// Dense (fp32 / fp16 / bf16) expert layers (moe_dense.cu).
+bool is_dense_fmt(int fmt);
+struct DenseLayout {
+  size_t err, counter, logits, act, part, total;
+  int s_gu, s_dn;  // K slices of the [in, out] kernels (0 / 1 for [out, in])
+};
+DenseLayout dense_layout(const TsbMoeSpec& sp, int T);
+int launch_dense_layer(const TsbMoeSpec& sp, const TsbExpert* ex, const void* x, int T, const void* router_w,
+                       const float* router_b, int32_t* ids, float* wts, void* out, char* ws, const DenseLayout& L,
+                       cudaStream_t st);
 int launch_dequant(int fmt, const void* w, const void* s, int64_t rows, int64_t cols, void* out, int odt,
                    cudaStream_t st);
 

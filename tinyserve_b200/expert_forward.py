@@ -17,6 +17,11 @@ and its GGUF linear layer (ggml_linear.py:48-117).
   chunked gate|up halves.  Biases in the layout (gate_up_proj_bias,
   down_proj_bias) are applied; the reference's inline MXFP4 forward ignores
   them.
+- ``build_inline_forward(layout, act_fn)``: dense bf16 / fp16 / fp32 experts
+  (tinyserve/expert_forward.py:109-194) through the C-ABI's dense layer, with
+  the reference's transpose rule for weights stored [in, out] (read in
+  place) and its activation rule (``act_fn`` SiLU over chunked halves, None
+  for the interleaved clamp-SwiGLU).
 - ``GGMLLinear``: one GGUF-quantised linear; every batch size is one
   multi-vector matvec call (the reference loops over tokens for batch > 1).
 """
@@ -26,8 +31,11 @@ import torch
 from torch import nn
 
 from . import ops
-from .formats import TSB_MXFP4
+from . import _lib
+from .formats import GGML_BF16, GGML_F16, GGML_F32, TSB_MXFP4
 from .moe import ExpertWeights, QuantMoE
+
+_DENSE_FMT = {torch.float32: GGML_F32, torch.float16: GGML_F16, torch.bfloat16: GGML_BF16}
 
 _DTYPE_SIZE = {}
 
@@ -165,25 +173,102 @@ def build_mxfp4_inline_forward(layout: TensorLayout, act_fn):
 
     def make(packed: torch.Tensor) -> QuantMoE:
         v = lambda n: _aligned(layout.view(packed, n))  # noqa: E731
-        gb = ub = db = None
-        if "gate_up_proj_bias" in specs:
-            b = layout.view(packed, "gate_up_proj_bias").view(specs["gate_up_proj_bias"][1]).float()
-            gb, ub = (b[0::2], b[1::2]) if gu_layout == "interleaved" else (b[:I], b[I:])
-            gb, ub = gb.contiguous(), ub.contiguous()
-        if "down_proj_bias" in specs:
-            db = layout.view(packed, "down_proj_bias").view(specs["down_proj_bias"][1]).float().contiguous()
+        biases = _Biases(layout, gu_layout, I, packed.device)
         ew = ExpertWeights(gate=v("gate_up_proj"), down=v("down_proj"), gate_scales=v("gate_up_proj_scales"),
-                           down_scales=v("down_proj_scales"), gate_bias=gb, up_bias=ub, down_bias=db)
+                           down_scales=v("down_proj_scales"), gate_bias=biases.gate, up_bias=biases.up,
+                           down_bias=biases.down)
         layer = QuantMoE([ew], fmt_gate_up=TSB_MXFP4, fmt_down=TSB_MXFP4, hidden=H, inter=I, top_k=1,
                          gate_up_layout=gu_layout, activation=activation)
-        layer._bias_refs = (gb, ub, db)  # keep the converted biases alive with the table
+        layer._biases = biases  # the table points at these buffers
         return layer
 
     names = ("gate_up_proj", "gate_up_proj_scales", "down_proj", "down_proj_scales")
     cache = _ExpertCache(make, lambda p: _all_aligned(*(layout.view(p, n) for n in names[::2])))
 
     def _forward(packed: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
-        return _run_one_expert(cache.get(packed), h)
+        layer = cache.get(packed)
+        layer._biases.refresh(packed)
+        return _run_one_expert(layer, h)
+
+    return _forward
+
+
+class _Biases:
+    """fp32 copies of an expert's biases for the device table.  The packed
+    bytes behind a cached layer can change while its address stays (a cache
+    slot refilled with another expert), so the copies are refreshed from the
+    packed views on every call (three small device copies)."""
+
+    def __init__(self, layout: TensorLayout, gu_layout: str, inter: int, device):
+        specs = layout.specs
+        self._layout = layout
+        self._gu = "gate_up_proj_bias" in specs
+        self._dn = "down_proj_bias" in specs
+        self._interleaved = gu_layout == "interleaved"
+        self.gate = self.up = self.down = None
+        if self._gu:
+            self.gate = torch.empty(inter, dtype=torch.float32, device=device)
+            self.up = torch.empty(inter, dtype=torch.float32, device=device)
+        if self._dn:
+            self.down = torch.empty(int(specs["down_proj_bias"][0][-1]), dtype=torch.float32, device=device)
+
+    def refresh(self, packed: torch.Tensor) -> None:
+        specs = self._layout.specs
+        if self._gu:
+            b = self._layout.view(packed, "gate_up_proj_bias").view(specs["gate_up_proj_bias"][1])
+            g, u = (b[0::2], b[1::2]) if self._interleaved else b.chunk(2)
+            self.gate.copy_(g)
+            self.up.copy_(u)
+        if self._dn:
+            self.down.copy_(self._layout.view(packed, "down_proj_bias").view(specs["down_proj_bias"][1]))
+
+
+def build_inline_forward(layout: TensorLayout, act_fn):
+    """(packed, h) -> out for dense experts (tinyserve/expert_forward.py:109-194);
+    None when the layout has no dense gate_up_proj / down_proj (MXFP4 layouts
+    go to build_mxfp4_inline_forward).
+
+    Transpose rule of the reference (expert_forward.py:140-149): gate_up is
+    stored [in, out] when its first dimension is the smaller one (hidden);
+    down is stored [in, out] when its first dimension equals max(gate_up
+    shape) // 2 -- for a square down projection (hidden == intermediate) that
+    rule reads the weight transposed, and so does this forward.  Weights are
+    read in place in either orientation.  ``h`` is rounded to bf16 (the
+    layer kernels take bf16 hidden states); the output has ``h``'s dtype."""
+    specs = layout.specs
+    if "gate_up_proj" not in specs or "down_proj" not in specs or "gate_up_proj_scales" in specs:
+        return None
+    gu_shape, gu_dtype = specs["gate_up_proj"]
+    dn_shape, dn_dtype = specs["down_proj"]
+    if gu_dtype not in _DENSE_FMT or dn_dtype not in _DENSE_FMT:
+        return None
+    gu_shape, dn_shape = tuple(int(d) for d in gu_shape), tuple(int(d) for d in dn_shape)
+    H = min(gu_shape)
+    I = max(gu_shape) // 2
+    gu_t = gu_shape[0] == H
+    dn_t = dn_shape[0] == I
+    if sorted(dn_shape) != sorted((H, I)):
+        raise ValueError("down_proj shape does not match gate_up_proj")
+    activation, gu_layout = ("swiglu_oai", "interleaved") if act_fn is None else (_act_kind(act_fn), "chunked")
+    transposed = (_lib.T_GATE_UP if gu_t else 0) | (_lib.T_DOWN if dn_t else 0)
+
+    def make(packed: torch.Tensor) -> QuantMoE:
+        biases = _Biases(layout, gu_layout, I, packed.device)
+        ew = ExpertWeights(gate=_aligned(layout.view(packed, "gate_up_proj")),
+                           down=_aligned(layout.view(packed, "down_proj")),
+                           gate_bias=biases.gate, up_bias=biases.up, down_bias=biases.down)
+        layer = QuantMoE([ew], fmt_gate_up=_DENSE_FMT[gu_dtype], fmt_down=_DENSE_FMT[dn_dtype], hidden=H, inter=I,
+                         top_k=1, gate_up_layout=gu_layout, activation=activation, transposed=transposed)
+        layer._biases = biases
+        return layer
+
+    names = ("gate_up_proj", "down_proj")
+    cache = _ExpertCache(make, lambda p: _all_aligned(*(layout.view(p, n) for n in names)))
+
+    def _forward(packed: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+        layer = cache.get(packed)
+        layer._biases.refresh(packed)
+        return _run_one_expert(layer, h)
 
     return _forward
 

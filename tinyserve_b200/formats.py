@@ -13,6 +13,11 @@ GGML_Q4_K = 12
 GGML_Q5_K = 13
 GGML_Q6_K = 14
 TSB_MXFP4 = 39
+# dense expert formats (GGUF ids of the float types, gguf_reader.py:15-29)
+GGML_F32 = 0
+GGML_F16 = 1
+GGML_BF16 = 30
+DENSE = {GGML_F32: 4, GGML_F16: 2, GGML_BF16: 2}  # id -> bytes per element
 
 # id -> (name, block_bytes, block_elements)
 FORMATS: dict[int, tuple[str, int, int]] = {

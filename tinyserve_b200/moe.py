@@ -42,18 +42,21 @@ class QuantMoE:
     def __init__(self, experts: list[ExpertWeights], *, fmt_gate_up: int, fmt_down: int, hidden: int, inter: int,
                  top_k: int, router_w: torch.Tensor | None = None, router_b: torch.Tensor | None = None,
                  gate_up_layout: str = "separate", activation: str = "swiglu_oai", limit: float = 7.0,
-                 alpha: float = 1.702, pack: bool | None = None):
+                 alpha: float = 1.702, pack: bool | None = None, transposed: int = 0):
         if not experts:
             raise ValueError("no experts")
         self.device = experts[0].gate.device
         if self.device.type != "cuda":
             raise RuntimeError("QuantMoE needs the expert weights on a CUDA device")
         self.experts = experts
+        # Dense experts (fmt GGML_F32 / F16 / BF16): weights are float tensors
+        # [out, in], or [in, out] where `transposed` has _lib.T_GATE_UP /
+        # _lib.T_DOWN set (read in place, tinyserve/expert_forward.py:140-149).
         self.spec = _lib.TsbMoeSpec(fmt_gate_up, fmt_down, hidden, inter, len(experts), top_k,
-                                    LAYOUTS[gate_up_layout], ACTIVATIONS[activation], limit, alpha, 0)
+                                    LAYOUTS[gate_up_layout], ACTIVATIONS[activation], limit, alpha, 0, transposed)
         # the same layer with an fp32 output (the unrounded combine)
         self.spec_f32 = _lib.TsbMoeSpec(fmt_gate_up, fmt_down, hidden, inter, len(experts), top_k,
-                                        LAYOUTS[gate_up_layout], ACTIVATIONS[activation], limit, alpha, 1)
+                                        LAYOUTS[gate_up_layout], ACTIVATIONS[activation], limit, alpha, 1, transposed)
         self.hidden, self.inter, self.top_k = hidden, inter, top_k
         self.router_w = router_w.contiguous() if router_w is not None else None
         self.router_b = router_b.float().contiguous() if router_b is not None else None
