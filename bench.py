@@ -356,18 +356,78 @@ def run_prefill(dev, steps: int = 10, warmup: int = 3):
 SWEEP_SHAPES = [(2880, 2880), (5760, 2880), (4096, 14336), (14336, 4096)]
 
 
+def _reference_kernels():
+    """The reference's own GPU matvec kernels for the same-box A/B, from the
+    unmodified install in baseline/_ref (None for each that is absent):
+    dot_scaled_vecmat (tinyserve/triton_dot_scaled.py:68-122, the MXFP4 decode
+    kernel) and torch.ops.tinyserve_ggml.ggml_mul_mat_vec
+    (tinyserve/csrc/ggml_ops.cu:461-574, built for sm_100a by
+    baseline/build_ggml_ref.py)."""
+    import torch
+    ref = Path(__file__).resolve().parent / "baseline" / "_ref"
+    dot_scaled = ggml = None
+    why = []
+    if (ref / "tinyserve").is_dir():
+        sys.path.insert(0, str(ref))
+        try:
+            from tinyserve.triton_dot_scaled import dot_scaled_vecmat as dot_scaled
+        except Exception as e:  # noqa: BLE001
+            why.append(f"dot_scaled_vecmat: {type(e).__name__}: {e}"[:160])
+    else:
+        why.append("baseline/_ref not installed")
+    so = sorted((ref / "ggml").glob("tinyserve_ggml*.so")) if (ref / "ggml").is_dir() else []
+    if so:
+        try:
+            torch.ops.load_library(str(so[0]))
+            ggml = torch.ops.tinyserve_ggml.ggml_mul_mat_vec
+        except Exception as e:  # noqa: BLE001
+            why.append(f"ggml_mul_mat_vec: {type(e).__name__}: {e}"[:160])
+    else:
+        why.append("ggml_ops extension not built (baseline/build_ggml_ref.py)")
+    return dot_scaled, ggml, "; ".join(why)
+
+
+def _graph_us(fn, calls: int, st) -> float:
+    """Microseconds per call of `calls` calls of fn(i) captured in one CUDA
+    graph (after 3 eager warm-up calls), CUDA events on the replay stream."""
+    import torch
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(st):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=st):
+            for i in range(calls):
+                fn(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        e0.record(st)
+        graph.replay()
+        e1.record(st)
+    torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) * 1e3 / calls
+
+
 def run_matvec_sweep(dev, reps: int = 6, calls: int = 24):
     """tsb_quant_matvec on each format x shape, batch 1,
     weights N(0, 0.02) quantised per format, bf16 N(0, 1) activations.  Each
     timing is a CUDA graph of `calls` matvecs cycling over `reps` distinct
     matrices (at least 26 MB apart in the cycle, so the timed reads come
-    from HBM for the large shapes), CUDA events."""
+    from HBM for the large shapes), CUDA events.  The reference's own GPU
+    kernel for the cell, where it has one, is timed the same way on the same
+    matrices: the Triton dot_scaled_vecmat for MXFP4, ggml_mul_mat_vec for
+    Q8_0 and for K-quants with K % 256 == 0 (it rejects K = 2880,
+    tinyserve/csrc/ggml_ops.cu:476-479)."""
     import torch
     from tinyserve_b200 import ops
     from tinyserve_b200 import quantize as Q
     from tinyserve_b200.formats import GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_Q8_0, TSB_MXFP4
     peak, _ = _peaks()
     names = {GGML_Q8_0: "Q8_0", GGML_Q4_K: "Q4_K", GGML_Q5_K: "Q5_K", GGML_Q6_K: "Q6_K", TSB_MXFP4: "MXFP4"}
+    dot_scaled, ggml, why = _reference_kernels()
     out = []
     st = torch.cuda.Stream(dev)
     for fmt in (GGML_Q8_0, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, TSB_MXFP4):
@@ -384,31 +444,34 @@ def run_matvec_sweep(dev, reps: int = 6, calls: int = 24):
                 del w
             x = torch.randn(1, K, generator=g, device=dev).to(torch.bfloat16)
             nbytes = ws[0][0].numel() + (ws[0][1].numel() if ws[0][1] is not None else 0)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(st):
-                for i in range(3):
-                    ops.quant_matvec(fmt, ws[i % reps][0], ws[i % reps][1], N, K, x)
-                torch.cuda.synchronize()
-                with torch.cuda.graph(graph, stream=st):
-                    for i in range(calls):
-                        ops.quant_matvec(fmt, ws[i % reps][0], ws[i % reps][1], N, K, x)
-            graph.replay()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(st):
-                e0.record(st)
-                graph.replay()
-                e1.record(st)
-            torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / calls
+            us = _graph_us(lambda i: ops.quant_matvec(fmt, ws[i % reps][0], ws[i % reps][1], N, K, x), calls, st)
             alg = nbytes + 2 * K + 2 * N  # weights + bf16 x + bf16 y
             gbs = alg / us / 1e3
-            out.append({"format": names[fmt], "rows": N, "cols": K, "us": us, "GB/s": gbs, "frac": gbs / peak})
-            del ws, graph
+            row = {"format": names[fmt], "rows": N, "cols": K, "us": us, "GB/s": gbs, "frac": gbs / peak}
+            ref_fn, ref_name = None, None
+            if fmt == TSB_MXFP4 and dot_scaled is not None:
+                mats = [(b.view(N, K // 32, 16), sc.view(N, K // 32)) for b, sc in ws]
+                ref_fn, ref_name = (lambda i: dot_scaled(x, *mats[i % reps])), "triton dot_scaled_vecmat"
+            elif fmt != TSB_MXFP4 and ggml is not None and (fmt == GGML_Q8_0 or K % 256 == 0):
+                ref_fn, ref_name = (lambda i: ggml(x, ws[i % reps][0], fmt, N, K)), "ggml_mul_mat_vec"
+            if ref_fn is not None:
+                try:
+                    # same inputs, outputs compared before timing
+                    mine = ops.quant_matvec(fmt, ws[0][0], ws[0][1], N, K, x).float()
+                    theirs = ref_fn(0).float().reshape(mine.shape)
+                    rel = float((mine - theirs).norm() / theirs.norm().clamp_min(1e-30))
+                    rus = _graph_us(ref_fn, calls, st)
+                    row.update({"ref_kernel": ref_name, "ref_us": rus, "ref_GB/s": alg / rus / 1e3,
+                                "speedup_vs_ref": rus / us, "rel_l2_vs_ref": rel})
+                except Exception as e:  # noqa: BLE001
+                    row.update({"ref_kernel": ref_name, "ref_error": f"{type(e).__name__}: {e}"[:200]})
+            out.append(row)
+            del ws
     torch.cuda.empty_cache()
     return {"metric": "quant_matvec_hbm_gbs", "unit": "GB/s", "peak": peak, "peak_source": "measured copy",
             "config": {"workload": "BASELINE config 2: batch-1 quantised matvec sweep (5 formats x 4 shapes)",
-                       "timing": f"CUDA graph of {calls} calls over {reps} distinct matrices, CUDA events"},
+                       "timing": f"CUDA graph of {calls} calls over {reps} distinct matrices, CUDA events",
+                       "reference_kernels": why or "dot_scaled_vecmat and ggml_mul_mat_vec loaded"},
             "results": out}
 
 
@@ -607,6 +670,135 @@ def cpu_decode(host_experts, router, xs, threads: int, warmup: int = 3):
     return xs.shape[0] / dt, len(cpu._cache)
 
 
+def _reference_cpu():
+    """The installed reference's CPU modules (baseline/_ref, unmodified), or
+    None when it is not installed: cpu_expert (CPUExpertForward,
+    tinyserve/cpu_expert.py:180-331), gguf_dequant_torch.dequant_tensor,
+    expert_store.TensorLayout, _model_hooks._extract_routing_fn and
+    ggml_forward.GGMLExpertForward."""
+    ref = Path(__file__).resolve().parent / "baseline" / "_ref"
+    if not (ref / "tinyserve").is_dir():
+        return None
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    import tinyserve._model_hooks as mh
+    import tinyserve.cpu_expert as ce
+    import tinyserve.expert_store as es
+    import tinyserve.ggml_forward as gf
+    import tinyserve.gguf_dequant_torch as gd
+    return {"ce": ce, "gd": gd, "es": es, "mh": mh, "gf": gf}
+
+
+def _ref_route(R, router_bf16, top_k: int):
+    """The reference's top-k-then-softmax routing function over a bf16 Linear."""
+    import torch
+    blk = torch.nn.Module()
+    blk.router = torch.nn.Linear(router_bf16.shape[1], router_bf16.shape[0], bias=False, dtype=torch.bfloat16)
+    with torch.no_grad():
+        blk.router.weight.copy_(router_bf16)
+    return R["mh"]._extract_routing_fn(blk, "router", top_k, "topk_then_softmax")
+
+
+def ref_cpu_decode(R, host_experts, router, xs, threads: int, fmt: int, warmup: int = 3, H: int = 2880,
+                   I: int = 2880):
+    """One MoE layer per token through the reference's own CPU expert path
+    (baseline/_ref): routing by _extract_routing_fn, each routed expert by
+    CPUExpertForward (Q4_K: weights decoded once by dequant_tensor into the
+    fused fp32 layout, gate_up [2I, H] interleaved and down stored [I, H] as
+    the reference's transpose rule reads a square down projection; MXFP4: the
+    MXFP4 layout, converted once to torch INT4 by its CPUINT4Forward), and
+    out += w * y.  Expert conversion happens before timing (the reference
+    caches it).  Returns (tokens/s, experts converted)."""
+    import time
+    import torch
+    from tinyserve_b200.formats import GGML_Q4_K, TSB_MXFP4
+    torch.set_num_threads(threads)
+    route = _ref_route(R, router, 4)
+    es, ce, gd = R["es"], R["ce"], R["gd"]
+    fwds: dict[int, tuple] = {}
+
+    def expert(e: int):
+        if e in fwds:
+            return fwds[e]
+        ex = host_experts[e]
+        if fmt == GGML_Q4_K:
+            wg = gd.dequant_tensor(torch.from_numpy(ex["gate"]), GGML_Q4_K, (I, H))
+            wu = gd.dequant_tensor(torch.from_numpy(ex["up"]), GGML_Q4_K, (I, H))
+            wd = gd.dequant_tensor(torch.from_numpy(ex["down"]), GGML_Q4_K, (H, I))
+            gu = torch.stack([wg, wu], 1).reshape(2 * I, H).float().contiguous()
+            dn = wd.float().t().contiguous()
+            lay = es.TensorLayout({"gate_up_proj": ((2 * I, H), torch.float32), "down_proj": ((I, H), torch.float32)})
+            packed = torch.cat([gu.view(-1).view(torch.uint8), dn.view(-1).view(torch.uint8)])
+        elif fmt == TSB_MXFP4:
+            t = {"gate_up_proj": torch.from_numpy(ex["gate"]).view(2 * I, H // 32, 16),
+                 "gate_up_proj_scales": torch.from_numpy(ex["gate_scales"]).view(2 * I, H // 32),
+                 "down_proj": torch.from_numpy(ex["down"]).view(H, I // 32, 16),
+                 "down_proj_scales": torch.from_numpy(ex["down_scales"]).view(H, I // 32)}
+            lay = es.TensorLayout.from_tensors(t)
+            packed = torch.cat([v.contiguous().view(-1) for v in t.values()])
+        else:
+            raise ValueError(fmt)
+        f = ce.CPUExpertForward(lay, act_fn=None, num_threads=threads)
+        fwds[e] = (f, packed)
+        return fwds[e]
+
+    def layer(h):
+        ids, w = route(h)
+        hf = h.float() if fmt == GGML_Q4_K else h
+        out = torch.zeros(h.shape, dtype=torch.float32)
+        for k in range(ids.shape[1]):
+            f, packed = expert(int(ids[0, k]))
+            out += float(w[0, k]) * f.forward(hf, packed).float()
+        return out
+
+    with torch.no_grad():
+        for i in range(xs.shape[0]):
+            for e in route(xs[i:i + 1])[0][0]:
+                f, packed = expert(int(e))
+                if fmt == TSB_MXFP4:
+                    f.forward(xs[:1], packed)  # the INT4 conversion, cached by the reference
+        for i in range(min(warmup, xs.shape[0])):
+            layer(xs[i:i + 1])
+        t0 = time.perf_counter()
+        for i in range(xs.shape[0]):
+            layer(xs[i:i + 1])
+        dt = time.perf_counter() - t0
+    return xs.shape[0] / dt, len(fwds)
+
+
+def ref_cpu_gguf_fallback(R, host_experts, router, xs, threads: int, H: int = 2880, I: int = 2880):
+    """The reference's as-shipped GGUF CPU path: GGMLExpertForward._fallback_forward
+    (tinyserve/ggml_forward.py:117-151), which decodes the expert's bytes with
+    dequant_tensor on every call and runs F.linear with SiLU; tokens/s of one
+    layer (4 routed experts) over the rows of xs."""
+    import time
+    import torch
+    from tinyserve_b200.formats import GGML_Q4_K
+    torch.set_num_threads(threads)
+    route = _ref_route(R, router, 4)
+    n = host_experts[0]["gate"].size
+    lay = R["es"].TensorLayout({"gate": ((n,), torch.uint8), "up": ((n,), torch.uint8), "down": ((n,), torch.uint8)})
+    fwd = R["gf"].GGMLExpertForward(lay, {"gate": GGML_Q4_K, "up": GGML_Q4_K, "down": GGML_Q4_K}, torch.nn.SiLU(),
+                                    {"gate": (H, I), "up": (H, I), "down": (I, H)})
+    packs = {}
+    with torch.no_grad():
+        fwd._fallback_forward(torch.from_numpy(
+            __import__("numpy").concatenate([host_experts[0][k] for k in ("gate", "up", "down")])), xs[:1].float())
+        t0 = time.perf_counter()
+        for i in range(xs.shape[0]):
+            h = xs[i:i + 1]
+            ids, w = route(h)
+            out = torch.zeros(h.shape, dtype=torch.float32)
+            for k in range(ids.shape[1]):
+                e = int(ids[0, k])
+                if e not in packs:
+                    import numpy as np
+                    packs[e] = torch.from_numpy(np.concatenate([host_experts[e][j] for j in ("gate", "up", "down")]))
+                out += float(w[0, k]) * fwd._fallback_forward(packs[e], h.float())
+        dt = time.perf_counter() - t0
+    return xs.shape[0] / dt
+
+
 def host_layer(seed: int, device):
     """Config-1 expert bytes and router on the host, generated with plain
     torch (the same seeded values as the GPU arm's replica `seed`); no
@@ -618,30 +810,76 @@ def host_layer(seed: int, device):
     return host, router.cpu()
 
 
+def cpu_baselines(host, router_cpu, xs, dev) -> dict:
+    """The reference's CPU expert path timed on this box's host cores (rank 0,
+    N = 1), on bounded samples of the bench's workloads: the headline Q4_K
+    config-1 layer (40 tokens of the GPU arm's stream), GPT-OSS's MXFP4 experts
+    through the reference's INT4 CPU path (4 tokens), and the as-shipped GGUF
+    fallback that decodes every expert on every call (2 tokens).  The
+    installed reference runs when present (kind "reference"), else the oracle
+    port of CPUExpertForward (kind "port", Q4_K only)."""
+    from tinyserve_b200.formats import GGML_Q4_K, TSB_MXFP4
+    from tinyserve_b200.workloads import hidden_states, layer_weights
+    threads = len(os.sched_getaffinity(0))
+    n = 40
+    R = _reference_cpu()
+    xq = xs[:n].cpu()
+    if R is None:
+        tps, nexp = cpu_decode(host, router_cpu, xq, threads)
+        return {"value": tps, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": cpu_model(),
+                "sample": f"{n} tokens of the same stream through replica 0 ({nexp} experts decoded once before "
+                          "timing; oracle port of CPUExpertForward)"}
+    tps, nexp = ref_cpu_decode(R, host, router_cpu, xq, threads, GGML_Q4_K)
+    out = {"value": tps, "unit": UNIT, "cores": threads, "kind": "reference", "cpu_model": cpu_model(),
+           "sample": f"{n} tokens of the same stream through replica 0 ({nexp} experts decoded once by "
+                     "dequant_tensor before timing; the installed reference's CPUExpertForward)"}
+    mx, mrouter, _ = layer_weights(TSB_MXFP4, seed=2000, device=dev)
+    mhost = [{k: v.cpu().numpy() for k, v in e.items()} for e in mx]
+    del mx
+    xm = hidden_states(4, seed=0, device=dev).cpu()
+    mtps, mexp = ref_cpu_decode(R, mhost, mrouter.cpu(), xm, threads, TSB_MXFP4, warmup=1)
+    out["mxfp4_int4_tok_s"] = mtps
+    out["mxfp4_int4_sample"] = (f"4 tokens, MXFP4 config-1 shape ({mexp} experts converted to torch INT4 before "
+                                "timing; the reference's CPUINT4Forward)")
+    out["gguf_fallback_tok_s"] = ref_cpu_gguf_fallback(R, host, router_cpu, xs[:2].cpu(), threads)
+    out["gguf_fallback_sample"] = ("2 tokens through GGMLExpertForward._fallback_forward (dequant_tensor of each "
+                                   "routed expert on every call, SiLU)")
+    return out
+
+
 def run_reference(args, ws, rank, local):
-    """--impl reference: the reference's CPU expert path (oracle port of
-    tinyserve/cpu_expert.py, the only implementation the reference has for
-    this layer on a server) on the host cores, same metric and config: the
-    first K tokens of the GPU arm's token stream through its replica-0 layer.
-    Weights and tokens come from plain torch (CUDA RNG when a GPU is present,
-    so the values match the GPU arm's); nothing of the product runs."""
+    """--impl reference: the reference's CPU expert path on the host cores,
+    same metric and config: the first K tokens of the GPU arm's token stream
+    through its replica-0 layer.  Runs the unmodified reference installed in
+    baseline/_ref (CPUExpertForward, dequant_tensor, its routing function:
+    kind "reference"); without the install, the oracle port of the same code
+    (kind "port").  Weights and tokens come from plain torch (CUDA RNG when a
+    GPU is present, so the values match the GPU arm's); nothing of the
+    product runs."""
     import torch
     if rank != 0:
         return None
     threads = len(os.sched_getaffinity(0))
     dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    from tinyserve_b200.formats import GGML_Q4_K
     from tinyserve_b200.workloads import hidden_states
     host, router = host_layer(0, dev)
     xs = hidden_states(args.steps, seed=0, device=dev).cpu()
-    tps, nexp = cpu_decode(host, router, xs, threads, warmup=args.warmup)
+    R = _reference_cpu()
+    if R is not None:
+        tps, nexp = ref_cpu_decode(R, host, router, xs, threads, GGML_Q4_K, warmup=args.warmup)
+        kind, what = "reference", "the installed reference's CPUExpertForward (baseline/_ref)"
+    else:
+        tps, nexp = cpu_decode(host, router, xs, threads, warmup=args.warmup)
+        kind, what = "port", "oracle port of CPUExpertForward (baseline/_ref not installed)"
     cfg = config1(ws)
     sample = (f"{args.steps} tokens of the GPU arm's stream through its replica-0 layer ({nexp} experts decoded "
-              f"once before timing); {threads} threads on {cpu_model()}")
+              f"once before timing); {what}; {threads} threads on {cpu_model()}")
     return {"impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp32 (weights decoded once by dequant_tensor)",
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) hidden)", "config": cfg,
-            "cpu_baseline": {"value": tps, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+            "cpu_baseline": {"value": tps, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample,
                              "cpu_model": cpu_model()},
             "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -656,6 +894,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the config-4 prefill leg (--steps layers after --warmup) and print its object")
+    ap.add_argument("--sweep-only", action="store_true",
+                    help="run only the config-2 matvec sweep (with the reference-kernel A/B) and print its object")
     ap.add_argument("--ep-only", action="store_true",
                     help="run only the config-5 expert-parallel legs and print their object")
     args = ap.parse_args()
@@ -676,6 +916,12 @@ def main():
             import torch.distributed as dist
             dist.barrier()
             dist.destroy_process_group()
+        return
+    if args.sweep_only:
+        import torch
+        sw = run_matvec_sweep(torch.device("cuda", local))
+        if rank == 0:
+            print(json.dumps(sw), flush=True)
         return
     if args.prefill_only:
         import torch
@@ -707,18 +953,15 @@ def main():
         if rank == 0:
             for r in run_matvec_sweep(dev)["results"]:
                 pf[f"matvec_{r['format']}_{r['rows']}x{r['cols']}_frac"] = round(r["frac"], 4)
+                if "speedup_vs_ref" in r:
+                    pf[f"matvec_{r['format']}_{r['rows']}x{r['cols']}_vs_ref"] = round(r["speedup_vs_ref"], 3)
         torch.cuda.empty_cache()
         ep = run_ep(dev, ws, rank)
         torch.cuda.empty_cache()
         pf.update({f"ep_{k}": (round(v, 4) if isinstance(v, float) else v) for k, v in ep.items()})
         res["prefill"] = pf
     if host is not None:
-        threads = len(os.sched_getaffinity(0))
-        n = 40
-        tps, nexp = cpu_decode(host, router_cpu, xs[:n].cpu(), threads)
-        res["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": cpu_model(),
-                               "sample": f"{n} tokens of the same stream through replica 0 ({nexp} experts decoded "
-                                         "once before timing; oracle port of CPUExpertForward)"}
+        res["cpu_baseline"] = cpu_baselines(host, router_cpu, xs, dev)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if ws > 1:
