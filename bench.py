@@ -308,6 +308,69 @@ DECODE_TRAFFIC = 62.28e6
 PREFILL_T = 4096
 
 
+C3_CTX = 4096  # decode at context 4096
+
+
+def run_config3(dev, steps: int = 64, warmup: int = 8, ctx: int = C3_CTX):
+    """the whole GPT-OSS-20B architecture (24 layers, 32
+    MXFP4 experts, top-4, 64/8 heads of 64, alternating 128-token sliding and
+    full attention, FP8 KV cache, vocabulary 201088), random init, batch-1
+    greedy decode after a `ctx`-token prompt of seeded uniform-random ids.
+    Decode = GptOssDecoder's per-token CUDA-graph replay (dense projections
+    on cuBLAS, the expert layers on the library's decode-packed kernel);
+    tokens are fed back on the device.  CUDA events around `steps` replays
+    after `warmup`."""
+    import torch
+    from tinyserve_b200.gptoss import GptOssDecoder
+    from tinyserve_b200.offload import load_and_offload
+    t0 = time.time()
+    lm = load_and_offload("gpt-oss-20b", device=str(dev), seed=0)
+    build_s = time.time() - t0
+    dec = GptOssDecoder(lm.model, lm.moe_layers, max_seq=ctx + steps + warmup + 8)
+    prompt = torch.randint(0, lm.config.vocab_size, (ctx,), generator=torch.Generator().manual_seed(0)).to(dev)
+    torch.cuda.synchronize(dev)
+    t0 = time.time()
+    logits = dec.prefill(prompt)
+    torch.cuda.synchronize(dev)
+    prefill_s = time.time() - t0
+    tok = logits.argmax().reshape(1)
+    for _ in range(warmup):
+        tok = dec.step(tok)
+    torch.cuda.synchronize(dev)
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        tok = dec.step(tok)
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    # bytes one decode step must read: every layer's 4 routed experts + router,
+    # attention projections, the KV cache up to the context, final norm + LM head
+    cfg = lm.config
+    L, H, D = cfg.num_hidden_layers, cfg.hidden_size, cfg.head_dim
+    q = lm.moe_layers[0]
+    e0b = sum(t.numel() for t in (q.experts[0].gate, q.experts[0].down, q.experts[0].gate_scales,
+                                  q.experts[0].down_scales))
+    moe_b = L * (cfg.num_experts_per_tok * e0b + cfg.num_local_experts * H * 2)
+    attn_b = L * 2 * H * (cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * D + L * 2 * cfg.num_attention_heads * D * H
+    ctx_mean = ctx + warmup + steps / 2
+    kv_b = sum(2 * cfg.num_key_value_heads * D * (min(ctx_mean, cfg.sliding_window) if sl else ctx_mean)
+               for sl in dec.sliding)
+    head_b = cfg.vocab_size * H * 2
+    alg = moe_b + attn_b + kv_b + head_b
+    peak, src = _peaks()
+    achieved = alg / (ms * 1e-3) / 1e9
+    out = {"c3_decode_tok_s": 1e3 / ms, "c3_ms_per_token": ms, "c3_context": ctx, "c3_steps": steps,
+           "c3_alg_bytes_per_token": alg, "c3_achieved_gbs": achieved, "c3_frac": achieved / peak,
+           "c3_moe_bytes": moe_b, "c3_kv": "float8_e4m3fn", "c3_prefill_s": prefill_s, "c3_build_s": build_s,
+           "c3_launch": "one CUDA graph per token",
+           "c3_errors": int(sum(q.device_error() for q in lm.moe_layers))}
+    del dec, lm
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_prefill(dev, steps: int = 10, warmup: int = 3):
     """one GPT-OSS-20B-shaped MXFP4 MoE layer, 4096 tokens,
     top-4 Zipf(1.1) routing over 32 experts; grouped GEMMs on tcgen05 including
@@ -894,6 +957,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill measurement")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the config-4 prefill leg (--steps layers after --warmup) and print its object")
+    ap.add_argument("--config3-only", action="store_true",
+                    help="run only the config-3 whole-model decode (GPT-OSS-20B, context 4096) and print its object")
     ap.add_argument("--sweep-only", action="store_true",
                     help="run only the config-2 matvec sweep (with the reference-kernel A/B) and print its object")
     ap.add_argument("--ep-only", action="store_true",
@@ -916,6 +981,12 @@ def main():
             import torch.distributed as dist
             dist.barrier()
             dist.destroy_process_group()
+        return
+    if args.config3_only:
+        import torch
+        c3 = run_config3(torch.device("cuda", local))
+        if rank == 0:
+            print(json.dumps(c3), flush=True)
         return
     if args.sweep_only:
         import torch

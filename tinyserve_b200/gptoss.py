@@ -1,0 +1,237 @@
+"""Whole-model GPT-OSS decode around the HBM-resident expert layers.
+
+The caller side of the expert path for BASELINE config 3 (GPT-OSS-20B, batch
+1, context 4096, FP8 KV cache): the reference decodes through Hugging Face's
+model with its ``StaticKVCache`` (tinyserve/static_kv_cache.py:28-147, keys
+and values stored as float8 e4m3 and read back as bf16) and its decode loop
+(tinyserve/offload.py:219-287).  Here the same arithmetic runs as one
+CUDA-graph replay per token:
+
+  embedding -> per layer [RMSNorm -> fused q|k|v projection -> RoPE (the
+  model's YaRN tables) -> K/V written to the FP8 cache at the position ->
+  attention with the per-head sink logit over the cached positions (full, or
+  the last ``sliding_window`` for sliding layers) -> o projection ->
+  residual -> RMSNorm -> QuantMoE (one decode-packed launch) -> residual] ->
+  RMSNorm -> LM head -> argmax.
+
+Dense projections are cuBLAS GEMVs on bf16 weights; the expert layers are the
+library's own kernels.  Prompt prefill runs the same layers over chunks of
+tokens (grouped expert GEMMs, causal attention over the cache).
+
+Positions and the token id live in device buffers, so the captured graph is
+replayed unchanged for every step.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (w * xf).to(torch.bfloat16)
+
+
+def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x [..., T, D] with the halves rotated (the GPT-OSS convention); cos/sin [T, D/2]."""
+    a, b = x.chunk(2, dim=-1)
+    return torch.cat((a * cos - b * sin, b * cos + a * sin), dim=-1)
+
+
+class GptOssDecoder:
+    """Batch-1 greedy decoder for a GPT-OSS model whose MoE blocks are
+    QuantMoE layers (``load_and_offload``).
+
+    model      the Hugging Face GptOssForCausalLM (dense weights are read from it
+               once and re-laid out: q|k|v fused per layer)
+    moe_layers one QuantMoE per decoder layer
+    max_seq    KV-cache capacity in tokens
+    kv_dtype   cache storage type: float8_e4m3fn (the reference's default) or bfloat16
+    """
+
+    def __init__(self, model, moe_layers, max_seq: int = 8192, kv_dtype: torch.dtype = torch.float8_e4m3fn,
+                 prefill_chunk: int = 1024):
+        cfg = model.config
+        self.cfg = cfg
+        m = model.model
+        dev = m.embed_tokens.weight.device
+        self.device = dev
+        self.L = cfg.num_hidden_layers
+        self.H = cfg.hidden_size
+        self.nq, self.nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        self.D = getattr(cfg, "head_dim", self.H // self.nq)
+        self.eps = cfg.rms_norm_eps
+        self.window = cfg.sliding_window
+        self.sliding = [t == "sliding_attention" for t in cfg.layer_types[:self.L]]
+        self.scale = self.D ** -0.5
+        self.max_seq = max_seq
+        self.chunk = prefill_chunk
+        bf = torch.bfloat16
+        with torch.no_grad():
+            self.embed = m.embed_tokens.weight.detach().to(bf)
+            self.lm_head = model.lm_head.weight.detach().to(bf)
+            self.norm_w = m.norm.weight.detach().float()
+            self.layers = []
+            for i, blk in enumerate(m.layers):
+                a = blk.self_attn
+                wqkv = torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight]).detach().to(bf).contiguous()
+                bqkv = None
+                if a.q_proj.bias is not None:
+                    bqkv = torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias]).detach().to(bf)
+                self.layers.append(dict(
+                    ln1=blk.input_layernorm.weight.detach().float(), ln2=blk.post_attention_layernorm.weight.detach().float(),
+                    wqkv=wqkv, bqkv=bqkv, wo=a.o_proj.weight.detach().to(bf).contiguous(),
+                    bo=None if a.o_proj.bias is None else a.o_proj.bias.detach().to(bf),
+                    sinks=a.sinks.detach().float(), moe=moe_layers[i]))
+            rot = m.rotary_emb
+            pos = torch.arange(max_seq, device=dev, dtype=torch.float32)
+            freqs = pos[:, None] * rot.inv_freq.float().to(dev)[None, :]
+            self.cos = (freqs.cos() * rot.attention_scaling).to(bf)
+            self.sin = (freqs.sin() * rot.attention_scaling).to(bf)
+        self.kv_dtype = kv_dtype
+        self.k_cache = torch.zeros(self.L, self.nkv, max_seq, self.D, dtype=kv_dtype, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.length = 0
+        self._graph = None
+        self._tok = torch.zeros(1, dtype=torch.long, device=dev)
+        self._pos = torch.zeros(1, dtype=torch.long, device=dev)
+        self._next = torch.zeros(1, dtype=torch.long, device=dev)
+        self._logits = None
+        self._j = torch.arange(max_seq, device=dev)
+
+    @property
+    def kv_bytes(self) -> int:
+        return 2 * self.k_cache.numel() * self.k_cache.element_size()
+
+    # ------------------------------------------------------------------ layers
+    def _attn(self, li: int, q: torch.Tensor, pos0, T: int, ctx: int, dyn_pos: torch.Tensor | None):
+        """q [nq, T, D] (roped) for positions pos0..pos0+T-1 against cached keys
+        [0, ctx); returns [T, nq*D] bf16.  dyn_pos (decode): the position as a
+        device tensor, with ctx = max_seq and masking from it."""
+        lay = self.layers[li]
+        G = self.nq // self.nkv
+        # cached values widened exactly (e4m3 and bf16 are subsets of fp32)
+        K = self.k_cache[li, :, :ctx].float()  # [nkv, ctx, D]
+        V = self.v_cache[li, :, :ctx].float()
+        qg = q.reshape(self.nkv, G * T, self.D)
+        s = torch.matmul(qg.float(), K.transpose(1, 2)).mul_(self.scale)  # [nkv, G*T, ctx]
+        s = s.view(self.nkv, G, T, ctx)
+        j = self._j[:ctx]
+        if dyn_pos is not None:
+            qp = dyn_pos.view(1)
+        else:
+            qp = torch.arange(pos0, pos0 + T, device=q.device)
+        valid = j[None, :] <= qp[:, None]                      # causal
+        if self.sliding[li]:
+            valid = valid & (j[None, :] > qp[:, None] - self.window)
+        s = s.masked_fill(~valid.view(1, 1, T, ctx), float("-inf"))
+        sink = lay["sinks"].view(self.nkv, G, 1, 1).expand(self.nkv, G, T, 1)
+        comb = torch.cat([s, sink], dim=-1)
+        p = torch.softmax(comb - comb.amax(-1, keepdim=True), dim=-1)[..., :ctx]
+        o = torch.matmul(p.reshape(self.nkv, G * T, ctx), V)   # [nkv, G*T, D]
+        o = o.view(self.nkv, G, T, self.D).permute(2, 0, 1, 3).reshape(T, self.nq * self.D)
+        return o.to(torch.bfloat16)
+
+    def _layer(self, li: int, x: torch.Tensor, pos0, dyn_pos=None) -> torch.Tensor:
+        """x bf16 [T, H] at positions pos0.. (an int, or dyn_pos for a decode step)."""
+        lay = self.layers[li]
+        T = x.shape[0]
+        h = _rms(x, lay["ln1"], self.eps)
+        qkv = F.linear(h, lay["wqkv"], lay["bqkv"])
+        nq, nkv, D = self.nq, self.nkv, self.D
+        q = qkv[:, :nq * D].view(T, nq, D).transpose(0, 1)
+        k = qkv[:, nq * D:(nq + nkv) * D].view(T, nkv, D).transpose(0, 1)
+        v = qkv[:, (nq + nkv) * D:].view(T, nkv, D).transpose(0, 1)
+        if dyn_pos is not None:
+            cos, sin = self.cos.index_select(0, dyn_pos), self.sin.index_select(0, dyn_pos)
+        else:
+            cos, sin = self.cos[pos0:pos0 + T], self.sin[pos0:pos0 + T]
+        q, k = _rope(q, cos, sin), _rope(k, cos, sin)
+        if dyn_pos is not None:
+            self.k_cache[li].index_copy_(1, dyn_pos, k.to(self.kv_dtype))
+            self.v_cache[li].index_copy_(1, dyn_pos, v.to(self.kv_dtype))
+            a = self._attn(li, q, None, 1, self.max_seq, dyn_pos)
+        else:
+            self.k_cache[li, :, pos0:pos0 + T] = k.to(self.kv_dtype)
+            self.v_cache[li, :, pos0:pos0 + T] = v.to(self.kv_dtype)
+            a = self._attn(li, q, pos0, T, pos0 + T, None)
+        x = x + F.linear(a, lay["wo"], lay["bo"])
+        h = _rms(x, lay["ln2"], self.eps)
+        y, _, _ = lay["moe"].decode(h.contiguous())
+        return x + y
+
+    def _logits_of(self, x: torch.Tensor) -> torch.Tensor:
+        return F.linear(_rms(x, self.norm_w, self.eps), self.lm_head)
+
+    # ------------------------------------------------------------------ API
+    @torch.no_grad()
+    def prefill(self, ids: torch.Tensor) -> torch.Tensor:
+        """Run prompt ids (1-D) from position 0, filling the cache; returns the
+        logits of the last prompt token (fp32 [V])."""
+        ids = ids.reshape(-1).to(self.device)
+        n = ids.numel()
+        if n > self.max_seq:
+            raise ValueError(f"prompt of {n} tokens exceeds the cache ({self.max_seq})")
+        last = None
+        for p0 in range(0, n, self.chunk):
+            x = self.embed.index_select(0, ids[p0:p0 + self.chunk])
+            for li in range(self.L):
+                x = self._layer(li, x, p0)
+            last = x[-1:]
+        self.length = n
+        return self._logits_of(last)[0].float()
+
+    def _step(self):
+        x = self.embed.index_select(0, self._tok)
+        for li in range(self.L):
+            x = self._layer(li, x, None, self._pos)
+        self._logits = self._logits_of(x)
+        self._next.copy_(self._logits.argmax(-1))
+
+    def _capture(self):
+        st = torch.cuda.Stream(self.device)
+        st.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(st):
+            for _ in range(2):  # warm-up: workspaces, cuBLAS handles, library state
+                self._step()
+        torch.cuda.current_stream(self.device).wait_stream(st)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            self._step()
+        self._graph = g
+
+    @torch.no_grad()
+    def step(self, token: int | torch.Tensor) -> torch.Tensor:
+        """Append one token at the current position; returns the next greedy
+        token as a device tensor (no host synchronisation)."""
+        if self.length >= self.max_seq:
+            raise ValueError("KV cache full")
+        if isinstance(token, torch.Tensor):
+            self._tok.copy_(token.reshape(1))
+        else:
+            self._tok.fill_(int(token))
+        self._pos.fill_(self.length)
+        if self._graph is None:
+            self._capture()
+            self._pos.fill_(self.length)  # the warm-up steps wrote this position; rewrite it in the replay
+        self._graph.replay()
+        self.length += 1
+        return self._next
+
+    @torch.no_grad()
+    def generate(self, prompt: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
+        """Greedy decode: prefill the prompt, then max_new_tokens graph steps."""
+        logits = self.prefill(prompt)
+        tok = logits.argmax().reshape(1)
+        out = [tok.clone()]
+        for _ in range(max_new_tokens - 1):
+            tok = self.step(tok)
+            out.append(tok.clone())
+        return torch.cat(out)
+
+    def reset(self) -> None:
+        self.length = 0
