@@ -102,6 +102,10 @@ class GptOssDecoder:
         self._logits = None
         self._j = torch.arange(max_seq, device=dev)
 
+    @staticmethod
+    def _bytes(t: torch.Tensor) -> torch.Tensor:
+        return t.view(torch.uint8) if t.element_size() == 1 else t
+
     @property
     def kv_bytes(self) -> int:
         return 2 * self.k_cache.numel() * self.k_cache.element_size()
@@ -151,8 +155,9 @@ class GptOssDecoder:
             cos, sin = self.cos[pos0:pos0 + T], self.sin[pos0:pos0 + T]
         q, k = _rope(q, cos, sin), _rope(k, cos, sin)
         if dyn_pos is not None:
-            self.k_cache[li].index_copy_(1, dyn_pos, k.to(self.kv_dtype))
-            self.v_cache[li].index_copy_(1, dyn_pos, v.to(self.kv_dtype))
+            # index_copy_ has no float8 kernel: write the bytes
+            self._bytes(self.k_cache[li]).index_copy_(1, dyn_pos, self._bytes(k.to(self.kv_dtype)))
+            self._bytes(self.v_cache[li]).index_copy_(1, dyn_pos, self._bytes(v.to(self.kv_dtype)))
             a = self._attn(li, q, None, 1, self.max_seq, dyn_pos)
         else:
             self.k_cache[li, :, pos0:pos0 + T] = k.to(self.kv_dtype)
