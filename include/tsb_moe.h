@@ -282,6 +282,33 @@ int tsb_ep_moe_prefill(const TsbMoeSpec* local_spec, const TsbExpert* local_expe
                        const int32_t* ids, const float* weights, void* out, void* nccl_comm, int32_t rank,
                        int32_t world, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- whole-model decode around the expert layers (GPT-OSS) ---------------
+ * The caller side of the MoE layer in a batch-1 decode step, as the reference
+ * runs it through Hugging Face attention with its StaticKVCache
+ * (tinyserve/static_kv_cache.py:28-147: keys/values stored as float8 e4m3 and
+ * read back exactly) inside its decode loop (tinyserve/offload.py:219-287).
+ *
+ * tsb_gqa_decode_attention: one token's grouped-query attention.  qkv is the
+ *   bf16 [n_q + 2 n_kv, head_dim] output of the fused q|k|v projection before
+ *   RoPE; cos / sin bf16 [max_seq, head_dim / 2] tables (halves rotated); pos a
+ *   device int64 holding the token's position (read on the device, so the call
+ *   can sit in a CUDA graph).  The new key (roped) and value are stored in the
+ *   caches [n_kv, max_seq, head_dim] (e4m3 when cache_fp8, else bf16) at pos;
+ *   scores over positions [0, pos] (the last `window` when window > 0) scaled
+ *   by `scale`, softmax with the per-query-head sink logit sinks[n_q] in the
+ *   denominator, out bf16 [n_q, head_dim].  head_dim must be 64, n_q / n_kv <=
+ *   16.  Workspace: tsb_gqa_decode_workspace bytes, 256-byte aligned,
+ *   zero-initialised once; one workspace serves successive calls on a stream.
+ * tsb_add_rmsnorm: x[r] += delta[r] (fp32 residual rows, delta fp32 or bf16 or
+ *   NULL), out[r] = bf16(weight * x[r] / sqrt(mean(x[r]^2) + eps)). */
+size_t tsb_gqa_decode_workspace(int32_t n_q_heads, int32_t n_kv_heads, int32_t max_seq);
+int tsb_gqa_decode_attention(const void* qkv, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
+                             const void* cos, const void* sin, const int64_t* pos, void* k_cache, void* v_cache,
+                             int32_t cache_fp8, int32_t max_seq, int32_t window, const float* sinks, float scale,
+                             void* out, void* workspace, size_t workspace_bytes, void* stream);
+int tsb_add_rmsnorm(float* x, const void* delta, int32_t delta_dtype, const float* weight, float eps, int32_t rows,
+                    int32_t hidden, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,92 @@
+"""The decode-step kernels of the whole-model path through the C-ABI against
+float64 torch math: tsb_gqa_decode_attention (RoPE, cache store, grouped
+sink attention over an e4m3 or bf16 cache, full and sliding windows, the
+semantics of GPT-OSS eager attention with tinyserve's StaticKVCache) and
+tsb_add_rmsnorm."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from tinyserve_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    return torch.device("cuda:0")
+
+
+def _rope(x, c, s):
+    a, b = x.chunk(2, dim=-1)
+    return torch.cat((a * c - b * s, b * c + a * s), dim=-1)
+
+
+@pytest.mark.parametrize("fp8", [True, False])
+@pytest.mark.parametrize("pos,window", [(0, 0), (37, 0), (1000, 0), (1000, 128), (5, 128), (4095, 0)])
+def test_gqa_decode_attention(dev, fp8, pos, window):
+    nq, nkv, D, S = 64, 8, 64, 4096
+    g = torch.Generator(device=dev).manual_seed(pos * 3 + window + fp8)
+    qkv = torch.randn(nq + 2 * nkv, D, generator=g, device=dev).to(torch.bfloat16)
+    ang = torch.arange(S, device=dev, dtype=torch.float32)[:, None] * (10000 ** (-torch.arange(D // 2, device=dev) / (D // 2)))
+    cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    kdt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    kc = (torch.randn(nkv, S, D, generator=g, device=dev) * 2).to(kdt)
+    vc = torch.randn(nkv, S, D, generator=g, device=dev).to(kdt)
+    sinks = torch.randn(nq, generator=g, device=dev)
+    scale = D ** -0.5
+    k_before, v_before = kc.clone(), vc.clone()
+    out = torch.empty(nq, D, dtype=torch.bfloat16, device=dev)
+    ws = torch.zeros(_lib.lib().tsb_gqa_decode_workspace(nq, nkv, S), dtype=torch.uint8, device=dev)
+    p = torch.tensor([pos], dtype=torch.int64, device=dev)
+    for _ in range(2):  # the counters reset themselves between calls
+        kc.copy_(k_before), vc.copy_(v_before)
+        _lib.check(_lib.lib().tsb_gqa_decode_attention(
+            qkv.data_ptr(), nq, nkv, D, cos.data_ptr(), sin.data_ptr(), p.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+            int(fp8), S, window, sinks.data_ptr(), scale, out.data_ptr(), ws.data_ptr(), ws.numel(),
+            torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+    # reference: rope in fp64 from the bf16 tables, the new key rounded to bf16 then to the cache type
+    q = qkv[:nq].double()
+    c, s = cos[pos].double(), sin[pos].double()
+    q = _rope(q, c, s)
+    knew = _rope(qkv[nq:nq + nkv].double(), c, s).to(torch.bfloat16).to(kdt)
+    vnew = qkv[nq + nkv:].to(kdt)
+    assert torch.equal(kc[:, pos].view(torch.uint8 if fp8 else torch.int16),
+                       knew.view(torch.uint8 if fp8 else torch.int16))
+    assert torch.equal(vc[:, pos].float(), vnew.float())
+    others = torch.ones(S, dtype=torch.bool, device=dev)
+    others[pos] = False
+    assert torch.equal(kc[:, others].float(), k_before[:, others].float())
+    K, V = kc.double(), vc.double()
+    lo = max(0, pos - window + 1) if window else 0
+    G = nq // nkv
+    ref = torch.empty(nq, D, dtype=torch.float64, device=dev)
+    for h in range(nq):
+        kv = h // G
+        sc = (K[kv, lo:pos + 1] @ q[h]) * scale
+        m = torch.maximum(sc.max(), sinks[h].double())
+        e = torch.exp(sc - m)
+        ref[h] = (e @ V[kv, lo:pos + 1]) / (e.sum() + torch.exp(sinks[h].double() - m))
+    err = ((out.double() - ref).norm() / ref.norm()).item()
+    assert err < 6e-3, err  # bf16 output rounding (~2e-3) plus fp32 accumulation
+
+
+def test_add_rmsnorm(dev):
+    g = torch.Generator(device=dev).manual_seed(0)
+    T, H = 3, 2880
+    x = torch.randn(T, H, generator=g, device=dev)
+    d = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    w = torch.randn(H, generator=g, device=dev)
+    x0 = x.clone()
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    _lib.check(_lib.lib().tsb_add_rmsnorm(x.data_ptr(), d.data_ptr(), _lib.DT_BF16, w.data_ptr(), 1e-5, T, H,
+                                          out.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    xr = x0.double() + d.double()
+    assert torch.allclose(x.double(), xr, rtol=0, atol=1e-6)
+    ref = w.double() * xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-5)
+    assert ((out.double() - ref).norm() / ref.norm()).item() < 4e-3

@@ -14,8 +14,10 @@ CUDA-graph replay per token:
   residual -> RMSNorm -> QuantMoE (one decode-packed launch) -> residual] ->
   RMSNorm -> LM head -> argmax.
 
-Dense projections are cuBLAS GEMVs on bf16 weights; the expert layers are the
-library's own kernels.  Prompt prefill runs the same layers over chunks of
+Dense projections are cuBLAS GEMVs on bf16 weights; attention (RoPE, cache
+store, sink softmax over the FP8 cache), the residual + RMSNorm steps and the
+expert layers are the library's own kernels; the residual stream is kept in
+fp32.  Prompt prefill runs the same layers over chunks of
 tokens (grouped expert GEMMs, causal attention over the cache).
 
 Positions and the token id live in device buffers, so the captured graph is
@@ -23,16 +25,10 @@ replayed unchanged for every step.
 """
 from __future__ import annotations
 
-import math
-
 import torch
 import torch.nn.functional as F
 
-
-def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
-    return (w * xf).to(torch.bfloat16)
+from . import _lib
 
 
 def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
@@ -101,6 +97,15 @@ class GptOssDecoder:
         self._next = torch.zeros(1, dtype=torch.long, device=dev)
         self._logits = None
         self._j = torch.arange(max_seq, device=dev)
+        # decode-step buffers (fixed addresses for the captured graph)
+        self._x = torch.zeros(1, self.H, dtype=torch.float32, device=dev)      # residual stream
+        self._h = torch.zeros(1, self.H, dtype=torch.bfloat16, device=dev)     # normed sublayer input
+        self._y = torch.zeros(1, self.H, dtype=torch.float32, device=dev)      # expert layer output
+        self._a = torch.zeros(1, self.nq * self.D, dtype=torch.bfloat16, device=dev)
+        nws = _lib.lib().tsb_gqa_decode_workspace(self.nq, self.nkv, max_seq)
+        if nws == 0:
+            raise ValueError("unsupported attention shape")
+        self._aws = torch.zeros(nws, dtype=torch.uint8, device=dev)
 
     @staticmethod
     def _bytes(t: torch.Tensor) -> torch.Tensor:
@@ -111,10 +116,9 @@ class GptOssDecoder:
         return 2 * self.k_cache.numel() * self.k_cache.element_size()
 
     # ------------------------------------------------------------------ layers
-    def _attn(self, li: int, q: torch.Tensor, pos0, T: int, ctx: int, dyn_pos: torch.Tensor | None):
-        """q [nq, T, D] (roped) for positions pos0..pos0+T-1 against cached keys
-        [0, ctx); returns [T, nq*D] bf16.  dyn_pos (decode): the position as a
-        device tensor, with ctx = max_seq and masking from it."""
+    def _attn(self, li: int, q: torch.Tensor, pos0: int, T: int, ctx: int):
+        """Prompt attention: q [nq, T, D] (roped) for positions pos0..pos0+T-1
+        against cached keys [0, ctx); returns [T, nq*D] bf16."""
         lay = self.layers[li]
         G = self.nq // self.nkv
         # cached values widened exactly (e4m3 and bf16 are subsets of fp32)
@@ -124,10 +128,7 @@ class GptOssDecoder:
         s = torch.matmul(qg.float(), K.transpose(1, 2)).mul_(self.scale)  # [nkv, G*T, ctx]
         s = s.view(self.nkv, G, T, ctx)
         j = self._j[:ctx]
-        if dyn_pos is not None:
-            qp = dyn_pos.view(1)
-        else:
-            qp = torch.arange(pos0, pos0 + T, device=q.device)
+        qp = torch.arange(pos0, pos0 + T, device=q.device)
         valid = j[None, :] <= qp[:, None]                      # causal
         if self.sliding[li]:
             valid = valid & (j[None, :] > qp[:, None] - self.window)
@@ -139,37 +140,34 @@ class GptOssDecoder:
         o = o.view(self.nkv, G, T, self.D).permute(2, 0, 1, 3).reshape(T, self.nq * self.D)
         return o.to(torch.bfloat16)
 
-    def _layer(self, li: int, x: torch.Tensor, pos0, dyn_pos=None) -> torch.Tensor:
-        """x bf16 [T, H] at positions pos0.. (an int, or dyn_pos for a decode step)."""
+    def _norm(self, x: torch.Tensor, delta, w: torch.Tensor, out: torch.Tensor) -> None:
+        """x (fp32 residual [T, H]) += delta (bf16 / fp32 / None); out = bf16 RMSNorm(x) * w."""
+        dt = 0 if delta is None or delta.dtype == torch.float32 else 1
+        _lib.check(_lib.lib().tsb_add_rmsnorm(
+            x.data_ptr(), None if delta is None else delta.data_ptr(), dt, w.data_ptr(), self.eps, x.shape[0],
+            self.H, out.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
+
+    def _prefill_layer(self, li: int, x: torch.Tensor, h: torch.Tensor, pos0: int, nxt_w: torch.Tensor) -> None:
+        """Prompt rows at positions pos0..: x fp32 residual [T, H] (in/out), h the
+        bf16 RMSNorm of x on entry, replaced by the next sublayer's norm input."""
         lay = self.layers[li]
         T = x.shape[0]
-        h = _rms(x, lay["ln1"], self.eps)
         qkv = F.linear(h, lay["wqkv"], lay["bqkv"])
         nq, nkv, D = self.nq, self.nkv, self.D
         q = qkv[:, :nq * D].view(T, nq, D).transpose(0, 1)
         k = qkv[:, nq * D:(nq + nkv) * D].view(T, nkv, D).transpose(0, 1)
         v = qkv[:, (nq + nkv) * D:].view(T, nkv, D).transpose(0, 1)
-        if dyn_pos is not None:
-            cos, sin = self.cos.index_select(0, dyn_pos), self.sin.index_select(0, dyn_pos)
-        else:
-            cos, sin = self.cos[pos0:pos0 + T], self.sin[pos0:pos0 + T]
+        cos, sin = self.cos[pos0:pos0 + T], self.sin[pos0:pos0 + T]
         q, k = _rope(q, cos, sin), _rope(k, cos, sin)
-        if dyn_pos is not None:
-            # index_copy_ has no float8 kernel: write the bytes
-            self._bytes(self.k_cache[li]).index_copy_(1, dyn_pos, self._bytes(k.to(self.kv_dtype)))
-            self._bytes(self.v_cache[li]).index_copy_(1, dyn_pos, self._bytes(v.to(self.kv_dtype)))
-            a = self._attn(li, q, None, 1, self.max_seq, dyn_pos)
-        else:
-            self.k_cache[li, :, pos0:pos0 + T] = k.to(self.kv_dtype)
-            self.v_cache[li, :, pos0:pos0 + T] = v.to(self.kv_dtype)
-            a = self._attn(li, q, pos0, T, pos0 + T, None)
-        x = x + F.linear(a, lay["wo"], lay["bo"])
-        h = _rms(x, lay["ln2"], self.eps)
-        y, _, _ = lay["moe"].decode(h.contiguous())
-        return x + y
+        self.k_cache[li, :, pos0:pos0 + T] = k.to(self.kv_dtype)
+        self.v_cache[li, :, pos0:pos0 + T] = v.to(self.kv_dtype)
+        a = self._attn(li, q, pos0, T, pos0 + T)
+        self._norm(x, F.linear(a, lay["wo"], lay["bo"]), lay["ln2"], h)
+        y, _, _ = lay["moe"].decode(h, out_dtype=torch.float32)
+        self._norm(x, y, nxt_w, h)
 
-    def _logits_of(self, x: torch.Tensor) -> torch.Tensor:
-        return F.linear(_rms(x, self.norm_w, self.eps), self.lm_head)
+    def _next_norm(self, li: int) -> torch.Tensor:
+        return self.layers[li + 1]["ln1"] if li + 1 < self.L else self.norm_w
 
     # ------------------------------------------------------------------ API
     @torch.no_grad()
@@ -182,18 +180,37 @@ class GptOssDecoder:
             raise ValueError(f"prompt of {n} tokens exceeds the cache ({self.max_seq})")
         last = None
         for p0 in range(0, n, self.chunk):
-            x = self.embed.index_select(0, ids[p0:p0 + self.chunk])
+            x = self.embed.index_select(0, ids[p0:p0 + self.chunk]).float()
+            h = torch.empty(x.shape, dtype=torch.bfloat16, device=self.device)
+            self._norm(x, None, self.layers[0]["ln1"], h)
             for li in range(self.L):
-                x = self._layer(li, x, p0)
-            last = x[-1:]
+                self._prefill_layer(li, x, h, p0, self._next_norm(li))
+            last = h[-1:]
         self.length = n
-        return self._logits_of(last)[0].float()
+        return F.linear(last, self.lm_head)[0].float()
 
     def _step(self):
-        x = self.embed.index_select(0, self._tok)
-        for li in range(self.L):
-            x = self._layer(li, x, None, self._pos)
-        self._logits = self._logits_of(x)
+        """One decode token through every layer (the captured graph's body):
+        fused q|k|v GEMV, the decode-attention kernel (RoPE, cache store,
+        sink attention), o GEMV, residual + RMSNorm kernel, the expert layer
+        (fp32 output) and the next residual + RMSNorm."""
+        L = _lib.lib()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        x, h = self._x, self._h
+        x.copy_(self.embed.index_select(0, self._tok))
+        self._norm(x, None, self.layers[0]["ln1"], h)
+        for li, lay in enumerate(self.layers):
+            qkv = F.linear(h, lay["wqkv"], lay["bqkv"])
+            _lib.check(L.tsb_gqa_decode_attention(
+                qkv.data_ptr(), self.nq, self.nkv, self.D, self.cos.data_ptr(), self.sin.data_ptr(),
+                self._pos.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
+                1 if self.kv_dtype == torch.float8_e4m3fn else 0, self.max_seq,
+                self.window if self.sliding[li] else 0, lay["sinks"].data_ptr(), self.scale, self._a.data_ptr(),
+                self._aws.data_ptr(), self._aws.numel(), stream))
+            self._norm(x, F.linear(self._a, lay["wo"], lay["bo"]), lay["ln2"], h)
+            lay["moe"].decode(h, out=self._y)
+            self._norm(x, self._y, self._next_norm(li), h)
+        self._logits = F.linear(h, self.lm_head)
         self._next.copy_(self._logits.argmax(-1))
 
     def _capture(self):
@@ -221,8 +238,7 @@ class GptOssDecoder:
             self._tok.fill_(int(token))
         self._pos.fill_(self.length)
         if self._graph is None:
-            self._capture()
-            self._pos.fill_(self.length)  # the warm-up steps wrote this position; rewrite it in the replay
+            self._capture()  # the warm-up steps write this position's K/V; the replay rewrites the same values
         self._graph.replay()
         self.length += 1
         return self._next
