@@ -308,6 +308,11 @@ int tsb_gqa_decode_attention(const void* qkv, int32_t n_q_heads, int32_t n_kv_he
                              void* out, void* workspace, size_t workspace_bytes, void* stream);
 int tsb_add_rmsnorm(float* x, const void* delta, int32_t delta_dtype, const float* weight, float eps, int32_t rows,
                     int32_t hidden, void* out, void* stream);
+/* y = bf16(W x + bias): one bf16 [N, K] weight (16-byte aligned, K % 8 == 0,
+ * K <= 16384), bf16 x [K], optional bf16 bias [N], bf16 y [N]; the batch-1
+ * attention projections of the decode step (nn.Linear in the reference's
+ * model). */
+int tsb_gemv_bf16(const void* weight, const void* bias, int32_t N, int32_t K, const void* x, void* y, void* stream);
 
 #ifdef __cplusplus
 }

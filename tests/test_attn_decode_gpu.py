@@ -90,3 +90,18 @@ def test_add_rmsnorm(dev):
     assert torch.allclose(x.double(), xr, rtol=0, atol=1e-6)
     ref = w.double() * xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-5)
     assert ((out.double() - ref).norm() / ref.norm()).item() < 4e-3
+
+
+@pytest.mark.parametrize("N,K", [(5120, 2880), (2880, 4096), (77, 64), (3, 16384)])
+def test_gemv_bf16(dev, N, K):
+    g = torch.Generator(device=dev).manual_seed(N + K)
+    W = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    b = torch.randn(N, generator=g, device=dev).to(torch.bfloat16)
+    x = torch.randn(K, generator=g, device=dev).to(torch.bfloat16)
+    y = torch.empty(N, dtype=torch.bfloat16, device=dev)
+    for bias in (b, None):
+        _lib.check(_lib.lib().tsb_gemv_bf16(W.data_ptr(), None if bias is None else bias.data_ptr(), N, K,
+                                            x.data_ptr(), y.data_ptr(), torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        ref = W.double() @ x.double() + (0 if bias is None else bias.double())
+        assert ((y.double() - ref).norm() / ref.norm()).item() < 4e-3

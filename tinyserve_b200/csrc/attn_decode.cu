@@ -150,22 +150,63 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(AttnArgs a) {
       }
     }
   }
-  __syncthreads();
   const int n = max(0, c1 - c0);
   const int64_t hb = (int64_t)h * a.max_seq * kD;
-  // scores: warp per position
-  for (int j = warp; j < n; j += kThreads / 32) {
-    const int p = c0 + j;
-    float2 k2;
-    if (p == pos)
-      k2 = make_float2(knew[2 * lane], knew[2 * lane + 1]);
-    else
-      k2 = load2<FP8>(a.kc, hb + (int64_t)p * kD + 2 * lane);
-    for (int g = 0; g < G; ++g) {
-      float v = qs[g * kD + 2 * lane] * k2.x + qs[g * kD + 2 * lane + 1] * k2.y;
+  // stage the slice's keys and values in shared memory with every thread's
+  // 16-byte loads in flight at once; rows padded by 16 B so the per-position
+  // row reads of the score pass are bank-conflict free
+  constexpr int EB = FP8 ? 1 : 2;         // bytes per cached element
+  constexpr int RB = kD * EB + 16;        // padded row bytes
+  constexpr int C16 = kD * EB / 16;       // 16-byte chunks per row
+  uint8_t* ks = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sc + G * a.cs_max) + 15) & ~uintptr_t(15));
+  uint8_t* vs = ks + (size_t)a.cs_max * RB;
+  {
+    const uint8_t* kg = static_cast<const uint8_t*>(a.kc) + (hb + (int64_t)c0 * kD) * EB;
+    const uint8_t* vg = static_cast<const uint8_t*>(a.vc) + (hb + (int64_t)c0 * kD) * EB;
+    for (int i = tid; i < n * C16; i += kThreads) {
+      const int j = i / C16, c = i % C16;
+      const uint4 kv = *reinterpret_cast<const uint4*>(kg + (size_t)j * kD * EB + c * 16);
+      const uint4 vv = *reinterpret_cast<const uint4*>(vg + (size_t)j * kD * EB + c * 16);
+      *reinterpret_cast<uint4*>(ks + (size_t)j * RB + c * 16) = kv;
+      *reinterpret_cast<uint4*>(vs + (size_t)j * RB + c * 16) = vv;
+    }
+  }
+  __syncthreads();
+  // the current position's key/value come from the prologue, not the cache
+  if (pos >= c0 && pos < c1) {
+    const int j = (int)pos - c0;
+    for (int d = tid; d < kD; d += kThreads) {
+      if constexpr (FP8) {
+        ks[(size_t)j * RB + d] = __nv_cvt_float_to_fp8(knew[d], __NV_NOSAT, __NV_E4M3);
+        vs[(size_t)j * RB + d] = __nv_cvt_float_to_fp8(vnew[d], __NV_NOSAT, __NV_E4M3);
+      } else {
+        reinterpret_cast<uint16_t*>(ks + (size_t)j * RB)[d] = f32_to_bf16_bits(knew[d]);
+        reinterpret_cast<uint16_t*>(vs + (size_t)j * RB)[d] = f32_to_bf16_bits(vnew[d]);
+      }
+    }
+  }
+  __syncthreads();
+  // scores: one position per thread, all G heads (q broadcast from shared memory)
+  for (int j = tid; j < n; j += kThreads) {
+    float kr[kD];
 #pragma unroll
-      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) sc[g * a.cs_max + j] = v * a.scale;
+    for (int d = 0; d < kD; d += 2) {
+      const float2 k2 = load2<FP8>(ks + (size_t)j * RB, d);
+      kr[d] = k2.x;
+      kr[d + 1] = k2.y;
+    }
+    for (int g = 0; g < G; ++g) {
+      const float4* q4 = reinterpret_cast<const float4*>(qs + g * kD);
+      float acc = 0.f;
+#pragma unroll
+      for (int d4 = 0; d4 < kD / 4; ++d4) {
+        const float4 q = q4[d4];
+        acc = fmaf(q.x, kr[4 * d4], acc);
+        acc = fmaf(q.y, kr[4 * d4 + 1], acc);
+        acc = fmaf(q.z, kr[4 * d4 + 2], acc);
+        acc = fmaf(q.w, kr[4 * d4 + 3], acc);
+      }
+      sc[g * a.cs_max + j] = acc * a.scale;
     }
   }
   __syncthreads();
@@ -191,18 +232,24 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(AttnArgs a) {
   __syncthreads();
   // P.V: thread (g, lane) -> dims 2 lane, 2 lane + 1 of head g
   for (int g = warp; g < G; g += kThreads / 32) {
-    float o0 = 0.f, o1 = 0.f;
+    float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
     const float* pg = sc + g * a.cs_max;
-    for (int j = 0; j < n; ++j) {
-      const int p = c0 + j;
-      float2 v2;
-      if (p == pos)
-        v2 = make_float2(vnew[2 * lane], vnew[2 * lane + 1]);
-      else
-        v2 = load2<FP8>(a.vc, hb + (int64_t)p * kD + 2 * lane);
-      o0 = fmaf(pg[j], v2.x, o0);
-      o1 = fmaf(pg[j], v2.y, o1);
+    int j = 0;
+    for (; j + 1 < n; j += 2) {
+      const float2 va = load2<FP8>(vs + (size_t)j * RB, 2 * lane);
+      const float2 vb = load2<FP8>(vs + (size_t)(j + 1) * RB, 2 * lane);
+      o0 = fmaf(pg[j], va.x, o0);
+      o1 = fmaf(pg[j], va.y, o1);
+      o2 = fmaf(pg[j + 1], vb.x, o2);
+      o3 = fmaf(pg[j + 1], vb.y, o3);
     }
+    if (j < n) {
+      const float2 va = load2<FP8>(vs + (size_t)j * RB, 2 * lane);
+      o0 = fmaf(pg[j], va.x, o0);
+      o1 = fmaf(pg[j], va.y, o1);
+    }
+    o0 += o2;
+    o1 += o3;
     float* dst = a.part + (((int64_t)h * a.S + s) * G + g) * (kD + 2);
     dst[2 * lane] = o0;
     dst[2 * lane + 1] = o1;
@@ -244,35 +291,102 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(AttnArgs a) {
 }
 
 // x[r] += delta[r] (fp32 residual, delta bf16 or fp32, optional);
-// out[r] = bf16(w * x[r] * rsqrt(mean(x[r]^2) + eps)).  One CTA per row.
-__global__ void __launch_bounds__(256) add_rmsnorm_kernel(float* x, const void* delta, int delta_f32, const float* w,
-                                                          float eps, int H, uint16_t* out) {
+// out[r] = bf16(w * x[r] * rsqrt(mean(x[r]^2) + eps)).  One CTA per row; each
+// thread keeps its (at most kPer) elements in registers so all loads of the
+// row are in flight together.
+constexpr int kNormThreads = 256, kPer = 16;
+
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __restrict__ x, const void* __restrict__ delta,
+                                                                   int delta_f32, const float* __restrict__ w, float eps,
+                                                                   int H, uint16_t* __restrict__ out) {
   const int r = blockIdx.x;
   float* xr = x + (int64_t)r * H;
+  float v[kPer];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float v = xr[i];
-    if (delta)
-      v += delta_f32 ? static_cast<const float*>(delta)[(int64_t)r * H + i]
-                     : bf(static_cast<const uint16_t*>(delta)[(int64_t)r * H + i]);
-    xr[i] = v;
-    ss = fmaf(v, v, ss);
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = threadIdx.x + k * kNormThreads;
+    v[k] = 0.f;
+    if (i < H) {
+      float d = 0.f;
+      if (delta)
+        d = delta_f32 ? static_cast<const float*>(delta)[(int64_t)r * H + i]
+                      : bf(static_cast<const uint16_t*>(delta)[(int64_t)r * H + i]);
+      v[k] = xr[i] + d;
+    }
   }
-  __shared__ float red[8];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int i = threadIdx.x + k * kNormThreads;
+    if (i < H) {
+      xr[i] = v[k];
+      ss = fmaf(v[k], v[k], ss);
+    }
+  }
+  __shared__ float red[kNormThreads / 32];
 #pragma unroll
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+  float t = 0.f;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (threadIdx.x == 0) red[0] = t;
+  for (int k = 0; k < kNormThreads / 32; ++k) t += red[k];
+  const float inv = rsqrtf(t / H + eps);
+  if (out) {
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = threadIdx.x + k * kNormThreads;
+      if (i < H) out[(int64_t)r * H + i] = f32_to_bf16_bits(w[i] * (v[k] * inv));
+    }
   }
+}
+
+// y[n] = bf16(W[n, :] . x + bias[n]) for bf16 W [N, K] (row-major), x [K]:
+// one warp per row, the row's 16-byte chunks loaded in batches of 8 per lane
+// before any arithmetic (the loads of a batch are in flight together), x
+// staged once per CTA as fp32 in shared memory.
+constexpr int kGemvWarps = 8;
+
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(const uint16_t* __restrict__ W,
+                                                                     const uint16_t* __restrict__ bias, int N, int K,
+                                                                     const uint16_t* __restrict__ x,
+                                                                     uint16_t* __restrict__ y) {
+  extern __shared__ float xs[];
+  for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = bf(x[i]);
   __syncthreads();
-  const float inv = rsqrtf(red[0] / H + eps);
-  if (out)
-    for (int i = threadIdx.x; i < H; i += blockDim.x) out[(int64_t)r * H + i] = f32_to_bf16_bits(w[i] * (xr[i] * inv));
+  const int lane = threadIdx.x & 31;
+  const int n = blockIdx.x * kGemvWarps + (threadIdx.x >> 5);
+  if (n >= N) return;
+  const uint4* row = reinterpret_cast<const uint4*>(W + (int64_t)n * K);
+  const int nc = K / 8;
+  float acc = 0.f;
+  for (int c0 = 0; c0 < nc; c0 += 8 * 32) {
+    uint4 w[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = c0 + u * 32 + lane;
+      w[u] = c < nc ? __ldcs(row + c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < nc) {
+        const float4* xv = reinterpret_cast<const float4*>(xs + 8 * c);
+        const float4 xa = xv[0], xb = xv[1];
+        acc = fmaf(__uint_as_float(w[u].x << 16), xa.x, acc);
+        acc = fmaf(__uint_as_float(w[u].x & 0xFFFF0000u), xa.y, acc);
+        acc = fmaf(__uint_as_float(w[u].y << 16), xa.z, acc);
+        acc = fmaf(__uint_as_float(w[u].y & 0xFFFF0000u), xa.w, acc);
+        acc = fmaf(__uint_as_float(w[u].z << 16), xb.x, acc);
+        acc = fmaf(__uint_as_float(w[u].z & 0xFFFF0000u), xb.y, acc);
+        acc = fmaf(__uint_as_float(w[u].w << 16), xb.z, acc);
+        acc = fmaf(__uint_as_float(w[u].w & 0xFFFF0000u), xb.w, acc);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) y[n] = f32_to_bf16_bits(acc + (bias ? bf(bias[n]) : 0.f));
 }
 
 }  // namespace
@@ -329,7 +443,9 @@ extern "C" int tsb_gqa_decode_attention(const void* qkv, int32_t n_q_heads, int3
   a.cs_max = (max_seq + a.S - 1) / a.S;
   a.scale = scale;
   if (n_kv_heads > 60) return set_error(TSB_ERR_UNSUPPORTED, "at most 60 KV heads (counter space)");
-  const size_t smem = sizeof(float) * ((size_t)a.G * kD + 2 * kD + (size_t)a.G * a.cs_max);
+  const size_t rowb = (cache_fp8 ? kD : 2 * kD) + 16;
+  const size_t smem = sizeof(float) * ((size_t)a.G * kD + 2 * kD + (size_t)a.G * a.cs_max) + 16 + 2 * rowb * a.cs_max;
+  if (smem > 200 * 1024) return set_error(TSB_ERR_UNSUPPORTED, "max_seq too large for the decode-attention slices");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (cache_fp8) {
@@ -348,11 +464,28 @@ extern "C" int tsb_add_rmsnorm(float* x, const void* delta, int32_t delta_dtype,
                                int32_t rows, int32_t hidden, void* out, void* stream) {
   if (!x || !weight) return set_error(TSB_ERR_INVALID, "null pointer");
   if (rows < 0 || hidden <= 0) return set_error(TSB_ERR_INVALID, "bad shape");
+  if (hidden > kNormThreads * kPer) return set_error(TSB_ERR_UNSUPPORTED, "hidden must be <= 4096");
   if (delta && delta_dtype != TSB_DT_F32 && delta_dtype != TSB_DT_BF16)
     return set_error(TSB_ERR_INVALID, "delta must be fp32 or bf16");
   if (rows == 0) return TSB_OK;
-  add_rmsnorm_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, delta, delta_dtype == TSB_DT_F32, weight,
+  add_rmsnorm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, delta, delta_dtype == TSB_DT_F32, weight,
                                                                            eps, hidden, static_cast<uint16_t*>(out));
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return TSB_OK;
+}
+
+extern "C" int tsb_gemv_bf16(const void* weight, const void* bias, int32_t N, int32_t K, const void* x, void* y,
+                             void* stream) {
+  if (!weight || !x || !y) return set_error(TSB_ERR_INVALID, "null pointer");
+  if (N < 0 || K <= 0 || K % 8 || K > 16384) return set_error(TSB_ERR_INVALID, "K must be a positive multiple of 8, <= 16384");
+  if (reinterpret_cast<uintptr_t>(weight) & 15) return set_error(TSB_ERR_INVALID, "weight must be 16-byte aligned");
+  if (N == 0) return TSB_OK;
+  const size_t smem = sizeof(float) * K;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  gemv_bf16_kernel<<<(N + kGemvWarps - 1) / kGemvWarps, kGemvWarps * 32, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(weight), static_cast<const uint16_t*>(bias), N, K, static_cast<const uint16_t*>(x),
+      static_cast<uint16_t*>(y));
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   return TSB_OK;

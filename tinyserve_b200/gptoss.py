@@ -14,10 +14,10 @@ CUDA-graph replay per token:
   residual -> RMSNorm -> QuantMoE (one decode-packed launch) -> residual] ->
   RMSNorm -> LM head -> argmax.
 
-Dense projections are cuBLAS GEMVs on bf16 weights; attention (RoPE, cache
+The attention projections (tsb_gemv_bf16), attention (RoPE, cache
 store, sink softmax over the FP8 cache), the residual + RMSNorm steps and the
 expert layers are the library's own kernels; the residual stream is kept in
-fp32.  Prompt prefill runs the same layers over chunks of
+fp32; the LM head is a cuBLAS GEMV.  Prompt prefill runs the same layers over chunks of
 tokens (grouped expert GEMMs, causal attention over the cache).
 
 Positions and the token id live in device buffers, so the captured graph is
@@ -102,6 +102,8 @@ class GptOssDecoder:
         self._h = torch.zeros(1, self.H, dtype=torch.bfloat16, device=dev)     # normed sublayer input
         self._y = torch.zeros(1, self.H, dtype=torch.float32, device=dev)      # expert layer output
         self._a = torch.zeros(1, self.nq * self.D, dtype=torch.bfloat16, device=dev)
+        self._o = torch.zeros(1, self.H, dtype=torch.bfloat16, device=dev)
+        self._qkv = torch.zeros(1, (self.nq + 2 * self.nkv) * self.D, dtype=torch.bfloat16, device=dev)
         nws = _lib.lib().tsb_gqa_decode_workspace(self.nq, self.nkv, max_seq)
         if nws == 0:
             raise ValueError("unsupported attention shape")
@@ -166,6 +168,11 @@ class GptOssDecoder:
         y, _, _ = lay["moe"].decode(h, out_dtype=torch.float32)
         self._norm(x, y, nxt_w, h)
 
+    def _gemv(self, w: torch.Tensor, b, x: torch.Tensor, y: torch.Tensor) -> None:
+        _lib.check(_lib.lib().tsb_gemv_bf16(w.data_ptr(), None if b is None else b.data_ptr(), w.shape[0], w.shape[1],
+                                            x.data_ptr(), y.data_ptr(),
+                                            torch.cuda.current_stream(self.device).cuda_stream))
+
     def _next_norm(self, li: int) -> torch.Tensor:
         return self.layers[li + 1]["ln1"] if li + 1 < self.L else self.norm_w
 
@@ -191,7 +198,7 @@ class GptOssDecoder:
 
     def _step(self):
         """One decode token through every layer (the captured graph's body):
-        fused q|k|v GEMV, the decode-attention kernel (RoPE, cache store,
+        fused q|k|v GEMV (tsb_gemv_bf16), the decode-attention kernel (RoPE, cache store,
         sink attention), o GEMV, residual + RMSNorm kernel, the expert layer
         (fp32 output) and the next residual + RMSNorm."""
         L = _lib.lib()
@@ -200,14 +207,16 @@ class GptOssDecoder:
         x.copy_(self.embed.index_select(0, self._tok))
         self._norm(x, None, self.layers[0]["ln1"], h)
         for li, lay in enumerate(self.layers):
-            qkv = F.linear(h, lay["wqkv"], lay["bqkv"])
+            qkv = self._qkv
+            self._gemv(lay["wqkv"], lay["bqkv"], h, qkv)
             _lib.check(L.tsb_gqa_decode_attention(
                 qkv.data_ptr(), self.nq, self.nkv, self.D, self.cos.data_ptr(), self.sin.data_ptr(),
                 self._pos.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
                 1 if self.kv_dtype == torch.float8_e4m3fn else 0, self.max_seq,
                 self.window if self.sliding[li] else 0, lay["sinks"].data_ptr(), self.scale, self._a.data_ptr(),
                 self._aws.data_ptr(), self._aws.numel(), stream))
-            self._norm(x, F.linear(self._a, lay["wo"], lay["bo"]), lay["ln2"], h)
+            self._gemv(lay["wo"], lay["bo"], self._a, self._o)
+            self._norm(x, self._o, lay["ln2"], h)
             lay["moe"].decode(h, out=self._y)
             self._norm(x, self._y, self._next_norm(li), h)
         self._logits = F.linear(h, self.lm_head)
