@@ -104,6 +104,32 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(AttnArgs a) {
   const int len = (int)pos - lo + 1;
   const int cs = (len + a.S - 1) / a.S;
   const int c0 = lo + s * cs, c1 = min((int)pos + 1, c0 + cs);
+  const int n = max(0, c1 - c0);
+  const int64_t hb = (int64_t)h * a.max_seq * kD;
+  // stage the slice's keys and values in shared memory with every thread's
+  // 16-byte loads in flight at once; rows padded by 16 B so the per-position
+  // row reads of the score pass are bank-conflict free
+  constexpr int EB = FP8 ? 1 : 2;         // bytes per cached element
+  constexpr int RB = kD * EB + 16;        // padded row bytes
+  constexpr int C16 = kD * EB / 16;       // 16-byte chunks per row
+  uint8_t* ks = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sc + G * a.cs_max) + 15) & ~uintptr_t(15));
+  uint8_t* vs = ks + (size_t)a.cs_max * RB;
+  {
+    const uint8_t* kg = static_cast<const uint8_t*>(a.kc) + (hb + (int64_t)c0 * kD) * EB;
+    const uint8_t* vg = static_cast<const uint8_t*>(a.vc) + (hb + (int64_t)c0 * kD) * EB;
+    for (int i = tid; i < n * C16; i += kThreads) {
+      const int j = i / C16, c = i % C16;
+      const uint4 kv = *reinterpret_cast<const uint4*>(kg + (size_t)j * kD * EB + c * 16);
+      const uint4 vv = *reinterpret_cast<const uint4*>(vg + (size_t)j * kD * EB + c * 16);
+      *reinterpret_cast<uint4*>(ks + (size_t)j * RB + c * 16) = kv;
+      *reinterpret_cast<uint4*>(vs + (size_t)j * RB + c * 16) = vv;
+    }
+  }
+  
+  // everything above reads only cache rows written by earlier steps;
+  // the projection output comes from the previous kernel
+  pdl_wait();
+  pdl_launch_dependents();
   // RoPE: q rows of the group, the new key; the new value as is
   const uint16_t* cr = a.cos + pos * (kD / 2);
   const uint16_t* sr = a.sin + pos * (kD / 2);
@@ -148,27 +174,6 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(AttnArgs a) {
             static_cast<uint16_t*>(a.vc)[o] = a.qkv[row * kD + dd];
         }
       }
-    }
-  }
-  const int n = max(0, c1 - c0);
-  const int64_t hb = (int64_t)h * a.max_seq * kD;
-  // stage the slice's keys and values in shared memory with every thread's
-  // 16-byte loads in flight at once; rows padded by 16 B so the per-position
-  // row reads of the score pass are bank-conflict free
-  constexpr int EB = FP8 ? 1 : 2;         // bytes per cached element
-  constexpr int RB = kD * EB + 16;        // padded row bytes
-  constexpr int C16 = kD * EB / 16;       // 16-byte chunks per row
-  uint8_t* ks = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sc + G * a.cs_max) + 15) & ~uintptr_t(15));
-  uint8_t* vs = ks + (size_t)a.cs_max * RB;
-  {
-    const uint8_t* kg = static_cast<const uint8_t*>(a.kc) + (hb + (int64_t)c0 * kD) * EB;
-    const uint8_t* vg = static_cast<const uint8_t*>(a.vc) + (hb + (int64_t)c0 * kD) * EB;
-    for (int i = tid; i < n * C16; i += kThreads) {
-      const int j = i / C16, c = i % C16;
-      const uint4 kv = *reinterpret_cast<const uint4*>(kg + (size_t)j * kD * EB + c * 16);
-      const uint4 vv = *reinterpret_cast<const uint4*>(vg + (size_t)j * kD * EB + c * 16);
-      *reinterpret_cast<uint4*>(ks + (size_t)j * RB + c * 16) = kv;
-      *reinterpret_cast<uint4*>(vs + (size_t)j * RB + c * 16) = vv;
     }
   }
   __syncthreads();
@@ -299,6 +304,8 @@ constexpr int kNormThreads = 256, kPer = 16;
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __restrict__ x, const void* __restrict__ delta,
                                                                    int delta_f32, const float* __restrict__ w, float eps,
                                                                    int H, uint16_t* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int r = blockIdx.x;
   float* xr = x + (int64_t)r * H;
   float v[kPer];
@@ -352,20 +359,30 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(const uint16
                                                                      const uint16_t* __restrict__ x,
                                                                      uint16_t* __restrict__ y) {
   extern __shared__ float xs[];
-  for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = bf(x[i]);
-  __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int n = blockIdx.x * kGemvWarps + (threadIdx.x >> 5);
-  if (n >= N) return;
+  const int n = min(blockIdx.x * kGemvWarps + (threadIdx.x >> 5), N - 1);  // tail warps repeat the last row, unused
   const uint4* row = reinterpret_cast<const uint4*>(W + (int64_t)n * K);
   const int nc = K / 8;
+  // the weights do not depend on the previous kernel: the first batch of this
+  // row's loads is issued before waiting for it
+  uint4 w[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int c = u * 32 + lane;
+    w[u] = c < nc ? __ldcs(row + c) : make_uint4(0, 0, 0, 0);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = bf(x[i]);
+  __syncthreads();
   float acc = 0.f;
   for (int c0 = 0; c0 < nc; c0 += 8 * 32) {
-    uint4 w[8];
+    if (c0 > 0) {
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int c = c0 + u * 32 + lane;
-      w[u] = c < nc ? __ldcs(row + c) : make_uint4(0, 0, 0, 0);
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        w[u] = c < nc ? __ldcs(row + c) : make_uint4(0, 0, 0, 0);
+      }
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -386,7 +403,25 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(const uint16
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) y[n] = f32_to_bf16_bits(acc + (bias ? bf(bias[n]) : 0.f));
+  if (lane == 0 && blockIdx.x * kGemvWarps + (threadIdx.x >> 5) < N) y[n] = f32_to_bf16_bits(acc + (bias ? bf(bias[n]) : 0.f));
+}
+
+// Launch with programmatic stream serialisation: the kernel may start while
+// the previous kernel on the stream finishes; it waits (griddepcontrol.wait)
+// before reading that kernel's outputs.
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern k, dim3 grid, int block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
 }  // namespace
@@ -450,12 +485,11 @@ extern "C" int tsb_gqa_decode_attention(const void* qkv, int32_t n_q_heads, int3
   cudaError_t e;
   if (cache_fp8) {
     if (smem > 48 * 1024) cudaFuncSetAttribute(gqa_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    gqa_decode_kernel<true><<<dim3(a.S, n_kv_heads), kThreads, smem, st>>>(a);
+    e = launch_pdl(gqa_decode_kernel<true>, dim3(a.S, n_kv_heads), kThreads, smem, st, a);
   } else {
     if (smem > 48 * 1024) cudaFuncSetAttribute(gqa_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    gqa_decode_kernel<false><<<dim3(a.S, n_kv_heads), kThreads, smem, st>>>(a);
+    e = launch_pdl(gqa_decode_kernel<false>, dim3(a.S, n_kv_heads), kThreads, smem, st, a);
   }
-  e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   return TSB_OK;
 }
@@ -468,9 +502,9 @@ extern "C" int tsb_add_rmsnorm(float* x, const void* delta, int32_t delta_dtype,
   if (delta && delta_dtype != TSB_DT_F32 && delta_dtype != TSB_DT_BF16)
     return set_error(TSB_ERR_INVALID, "delta must be fp32 or bf16");
   if (rows == 0) return TSB_OK;
-  add_rmsnorm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, delta, delta_dtype == TSB_DT_F32, weight,
-                                                                           eps, hidden, static_cast<uint16_t*>(out));
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch_pdl(add_rmsnorm_kernel, dim3(rows), kNormThreads, 0, static_cast<cudaStream_t>(stream),
+                                   x, delta, (int)(delta_dtype == TSB_DT_F32), weight, eps, (int)hidden,
+                                   static_cast<uint16_t*>(out));
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   return TSB_OK;
 }
@@ -483,10 +517,10 @@ extern "C" int tsb_gemv_bf16(const void* weight, const void* bias, int32_t N, in
   if (N == 0) return TSB_OK;
   const size_t smem = sizeof(float) * K;
   if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  gemv_bf16_kernel<<<(N + kGemvWarps - 1) / kGemvWarps, kGemvWarps * 32, smem, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(weight), static_cast<const uint16_t*>(bias), N, K, static_cast<const uint16_t*>(x),
-      static_cast<uint16_t*>(y));
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch_pdl(gemv_bf16_kernel, dim3((N + kGemvWarps - 1) / kGemvWarps), kGemvWarps * 32, smem,
+                                   static_cast<cudaStream_t>(stream), static_cast<const uint16_t*>(weight),
+                                   static_cast<const uint16_t*>(bias), (int)N, (int)K, static_cast<const uint16_t*>(x),
+                                   static_cast<uint16_t*>(y));
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   return TSB_OK;
 }
