@@ -313,6 +313,18 @@ int tsb_add_rmsnorm(float* x, const void* delta, int32_t delta_dtype, const floa
  * attention projections of the decode step (nn.Linear in the reference's
  * model). */
 int tsb_gemv_bf16(const void* weight, const void* bias, int32_t N, int32_t K, const void* x, void* y, void* stream);
+/* The same GEMV with the sublayer's RMSNorm in front: x = bf16(norm_weight *
+ * RMSNorm(x_in + delta)) (x_in fp32 [K], delta fp32 [K] or NULL), computed by
+ * every CTA; x_in + delta is also stored to x_out (fp32 [K], not aliasing
+ * x_in or delta).  y = bf16(W x + bias). */
+int tsb_norm_gemv_bf16(const float* x_in, const float* delta, float* x_out, const float* norm_weight, float eps,
+                       const void* weight, const void* bias, int32_t N, int32_t K, void* y, void* stream);
+/* The same GEMV adding its bf16 result into an fp32 residual (resid[N] +=
+ * bf16(W x + bias)); the last CTA then writes h_out = bf16(norm_weight *
+ * RMSNorm(resid)) [N].  counter: a device uint32, zero-initialised once
+ * (the kernel resets it). */
+int tsb_gemv_bf16_residual(const void* weight, const void* bias, int32_t N, int32_t K, const void* x, float* resid,
+                           const float* norm_weight, float eps, void* h_out, uint32_t* counter, void* stream);
 
 #ifdef __cplusplus
 }

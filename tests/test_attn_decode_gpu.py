@@ -105,3 +105,45 @@ def test_gemv_bf16(dev, N, K):
         torch.cuda.synchronize()
         ref = W.double() @ x.double() + (0 if bias is None else bias.double())
         assert ((y.double() - ref).norm() / ref.norm()).item() < 4e-3
+
+
+def test_norm_gemv_and_residual_gemv(dev):
+    """tsb_norm_gemv_bf16 (RMSNorm of x_in + delta in front of the GEMV, the sum
+    stored to x_out) and tsb_gemv_bf16_residual (resid += bf16(W x + b), then
+    the last CTA's RMSNorm of resid), twice in a row (the counter resets)."""
+    L = _lib.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device=dev).manual_seed(9)
+    H, N1, K2 = 2880, 5120, 4096
+    x_in = torch.randn(H, generator=g, device=dev)
+    delta = torch.randn(H, generator=g, device=dev)
+    nw = torch.rand(H, generator=g, device=dev) + 0.5
+    W1 = (torch.randn(N1, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    b1 = torch.randn(N1, generator=g, device=dev).to(torch.bfloat16)
+    x_out = torch.empty(H, device=dev)
+    y = torch.empty(N1, dtype=torch.bfloat16, device=dev)
+    _lib.check(L.tsb_norm_gemv_bf16(x_in.data_ptr(), delta.data_ptr(), x_out.data_ptr(), nw.data_ptr(), 1e-5,
+                                    W1.data_ptr(), b1.data_ptr(), N1, H, y.data_ptr(), st))
+    torch.cuda.synchronize()
+    v = x_in.double() + delta.double()
+    assert torch.allclose(x_out.double(), v, rtol=0, atol=1e-6)
+    hn = (nw.double() * v * torch.rsqrt(v.pow(2).mean() + 1e-5)).to(torch.bfloat16).double()
+    ref = W1.double() @ hn + b1.double()
+    assert ((y.double() - ref).norm() / ref.norm()).item() < 4e-3
+    W2 = (torch.randn(H, K2, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    b2 = torch.randn(H, generator=g, device=dev).to(torch.bfloat16)
+    a = torch.randn(K2, generator=g, device=dev).to(torch.bfloat16)
+    cnt = torch.zeros(1, dtype=torch.int32, device=dev)
+    h = torch.empty(H, dtype=torch.bfloat16, device=dev)
+    resid = x_out.clone()
+    for it in range(2):
+        before = resid.double().clone()
+        _lib.check(L.tsb_gemv_bf16_residual(W2.data_ptr(), b2.data_ptr(), H, K2, a.data_ptr(), resid.data_ptr(),
+                                            nw.data_ptr(), 1e-5, h.data_ptr(), cnt.data_ptr(), st))
+        torch.cuda.synchronize()
+        o = (W2.double() @ a.double() + b2.double())
+        want = before + o.to(torch.bfloat16).double()
+        assert ((resid.double() - want).norm() / want.norm()).item() < 1e-3
+        hr = nw.double() * resid.double() * torch.rsqrt(resid.double().pow(2).mean() + 1e-5)
+        assert ((h.double() - hr).norm() / hr.norm()).item() < 4e-3
+        assert int(cnt.item()) == 0

@@ -348,23 +348,57 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
   }
 }
 
-// y[n] = bf16(W[n, :] . x + bias[n]) for bf16 W [N, K] (row-major), x [K]:
-// one warp per row, the row's 16-byte chunks loaded in batches of 8 per lane
-// before any arithmetic (the loads of a batch are in flight together), x
-// staged once per CTA as fp32 in shared memory.
+// y[n] = bf16(W[n, :] . x + bias[n]) for bf16 W [N, K] (row-major): one warp
+// per row, the row's 16-byte chunks loaded in batches of 8 per lane before any
+// arithmetic (the first batch before waiting for the previous kernel, since
+// the weights do not depend on it), the input vector staged once per CTA as
+// fp32 in shared memory.  Three forms share the body:
+//  GV_PLAIN    x is a bf16 vector;
+//  GV_NORM     x = bf16(RMSNorm(x_in + delta) * norm_w), computed by every CTA
+//              from the fp32 residual stream; CTA 0 stores x_in + delta to
+//              x_out (the residual for the rest of the layer);
+//  GV_RESIDUAL resid[n] += bf16(y[n]) (y is not stored); the last CTA to finish
+//              writes h_out = bf16(RMSNorm(resid) * norm_w) for the next sublayer.
 constexpr int kGemvWarps = 8;
+enum { GV_PLAIN = 0, GV_NORM = 1, GV_RESIDUAL = 2 };
 
-__global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(const uint16_t* __restrict__ W,
-                                                                     const uint16_t* __restrict__ bias, int N, int K,
-                                                                     const uint16_t* __restrict__ x,
-                                                                     uint16_t* __restrict__ y) {
+struct GemvArgs {
+  const uint16_t* W;
+  const uint16_t* bias;
+  int N, K;
+  const uint16_t* x;     // GV_PLAIN / GV_RESIDUAL
+  uint16_t* y;           // GV_PLAIN / GV_NORM
+  const float* x_in;     // GV_NORM
+  const float* delta;    // GV_NORM (nullable)
+  float* x_out;          // GV_NORM
+  float* resid;          // GV_RESIDUAL
+  const float* norm_w;   // GV_NORM / GV_RESIDUAL
+  float eps;
+  uint16_t* h_out;       // GV_RESIDUAL
+  unsigned* counter;     // GV_RESIDUAL
+};
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int k = 0; k < (int)(blockDim.x >> 5); ++k) t += red[k];
+  return t;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(GemvArgs a) {
   extern __shared__ float xs[];
+  __shared__ float red[kGemvWarps];
+  __shared__ int s_last;
   const int lane = threadIdx.x & 31;
-  const int n = min(blockIdx.x * kGemvWarps + (threadIdx.x >> 5), N - 1);  // tail warps repeat the last row, unused
-  const uint4* row = reinterpret_cast<const uint4*>(W + (int64_t)n * K);
+  const int K = a.K, N = a.N;
+  const int n = min((int)(blockIdx.x * kGemvWarps + (threadIdx.x >> 5)), N - 1);  // tail warps redo the last row
+  const uint4* row = reinterpret_cast<const uint4*>(a.W + (int64_t)n * K);
   const int nc = K / 8;
-  // the weights do not depend on the previous kernel: the first batch of this
-  // row's loads is issued before waiting for it
   uint4 w[8];
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
@@ -373,7 +407,19 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(const uint16
   }
   pdl_wait();
   pdl_launch_dependents();
-  for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = bf(x[i]);
+  if constexpr (MODE == GV_NORM) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+      const float v = a.x_in[i] + (a.delta ? a.delta[i] : 0.f);
+      xs[i] = v;
+      ss = fmaf(v, v, ss);
+      if (blockIdx.x == 0) a.x_out[i] = v;
+    }
+    const float inv = rsqrtf(block_sum(ss, red) / K + a.eps);
+    for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = round_bf16(a.norm_w[i] * (xs[i] * inv));
+  } else {
+    for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = bf(a.x[i]);
+  }
   __syncthreads();
   float acc = 0.f;
   for (int c0 = 0; c0 < nc; c0 += 8 * 32) {
@@ -403,7 +449,32 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(const uint16
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0 && blockIdx.x * kGemvWarps + (threadIdx.x >> 5) < N) y[n] = f32_to_bf16_bits(acc + (bias ? bf(bias[n]) : 0.f));
+  const bool mine = lane == 0 && (int)(blockIdx.x * kGemvWarps + (threadIdx.x >> 5)) < N;
+  const uint16_t yb = f32_to_bf16_bits(acc + (a.bias ? bf(a.bias[n]) : 0.f));
+  if constexpr (MODE != GV_RESIDUAL) {
+    if (mine) a.y[n] = yb;
+  } else {
+    if (mine) a.resid[n] += bf(yb);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned prev;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.counter) : "memory");
+      s_last = prev == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+      const float v = __ldcg(a.resid + i);
+      xs[i] = v;
+      ss = fmaf(v, v, ss);
+    }
+    const float inv = rsqrtf(block_sum(ss, red) / N + a.eps);
+    for (int i = threadIdx.x; i < N; i += blockDim.x) a.h_out[i] = f32_to_bf16_bits(a.norm_w[i] * (xs[i] * inv));
+    if (threadIdx.x == 0) *a.counter = 0u;
+  }
 }
 
 // Launch with programmatic stream serialisation: the kernel may start while
@@ -509,18 +580,80 @@ extern "C" int tsb_add_rmsnorm(float* x, const void* delta, int32_t delta_dtype,
   return TSB_OK;
 }
 
-extern "C" int tsb_gemv_bf16(const void* weight, const void* bias, int32_t N, int32_t K, const void* x, void* y,
-                             void* stream) {
-  if (!weight || !x || !y) return set_error(TSB_ERR_INVALID, "null pointer");
-  if (N < 0 || K <= 0 || K % 8 || K > 16384) return set_error(TSB_ERR_INVALID, "K must be a positive multiple of 8, <= 16384");
-  if (reinterpret_cast<uintptr_t>(weight) & 15) return set_error(TSB_ERR_INVALID, "weight must be 16-byte aligned");
-  if (N == 0) return TSB_OK;
-  const size_t smem = sizeof(float) * K;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  const cudaError_t e = launch_pdl(gemv_bf16_kernel, dim3((N + kGemvWarps - 1) / kGemvWarps), kGemvWarps * 32, smem,
-                                   static_cast<cudaStream_t>(stream), static_cast<const uint16_t*>(weight),
-                                   static_cast<const uint16_t*>(bias), (int)N, (int)K, static_cast<const uint16_t*>(x),
-                                   static_cast<uint16_t*>(y));
+static int run_gemv(int mode, GemvArgs a, void* stream) {
+  if (!a.W) return set_error(TSB_ERR_INVALID, "null pointer");
+  if (a.N <= 0 || a.K <= 0 || a.K % 8 || a.K > 16384) return set_error(TSB_ERR_INVALID, "N must be positive, K a positive multiple of 8 up to 16384");
+  if (reinterpret_cast<uintptr_t>(a.W) & 15) return set_error(TSB_ERR_INVALID, "weight must be 16-byte aligned");
+  if (mode == GV_RESIDUAL && a.N > 16384) return set_error(TSB_ERR_INVALID, "N must be <= 16384 for the residual form");
+  const int smem_elems = mode == GV_RESIDUAL ? (a.K > a.N ? a.K : a.N) : a.K;
+  const size_t smem = sizeof(float) * smem_elems;
+  const dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  switch (mode) {
+    case GV_NORM:
+      if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_bf16_kernel<GV_NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      e = launch_pdl(gemv_bf16_kernel<GV_NORM>, grid, kGemvWarps * 32, smem, st, a);
+      break;
+    case GV_RESIDUAL:
+      if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_bf16_kernel<GV_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      e = launch_pdl(gemv_bf16_kernel<GV_RESIDUAL>, grid, kGemvWarps * 32, smem, st, a);
+      break;
+    default:
+      if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_bf16_kernel<GV_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      e = launch_pdl(gemv_bf16_kernel<GV_PLAIN>, grid, kGemvWarps * 32, smem, st, a);
+  }
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   return TSB_OK;
+}
+
+extern "C" int tsb_gemv_bf16(const void* weight, const void* bias, int32_t N, int32_t K, const void* x, void* y,
+                             void* stream) {
+  if (N == 0) return TSB_OK;
+  if (!x || !y) return set_error(TSB_ERR_INVALID, "null pointer");
+  GemvArgs a{};
+  a.W = static_cast<const uint16_t*>(weight);
+  a.bias = static_cast<const uint16_t*>(bias);
+  a.N = N;
+  a.K = K;
+  a.x = static_cast<const uint16_t*>(x);
+  a.y = static_cast<uint16_t*>(y);
+  return run_gemv(GV_PLAIN, a, stream);
+}
+
+extern "C" int tsb_norm_gemv_bf16(const float* x_in, const float* delta, float* x_out, const float* norm_weight,
+                                  float eps, const void* weight, const void* bias, int32_t N, int32_t K, void* y,
+                                  void* stream) {
+  if (!x_in || !x_out || !norm_weight || !y) return set_error(TSB_ERR_INVALID, "null pointer");
+  if (x_out == x_in || (delta && x_out == delta)) return set_error(TSB_ERR_INVALID, "x_out must not alias x_in or delta");
+  GemvArgs a{};
+  a.W = static_cast<const uint16_t*>(weight);
+  a.bias = static_cast<const uint16_t*>(bias);
+  a.N = N;
+  a.K = K;
+  a.y = static_cast<uint16_t*>(y);
+  a.x_in = x_in;
+  a.delta = delta;
+  a.x_out = x_out;
+  a.norm_w = norm_weight;
+  a.eps = eps;
+  return run_gemv(GV_NORM, a, stream);
+}
+
+extern "C" int tsb_gemv_bf16_residual(const void* weight, const void* bias, int32_t N, int32_t K, const void* x,
+                                      float* resid, const float* norm_weight, float eps, void* h_out,
+                                      uint32_t* counter, void* stream) {
+  if (!x || !resid || !norm_weight || !h_out || !counter) return set_error(TSB_ERR_INVALID, "null pointer");
+  GemvArgs a{};
+  a.W = static_cast<const uint16_t*>(weight);
+  a.bias = static_cast<const uint16_t*>(bias);
+  a.N = N;
+  a.K = K;
+  a.x = static_cast<const uint16_t*>(x);
+  a.resid = resid;
+  a.norm_w = norm_weight;
+  a.eps = eps;
+  a.h_out = static_cast<uint16_t*>(h_out);
+  a.counter = counter;
+  return run_gemv(GV_RESIDUAL, a, stream);
 }

@@ -14,7 +14,8 @@ CUDA-graph replay per token:
   residual -> RMSNorm -> QuantMoE (one decode-packed launch) -> residual] ->
   RMSNorm -> LM head -> argmax.
 
-The attention projections (tsb_gemv_bf16), attention (RoPE, cache
+The attention projections (bf16 GEMVs with the RMSNorm and residual steps
+fused in), attention (RoPE, cache
 store, sink softmax over the FP8 cache), the residual + RMSNorm steps and the
 expert layers are the library's own kernels; the residual stream is kept in
 fp32; the LM head is a cuBLAS GEMV.  Prompt prefill runs the same layers over chunks of
@@ -98,11 +99,13 @@ class GptOssDecoder:
         self._logits = None
         self._j = torch.arange(max_seq, device=dev)
         # decode-step buffers (fixed addresses for the captured graph)
-        self._x = torch.zeros(1, self.H, dtype=torch.float32, device=dev)      # residual stream
+        self._xe = torch.zeros(1, self.H, dtype=torch.float32, device=dev)     # embedding row
+        self._xa = torch.zeros(1, self.H, dtype=torch.float32, device=dev)     # residual stream, two buffers
+        self._xb = torch.zeros(1, self.H, dtype=torch.float32, device=dev)
+        self._cnt = torch.zeros(1, dtype=torch.int32, device=dev)
         self._h = torch.zeros(1, self.H, dtype=torch.bfloat16, device=dev)     # normed sublayer input
         self._y = torch.zeros(1, self.H, dtype=torch.float32, device=dev)      # expert layer output
         self._a = torch.zeros(1, self.nq * self.D, dtype=torch.bfloat16, device=dev)
-        self._o = torch.zeros(1, self.H, dtype=torch.bfloat16, device=dev)
         self._qkv = torch.zeros(1, (self.nq + 2 * self.nkv) * self.D, dtype=torch.bfloat16, device=dev)
         nws = _lib.lib().tsb_gqa_decode_workspace(self.nq, self.nkv, max_seq)
         if nws == 0:
@@ -168,11 +171,6 @@ class GptOssDecoder:
         y, _, _ = lay["moe"].decode(h, out_dtype=torch.float32)
         self._norm(x, y, nxt_w, h)
 
-    def _gemv(self, w: torch.Tensor, b, x: torch.Tensor, y: torch.Tensor) -> None:
-        _lib.check(_lib.lib().tsb_gemv_bf16(w.data_ptr(), None if b is None else b.data_ptr(), w.shape[0], w.shape[1],
-                                            x.data_ptr(), y.data_ptr(),
-                                            torch.cuda.current_stream(self.device).cuda_stream))
-
     def _next_norm(self, li: int) -> torch.Tensor:
         return self.layers[li + 1]["ln1"] if li + 1 < self.L else self.norm_w
 
@@ -197,29 +195,37 @@ class GptOssDecoder:
         return F.linear(last, self.lm_head)[0].float()
 
     def _step(self):
-        """One decode token through every layer (the captured graph's body):
-        fused q|k|v GEMV (tsb_gemv_bf16), the decode-attention kernel (RoPE, cache store,
-        sink attention), o GEMV, residual + RMSNorm kernel, the expert layer
-        (fp32 output) and the next residual + RMSNorm."""
+        """One decode token through every layer (the captured graph's body), four
+        launches per layer: RMSNorm + fused q|k|v GEMV (tsb_norm_gemv_bf16, which
+        also folds the previous expert output into the residual), the
+        decode-attention kernel (RoPE, cache store, sink attention), the o GEMV
+        adding into the residual and normalising it for the expert layer
+        (tsb_gemv_bf16_residual), and the expert layer (fp32 output)."""
         L = _lib.lib()
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        x, h = self._x, self._h
-        x.copy_(self.embed.index_select(0, self._tok))
-        self._norm(x, None, self.layers[0]["ln1"], h)
+        xin, xout = self._xe, self._xa
+        xin.copy_(self.embed.index_select(0, self._tok))
+        delta = None
         for li, lay in enumerate(self.layers):
-            qkv = self._qkv
-            self._gemv(lay["wqkv"], lay["bqkv"], h, qkv)
+            _lib.check(L.tsb_norm_gemv_bf16(
+                xin.data_ptr(), None if delta is None else delta.data_ptr(), xout.data_ptr(), lay["ln1"].data_ptr(),
+                self.eps, lay["wqkv"].data_ptr(), None if lay["bqkv"] is None else lay["bqkv"].data_ptr(),
+                lay["wqkv"].shape[0], self.H, self._qkv.data_ptr(), stream))
             _lib.check(L.tsb_gqa_decode_attention(
-                qkv.data_ptr(), self.nq, self.nkv, self.D, self.cos.data_ptr(), self.sin.data_ptr(),
+                self._qkv.data_ptr(), self.nq, self.nkv, self.D, self.cos.data_ptr(), self.sin.data_ptr(),
                 self._pos.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
                 1 if self.kv_dtype == torch.float8_e4m3fn else 0, self.max_seq,
                 self.window if self.sliding[li] else 0, lay["sinks"].data_ptr(), self.scale, self._a.data_ptr(),
                 self._aws.data_ptr(), self._aws.numel(), stream))
-            self._gemv(lay["wo"], lay["bo"], self._a, self._o)
-            self._norm(x, self._o, lay["ln2"], h)
-            lay["moe"].decode(h, out=self._y)
-            self._norm(x, self._y, self._next_norm(li), h)
-        self._logits = F.linear(h, self.lm_head)
+            _lib.check(L.tsb_gemv_bf16_residual(
+                lay["wo"].data_ptr(), None if lay["bo"] is None else lay["bo"].data_ptr(), self.H, self.nq * self.D,
+                self._a.data_ptr(), xout.data_ptr(), lay["ln2"].data_ptr(), self.eps, self._h.data_ptr(),
+                self._cnt.data_ptr(), stream))
+            lay["moe"].decode(self._h, out=self._y)
+            delta = self._y
+            xin, xout = xout, (self._xb if xout is self._xa else self._xa)
+        self._norm(xin, delta, self.norm_w, self._h)
+        self._logits = F.linear(self._h, self.lm_head)
         self._next.copy_(self._logits.argmax(-1))
 
     def _capture(self):
