@@ -26,6 +26,8 @@
 // Memory-bound on the cache slice (D bytes per position per KV head for e4m3).
 #include <cuda_fp8.h>
 
+#include <cstdlib>
+
 #include "../../include/tsb_moe.h"
 #include "tsb_common.cuh"
 #include "tsb_internal.h"
@@ -480,6 +482,15 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(GemvArgs a) 
 // Launch with programmatic stream serialisation: the kernel may start while
 // the previous kernel on the stream finishes; it waits (griddepcontrol.wait)
 // before reading that kernel's outputs.
+// TSB_DECODE_PDL=0 launches them plainly (for A/B timing).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("TSB_DECODE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 template <typename Kern, typename... Args>
 cudaError_t launch_pdl(Kern k, dim3 grid, int block, size_t smem, cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
@@ -491,7 +502,7 @@ cudaError_t launch_pdl(Kern k, dim3 grid, int block, size_t smem, cudaStream_t s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
