@@ -119,12 +119,27 @@ __global__ void __launch_bounds__(kThreads) gqa_decode_kernel(AttnArgs a) {
   {
     const uint8_t* kg = static_cast<const uint8_t*>(a.kc) + (hb + (int64_t)c0 * kD) * EB;
     const uint8_t* vg = static_cast<const uint8_t*>(a.vc) + (hb + (int64_t)c0 * kD) * EB;
-    for (int i = tid; i < n * C16; i += kThreads) {
-      const int j = i / C16, c = i % C16;
-      const uint4 kv = *reinterpret_cast<const uint4*>(kg + (size_t)j * kD * EB + c * 16);
-      const uint4 vv = *reinterpret_cast<const uint4*>(vg + (size_t)j * kD * EB + c * 16);
-      *reinterpret_cast<uint4*>(ks + (size_t)j * RB + c * 16) = kv;
-      *reinterpret_cast<uint4*>(vs + (size_t)j * RB + c * 16) = vv;
+    // all of a thread's loads (up to 4 chunks of each) before any store
+    for (int base = 0; base < n * C16; base += 4 * kThreads) {
+      uint4 kv[4], vv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = base + u * kThreads + tid;
+        if (i < n * C16) {
+          const int j = i / C16, c = i % C16;
+          kv[u] = *reinterpret_cast<const uint4*>(kg + (size_t)j * kD * EB + c * 16);
+          vv[u] = *reinterpret_cast<const uint4*>(vg + (size_t)j * kD * EB + c * 16);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = base + u * kThreads + tid;
+        if (i < n * C16) {
+          const int j = i / C16, c = i % C16;
+          *reinterpret_cast<uint4*>(ks + (size_t)j * RB + c * 16) = kv[u];
+          *reinterpret_cast<uint4*>(vs + (size_t)j * RB + c * 16) = vv[u];
+        }
+      }
     }
   }
   
@@ -364,6 +379,99 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
 constexpr int kGemvWarps = 8;
 enum { GV_PLAIN = 0, GV_NORM = 1, GV_RESIDUAL = 2 };
 
+// Vector staging helpers: each thread issues up to 4 independent 16-byte loads
+// before storing any of them, so a staging pass costs one memory round trip
+// (a load/store loop would serialise them: the shared-memory stores may alias
+// the loads as far as the compiler knows).
+__device__ __forceinline__ void stage_bf16_f32(float* __restrict__ xs, const uint16_t* __restrict__ x, int K) {
+  const uint4* src = reinterpret_cast<const uint4*>(x);
+  const int n16 = K / 8;
+  for (int base = 0; base < n16; base += 4 * (int)blockDim.x) {
+    uint4 r[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * blockDim.x + threadIdx.x;
+      if (i < n16) r[u] = src[i];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * blockDim.x + threadIdx.x;
+      if (i < n16) {
+        float4* d = reinterpret_cast<float4*>(xs + 8 * i);
+        d[0] = make_float4(__uint_as_float(r[u].x << 16), __uint_as_float(r[u].x & 0xFFFF0000u),
+                           __uint_as_float(r[u].y << 16), __uint_as_float(r[u].y & 0xFFFF0000u));
+        d[1] = make_float4(__uint_as_float(r[u].z << 16), __uint_as_float(r[u].z & 0xFFFF0000u),
+                           __uint_as_float(r[u].w << 16), __uint_as_float(r[u].w & 0xFFFF0000u));
+      }
+    }
+  }
+}
+
+// xs = v = a + b (b nullable; fp32, K % 4 == 0); returns this thread's sum of v^2.
+// When out is given it receives v too.  CG: read a through L2 (data other CTAs
+// of the running kernel wrote).
+template <bool CG = false>
+__device__ __forceinline__ float stage_sum_f32(float* __restrict__ xs, const float* __restrict__ a,
+                                               const float* __restrict__ b, float* __restrict__ out, int K) {
+  const float4* pa = reinterpret_cast<const float4*>(a);
+  const float4* pb = reinterpret_cast<const float4*>(b);
+  const int n4 = K / 4;
+  float ss = 0.f;
+  for (int base = 0; base < n4; base += 4 * (int)blockDim.x) {
+    float4 ra[4], rb[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * blockDim.x + threadIdx.x;
+      if (i < n4) {
+        ra[u] = CG ? __ldcg(pa + i) : pa[i];
+        rb[u] = b ? pb[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * blockDim.x + threadIdx.x;
+      if (i < n4) {
+        const float4 v = make_float4(ra[u].x + rb[u].x, ra[u].y + rb[u].y, ra[u].z + rb[u].z, ra[u].w + rb[u].w);
+        reinterpret_cast<float4*>(xs)[i] = v;
+        if (out) reinterpret_cast<float4*>(out)[i] = v;
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+      }
+    }
+  }
+  return ss;
+}
+
+// xs[i] = round_bf16(w[i] * xs[i] * inv) (store_bf16 == nullptr) or
+// store_bf16[i] = bf16(w[i] * xs[i] * inv); K % 4 == 0.
+__device__ __forceinline__ void apply_norm(float* __restrict__ xs, const float* __restrict__ w, float inv, int K,
+                                           uint16_t* __restrict__ store_bf16) {
+  const float4* pw = reinterpret_cast<const float4*>(w);
+  const int n4 = K / 4;
+  for (int base = 0; base < n4; base += 4 * (int)blockDim.x) {
+    float4 rw[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * blockDim.x + threadIdx.x;
+      if (i < n4) rw[u] = pw[i];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * blockDim.x + threadIdx.x;
+      if (i < n4) {
+        const float4 v = reinterpret_cast<const float4*>(xs)[i];
+        const float o[4] = {rw[u].x * (v.x * inv), rw[u].y * (v.y * inv), rw[u].z * (v.z * inv), rw[u].w * (v.w * inv)};
+        if (store_bf16) {
+          const uint2 pk = make_uint2(f32_to_bf16_bits(o[0]) | ((uint32_t)f32_to_bf16_bits(o[1]) << 16),
+                                      f32_to_bf16_bits(o[2]) | ((uint32_t)f32_to_bf16_bits(o[3]) << 16));
+          reinterpret_cast<uint2*>(store_bf16)[i] = pk;
+        } else {
+          reinterpret_cast<float4*>(xs)[i] = make_float4(round_bf16(o[0]), round_bf16(o[1]), round_bf16(o[2]), round_bf16(o[3]));
+        }
+      }
+    }
+  }
+}
+
 struct GemvArgs {
   const uint16_t* W;
   const uint16_t* bias;
@@ -392,7 +500,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_bf16_kernel(GemvArgs a) {
   extern __shared__ float xs[];
   __shared__ float red[kGemvWarps];
   __shared__ int s_last;
@@ -410,17 +518,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(GemvArgs a) 
   pdl_wait();
   pdl_launch_dependents();
   if constexpr (MODE == GV_NORM) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-      const float v = a.x_in[i] + (a.delta ? a.delta[i] : 0.f);
-      xs[i] = v;
-      ss = fmaf(v, v, ss);
-      if (blockIdx.x == 0) a.x_out[i] = v;
-    }
+    const float ss = stage_sum_f32(xs, a.x_in, a.delta, blockIdx.x == 0 ? a.x_out : nullptr, K);
     const float inv = rsqrtf(block_sum(ss, red) / K + a.eps);
-    for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = round_bf16(a.norm_w[i] * (xs[i] * inv));
+    apply_norm(xs, a.norm_w, inv, K, nullptr);
   } else {
-    for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = bf(a.x[i]);
+    stage_bf16_f32(xs, a.x, K);
   }
   __syncthreads();
   float acc = 0.f;
@@ -467,14 +569,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_bf16_kernel(GemvArgs a) 
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < N; i += blockDim.x) {
-      const float v = __ldcg(a.resid + i);
-      xs[i] = v;
-      ss = fmaf(v, v, ss);
-    }
+    // other CTAs' residual rows, read through L2 (the acq_rel counter above
+    // orders them after their writes)
+    const float ss = stage_sum_f32<true>(xs, a.resid, nullptr, nullptr, N);
     const float inv = rsqrtf(block_sum(ss, red) / N + a.eps);
-    for (int i = threadIdx.x; i < N; i += blockDim.x) a.h_out[i] = f32_to_bf16_bits(a.norm_w[i] * (xs[i] * inv));
+    apply_norm(xs, a.norm_w, inv, N, a.h_out);
     if (threadIdx.x == 0) *a.counter = 0u;
   }
 }
@@ -595,7 +694,7 @@ static int run_gemv(int mode, GemvArgs a, void* stream) {
   if (!a.W) return set_error(TSB_ERR_INVALID, "null pointer");
   if (a.N <= 0 || a.K <= 0 || a.K % 8 || a.K > 16384) return set_error(TSB_ERR_INVALID, "N must be positive, K a positive multiple of 8 up to 16384");
   if (reinterpret_cast<uintptr_t>(a.W) & 15) return set_error(TSB_ERR_INVALID, "weight must be 16-byte aligned");
-  if (mode == GV_RESIDUAL && a.N > 16384) return set_error(TSB_ERR_INVALID, "N must be <= 16384 for the residual form");
+  if (mode == GV_RESIDUAL && (a.N > 16384 || a.N % 4)) return set_error(TSB_ERR_INVALID, "N must be a multiple of 4, <= 16384, for the residual form");
   const int smem_elems = mode == GV_RESIDUAL ? (a.K > a.N ? a.K : a.N) : a.K;
   const size_t smem = sizeof(float) * smem_elems;
   const dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps);
