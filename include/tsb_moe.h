@@ -308,6 +308,17 @@ int tsb_gqa_decode_attention(const void* qkv, int32_t n_q_heads, int32_t n_kv_he
                              void* out, void* workspace, size_t workspace_bytes, void* stream);
 int tsb_add_rmsnorm(float* x, const void* delta, int32_t delta_dtype, const float* weight, float eps, int32_t rows,
                     int32_t hidden, void* out, void* stream);
+/* The same attention for `batch` sequences decoding together (several
+ * requests served at once, tinyserve/server.py:48-150): row b of qkv / out,
+ * position pos[b], cache slot slots[b] (the caches hold slots slot_stride
+ * elements apart, each [n_kv, max_seq, head_dim]).  Workspace from
+ * tsb_gqa_decode_batch_workspace for that batch size. */
+size_t tsb_gqa_decode_batch_workspace(int32_t n_q_heads, int32_t n_kv_heads, int32_t max_seq, int32_t batch);
+int tsb_gqa_decode_attention_batch(const void* qkv, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
+                                   const void* cos, const void* sin, const int64_t* pos, const int32_t* slots,
+                                   int64_t slot_stride, void* k_cache, void* v_cache, int32_t cache_fp8,
+                                   int32_t max_seq, int32_t window, const float* sinks, float scale, void* out,
+                                   int32_t batch, void* workspace, size_t workspace_bytes, void* stream);
 /* y = bf16(W x + bias): one bf16 [N, K] weight (16-byte aligned, K % 8 == 0,
  * K <= 16384), bf16 x [K], optional bf16 bias [N], bf16 y [N]; the batch-1
  * attention projections of the decode step (nn.Linear in the reference's

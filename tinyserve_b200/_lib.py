@@ -33,7 +33,8 @@ EXPORTS = (
     "tsb_moe_packed_bytes", "tsb_moe_pack", "tsb_moe_decode_packed_workspace", "tsb_moe_decode_packed",
     "tsb_moe_route", "tsb_ep_decode_workspace", "tsb_ep_moe_decode", "tsb_ep_prefill_workspace",
     "tsb_ep_moe_prefill", "tsb_gqa_decode_workspace", "tsb_gqa_decode_attention", "tsb_add_rmsnorm",
-    "tsb_gemv_bf16", "tsb_norm_gemv_bf16", "tsb_gemv_bf16_residual",
+    "tsb_gemv_bf16", "tsb_norm_gemv_bf16", "tsb_gemv_bf16_residual", "tsb_gqa_decode_batch_workspace",
+    "tsb_gqa_decode_attention_batch",
 )
 
 
@@ -94,6 +95,10 @@ def _declare(L: ctypes.CDLL) -> None:
     L.tsb_gqa_decode_workspace.restype = _sz
     L.tsb_gqa_decode_attention.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp,
                                            ctypes.c_float, _vp, _vp, _sz, _vp]
+    L.tsb_gqa_decode_batch_workspace.argtypes = [_i32, _i32, _i32, _i32]
+    L.tsb_gqa_decode_batch_workspace.restype = _sz
+    L.tsb_gqa_decode_attention_batch.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i32, _i32,
+                                                 _i32, _vp, ctypes.c_float, _vp, _i32, _vp, _sz, _vp]
     L.tsb_gemv_bf16.argtypes = [_vp, _vp, _i32, _i32, _vp, _vp, _vp]
     L.tsb_norm_gemv_bf16.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _i32, _i32, _vp, _vp]
     L.tsb_gemv_bf16_residual.argtypes = [_vp, _vp, _i32, _i32, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp]

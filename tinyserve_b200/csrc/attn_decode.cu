@@ -47,8 +47,10 @@ struct AttnArgs {
   void* vc;
   const float* sinks;    // [nq]
   uint16_t* out;         // bf16 [nq, D]
-  float* part;           // [nkv, S, G, D + 2]
-  unsigned* counters;    // [nkv]
+  float* part;           // [batch][nkv, S, G, D + 2]
+  unsigned* counters;    // [batch][nkv]
+  const int32_t* slots;  // [batch] cache slot of each row (nullptr: slot 0)
+  int64_t slot_stride;   // cache elements between slots
   int32_t* err;
   int nq, nkv, G, S, max_seq, window, cs_max;
   float scale;
@@ -86,8 +88,22 @@ __device__ __forceinline__ float bf(uint16_t b) { return __uint_as_float(static_
 __device__ __forceinline__ float round_bf16(float x) { return bf(f32_to_bf16_bits(x)); }
 
 template <bool FP8>
-__global__ void __launch_bounds__(kThreads) gqa_decode_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kThreads) gqa_decode_kernel(const AttnArgs a0) {
   extern __shared__ float sm[];
+  // batch row b: its token's projections, position, cache slot, output and scratch
+  AttnArgs a = a0;
+  {
+    const int b = blockIdx.z;
+    const int64_t slot = a0.slots ? a0.slots[b] : 0;
+    constexpr int EB0 = FP8 ? 1 : 2;
+    a.qkv = a0.qkv + (int64_t)b * (a0.nq + 2 * a0.nkv) * kD;
+    a.pos = a0.pos + b;
+    a.out = a0.out + (int64_t)b * a0.nq * kD;
+    a.kc = static_cast<uint8_t*>(a0.kc) + slot * a0.slot_stride * EB0;
+    a.vc = static_cast<uint8_t*>(a0.vc) + slot * a0.slot_stride * EB0;
+    a.part = a0.part + (int64_t)b * a0.nkv * a0.S * a0.G * (kD + 2);
+    a.counters = a0.counters + (int64_t)b * a0.nkv;
+  }
   const int G = a.G, h = blockIdx.y, s = blockIdx.x;
   float* qs = sm;                 // [G][D]
   float* knew = qs + G * kD;      // [D]
@@ -500,7 +516,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_bf16_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kGemvWarps * 32, MODE == GV_PLAIN ? 4 : 3) gemv_bf16_kernel(GemvArgs a) {
   extern __shared__ float xs[];
   __shared__ float red[kGemvWarps];
   __shared__ int s_last;
@@ -515,12 +531,16 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_bf16_kernel(GemvArgs 
     const int c = u * 32 + lane;
     w[u] = c < nc ? __ldcs(row + c) : make_uint4(0, 0, 0, 0);
   }
+  if constexpr (MODE == GV_NORM) {
+    // the norm weights are constants too: staged before the wait
+    stage_sum_f32(xs + K, a.norm_w, nullptr, nullptr, K);
+  }
   pdl_wait();
   pdl_launch_dependents();
   if constexpr (MODE == GV_NORM) {
     const float ss = stage_sum_f32(xs, a.x_in, a.delta, blockIdx.x == 0 ? a.x_out : nullptr, K);
     const float inv = rsqrtf(block_sum(ss, red) / K + a.eps);
-    apply_norm(xs, a.norm_w, inv, K, nullptr);
+    apply_norm(xs, xs + K, inv, K, nullptr);
   } else {
     stage_bf16_f32(xs, a.x, K);
   }
@@ -616,25 +636,37 @@ int attn_slices(int max_seq) {
 
 using namespace tsb;
 
-extern "C" size_t tsb_gqa_decode_workspace(int32_t n_q_heads, int32_t n_kv_heads, int32_t max_seq) {
-  if (n_q_heads <= 0 || n_kv_heads <= 0 || max_seq <= 0 || n_q_heads % n_kv_heads) return 0;
-  const int S = attn_slices(max_seq), G = n_q_heads / n_kv_heads;
-  return 256 + sizeof(float) * (size_t)n_kv_heads * S * G * (kD + 2);
+static size_t attn_ws_bytes(int nq, int nkv, int max_seq, int batch) {
+  if (nq <= 0 || nkv <= 0 || max_seq <= 0 || batch <= 0 || nq % nkv) return 0;
+  const int S = attn_slices(max_seq), G = nq / nkv;
+  const size_t cnt = ((size_t)batch * nkv * 4 + 255) & ~size_t(255);
+  return 256 + cnt + sizeof(float) * (size_t)batch * nkv * S * G * (kD + 2);
 }
 
-extern "C" int tsb_gqa_decode_attention(const void* qkv, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
-                                        const void* cos, const void* sin, const int64_t* pos, void* k_cache,
-                                        void* v_cache, int32_t cache_fp8, int32_t max_seq, int32_t window,
-                                        const float* sinks, float scale, void* out, void* workspace,
-                                        size_t workspace_bytes, void* stream) {
+extern "C" size_t tsb_gqa_decode_batch_workspace(int32_t n_q_heads, int32_t n_kv_heads, int32_t max_seq, int32_t batch) {
+  return attn_ws_bytes(n_q_heads, n_kv_heads, max_seq, batch);
+}
+
+extern "C" size_t tsb_gqa_decode_workspace(int32_t n_q_heads, int32_t n_kv_heads, int32_t max_seq) {
+  return attn_ws_bytes(n_q_heads, n_kv_heads, max_seq, 1);
+}
+
+extern "C" int tsb_gqa_decode_attention_batch(const void* qkv, int32_t n_q_heads, int32_t n_kv_heads,
+                                              int32_t head_dim, const void* cos, const void* sin, const int64_t* pos,
+                                              const int32_t* slots, int64_t slot_stride, void* k_cache,
+                                              void* v_cache, int32_t cache_fp8, int32_t max_seq, int32_t window,
+                                              const float* sinks, float scale, void* out, int32_t batch,
+                                              void* workspace, size_t workspace_bytes, void* stream) {
   if (!qkv || !cos || !sin || !pos || !k_cache || !v_cache || !sinks || !out || !workspace)
     return set_error(TSB_ERR_INVALID, "null pointer");
   if (head_dim != kD) return set_error(TSB_ERR_UNSUPPORTED, "head_dim must be 64");
   if (n_kv_heads <= 0 || n_q_heads <= 0 || n_q_heads % n_kv_heads || n_q_heads / n_kv_heads > 16 || n_kv_heads > 65535)
     return set_error(TSB_ERR_INVALID, "n_q_heads must be a multiple of n_kv_heads, at most 16 per KV head");
   if (max_seq <= 0 || window < 0) return set_error(TSB_ERR_INVALID, "bad max_seq / window");
+  if (batch <= 0 || batch > 65535) return set_error(TSB_ERR_INVALID, "batch must be in [1, 65535]");
+  if (slots && slot_stride < (int64_t)n_kv_heads * max_seq * kD) return set_error(TSB_ERR_INVALID, "slot_stride too small");
   if (cache_fp8 != 0 && cache_fp8 != 1) return set_error(TSB_ERR_INVALID, "cache_fp8 must be 0 or 1");
-  if (workspace_bytes < tsb_gqa_decode_workspace(n_q_heads, n_kv_heads, max_seq))
+  if (workspace_bytes < attn_ws_bytes(n_q_heads, n_kv_heads, max_seq, batch))
     return set_error(TSB_ERR_WORKSPACE, "workspace too small");
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return set_error(TSB_ERR_INVALID, "workspace must be 256-byte aligned");
   AttnArgs a{};
@@ -646,10 +678,12 @@ extern "C" int tsb_gqa_decode_attention(const void* qkv, int32_t n_q_heads, int3
   a.vc = v_cache;
   a.sinks = sinks;
   a.out = static_cast<uint16_t*>(out);
+  a.slots = slots;
+  a.slot_stride = slot_stride;
   char* ws = static_cast<char*>(workspace);
   a.err = reinterpret_cast<int32_t*>(ws);
-  a.counters = reinterpret_cast<unsigned*>(ws + 4);
-  a.part = reinterpret_cast<float*>(ws + 256);
+  a.counters = reinterpret_cast<unsigned*>(ws + 256);
+  a.part = reinterpret_cast<float*>(ws + 256 + (((size_t)batch * n_kv_heads * 4 + 255) & ~size_t(255)));
   a.nq = n_q_heads;
   a.nkv = n_kv_heads;
   a.G = n_q_heads / n_kv_heads;
@@ -658,21 +692,31 @@ extern "C" int tsb_gqa_decode_attention(const void* qkv, int32_t n_q_heads, int3
   a.window = window;
   a.cs_max = (max_seq + a.S - 1) / a.S;
   a.scale = scale;
-  if (n_kv_heads > 60) return set_error(TSB_ERR_UNSUPPORTED, "at most 60 KV heads (counter space)");
   const size_t rowb = (cache_fp8 ? kD : 2 * kD) + 16;
   const size_t smem = sizeof(float) * ((size_t)a.G * kD + 2 * kD + (size_t)a.G * a.cs_max) + 16 + 2 * rowb * a.cs_max;
   if (smem > 200 * 1024) return set_error(TSB_ERR_UNSUPPORTED, "max_seq too large for the decode-attention slices");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid(a.S, n_kv_heads, batch);
   cudaError_t e;
   if (cache_fp8) {
     if (smem > 48 * 1024) cudaFuncSetAttribute(gqa_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    e = launch_pdl(gqa_decode_kernel<true>, dim3(a.S, n_kv_heads), kThreads, smem, st, a);
+    e = launch_pdl(gqa_decode_kernel<true>, grid, kThreads, smem, st, a);
   } else {
     if (smem > 48 * 1024) cudaFuncSetAttribute(gqa_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    e = launch_pdl(gqa_decode_kernel<false>, dim3(a.S, n_kv_heads), kThreads, smem, st, a);
+    e = launch_pdl(gqa_decode_kernel<false>, grid, kThreads, smem, st, a);
   }
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
   return TSB_OK;
+}
+
+extern "C" int tsb_gqa_decode_attention(const void* qkv, int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim,
+                                        const void* cos, const void* sin, const int64_t* pos, void* k_cache,
+                                        void* v_cache, int32_t cache_fp8, int32_t max_seq, int32_t window,
+                                        const float* sinks, float scale, void* out, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  return tsb_gqa_decode_attention_batch(qkv, n_q_heads, n_kv_heads, head_dim, cos, sin, pos, nullptr, 0, k_cache,
+                                        v_cache, cache_fp8, max_seq, window, sinks, scale, out, 1, workspace,
+                                        workspace_bytes, stream);
 }
 
 extern "C" int tsb_add_rmsnorm(float* x, const void* delta, int32_t delta_dtype, const float* weight, float eps,
@@ -695,7 +739,7 @@ static int run_gemv(int mode, GemvArgs a, void* stream) {
   if (a.N <= 0 || a.K <= 0 || a.K % 8 || a.K > 16384) return set_error(TSB_ERR_INVALID, "N must be positive, K a positive multiple of 8 up to 16384");
   if (reinterpret_cast<uintptr_t>(a.W) & 15) return set_error(TSB_ERR_INVALID, "weight must be 16-byte aligned");
   if (mode == GV_RESIDUAL && (a.N > 16384 || a.N % 4)) return set_error(TSB_ERR_INVALID, "N must be a multiple of 4, <= 16384, for the residual form");
-  const int smem_elems = mode == GV_RESIDUAL ? (a.K > a.N ? a.K : a.N) : a.K;
+  const int smem_elems = mode == GV_RESIDUAL ? (a.K > a.N ? a.K : a.N) : (mode == GV_NORM ? 2 * a.K : a.K);
   const size_t smem = sizeof(float) * smem_elems;
   const dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps);
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -121,14 +121,15 @@ class GptOssDecoder:
         return 2 * self.k_cache.numel() * self.k_cache.element_size()
 
     # ------------------------------------------------------------------ layers
-    def _attn(self, li: int, q: torch.Tensor, pos0: int, T: int, ctx: int):
+    def _attn(self, li: int, q: torch.Tensor, pos0: int, T: int, ctx: int, kc: torch.Tensor, vc: torch.Tensor):
         """Prompt attention: q [nq, T, D] (roped) for positions pos0..pos0+T-1
-        against cached keys [0, ctx); returns [T, nq*D] bf16."""
+        against the layer's cached keys kc / vc [nkv, S, D] at [0, ctx); returns
+        [T, nq*D] bf16."""
         lay = self.layers[li]
         G = self.nq // self.nkv
         # cached values widened exactly (e4m3 and bf16 are subsets of fp32)
-        K = self.k_cache[li, :, :ctx].float()  # [nkv, ctx, D]
-        V = self.v_cache[li, :, :ctx].float()
+        K = kc[:, :ctx].float()  # [nkv, ctx, D]
+        V = vc[:, :ctx].float()
         qg = q.reshape(self.nkv, G * T, self.D)
         s = torch.matmul(qg.float(), K.transpose(1, 2)).mul_(self.scale)  # [nkv, G*T, ctx]
         s = s.view(self.nkv, G, T, ctx)
@@ -152,7 +153,8 @@ class GptOssDecoder:
             x.data_ptr(), None if delta is None else delta.data_ptr(), dt, w.data_ptr(), self.eps, x.shape[0],
             self.H, out.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream))
 
-    def _prefill_layer(self, li: int, x: torch.Tensor, h: torch.Tensor, pos0: int, nxt_w: torch.Tensor) -> None:
+    def _prefill_layer(self, li: int, x: torch.Tensor, h: torch.Tensor, pos0: int, nxt_w: torch.Tensor,
+                       kc: torch.Tensor, vc: torch.Tensor) -> None:
         """Prompt rows at positions pos0..: x fp32 residual [T, H] (in/out), h the
         bf16 RMSNorm of x on entry, replaced by the next sublayer's norm input."""
         lay = self.layers[li]
@@ -164,9 +166,9 @@ class GptOssDecoder:
         v = qkv[:, (nq + nkv) * D:].view(T, nkv, D).transpose(0, 1)
         cos, sin = self.cos[pos0:pos0 + T], self.sin[pos0:pos0 + T]
         q, k = _rope(q, cos, sin), _rope(k, cos, sin)
-        self.k_cache[li, :, pos0:pos0 + T] = k.to(self.kv_dtype)
-        self.v_cache[li, :, pos0:pos0 + T] = v.to(self.kv_dtype)
-        a = self._attn(li, q, pos0, T, pos0 + T)
+        kc[:, pos0:pos0 + T] = k.to(self.kv_dtype)
+        vc[:, pos0:pos0 + T] = v.to(self.kv_dtype)
+        a = self._attn(li, q, pos0, T, pos0 + T, kc, vc)
         self._norm(x, F.linear(a, lay["wo"], lay["bo"]), lay["ln2"], h)
         y, _, _ = lay["moe"].decode(h, out_dtype=torch.float32)
         self._norm(x, y, nxt_w, h)
@@ -176,9 +178,13 @@ class GptOssDecoder:
 
     # ------------------------------------------------------------------ API
     @torch.no_grad()
-    def prefill(self, ids: torch.Tensor) -> torch.Tensor:
-        """Run prompt ids (1-D) from position 0, filling the cache; returns the
-        logits of the last prompt token (fp32 [V])."""
+    def prefill(self, ids: torch.Tensor, k_cache: torch.Tensor | None = None,
+                v_cache: torch.Tensor | None = None) -> torch.Tensor:
+        """Run prompt ids (1-D) from position 0, filling the cache (this
+        decoder's, or the given [L, nkv, S, D] caches); returns the logits of
+        the last prompt token (fp32 [V])."""
+        kc_all = self.k_cache if k_cache is None else k_cache
+        vc_all = self.v_cache if v_cache is None else v_cache
         ids = ids.reshape(-1).to(self.device)
         n = ids.numel()
         if n > self.max_seq:
@@ -189,9 +195,10 @@ class GptOssDecoder:
             h = torch.empty(x.shape, dtype=torch.bfloat16, device=self.device)
             self._norm(x, None, self.layers[0]["ln1"], h)
             for li in range(self.L):
-                self._prefill_layer(li, x, h, p0, self._next_norm(li))
+                self._prefill_layer(li, x, h, p0, self._next_norm(li), kc_all[li], vc_all[li])
             last = h[-1:]
-        self.length = n
+        if k_cache is None:
+            self.length = n
         return F.linear(last, self.lm_head)[0].float()
 
     def _step(self):
