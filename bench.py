@@ -366,7 +366,33 @@ def run_config3(dev, steps: int = 64, warmup: int = 8, ctx: int = C3_CTX):
            "c3_moe_bytes": moe_b, "c3_kv": "float8_e4m3fn", "c3_prefill_s": prefill_s, "c3_build_s": build_s,
            "c3_launch": "one CUDA graph per token",
            "c3_errors": int(sum(q.device_error() for q in lm.moe_layers))}
-    del dec, lm
+    del dec
+    torch.cuda.empty_cache()
+    # several requests at once: 64 requests with 128-token prompts decoding in
+    # lockstep through ServingEngine (batched attention over per-request FP8
+    # cache slots, one expert-layer call per step with T = 64)
+    from tinyserve_b200.serving import ServingEngine
+    B, P, NEW = 64, 128, 24
+    eng = ServingEngine(lm.model, lm.moe_layers, max_batch=B, max_seq=P + NEW + 8)
+    g = torch.Generator().manual_seed(1)
+    for _ in range(B):
+        eng.submit(torch.randint(0, cfg.vocab_size, (P,), generator=g), NEW)
+    eng.step()  # admits (prefills) every request and runs the first batched step
+    for _ in range(3):
+        eng.step()
+    torch.cuda.synchronize(dev)
+    n_steps = 16
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(n_steps):
+        assert eng.step() == B
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms_b = e0.elapsed_time(e1) / n_steps
+    out.update({"c3_batch64_tok_s": B * 1e3 / ms_b, "c3_batch64_ms_per_step": ms_b,
+                "c3_batch64": f"{B} requests x {P}-token prompts, greedy, ServingEngine.step (eager, one host sync "
+                              "per step for the sampled tokens)"})
+    del eng, lm
     torch.cuda.empty_cache()
     return out
 
