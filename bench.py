@@ -1056,6 +1056,11 @@ def main():
         ep = run_ep(dev, ws, rank)
         torch.cuda.empty_cache()
         pf.update({f"ep_{k}": (round(v, 4) if isinstance(v, float) else v) for k, v in ep.items()})
+        if rank == 0 and ws == 1:
+            # BASELINE config 3 (whole GPT-OSS-20B decode at context 4096) and a
+            # 64-request serving step, on the single-GPU run
+            pf.update(run_config3(dev))
+            torch.cuda.empty_cache()
         res["prefill"] = pf
     if host is not None:
         res["cpu_baseline"] = cpu_baselines(host, router_cpu, xs, dev)
