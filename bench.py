@@ -311,6 +311,70 @@ PREFILL_T = 4096
 C3_CTX = 4096  # decode at context 4096
 
 
+def _config3_breakdown(dec) -> dict:
+    """Microseconds per layer of each launch of GptOssDecoder's step (and of
+    the LM head per token): 24 calls of one kind captured in a CUDA graph on
+    the decoder's own buffers at its current position, CUDA events around 3
+    replays."""
+    import torch
+    import torch.nn.functional as F
+    from tinyserve_b200 import _lib
+    L = _lib.lib()
+    fp8 = 1 if dec.kv_dtype == torch.float8_e4m3fn else 0
+
+    def sid():
+        return torch.cuda.current_stream(dec.device).cuda_stream
+
+    def qkv():
+        for lay in dec.layers:
+            L.tsb_norm_gemv_bf16(dec._xa.data_ptr(), dec._y.data_ptr(), dec._xb.data_ptr(), lay["ln1"].data_ptr(),
+                                 dec.eps, lay["wqkv"].data_ptr(), lay["bqkv"].data_ptr(), lay["wqkv"].shape[0], dec.H,
+                                 dec._qkv.data_ptr(), sid())
+
+    def attn():
+        for li, lay in enumerate(dec.layers):
+            L.tsb_gqa_decode_attention(dec._qkv.data_ptr(), dec.nq, dec.nkv, dec.D, dec.cos.data_ptr(),
+                                       dec.sin.data_ptr(), dec._pos.data_ptr(), dec.k_cache[li].data_ptr(),
+                                       dec.v_cache[li].data_ptr(), fp8, dec.max_seq,
+                                       dec.window if dec.sliding[li] else 0, lay["sinks"].data_ptr(), dec.scale,
+                                       dec._a.data_ptr(), dec._aws.data_ptr(), dec._aws.numel(), sid())
+
+    def oproj():
+        for lay in dec.layers:
+            L.tsb_gemv_bf16_residual(lay["wo"].data_ptr(), lay["bo"].data_ptr(), dec.H, dec.nq * dec.D,
+                                     dec._a.data_ptr(), dec._xb.data_ptr(), lay["ln2"].data_ptr(), dec.eps,
+                                     dec._h.data_ptr(), dec._cnt.data_ptr(), sid())
+
+    def experts():
+        for lay in dec.layers:
+            lay["moe"].decode(dec._h, out=dec._y)
+
+    def head():
+        F.linear(dec._h, dec.lm_head)
+
+    res = {}
+    st = torch.cuda.Stream(dec.device)
+    for name, fn, per in (("qkv_norm_gemv", qkv, 24), ("attention", attn, 24), ("o_residual_gemv", oproj, 24),
+                          ("expert_layer", experts, 24), ("lm_head", head, 1)):
+        with torch.cuda.stream(st):
+            fn()
+            torch.cuda.synchronize(dec.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=st):
+                fn()
+            g.replay()
+            torch.cuda.synchronize(dec.device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(3):
+                g.replay()
+            e1.record(st)
+        torch.cuda.synchronize(dec.device)
+        res[name] = e0.elapsed_time(e1) * 1e3 / 3 / per
+        del g
+    return res
+
+
 def run_config3(dev, steps: int = 64, warmup: int = 8, ctx: int = C3_CTX):
     """the whole GPT-OSS-20B architecture (24 layers, 32
     MXFP4 experts, top-4, 64/8 heads of 64, alternating 128-token sliding and
@@ -366,6 +430,7 @@ def run_config3(dev, steps: int = 64, warmup: int = 8, ctx: int = C3_CTX):
            "c3_moe_bytes": moe_b, "c3_kv": "float8_e4m3fn", "c3_prefill_s": prefill_s, "c3_build_s": build_s,
            "c3_launch": "one CUDA graph per token",
            "c3_errors": int(sum(q.device_error() for q in lm.moe_layers))}
+    out.update({f"c3_us_{k}": v for k, v in _config3_breakdown(dec).items()})
     del dec
     torch.cuda.empty_cache()
     # several requests at once: 64 requests with 128-token prompts decoding in
