@@ -275,3 +275,26 @@ def test_prefill_config4_full_shape(dev):
         tok, kk = np.nonzero(idl == e)
         ref[tok] += wl[tok, kk][:, None] * OE.expert_forward(xs[tok], wg, wu, wd)
     assert_layer(out[torch.from_numpy(sample).to(dev)], ref)
+
+
+@pytest.mark.parametrize("E,T", [(128, 1), (128, 3), (32, 64), (128, 257)])
+def test_standalone_router_matches_oracle(dev, E, T):
+    """tsb_moe_route (the router of the grouped path and of expert
+    parallelism), including the GPT-OSS-120B expert count, against the
+    oracle's routing; near-ties may order differently."""
+    from tinyserve_b200.moe import Router
+    H, k = 2880, 4
+    g = torch.Generator().manual_seed(E + T)
+    w = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16)
+    b = torch.randn(E, generator=g) * 0.01
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    ids, wts = Router(w.to(dev), k, b.to(dev))(x.to(dev))
+    torch.cuda.synchronize()
+    ids_o, wts_o, lg = OE.router_topk_softmax(x.float().numpy(), w.float().numpy(), k, bias=b.double().numpy())
+    ids_g, wts_g = ids.cpu().numpy(), wts.cpu().numpy()
+    for t in range(T):
+        if list(ids_g[t]) != list(ids_o[t]):
+            srt = np.sort(lg[t])[::-1]
+            assert abs(srt[k - 1] - srt[k]) <= 1e-2 * abs(srt[k - 1]) + 1e-6, "routing differs away from a tie"
+        else:
+            np.testing.assert_allclose(wts_g[t], wts_o[t], rtol=2e-6, atol=1e-7)

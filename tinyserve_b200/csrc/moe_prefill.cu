@@ -937,41 +937,76 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
 }
 
 // ------------------------------------------------------------------ router (T tokens)
-// One warp per token: logits[e] = bf16(x . W[e] + b[e]) for all E experts
-// (kept in shared memory), then top-k (ties -> lower id, NaN lowest) and a
-// softmax over the k selected logits, the decode router's rule
-// (tinyserve/_model_hooks.py:466-473).
-__global__ void __launch_bounds__(128) prefill_router_kernel(const uint16_t* __restrict__ x,
-                                                             const uint16_t* __restrict__ W,
-                                                             const float* __restrict__ b, int H, int E, int T,
-                                                             int top_k, int32_t* __restrict__ ids,
-                                                             float* __restrict__ wts) {
-  extern __shared__ float slog[];  // [4][E]
+// One 16-warp CTA per token: x staged once in shared memory, warp w computes
+// logits[e] = bf16(x . W[e] + b[e]) for experts w, w + 16, ... two at a time
+// with all of a lane's loads of both rows in flight (a token's logits cost a
+// few memory round trips, not one per expert); then warp 0 takes the top-k
+// (ties -> lower id, NaN lowest) and a softmax over the k selected logits, the
+// decode router's rule (tinyserve/_model_hooks.py:466-473).
+constexpr int kRouteThreads = 512;
+
+__global__ void __launch_bounds__(kRouteThreads, 2) prefill_router_kernel(const uint16_t* __restrict__ x,
+                                                                       const uint16_t* __restrict__ W,
+                                                                       const float* __restrict__ b, int H, int E,
+                                                                       int T, int top_k, int32_t* __restrict__ ids,
+                                                                       float* __restrict__ wts) {
+  extern __shared__ float slog[];  // [E] logits, then x as uint4 [H / 8]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 4 + warp;
-  if (t >= T) return;
-  float* lg = slog + warp * E;
+  const int t = blockIdx.x;
+  float* lg = slog;
+  uint4* xs = reinterpret_cast<uint4*>(slog + ((E + 3) & ~3));
   const int n8 = H / 8;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)t * H);
-  for (int e = 0; e < E; ++e) {
-    const uint4* wr = reinterpret_cast<const uint4*>(W + (int64_t)e * H);
-    float acc = 0.f;
-    for (int c = lane; c < n8; c += 32) {
-      const uint4 a = xr[c], w = __ldg(wr + c);
-      const uint32_t av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
+  for (int c = threadIdx.x; c < n8; c += kRouteThreads) xs[c] = xr[c];
+  __syncthreads();
+  auto dot8 = [](uint4 a, uint4 w, float acc) {
+    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        acc = fmaf(__uint_as_float(av[q] << 16), __uint_as_float(wv[q] << 16), acc);
-        acc = fmaf(__uint_as_float(av[q] & 0xFFFF0000u), __uint_as_float(wv[q] & 0xFFFF0000u), acc);
+    for (int q = 0; q < 4; ++q) {
+      acc = fmaf(__uint_as_float(av[q] << 16), __uint_as_float(wv[q] << 16), acc);
+      acc = fmaf(__uint_as_float(av[q] & 0xFFFF0000u), __uint_as_float(wv[q] & 0xFFFF0000u), acc);
+    }
+    return acc;
+  };
+  for (int e0 = warp; e0 < E; e0 += 2 * (kRouteThreads / 32)) {
+    const int e1 = e0 + kRouteThreads / 32;
+    const uint4* w0 = reinterpret_cast<const uint4*>(W + (int64_t)e0 * H);
+    const uint4* w1 = reinterpret_cast<const uint4*>(W + (int64_t)(e1 < E ? e1 : e0) * H);
+    float a0 = 0.f, a1 = 0.f;
+    for (int c0 = 0; c0 < n8; c0 += 4 * 32) {
+      uint4 r0[4], r1[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + u * 32 + lane;
+        r0[u] = c < n8 ? __ldg(w0 + c) : make_uint4(0, 0, 0, 0);
+        r1[u] = c < n8 ? __ldg(w1 + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < n8) {
+          const uint4 xv = xs[c];
+          a0 = dot8(xv, r0[u], a0);
+          a1 = dot8(xv, r1[u], a1);
+        }
       }
     }
 #pragma unroll
-    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    for (int o = 16; o; o >>= 1) {
+      a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+      a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+    }
     if (lane == 0) {
-      if (b) acc += b[e];
-      lg[e] = bf16_bits_to_f32(f32_to_bf16_bits(acc));
+      if (b) a0 += b[e0];
+      lg[e0] = bf16_bits_to_f32(f32_to_bf16_bits(a0));
+      if (e1 < E) {
+        if (b) a1 += b[e1];
+        lg[e1] = bf16_bits_to_f32(f32_to_bf16_bits(a1));
+      }
     }
   }
+  __syncthreads();
+  if (warp != 0) return;
   __syncwarp();
   float sel[8];
   int sid[8];
@@ -1155,8 +1190,9 @@ static int launch_gemm_pair(const GemmArgs& g, int tiles_max, cudaStream_t st) {
 
 int launch_route(const TsbMoeSpec& sp, const void* x, int T, const void* rw, const float* rb, int32_t* ids,
                  float* wts, cudaStream_t st) {
-  const size_t sm = 4 * sizeof(float) * (size_t)sp.n_experts;
-  prefill_router_kernel<<<(T + 3) / 4, 128, sm, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(rw),
+  const size_t sm = sizeof(float) * (size_t)((sp.n_experts + 3) & ~3) + 2 * (size_t)sp.hidden;
+  if (sm > 48 * 1024) cudaFuncSetAttribute(prefill_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  prefill_router_kernel<<<T, kRouteThreads, sm, st>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(rw),
                                                        rb, sp.hidden, sp.n_experts, T, sp.top_k, ids, wts);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
