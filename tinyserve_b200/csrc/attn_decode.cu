@@ -627,8 +627,10 @@ cudaError_t launch_pdl(Kern k, dim3 grid, int block, size_t smem, cudaStream_t s
 
 }  // namespace
 
+// Position slices per KV head: about 128 positions each (8 KV heads x 33
+// slices = 264 CTAs at a 4 K context, two per SM), at most 64.
 int attn_slices(int max_seq) {
-  int S = (max_seq + 255) / 256;
+  int S = (max_seq + 127) / 128;
   return S < 1 ? 1 : (S > 64 ? 64 : S);
 }
 
