@@ -319,6 +319,19 @@ int tsb_gqa_decode_attention_batch(const void* qkv, int32_t n_q_heads, int32_t n
                                    int64_t slot_stride, void* k_cache, void* v_cache, int32_t cache_fp8,
                                    int32_t max_seq, int32_t window, const float* sinks, float scale, void* out,
                                    int32_t batch, void* workspace, size_t workspace_bytes, void* stream);
+/* RMSNorm + fused q|k|v projection + tsb_gqa_decode_attention in one launch
+ * (thread-block clusters of 8 or 16 CTAs per KV head exchange the head
+ * group's projections through distributed shared memory): x_in / delta /
+ * x_out / norm_weight as tsb_norm_gemv_bf16, weight / bias the bf16 q|k|v
+ * projection [(n_q + 2 n_kv) * head_dim, hidden] (16-byte aligned), the rest
+ * as tsb_gqa_decode_attention; no workspace.  TSB_ERR_UNSUPPORTED when the
+ * shape does not fit the kernel's shared memory (callers then use the two
+ * separate entry points). */
+int tsb_norm_qkv_attention(const float* x_in, const float* delta, float* x_out, const float* norm_weight, float eps,
+                           const void* weight, const void* bias, int32_t hidden, int32_t n_q_heads,
+                           int32_t n_kv_heads, int32_t head_dim, const void* cos, const void* sin,
+                           const int64_t* pos, void* k_cache, void* v_cache, int32_t cache_fp8, int32_t max_seq,
+                           int32_t window, const float* sinks, float scale, void* out, void* stream);
 /* y = bf16(W x + bias): one bf16 [N, K] weight (16-byte aligned, K % 8 == 0,
  * K <= 16384), bf16 x [K], optional bf16 bias [N], bf16 y [N]; the batch-1
  * attention projections of the decode step (nn.Linear in the reference's

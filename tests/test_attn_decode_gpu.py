@@ -147,3 +147,54 @@ def test_norm_gemv_and_residual_gemv(dev):
         hr = nw.double() * resid.double() * torch.rsqrt(resid.double().pow(2).mean() + 1e-5)
         assert ((h.double() - hr).norm() / hr.norm()).item() < 4e-3
         assert int(cnt.item()) == 0
+
+
+@pytest.mark.parametrize("fp8", [True, False])
+@pytest.mark.parametrize("pos,window", [(3, 0), (2000, 0), (2000, 128)])
+def test_fused_norm_qkv_attention_matches_two_launches(dev, fp8, pos, window):
+    """tsb_norm_qkv_attention (clusters per KV head, projections exchanged in
+    distributed shared memory) against tsb_norm_gemv_bf16 followed by
+    tsb_gqa_decode_attention on the same inputs: the residual and the cached
+    key/value bytes identical, the attention output within bf16 rounding."""
+    L = _lib.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    nq, nkv, D, H, S = 64, 8, 64, 2880, 4096
+    g = torch.Generator(device=dev).manual_seed(pos + window + fp8)
+    x_in = torch.randn(H, generator=g, device=dev)
+    delta = torch.randn(H, generator=g, device=dev)
+    nw = torch.rand(H, generator=g, device=dev) + 0.5
+    W = (torch.randn((nq + 2 * nkv) * D, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    b = (torch.randn((nq + 2 * nkv) * D, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    ang = torch.arange(S, device=dev, dtype=torch.float32)[:, None] * (10000 ** (-torch.arange(D // 2, device=dev) / (D // 2)))
+    cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    kdt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    k0 = (torch.randn(nkv, S, D, generator=g, device=dev) * 2).to(kdt)
+    v0 = torch.randn(nkv, S, D, generator=g, device=dev).to(kdt)
+    sinks = torch.randn(nq, generator=g, device=dev)
+    p = torch.tensor([pos], dtype=torch.int64, device=dev)
+    # two launches
+    kc1, vc1 = k0.clone(), v0.clone()
+    x1 = torch.empty(H, device=dev)
+    qkv = torch.empty((nq + 2 * nkv) * D, dtype=torch.bfloat16, device=dev)
+    out1 = torch.empty(nq * D, dtype=torch.bfloat16, device=dev)
+    ws = torch.zeros(L.tsb_gqa_decode_workspace(nq, nkv, S), dtype=torch.uint8, device=dev)
+    _lib.check(L.tsb_norm_gemv_bf16(x_in.data_ptr(), delta.data_ptr(), x1.data_ptr(), nw.data_ptr(), 1e-5,
+                                    W.data_ptr(), b.data_ptr(), W.shape[0], H, qkv.data_ptr(), st))
+    _lib.check(L.tsb_gqa_decode_attention(qkv.data_ptr(), nq, nkv, D, cos.data_ptr(), sin.data_ptr(), p.data_ptr(),
+                                          kc1.data_ptr(), vc1.data_ptr(), int(fp8), S, window, sinks.data_ptr(),
+                                          D ** -0.5, out1.data_ptr(), ws.data_ptr(), ws.numel(), st))
+    # one launch, twice (nothing carries over between calls)
+    for _ in range(2):
+        kc2, vc2 = k0.clone(), v0.clone()
+        x2 = torch.empty(H, device=dev)
+        out2 = torch.empty(nq * D, dtype=torch.bfloat16, device=dev)
+        _lib.check(L.tsb_norm_qkv_attention(x_in.data_ptr(), delta.data_ptr(), x2.data_ptr(), nw.data_ptr(), 1e-5,
+                                            W.data_ptr(), b.data_ptr(), H, nq, nkv, D, cos.data_ptr(), sin.data_ptr(),
+                                            p.data_ptr(), kc2.data_ptr(), vc2.data_ptr(), int(fp8), S, window,
+                                            sinks.data_ptr(), D ** -0.5, out2.data_ptr(), st))
+        torch.cuda.synchronize()
+        assert torch.equal(x2, x1)
+        bt = torch.uint8 if fp8 else torch.int16
+        assert torch.equal(kc2.view(bt), kc1.view(bt)) and torch.equal(vc2.view(bt), vc1.view(bt))
+        err = ((out2.double() - out1.double()).norm() / out1.double().norm()).item()
+        assert err < 5e-3, err

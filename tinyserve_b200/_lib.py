@@ -34,7 +34,7 @@ EXPORTS = (
     "tsb_moe_route", "tsb_ep_decode_workspace", "tsb_ep_moe_decode", "tsb_ep_prefill_workspace",
     "tsb_ep_moe_prefill", "tsb_gqa_decode_workspace", "tsb_gqa_decode_attention", "tsb_add_rmsnorm",
     "tsb_gemv_bf16", "tsb_norm_gemv_bf16", "tsb_gemv_bf16_residual", "tsb_gqa_decode_batch_workspace",
-    "tsb_gqa_decode_attention_batch",
+    "tsb_gqa_decode_attention_batch", "tsb_norm_qkv_attention",
 )
 
 
@@ -100,6 +100,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.tsb_gqa_decode_attention_batch.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i32, _i32,
                                                  _i32, _vp, ctypes.c_float, _vp, _i32, _vp, _sz, _vp]
     L.tsb_gemv_bf16.argtypes = [_vp, _vp, _i32, _i32, _vp, _vp, _vp]
+    L.tsb_norm_qkv_attention.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _i32, _i32, _i32, _i32, _vp,
+                                         _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, ctypes.c_float, _vp, _vp]
     L.tsb_norm_gemv_bf16.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _i32, _i32, _vp, _vp]
     L.tsb_gemv_bf16_residual.argtypes = [_vp, _vp, _i32, _i32, _vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp]
     L.tsb_add_rmsnorm.argtypes = [_vp, _vp, _i32, _vp, ctypes.c_float, _i32, _i32, _vp, _vp]

@@ -625,6 +625,315 @@ cudaError_t launch_pdl(Kern k, dim3 grid, int block, size_t smem, cudaStream_t s
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
+
+// ---------------------------------------------------------------------------
+// RMSNorm + q|k|v projection + decode attention of one token in one launch.
+// One thread-block cluster of CN CTAs per KV head h:
+//  1. every CTA normalises the residual (x_in + delta; CTA 0 of cluster 0
+//     stores it to x_out) and computes its share of the head group's
+//     (G + 2) * 64 projection rows (the group's q heads, its k and v rows),
+//     warp per row as in gemv_bf16_kernel, bf16-rounded with the bias;
+//  2. each row's value is stored into every CTA of the cluster (distributed
+//     shared memory), a cluster barrier makes the group's q/k/v complete in
+//     all of them;
+//  3. every CTA runs the decode attention of gqa_decode_kernel over its
+//     slice of the positions (the slice's cached K/V were staged in shared
+//     memory before the dependency wait), CTA 0 stores the new key/value;
+//  4. the slices' (max, sum, o) go to CTA 0's shared memory, a second
+//     cluster barrier, and CTA 0 merges them with the sink logits.
+// Every CTA passes both cluster barriers (no early exit once running), so no
+// barrier waits on a CTA that left.
+struct QkvAttnArgs {
+  const float* x_in;
+  const float* delta;
+  float* x_out;
+  const float* norm_w;
+  float eps;
+  const uint16_t* W;      // [(nq + 2 nkv) * D, H]
+  const uint16_t* bias;   // [(nq + 2 nkv) * D] or null
+  const uint16_t* cos;
+  const uint16_t* sin;
+  const int64_t* pos;
+  void* kc;
+  void* vc;
+  const float* sinks;
+  uint16_t* out;          // [nq * D]
+  int nq, nkv, G, H, CN, max_seq, window, cs_max;
+  float scale;
+};
+
+__device__ __forceinline__ void st_remote_f32(float* local, uint32_t rank, float v) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t my_cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_barrier_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <bool FP8>
+__global__ void __launch_bounds__(kThreads, 1) qkv_attn_kernel(const QkvAttnArgs a) {
+  extern __shared__ __align__(16) float sm2[];
+  const int G = a.G, H = a.H, CN = a.CN;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = (int)my_cluster_rank(), h = blockIdx.x / CN;
+  const int R = (G + 2) * kD;                       // projection rows of the head group
+  float* xs = sm2;                                  // [H] normalised input
+  float* nws = xs + H;                              // [H] norm weights
+  float* qkv = nws + H;                             // [R] the group's projections (all CTAs)
+  float* qs = qkv + R;                              // [G][D] roped q
+  float* knew = qs + G * kD;                        // [D]
+  float* vnew = knew + kD;                          // [D]
+  float* sc = vnew + kD;                            // [G][cs_max]
+  float* mrg = sc + G * a.cs_max;                   // [CN][G][D + 2] (read in CTA 0)
+  constexpr int EB = FP8 ? 1 : 2, RB = kD * EB + 16, C16 = kD * EB / 16;
+  uint8_t* ks = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(mrg + (size_t)CN * G * (kD + 2)) + 15) &
+                                           ~uintptr_t(15));
+  uint8_t* vs = ks + (size_t)a.cs_max * RB;
+  __shared__ float red[kThreads / 32];
+  __shared__ float s_m[16], s_l[16];
+  // this CTA is running: remote stores into it may start once every CTA of
+  // the cluster has arrived here (the wait comes before the first such store)
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  const int64_t pos = *a.pos;  // written before the graph / launch by the host
+  const bool pos_ok = pos >= 0 && pos < a.max_seq;
+  const int64_t lo64 = pos - a.window + 1;
+  const int lo = (a.window > 0 && lo64 > 0) ? (int)lo64 : 0;
+  const int len = pos_ok ? (int)pos - lo + 1 : 0;
+  const int cs = (len + CN - 1) / CN;
+  const int c0 = lo + c * cs, c1 = min((int)pos + 1, c0 + cs);
+  const int n = pos_ok ? max(0, c1 - c0) : 0;
+  const int64_t hb = (int64_t)h * a.max_seq * kD;
+  // ---- independent of the previous kernel: norm weights, the K/V slice
+  stage_sum_f32(nws, a.norm_w, nullptr, nullptr, H);
+  {
+    const uint8_t* kg = static_cast<const uint8_t*>(a.kc) + (hb + (int64_t)c0 * kD) * EB;
+    const uint8_t* vg = static_cast<const uint8_t*>(a.vc) + (hb + (int64_t)c0 * kD) * EB;
+    for (int base = 0; base < n * C16; base += 4 * kThreads) {
+      uint4 kv[4], vv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = base + u * kThreads + tid;
+        if (i < n * C16) {
+          const int j = i / C16, q = i % C16;
+          kv[u] = *reinterpret_cast<const uint4*>(kg + (size_t)j * kD * EB + q * 16);
+          vv[u] = *reinterpret_cast<const uint4*>(vg + (size_t)j * kD * EB + q * 16);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = base + u * kThreads + tid;
+        if (i < n * C16) {
+          const int j = i / C16, q = i % C16;
+          *reinterpret_cast<uint4*>(ks + (size_t)j * RB + q * 16) = kv[u];
+          *reinterpret_cast<uint4*>(vs + (size_t)j * RB + q * 16) = vv[u];
+        }
+      }
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  // ---- 1. RMSNorm of the residual
+  {
+    const float ss = stage_sum_f32(xs, a.x_in, a.delta, (h == 0 && c == 0) ? a.x_out : nullptr, H);
+    const float inv = rsqrtf(block_sum(ss, red) / H + a.eps);
+    apply_norm(xs, nws, inv, H, nullptr);
+  }
+  __syncthreads();
+  // ---- 1b. this CTA's projection rows, stored into every CTA of the cluster
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  const int rpc = (R + CN - 1) / CN;
+  const int nc = H / 8;
+  for (int lr = c * rpc + warp; lr < min(R, (c + 1) * rpc); lr += kThreads / 32) {
+    const int grow = lr < G * kD ? h * G * kD + lr
+                     : lr < (G + 1) * kD ? a.nq * kD + h * kD + (lr - G * kD)
+                                         : (a.nq + a.nkv) * kD + h * kD + (lr - (G + 1) * kD);
+    const uint4* row = reinterpret_cast<const uint4*>(a.W + (int64_t)grow * H);
+    float acc = 0.f;
+    for (int cb = 0; cb < nc; cb += 8 * 32) {
+      uint4 w[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int q = cb + u * 32 + lane;
+        w[u] = q < nc ? __ldcs(row + q) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int q = cb + u * 32 + lane;
+        if (q < nc) {
+          const float4* xv = reinterpret_cast<const float4*>(xs + 8 * q);
+          const float4 xa = xv[0], xb = xv[1];
+          acc = fmaf(__uint_as_float(w[u].x << 16), xa.x, acc);
+          acc = fmaf(__uint_as_float(w[u].x & 0xFFFF0000u), xa.y, acc);
+          acc = fmaf(__uint_as_float(w[u].y << 16), xa.z, acc);
+          acc = fmaf(__uint_as_float(w[u].y & 0xFFFF0000u), xa.w, acc);
+          acc = fmaf(__uint_as_float(w[u].z << 16), xb.x, acc);
+          acc = fmaf(__uint_as_float(w[u].z & 0xFFFF0000u), xb.y, acc);
+          acc = fmaf(__uint_as_float(w[u].w << 16), xb.z, acc);
+          acc = fmaf(__uint_as_float(w[u].w & 0xFFFF0000u), xb.w, acc);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    const float v = round_bf16(acc + (a.bias ? bf(a.bias[grow]) : 0.f));
+    for (int r = lane; r < CN; r += 32) st_remote_f32(qkv + lr, (uint32_t)r, v);
+  }
+  cluster_barrier_sync();  // the group's q/k/v are complete in every CTA
+  // ---- 3. attention over this CTA's slice (gqa_decode_kernel's steps)
+  if (pos_ok) {
+    const uint16_t* cr = a.cos + pos * (kD / 2);
+    const uint16_t* sr = a.sin + pos * (kD / 2);
+    for (int i = tid; i < (G + 2) * (kD / 2); i += kThreads) {
+      const int r = i / (kD / 2), d = i % (kD / 2);
+      if (r <= G) {
+        const float x1 = qkv[r * kD + d], x2 = qkv[r * kD + d + kD / 2];
+        const float cc = bf(cr[d]), sn = bf(sr[d]);
+        float y1 = x1 * cc - x2 * sn, y2 = x2 * cc + x1 * sn;
+        if (r < G) {
+          qs[r * kD + d] = y1;
+          qs[r * kD + d + kD / 2] = y2;
+        } else {
+          uint8_t b1, b2;
+          y1 = cache_round<FP8>(round_bf16(y1), &b1);
+          y2 = cache_round<FP8>(round_bf16(y2), &b2);
+          knew[d] = y1;
+          knew[d + kD / 2] = y2;
+          if (c == 0) {
+            const int64_t o = ((int64_t)h * a.max_seq + pos) * kD;
+            if constexpr (FP8) {
+              static_cast<uint8_t*>(a.kc)[o + d] = b1;
+              static_cast<uint8_t*>(a.kc)[o + d + kD / 2] = b2;
+            } else {
+              static_cast<uint16_t*>(a.kc)[o + d] = f32_to_bf16_bits(y1);
+              static_cast<uint16_t*>(a.kc)[o + d + kD / 2] = f32_to_bf16_bits(y2);
+            }
+          }
+        }
+      } else {
+        for (int dd = d; dd < kD; dd += kD / 2) {
+          uint8_t b;
+          const float v = cache_round<FP8>(qkv[(G + 1) * kD + dd], &b);
+          vnew[dd] = v;
+          if (c == 0) {
+            const int64_t o = ((int64_t)h * a.max_seq + pos) * kD + dd;
+            if constexpr (FP8)
+              static_cast<uint8_t*>(a.vc)[o] = b;
+            else
+              static_cast<uint16_t*>(a.vc)[o] = f32_to_bf16_bits(v);
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (pos >= c0 && pos < c1) {
+      const int j = (int)pos - c0;
+      for (int d = tid; d < kD; d += kThreads) {
+        if constexpr (FP8) {
+          ks[(size_t)j * RB + d] = __nv_cvt_float_to_fp8(knew[d], __NV_NOSAT, __NV_E4M3);
+          vs[(size_t)j * RB + d] = __nv_cvt_float_to_fp8(vnew[d], __NV_NOSAT, __NV_E4M3);
+        } else {
+          reinterpret_cast<uint16_t*>(ks + (size_t)j * RB)[d] = f32_to_bf16_bits(knew[d]);
+          reinterpret_cast<uint16_t*>(vs + (size_t)j * RB)[d] = f32_to_bf16_bits(vnew[d]);
+        }
+      }
+    }
+    __syncthreads();
+    for (int j = tid; j < n; j += kThreads) {
+      float kr[kD];
+#pragma unroll
+      for (int d = 0; d < kD; d += 2) {
+        const float2 k2 = load2<FP8>(ks + (size_t)j * RB, d);
+        kr[d] = k2.x;
+        kr[d + 1] = k2.y;
+      }
+      for (int g = 0; g < G; ++g) {
+        const float4* q4 = reinterpret_cast<const float4*>(qs + g * kD);
+        float acc = 0.f;
+#pragma unroll
+        for (int d4 = 0; d4 < kD / 4; ++d4) {
+          const float4 q = q4[d4];
+          acc = fmaf(q.x, kr[4 * d4], acc);
+          acc = fmaf(q.y, kr[4 * d4 + 1], acc);
+          acc = fmaf(q.z, kr[4 * d4 + 2], acc);
+          acc = fmaf(q.w, kr[4 * d4 + 3], acc);
+        }
+        sc[g * a.cs_max + j] = acc * a.scale;
+      }
+    }
+    __syncthreads();
+    for (int g = warp; g < G; g += kThreads / 32) {
+      float m = -INFINITY;
+      for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[g * a.cs_max + j]);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float l = 0.f;
+      for (int j = lane; j < n; j += 32) {
+        const float e = __expf(sc[g * a.cs_max + j] - m);
+        sc[g * a.cs_max + j] = e;
+        l += e;
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      if (lane == 0) {
+        s_m[g] = m;
+        s_l[g] = l;
+      }
+    }
+    __syncthreads();
+  }
+  // ---- 4. this slice's (o, max, sum) into CTA 0's shared memory
+  for (int g = warp; g < G; g += kThreads / 32) {
+    float o0 = 0.f, o1 = 0.f;
+    if (pos_ok) {
+      const float* pg = sc + g * a.cs_max;
+      for (int j = 0; j < n; ++j) {
+        const float2 va = load2<FP8>(vs + (size_t)j * RB, 2 * lane);
+        o0 = fmaf(pg[j], va.x, o0);
+        o1 = fmaf(pg[j], va.y, o1);
+      }
+    }
+    float* dst = mrg + ((size_t)c * G + g) * (kD + 2);
+    st_remote_f32(dst + 2 * lane, 0u, o0);
+    st_remote_f32(dst + 2 * lane + 1, 0u, o1);
+    if (lane == 0) {
+      st_remote_f32(dst + kD, 0u, pos_ok && n > 0 ? s_m[g] : -INFINITY);
+      st_remote_f32(dst + kD + 1, 0u, pos_ok && n > 0 ? s_l[g] : 0.f);
+    }
+  }
+  cluster_barrier_sync();
+  if (c != 0 || !pos_ok) return;
+  for (int g = warp; g < G; g += kThreads / 32) {
+    const float sink = a.sinks[h * G + g];
+    float M = sink;
+    for (int t = 0; t < CN; ++t) M = fmaxf(M, mrg[((size_t)t * G + g) * (kD + 2) + kD]);
+    float den = __expf(sink - M), o0 = 0.f, o1 = 0.f;
+    for (int t = 0; t < CN; ++t) {
+      const float* q = mrg + ((size_t)t * G + g) * (kD + 2);
+      const float w = q[kD + 1] > 0.f ? __expf(q[kD] - M) : 0.f;
+      den = fmaf(w, q[kD + 1], den);
+      o0 = fmaf(w, q[2 * lane], o0);
+      o1 = fmaf(w, q[2 * lane + 1], o1);
+    }
+    const float inv = 1.f / den;
+    uint16_t* o = a.out + (h * G + g) * kD;
+    o[2 * lane] = f32_to_bf16_bits(o0 * inv);
+    o[2 * lane + 1] = f32_to_bf16_bits(o1 * inv);
+  }
+}
+
+size_t qkv_attn_smem(int G, int H, int CN, int max_seq, bool fp8) {
+  const int cs_max = (max_seq + CN - 1) / CN;
+  const size_t rowb = (fp8 ? kD : 2 * kD) + 16;
+  return sizeof(float) * (2 * (size_t)H + (size_t)(G + 2) * kD + (size_t)G * kD + 2 * kD + (size_t)G * cs_max +
+                          (size_t)CN * G * (kD + 2)) + 16 + 2 * rowb * cs_max;
+}
+
 }  // namespace
 
 // Position slices per KV head: about 128 positions each (8 KV heads x 33
@@ -812,4 +1121,98 @@ extern "C" int tsb_gemv_bf16_residual(const void* weight, const void* bias, int3
   a.h_out = static_cast<uint16_t*>(h_out);
   a.counter = counter;
   return run_gemv(GV_RESIDUAL, a, stream);
+}
+
+extern "C" int tsb_norm_qkv_attention(const float* x_in, const float* delta, float* x_out, const float* norm_weight,
+                                      float eps, const void* weight, const void* bias, int32_t hidden,
+                                      int32_t n_q_heads, int32_t n_kv_heads, int32_t head_dim, const void* cos,
+                                      const void* sin, const int64_t* pos, void* k_cache, void* v_cache,
+                                      int32_t cache_fp8, int32_t max_seq, int32_t window, const float* sinks,
+                                      float scale, void* out, void* stream) {
+  if (!x_in || !x_out || !norm_weight || !weight || !cos || !sin || !pos || !k_cache || !v_cache || !sinks || !out)
+    return set_error(TSB_ERR_INVALID, "null pointer");
+  if (x_out == x_in || (delta && x_out == delta)) return set_error(TSB_ERR_INVALID, "x_out must not alias x_in or delta");
+  if (head_dim != kD) return set_error(TSB_ERR_UNSUPPORTED, "head_dim must be 64");
+  if (n_kv_heads <= 0 || n_q_heads <= 0 || n_q_heads % n_kv_heads || n_q_heads / n_kv_heads > 16)
+    return set_error(TSB_ERR_INVALID, "n_q_heads must be a multiple of n_kv_heads, at most 16 per KV head");
+  if (hidden <= 0 || hidden % 8 || hidden > 8192) return set_error(TSB_ERR_INVALID, "hidden must be a multiple of 8, <= 8192");
+  if (max_seq <= 0 || window < 0) return set_error(TSB_ERR_INVALID, "bad max_seq / window");
+  if (cache_fp8 != 0 && cache_fp8 != 1) return set_error(TSB_ERR_INVALID, "cache_fp8 must be 0 or 1");
+  if (reinterpret_cast<uintptr_t>(weight) & 15) return set_error(TSB_ERR_INVALID, "weight must be 16-byte aligned");
+  const int G = n_q_heads / n_kv_heads;
+  // cluster size: 16 CTAs per KV head when the device can co-schedule all
+  // of the grid's clusters that way, else 8 (the portable maximum)
+  int CN = 0;
+  size_t smem = 0;
+  auto kern = cache_fp8 ? qkv_attn_kernel<true> : qkv_attn_kernel<false>;
+  {
+    for (int cand : {16, 8}) {
+      const size_t sm = qkv_attn_smem(G, hidden, cand, max_seq, cache_fp8);
+      if (sm > 220 * 1024) continue;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      if (cand > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(n_kv_heads * cand);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = sm;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = cand;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters >= n_kv_heads) {
+        CN = cand;
+        break;
+      }
+      cudaGetLastError();
+    }
+  }
+  if (CN == 0) return set_error(TSB_ERR_UNSUPPORTED, "the fused q|k|v + attention kernel does not fit this shape");
+  smem = qkv_attn_smem(G, hidden, CN, max_seq, cache_fp8);
+  if (smem > 220 * 1024) return set_error(TSB_ERR_UNSUPPORTED, "max_seq too large for the fused kernel");
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  QkvAttnArgs a{};
+  a.x_in = x_in;
+  a.delta = delta;
+  a.x_out = x_out;
+  a.norm_w = norm_weight;
+  a.eps = eps;
+  a.W = static_cast<const uint16_t*>(weight);
+  a.bias = static_cast<const uint16_t*>(bias);
+  a.cos = static_cast<const uint16_t*>(cos);
+  a.sin = static_cast<const uint16_t*>(sin);
+  a.pos = pos;
+  a.kc = k_cache;
+  a.vc = v_cache;
+  a.sinks = sinks;
+  a.out = static_cast<uint16_t*>(out);
+  a.nq = n_q_heads;
+  a.nkv = n_kv_heads;
+  a.G = G;
+  a.H = hidden;
+  a.CN = CN;
+  a.max_seq = max_seq;
+  a.window = window;
+  a.cs_max = (max_seq + CN - 1) / CN;
+  a.scale = scale;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_kv_heads * CN);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CN;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess) return set_error(TSB_ERR_CUDA, cudaGetErrorString(e));
+  return TSB_OK;
 }

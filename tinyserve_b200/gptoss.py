@@ -26,6 +26,8 @@ replayed unchanged for every step.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F
 
@@ -93,6 +95,10 @@ class GptOssDecoder:
         self.v_cache = torch.zeros_like(self.k_cache)
         self.length = 0
         self._graph = None
+        # RMSNorm + q|k|v + attention as one clustered launch when the shape
+        # fits it (None: decided by the first step); TSB_DECODE_FUSED=0 keeps
+        # the two-launch form
+        self._fused = False if os.environ.get("TSB_DECODE_FUSED", "1") == "0" else None
         self._tok = torch.zeros(1, dtype=torch.long, device=dev)
         self._pos = torch.zeros(1, dtype=torch.long, device=dev)
         self._next = torch.zeros(1, dtype=torch.long, device=dev)
@@ -202,28 +208,45 @@ class GptOssDecoder:
         return F.linear(last, self.lm_head)[0].float()
 
     def _step(self):
-        """One decode token through every layer (the captured graph's body), four
-        launches per layer: RMSNorm + fused q|k|v GEMV (tsb_norm_gemv_bf16, which
-        also folds the previous expert output into the residual), the
-        decode-attention kernel (RoPE, cache store, sink attention), the o GEMV
-        adding into the residual and normalising it for the expert layer
-        (tsb_gemv_bf16_residual), and the expert layer (fp32 output)."""
+        """One decode token through every layer (the captured graph's body), three
+        launches per layer: RMSNorm (folding the previous expert output into
+        the residual) + q|k|v projection + attention (RoPE, cache store, sink
+        softmax) in one clustered kernel (tsb_norm_qkv_attention; or its two
+        halves tsb_norm_gemv_bf16 and tsb_gqa_decode_attention when the shape
+        does not fit it), the o GEMV adding into the residual and normalising it
+        for the expert layer (tsb_gemv_bf16_residual), and the expert layer
+        (fp32 output)."""
         L = _lib.lib()
         stream = torch.cuda.current_stream(self.device).cuda_stream
         xin, xout = self._xe, self._xa
         xin.copy_(self.embed.index_select(0, self._tok))
         delta = None
+        fp8 = 1 if self.kv_dtype == torch.float8_e4m3fn else 0
         for li, lay in enumerate(self.layers):
-            _lib.check(L.tsb_norm_gemv_bf16(
-                xin.data_ptr(), None if delta is None else delta.data_ptr(), xout.data_ptr(), lay["ln1"].data_ptr(),
-                self.eps, lay["wqkv"].data_ptr(), None if lay["bqkv"] is None else lay["bqkv"].data_ptr(),
-                lay["wqkv"].shape[0], self.H, self._qkv.data_ptr(), stream))
-            _lib.check(L.tsb_gqa_decode_attention(
-                self._qkv.data_ptr(), self.nq, self.nkv, self.D, self.cos.data_ptr(), self.sin.data_ptr(),
-                self._pos.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(),
-                1 if self.kv_dtype == torch.float8_e4m3fn else 0, self.max_seq,
-                self.window if self.sliding[li] else 0, lay["sinks"].data_ptr(), self.scale, self._a.data_ptr(),
-                self._aws.data_ptr(), self._aws.numel(), stream))
+            dptr = None if delta is None else delta.data_ptr()
+            bq = None if lay["bqkv"] is None else lay["bqkv"].data_ptr()
+            win = self.window if self.sliding[li] else 0
+            rc = 1
+            if self._fused is not False:
+                rc = L.tsb_norm_qkv_attention(
+                    xin.data_ptr(), dptr, xout.data_ptr(), lay["ln1"].data_ptr(), self.eps, lay["wqkv"].data_ptr(), bq,
+                    self.H, self.nq, self.nkv, self.D, self.cos.data_ptr(), self.sin.data_ptr(),
+                    self._pos.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), fp8,
+                    self.max_seq, win, lay["sinks"].data_ptr(), self.scale, self._a.data_ptr(), stream)
+                if self._fused is None and rc == _lib.TSB_ERR_UNSUPPORTED:
+                    self._fused = False  # the shape does not fit the fused kernel: two launches
+                else:
+                    _lib.check(rc)
+                    self._fused = True
+            if not self._fused:
+                _lib.check(L.tsb_norm_gemv_bf16(
+                    xin.data_ptr(), dptr, xout.data_ptr(), lay["ln1"].data_ptr(), self.eps, lay["wqkv"].data_ptr(),
+                    bq, lay["wqkv"].shape[0], self.H, self._qkv.data_ptr(), stream))
+                _lib.check(L.tsb_gqa_decode_attention(
+                    self._qkv.data_ptr(), self.nq, self.nkv, self.D, self.cos.data_ptr(), self.sin.data_ptr(),
+                    self._pos.data_ptr(), self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), fp8,
+                    self.max_seq, win, lay["sinks"].data_ptr(), self.scale, self._a.data_ptr(),
+                    self._aws.data_ptr(), self._aws.numel(), stream))
             _lib.check(L.tsb_gemv_bf16_residual(
                 lay["wo"].data_ptr(), None if lay["bo"] is None else lay["bo"].data_ptr(), self.H, self.nq * self.D,
                 self._a.data_ptr(), xout.data_ptr(), lay["ln2"].data_ptr(), self.eps, self._h.data_ptr(),
