@@ -339,6 +339,15 @@ def _config3_breakdown(dec) -> dict:
                                        dec.window if dec.sliding[li] else 0, lay["sinks"].data_ptr(), dec.scale,
                                        dec._a.data_ptr(), dec._aws.data_ptr(), dec._aws.numel(), sid())
 
+    def fused():
+        for li, lay in enumerate(dec.layers):
+            L.tsb_norm_qkv_attention(dec._xa.data_ptr(), dec._y.data_ptr(), dec._xb.data_ptr(), lay["ln1"].data_ptr(),
+                                     dec.eps, lay["wqkv"].data_ptr(), lay["bqkv"].data_ptr(), dec.H, dec.nq, dec.nkv,
+                                     dec.D, dec.cos.data_ptr(), dec.sin.data_ptr(), dec._pos.data_ptr(),
+                                     dec.k_cache[li].data_ptr(), dec.v_cache[li].data_ptr(), fp8, dec.max_seq,
+                                     dec.window if dec.sliding[li] else 0, lay["sinks"].data_ptr(), dec.scale,
+                                     dec._a.data_ptr(), sid())
+
     def oproj():
         for lay in dec.layers:
             L.tsb_gemv_bf16_residual(lay["wo"].data_ptr(), lay["bo"].data_ptr(), dec.H, dec.nq * dec.D,
@@ -354,7 +363,8 @@ def _config3_breakdown(dec) -> dict:
 
     res = {}
     st = torch.cuda.Stream(dec.device)
-    for name, fn, per in (("qkv_norm_gemv", qkv, 24), ("attention", attn, 24), ("o_residual_gemv", oproj, 24),
+    for name, fn, per in (("qkv_norm_gemv", qkv, 24), ("attention", attn, 24),
+                          ("norm_qkv_attention_fused", fused, 24), ("o_residual_gemv", oproj, 24),
                           ("expert_layer", experts, 24), ("lm_head", head, 1)):
         with torch.cuda.stream(st):
             fn()
@@ -429,6 +439,7 @@ def run_config3(dev, steps: int = 64, warmup: int = 8, ctx: int = C3_CTX):
            "c3_alg_bytes_per_token": alg, "c3_achieved_gbs": achieved, "c3_frac": achieved / peak,
            "c3_moe_bytes": moe_b, "c3_kv": "float8_e4m3fn", "c3_prefill_s": prefill_s, "c3_build_s": build_s,
            "c3_launch": "one CUDA graph per token",
+           "c3_fused_qkv_attention": bool(dec._fused),
            "c3_errors": int(sum(q.device_error() for q in lm.moe_layers))}
     out.update({f"c3_us_{k}": v for k, v in _config3_breakdown(dec).items()})
     del dec
